@@ -1,0 +1,148 @@
+"""ctypes binding of ``libats_b200.so`` (the C ABI in include/ats_b200.h).
+
+The library is loaded on first use from this package's directory.  If it is
+missing the import of any op fails with an error that says how to build it:
+there is no fallback implementation behind these entry points.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from ctypes import POINTER, c_char_p, c_float, c_int, c_int64, c_size_t, c_void_p
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "libats_b200.so"
+
+ATS_OK = 0
+ATS_EBADARG = -1
+ATS_EUNSUPPORTED = -2
+ATS_ECUDA = -3
+ATS_ETIMEOUT = -4
+
+ATS_F32 = 0
+ATS_BF16 = 1
+
+_I64x3 = c_int64 * 3
+
+# name -> (restype, argtypes); mirrors include/ats_b200.h
+SIGNATURES: dict[str, tuple] = {
+    "ats_abi_version": (c_int, []),
+    "ats_strerror": (c_char_p, [c_int]),
+    "ats_last_error_message": (c_char_p, []),
+    "ats_kernel_launches": (ctypes.c_uint64, []),
+    "ats_rmsnorm_fwd": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_int, c_void_p, c_int64, c_void_p,
+                                c_int64, c_int64, c_float, c_void_p]),
+    "ats_rmsnorm_bwd_workspace_bytes": (c_size_t, [c_int64, c_int64]),
+    "ats_rmsnorm_bwd": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_void_p,
+                                c_size_t, c_int64, c_int64, c_float, c_void_p]),
+    "ats_rmsnorm_residual_fwd": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int64,
+                                         c_int64, c_float, c_void_p]),
+    "ats_rmsnorm_residual_bwd": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p,
+                                         c_void_p, c_void_p, c_size_t, c_int64, c_int64, c_float, c_void_p]),
+    "ats_rope_apply": (c_int, [c_void_p, c_void_p, c_int64, POINTER(c_int64), POINTER(c_int64),
+                               c_void_p, c_void_p, c_int64, POINTER(c_int64), POINTER(c_int64),
+                               c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int, c_int, c_void_p]),
+    "ats_moe_topk": (c_int, [c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "ats_moe_max_rows": (c_int64, [c_int64, c_int, c_int, c_int64]),
+    "ats_moe_workspace_bytes": (c_size_t, [c_int64, c_int, c_int, c_int64]),
+    "ats_moe_route_plan": (c_int, [c_void_p, c_int64, c_int, c_int, c_int64, c_float, c_void_p, c_void_p,
+                                   c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "ats_moe_gather": (c_int, [c_void_p, c_void_p, c_int, c_int64, c_int64, c_int, c_int, c_int64,
+                               c_void_p, c_size_t, c_void_p]),
+    "ats_moe_experts_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
+                                    c_int64, c_int, c_int, c_int64, c_int64, c_int64, c_void_p, c_size_t,
+                                    c_void_p]),
+    "ats_moe_combine": (c_int, [c_void_p, c_void_p, c_int, c_int64, c_int64, c_int, c_int, c_int64,
+                                c_void_p, c_size_t, c_void_p]),
+    "ats_moe_combine_bwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int64, c_int64, c_int,
+                                    c_int, c_int64, c_void_p, c_size_t, c_void_p]),
+    "ats_moe_experts_bwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                    c_void_p, c_void_p, c_void_p, c_int, c_int64, c_int, c_int, c_int64,
+                                    c_int64, c_int64, c_void_p, c_size_t, c_void_p]),
+    "ats_moe_scatter_grad": (c_int, [c_void_p, c_void_p, c_int, c_int64, c_int64, c_int, c_int, c_int64,
+                                     c_void_p, c_size_t, c_void_p]),
+    "ats_moe_route_bwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64,
+                                  c_int, c_int, c_int64, c_float, c_void_p, c_size_t, c_void_p]),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+class AtsError(RuntimeError):
+    """A non-zero status from the C ABI."""
+
+    def __init__(self, fn: str, status: int, detail: str):
+        super().__init__(f"{fn} failed: {detail} (status {status})")
+        self.status = status
+
+
+def load() -> ctypes.CDLL:
+    """Load (once) and return the library; raise if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                raise ImportError(
+                    f"{LIB_PATH} is missing. Build it with `python -m ats_v2_b200._build` "
+                    "(nvcc for sm_100a); ats_v2_b200 has no implementation without it.")
+            lib = ctypes.CDLL(os.fspath(LIB_PATH))
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = lib
+    return _lib
+
+
+def call(name: str, *args) -> None:
+    """Call a status-returning entry point; raise AtsError on failure."""
+    lib = load()
+    st = getattr(lib, name)(*args)
+    if st != ATS_OK:
+        detail = lib.ats_last_error_message().decode(errors="replace") or lib.ats_strerror(st).decode()
+        raise AtsError(name, st, detail)
+
+
+def query(name: str, *args):
+    return getattr(load(), name)(*args)
+
+
+def dtype_code(t: torch.dtype) -> int:
+    if t == torch.float32:
+        return ATS_F32
+    if t == torch.bfloat16:
+        return ATS_BF16
+    raise TypeError(f"ats_v2_b200 kernels take float32 or bfloat16 tensors, got {t}")
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def stream_of(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def strides3(*s: int):
+    return _I64x3(*s)
+
+
+def require_cuda(name: str, *tensors: torch.Tensor) -> None:
+    """Every tensor must live on one CUDA device: there is no CPU path."""
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError(f"{name}: ats_v2_b200 runs on CUDA tensors only (got a {t.device} tensor)")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError(f"{name}: tensors on different devices ({dev} and {t.device})")

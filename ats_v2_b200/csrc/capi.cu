@@ -1,0 +1,56 @@
+// Library-wide C ABI pieces: version, status strings, last-error text, SM count.
+#include "common.cuh"
+
+#include <atomic>
+#include <string.h>
+
+namespace ats {
+
+static thread_local char g_last_error[512] = "";
+static std::atomic<unsigned long long> g_launches{0};
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+}
+
+int num_sms() {
+  // Per-device cache; device ordinals are small.  Written before first read
+  // on each thread that asks, and the value never changes, so a benign race.
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+}  // namespace ats
+
+extern "C" {
+
+int ats_abi_version(void) { return ATS_ABI_VERSION; }
+
+const char* ats_strerror(int status) {
+  switch (status) {
+    case ATS_OK: return "ok";
+    case ATS_EBADARG: return "invalid argument";
+    case ATS_EUNSUPPORTED: return "unsupported configuration";
+    case ATS_ECUDA: return "CUDA error";
+    case ATS_ETIMEOUT: return "device wait timed out";
+    default: return "unknown status";
+  }
+}
+
+const char* ats_last_error_message(void) { return ats::g_last_error; }
+
+uint64_t ats_kernel_launches(void) { return ats::g_launches.load(std::memory_order_relaxed); }
+
+}  // extern "C"

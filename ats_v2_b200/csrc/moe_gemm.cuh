@@ -1,0 +1,37 @@
+// Shared pieces of the expert GEMM paths.
+#pragma once
+
+#include "moe_plan.cuh"
+
+namespace ats {
+
+// a = round(round(silu(g)) * u): torch's silu (x / (1 + exp(-x)), float32 math,
+// rounded to T) followed by the product rounded to T (ffn.py:44).
+template <typename T>
+__device__ __forceinline__ float silu_mul(float g, float u) {
+  const float s = round_to<T>(g / (1.0f + expf(-g)));
+  return round_to<T>(s * u);
+}
+
+// Gradients of a = round(round(silu(g)) * u) for upstream da:
+//   du = round(da * s), ds = round(da * u), dg = round(ds * sig * (1 + g * (1 - sig)))
+// (torch's mul and silu_backward formulas, float32 math rounded to T).
+template <typename T>
+__device__ __forceinline__ void swiglu_grad(float g, float u, float da, float& dg, float& du) {
+  const float e = expf(-g);
+  const float s = round_to<T>(g / (1.0f + e));
+  const float sig = 1.0f / (1.0f + e);
+  du = round_to<T>(da * s);
+  const float ds = round_to<T>(da * u);
+  dg = round_to<T>((ds * sig) * (1.0f + g * (1.0f - sig)));
+}
+
+// tcgen05 tensor-core expert GEMMs (bf16).  Return ATS_EUNSUPPORTED for shapes
+// the tensor-core tiling does not cover; the caller then uses the CUDA-core path.
+int tc_experts_fwd(const void* xp, const void* wgu, const void* wd, void* h, void* a, void* y, int E, int64_t H,
+                   int64_t F, const MoePlan& plan, cudaStream_t st);
+int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a, const void* wgu, const void* wd,
+                   void* dh, void* dxp, void* dwgu, void* dwd, int E, int64_t H, int64_t F, const MoePlan& plan,
+                   cudaStream_t st);
+
+}  // namespace ats

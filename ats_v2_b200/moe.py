@@ -1,0 +1,310 @@
+"""Mixture-of-Experts layer on the sm_100a kernels -- mirror of ats/model/moe.py.
+
+``MoELayer(hidden_size, intermediate_size, num_experts, num_layers, top_k=2,
+capacity_factor=1.25, load_balancing_weight=0.01, ep_size=1, quantization)``
+keeps the reference constructor (moe.py:167-230), attribute names
+(``uses_deepspeed``, ``moe.gate``, ``moe.experts[i].gate_up_proj/down_proj``,
+``moe.compute_routing``, ``last_expert_utilization``) and the forward
+contract ``(output [B,S,H], aux_loss scalar)`` (moe.py:232-274), with the
+semantics of the single-process fallback _PyTorchMoEFallback (moe.py:36-164):
+softmax -> top-k -> renormalise, capacity ``max(1, int(cf*T*k/E))``, per expert
+the first `capacity` tokens in ascending token order, SwiGLU experts, gate-
+weighted combine in ascending expert order, Switch aux loss.
+
+What changes is how it runs.  The router is float32 (logits from a float32
+matmul of the tokens with the gate weight).  Everything after the logits is a
+fixed sequence of device stages with no host synchronisation (the reference
+synchronises once per expert in ``nonzero`` and once per expert in ``.item()``):
+route+plan+permute, gather, grouped SwiGLU experts (tcgen05 tensor cores for
+bf16), combine; the backward runs the adjoint stages.  The utilisation dict is
+filled lazily from a device tensor the first time it is read.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from ats_v2_b200 import _lib
+from ats_v2_b200.ffn import SwiGLU
+
+BASE_LINEAR_STD = 0.02
+
+
+def residual_output_std(num_layers: int) -> float:
+    """Depth-scaled std of residual-stream projections (initialization.py:541-546)."""
+    if num_layers <= 0:
+        raise ValueError(f"num_layers must be positive, got {num_layers}.")
+    return BASE_LINEAR_STD / math.sqrt(2 * num_layers)
+
+
+def init_residual_projection(module: nn.Linear, num_layers: int) -> None:
+    """N(0, residual_output_std) init, marked so a later blanket init skips it
+    (initialization.py:549-562)."""
+    nn.init.normal_(module.weight, mean=0.0, std=residual_output_std(num_layers))
+    if module.bias is not None:
+        nn.init.zeros_(module.bias)
+    module.weight._ats_residual_init = True  # type: ignore[attr-defined]
+
+
+def capacity_for(num_tokens: int, top_k: int, num_experts: int, capacity_factor: float) -> int:
+    """moe.py:103-105."""
+    return max(1, int(capacity_factor * num_tokens * top_k / num_experts))
+
+
+def stacked(params: list[torch.Tensor]) -> torch.Tensor:
+    """Return an [E, ...] tensor whose slice e IS params[e]'s storage.
+
+    If the parameters are not already consecutive views of one buffer (a fresh
+    module, or one moved with .to()), they are copied into a new stacked
+    buffer and each parameter is re-pointed at its slice, once."""
+    p0 = params[0]
+    E = len(params)
+    n = p0.numel()
+    d0 = p0.data
+    ok = d0.is_contiguous() and all(
+        p.data.is_contiguous() and p.dtype == p0.dtype and p.device == p0.device
+        and p.data.untyped_storage().data_ptr() == d0.untyped_storage().data_ptr()
+        and p.data.storage_offset() == d0.storage_offset() + e * n for e, p in enumerate(params))
+    if ok:
+        return torch.as_strided(d0, (E,) + tuple(p0.shape), (n,) + tuple(d0.stride()), d0.storage_offset())
+    stack = torch.stack([p.data for p in params])
+    for e, p in enumerate(params):
+        p.data = stack[e]
+    return stack
+
+
+class LazyUtilization(dict):
+    """dict[int, float] of per-expert utilisation, read from the device the
+    first time any entry is accessed (no synchronisation inside forward)."""
+
+    def __init__(self, t: torch.Tensor) -> None:
+        super().__init__()
+        self._t: torch.Tensor | None = t
+
+    def _fill(self) -> None:
+        if self._t is not None:
+            vals = self._t.tolist()
+            self._t = None
+            dict.update(self, {i: float(v) for i, v in enumerate(vals)})
+
+    def __getitem__(self, key):
+        self._fill()
+        return dict.__getitem__(self, key)
+
+    def __iter__(self):
+        self._fill()
+        return dict.__iter__(self)
+
+    def __len__(self):
+        self._fill()
+        return dict.__len__(self)
+
+    def __contains__(self, key):
+        self._fill()
+        return dict.__contains__(self, key)
+
+    def __eq__(self, other):
+        self._fill()
+        return dict.__eq__(self, other)
+
+    __hash__ = None  # type: ignore[assignment]
+
+    def __repr__(self):
+        self._fill()
+        return dict.__repr__(self)
+
+    def keys(self):
+        self._fill()
+        return dict.keys(self)
+
+    def values(self):
+        self._fill()
+        return dict.values(self)
+
+    def items(self):
+        self._fill()
+        return dict.items(self)
+
+    def get(self, key, default=None):
+        self._fill()
+        return dict.get(self, key, default)
+
+
+class _MoEFn(torch.autograd.Function):
+    """Device stages of the MoE layer on flattened tokens x2 [T,H].
+
+    Inputs: x2, logits [T,E] f32, meta=(E,k,C,lbw,F), the two weight stacks,
+    then the per-expert weights (only so autograd routes their gradients)."""
+
+    @staticmethod
+    def forward(ctx, x2, logits, meta, wgu_stack, wd_stack, *expert_weights):
+        E, k, C, lbw, Fdim = meta
+        T, H = x2.shape
+        dev = x2.device
+        dt = _lib.dtype_code(x2.dtype)
+        st = _lib.stream_of(x2)
+        ws_bytes = _lib.query("ats_moe_workspace_bytes", T, E, k, C)
+        max_rows = _lib.query("ats_moe_max_rows", T, E, k, C)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+        gates = torch.empty((T, k), dtype=torch.float32, device=dev)
+        idx = torch.empty((T, k), dtype=torch.int64, device=dev)
+        aux = torch.empty((), dtype=torch.float32, device=dev)
+        util = torch.empty(E, dtype=torch.float32, device=dev)
+        counts = torch.empty(E, dtype=torch.int32, device=dev)
+        _lib.call("ats_moe_route_plan", logits.data_ptr(), T, E, k, C, float(lbw), gates.data_ptr(),
+                  idx.data_ptr(), aux.data_ptr(), util.data_ptr(), counts.data_ptr(), ws.data_ptr(), ws_bytes,
+                  st)
+        xp = torch.empty((max_rows, H), dtype=x2.dtype, device=dev)
+        _lib.call("ats_moe_gather", x2.data_ptr(), xp.data_ptr(), dt, T, H, E, k, C, ws.data_ptr(), ws_bytes, st)
+        h = torch.empty((max_rows, 2 * Fdim), dtype=x2.dtype, device=dev)
+        a = torch.empty((max_rows, Fdim), dtype=x2.dtype, device=dev)
+        y = torch.empty((max_rows, H), dtype=x2.dtype, device=dev)
+        _lib.call("ats_moe_experts_fwd", xp.data_ptr(), wgu_stack.data_ptr(), wd_stack.data_ptr(), h.data_ptr(),
+                  a.data_ptr(), y.data_ptr(), dt, T, E, k, C, H, Fdim, ws.data_ptr(), ws_bytes, st)
+        out = torch.empty((T, H), dtype=x2.dtype, device=dev)
+        _lib.call("ats_moe_combine", y.data_ptr(), out.data_ptr(), dt, T, H, E, k, C, ws.data_ptr(), ws_bytes, st)
+        ctx.save_for_backward(logits, gates, idx, ws, xp, h, a, y, wgu_stack, wd_stack)
+        ctx.meta = (E, k, C, lbw, Fdim, T, H, ws_bytes, max_rows)
+        ctx.mark_non_differentiable(util, counts, idx)
+        return out, aux, util, counts, idx
+
+    @staticmethod
+    def backward(ctx, dout, daux, _dutil, _dcounts, _didx):
+        logits, gates, idx, ws, xp, h, a, y, wgu_stack, wd_stack = ctx.saved_tensors
+        E, k, C, lbw, Fdim, T, H, ws_bytes, max_rows = ctx.meta
+        dev = xp.device
+        dt = _lib.dtype_code(xp.dtype)
+        st = _lib.stream_of(xp)
+        if dout is None:
+            dout = torch.zeros((T, H), dtype=xp.dtype, device=dev)
+        dout = dout.to(xp.dtype).contiguous()
+        dy = torch.empty((max_rows, H), dtype=xp.dtype, device=dev)
+        dgate_row = torch.empty(max_rows, dtype=torch.float32, device=dev)
+        _lib.call("ats_moe_combine_bwd", dout.data_ptr(), y.data_ptr(), dy.data_ptr(), dgate_row.data_ptr(), dt,
+                  T, H, E, k, C, ws.data_ptr(), ws_bytes, st)
+        dh = torch.empty((max_rows, 2 * Fdim), dtype=xp.dtype, device=dev)
+        dxp = torch.empty((max_rows, H), dtype=xp.dtype, device=dev)
+        dwgu = torch.empty_like(wgu_stack)
+        dwd = torch.empty_like(wd_stack)
+        _lib.call("ats_moe_experts_bwd", dy.data_ptr(), xp.data_ptr(), h.data_ptr(), a.data_ptr(),
+                  wgu_stack.data_ptr(), wd_stack.data_ptr(), dh.data_ptr(), dxp.data_ptr(), dwgu.data_ptr(),
+                  dwd.data_ptr(), dt, T, E, k, C, H, Fdim, ws.data_ptr(), ws_bytes, st)
+        dx = torch.empty((T, H), dtype=xp.dtype, device=dev)
+        _lib.call("ats_moe_scatter_grad", dxp.data_ptr(), dx.data_ptr(), dt, T, H, E, k, C, ws.data_ptr(),
+                  ws_bytes, st)
+        dlogits = torch.empty((T, E), dtype=torch.float32, device=dev)
+        daux_t = daux.to(torch.float32).contiguous() if daux is not None else None
+        _lib.call("ats_moe_route_bwd", logits.data_ptr(), gates.data_ptr(), idx.data_ptr(), dgate_row.data_ptr(),
+                  _lib.ptr(daux_t), dlogits.data_ptr(), T, E, k, C, float(lbw), ws.data_ptr(), ws_bytes, st)
+        grads = [dwgu[e] for e in range(E)] + [dwd[e] for e in range(E)]
+        return (dx, dlogits, None, None, None, *grads)
+
+
+def moe_apply(x2: torch.Tensor, logits: torch.Tensor, wgu: list[torch.Tensor], wd: list[torch.Tensor],
+              top_k: int, capacity: int, lbw: float):
+    """Run the device MoE stages; returns (out [T,H], aux (0-dim), util [E], counts [E], idx [T,k])."""
+    E = len(wgu)
+    Fdim = wgu[0].shape[0] // 2
+    wgu_stack = stacked(wgu)
+    wd_stack = stacked(wd)
+    logits = logits.float().contiguous()
+    return _MoEFn.apply(x2.contiguous(), logits, (E, top_k, capacity, lbw, Fdim), wgu_stack, wd_stack,
+                        *wgu, *wd)
+
+
+def dense_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor) -> torch.Tensor:
+    """One SwiGLU FFN (ffn.py:42-44) on the grouped kernels: a single expert
+    that every token selects with gate 1.0."""
+    _lib.require_cuda("SwiGLU", x, w_gate_up, w_down)
+    H = x.shape[-1]
+    x2 = x.reshape(-1, H)
+    if x2.dtype != w_gate_up.dtype:
+        raise TypeError(f"SwiGLU: input dtype {x2.dtype} does not match weight dtype {w_gate_up.dtype}")
+    T = x2.shape[0]
+    logits = torch.zeros((T, 1), dtype=torch.float32, device=x.device)
+    out = moe_apply(x2, logits, [w_gate_up], [w_down], 1, max(1, T), 0.0)[0]
+    return out.view(x.shape)
+
+
+class _CudaMoE(nn.Module):
+    """Counterpart of _PyTorchMoEFallback (moe.py:36-164) on the device stages."""
+
+    def __init__(self, hidden_size: int, intermediate_size: int, num_experts: int, top_k: int,
+                 capacity_factor: float, load_balancing_weight: float, num_layers: int,
+                 quantization: str = "none") -> None:
+        super().__init__()
+        if not 1 <= top_k <= min(num_experts, 16):
+            raise ValueError(f"MoE top_k must be in [1, min(num_experts, 16)], got {top_k}")
+        self.hidden_size = hidden_size
+        self.intermediate_size = intermediate_size
+        self.num_experts = num_experts
+        self.top_k = top_k
+        self.capacity_factor = capacity_factor
+        self.load_balancing_weight = load_balancing_weight
+        self.gate = nn.Linear(hidden_size, num_experts, bias=False)
+        self.experts = nn.ModuleList(
+            [SwiGLU(hidden_size, intermediate_size, quantization=quantization) for _ in range(num_experts)])
+        for expert in self.experts:
+            init_residual_projection(expert.down_proj, num_layers)
+        self.last_expert_utilization: dict[int, float] | None = None
+        self.last_counts: torch.Tensor | None = None
+
+    def router_logits(self, flat_x: torch.Tensor) -> torch.Tensor:
+        """float32 router: x @ Wg^T in float32 whatever the token dtype."""
+        return F.linear(flat_x.float(), self.gate.weight.float())
+
+    def compute_routing(self, flat_x: torch.Tensor):
+        """(top_k_probs [T,k] f32, top_k_idx [T,k] int64, router_probs [T,E] f32)
+        as moe.py:76-90, on the router kernel; no gradient is tracked."""
+        _lib.require_cuda("compute_routing", flat_x)
+        with torch.no_grad():
+            logits = self.router_logits(flat_x).contiguous()
+        from ats_v2_b200.moe_fused import _topk
+
+        return _topk(logits, self.top_k, want_probs=True)
+
+    def _weights(self):
+        return ([e.gate_up_proj.weight for e in self.experts], [e.down_proj.weight for e in self.experts])
+
+    def forward(self, x: torch.Tensor):
+        batch, seq_len, hidden_size = x.shape
+        if hidden_size != self.hidden_size:
+            raise ValueError(f"MoE expected hidden_size={self.hidden_size}, got {hidden_size}.")
+        _lib.require_cuda("MoELayer", x)
+        flat_x = x.reshape(-1, hidden_size)
+        T = flat_x.shape[0]
+        cap = capacity_for(T, self.top_k, self.num_experts, self.capacity_factor)
+        wgu, wd = self._weights()
+        if wgu[0].dtype != flat_x.dtype:
+            raise TypeError(f"MoE: token dtype {flat_x.dtype} does not match expert weight dtype {wgu[0].dtype}")
+        logits = self.router_logits(flat_x)
+        out, aux, util, counts, _ = moe_apply(flat_x, logits, wgu, wd, self.top_k, cap,
+                                              self.load_balancing_weight)
+        self.last_expert_utilization = LazyUtilization(util)
+        self.last_counts = counts
+        return out.view(batch, seq_len, hidden_size), aux
+
+
+class MoELayer(nn.Module):
+    """Drop-in for ats.model.moe.MoELayer; always the CUDA path (uses_deepspeed=False)."""
+
+    def __init__(self, hidden_size: int, intermediate_size: int, num_experts: int, num_layers: int,
+                 top_k: int = 2, capacity_factor: float = 1.25, load_balancing_weight: float = 0.01,
+                 ep_size: int = 1, quantization: str = "none") -> None:
+        super().__init__()
+        self.hidden_size = hidden_size
+        self.uses_deepspeed = False
+        self.ep_size = ep_size
+        self.last_expert_utilization: dict[int, float] | None = None
+        self.load_balancing_weight = load_balancing_weight
+        self.moe = _CudaMoE(hidden_size, intermediate_size, num_experts, top_k, capacity_factor,
+                            load_balancing_weight, num_layers=num_layers, quantization=quantization)
+
+    def forward(self, x: torch.Tensor):
+        output, aux_loss = self.moe(x)
+        self.last_expert_utilization = self.moe.last_expert_utilization
+        return output, aux_loss

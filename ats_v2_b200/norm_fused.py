@@ -1,0 +1,77 @@
+"""Fused RMSNorm + residual on the sm_100a kernels -- mirror of
+ats/model/norm_triton.py.
+
+``fused_rmsnorm_residual(x, residual, weight, eps=1e-6)`` validates like the
+reference (norm_triton.py:111-120) and computes the reference's PyTorch
+formula (norm_triton.py:88-98), ``residual + (x*rsqrt(mean(x^2)+eps)).to(x.dtype)
+* weight``, with torch's type promotion at each step, in one CUDA pass.
+Unlike the reference's Triton kernel it is differentiable (x, residual and
+weight).  ``_cuda_rmsnorm_residual`` is the kernel call without validation,
+the counterpart of the reference's ``_triton_rmsnorm_residual``.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from ats_v2_b200 import _lib
+
+
+def _out_dtype(x: torch.Tensor, w: torch.Tensor) -> torch.dtype:
+    return torch.promote_types(x.dtype, w.dtype)
+
+
+class _RMSNormResidualFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, residual, weight, eps):
+        H = x.shape[-1]
+        x2 = x.reshape(-1, H).contiguous()
+        r2 = residual.reshape(-1, H).contiguous()
+        w = weight.contiguous()
+        out = torch.empty(x2.shape, dtype=_out_dtype(x, weight), device=x.device)
+        _lib.call("ats_rmsnorm_residual_fwd", x2.data_ptr(), r2.data_ptr(), _lib.dtype_code(x.dtype),
+                  w.data_ptr(), _lib.dtype_code(w.dtype), out.data_ptr(), x2.shape[0], H, float(eps),
+                  _lib.stream_of(x))
+        ctx.save_for_backward(x2, w)
+        ctx.eps = eps
+        ctx.shape = x.shape
+        return out.view(x.shape)
+
+    @staticmethod
+    def backward(ctx, dout):
+        x2, w = ctx.saved_tensors
+        rows, H = x2.shape
+        d2 = dout.reshape(rows, H).to(_out_dtype(x2, w)).contiguous()
+        dx = torch.empty_like(x2)
+        dres = torch.empty_like(x2)
+        dw = torch.empty(H, dtype=w.dtype, device=w.device)
+        ws_bytes = _lib.query("ats_rmsnorm_bwd_workspace_bytes", rows, H)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x2.device)
+        _lib.call("ats_rmsnorm_residual_bwd", d2.data_ptr(), x2.data_ptr(), _lib.dtype_code(x2.dtype),
+                  w.data_ptr(), _lib.dtype_code(w.dtype), dx.data_ptr(), dres.data_ptr(), dw.data_ptr(),
+                  ws.data_ptr(), ws_bytes, rows, H, float(ctx.eps), _lib.stream_of(x2))
+        return dx.view(ctx.shape), dres.view(ctx.shape), dw, None
+
+
+def _cuda_rmsnorm_residual(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor,
+                           eps: float) -> torch.Tensor:
+    _lib.require_cuda("fused_rmsnorm_residual", x, residual, weight)
+    if residual.dtype != x.dtype:
+        raise TypeError(f"fused_rmsnorm_residual: residual dtype {residual.dtype} must equal x dtype {x.dtype}")
+    return _RMSNormResidualFn.apply(x, residual, weight, eps)
+
+
+def fused_rmsnorm_residual(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor,
+                           eps: float = 1e-6) -> torch.Tensor:
+    """``residual + rms_norm(x) * weight`` in one memory pass (CUDA tensors only)."""
+    if x.shape != residual.shape:
+        raise ValueError(
+            f"fused_rmsnorm_residual: x shape {tuple(x.shape)} must match "
+            f"residual shape {tuple(residual.shape)}."
+        )
+    if weight.shape[-1] != x.shape[-1]:
+        raise ValueError(
+            f"fused_rmsnorm_residual: weight last dim {weight.shape[-1]} must match "
+            f"x last dim {x.shape[-1]}."
+        )
+    return _cuda_rmsnorm_residual(x, residual, weight, eps)

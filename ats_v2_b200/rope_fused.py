@@ -1,0 +1,35 @@
+"""Single-tensor fused RoPE -- mirror of ats/model/rope_triton.py.
+
+``fused_apply_rope(x, cos, sin)`` validates like rope_triton.py:203-212 and
+applies the rotate-half rotation of rope.py:83-86 to one [B,H,S,D] tensor in
+one CUDA pass, reading x through its strides (the reference's Triton wrapper
+copied x to contiguous first, rope_triton.py:170).  It is differentiable.
+``_cuda_apply_rope`` is the kernel call without validation, the counterpart
+of the reference's ``_triton_apply_rope``.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from ats_v2_b200.rope import _prepare, _RopeFn
+
+
+def _cuda_apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    x, _, cos, sin, cs = _prepare(x, None, cos, sin, "fused_apply_rope")
+    return _RopeFn.apply(x, None, cos, sin, cs)[0]
+
+
+def fused_apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """RoPE on x [batch, heads, seq_len, head_dim] with cos/sin [seq_len, head_dim] (CUDA only)."""
+    if x.dim() != 4:
+        raise ValueError(
+            f"fused_apply_rope expected x of shape [batch, heads, seq_len, head_dim], "
+            f"got {tuple(x.shape)}."
+        )
+    if x.shape[-1] != cos.shape[-1]:
+        raise ValueError(
+            f"fused_apply_rope: x head_dim ({x.shape[-1]}) must match cos/sin dim "
+            f"({cos.shape[-1]})."
+        )
+    return _cuda_apply_rope(x, cos, sin)

@@ -1,0 +1,622 @@
+"""Benchmark of the ats-v2 hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+
+Workloads (synthetic, seeded; the reference publishes no dataset for this path):
+  rmsnorm   RMSNorm forward+backward, x [4,4096,4096] bf16, weight fp32, eps 1e-5
+            (metric: HBM GB/s of algorithmic traffic)                       -- default
+  rope      fused q/k RoPE forward+backward, q [4,4096,32,128], k [4,4096,8,128]
+            bf16, theta 5e5 (metric: HBM GB/s)
+  moe       MoE layer forward+backward, 8192 tokens, hidden 2048, 8 experts
+            top-2, ffn 5632, bf16, fp32 router, no capacity drop (metric: tokens/s)
+
+One JSON line is printed by rank 0.  ``value`` is the device-timed throughput
+with inputs resident in HBM (CUDA events on the launching stream, K steps
+after W warm-up steps, barrier + synchronize on both sides, max over ranks);
+``e2e`` is the same metric through the public module API with pinned host
+inputs copied in and all results copied out inside the timed region;
+``roofline`` times the dominant kernel with CUDA events inside the timed
+region; ``cpu_baseline`` times the numpy restatement of the reference's
+algorithm (``oracle/``) on the host cores on a bounded sample.  With the
+default workload the line also carries ``extras`` with the other two
+workloads measured the same way.  Under torchrun every rank runs its own
+shard (weak scaling, no collective on the data path).
+
+``--impl reference`` times the reference's algorithm on the host CPU (the
+oracle port; the reference itself is Python and is not present here) on the
+same metric, rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from concurrent.futures import ThreadPoolExecutor
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks() -> tuple[dict, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()), "measured"
+        except Exception:
+            pass
+    return dict(PEAKS_FALLBACK), "fallback"
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        time.sleep(0.25)
+        return self
+
+    def __exit__(self, *exc):
+        self.summary = {"error": "nvidia-smi unavailable"}
+        if self.proc is None:
+            return False
+        time.sleep(0.15)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out = ""
+        mhz, mx, reasons, power = [], None, set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                mhz.append(float(parts[1]))
+                mx = float(parts[2])
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[4:8]):
+                if v.lower() in ("active", "1", "yes"):
+                    reasons.add(nm)
+        if mhz:
+            self.summary = {"sm_mhz": statistics.median(mhz), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                            "samples": len(mhz), "power_w_max": max(power) if power else None}
+        return False
+
+
+# ---------------------------------------------------------------- helpers
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def cpu_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def run_threads(fn, chunks, threads):
+    with ThreadPoolExecutor(max_workers=threads) as ex:
+        return list(ex.map(fn, chunks))
+
+
+# ---------------------------------------------------------------- workloads
+class Workload:
+    name = ""
+    metric = ""
+    unit = ""
+    dtype = "bf16"
+
+    def __init__(self, torch, rank: int, world: int, peaks: dict, peaks_kind: str):
+        self.torch = torch
+        self.rank, self.world = rank, world
+        self.peaks, self.peaks_kind = peaks, peaks_kind
+
+
+class RMSNormWorkload(Workload):
+    name = "rmsnorm"
+    metric = "rmsnorm_fwd_bwd_hbm_gbs"
+    unit = "GB/s"
+    ROWS, H = 16384, 4096
+
+    def bytes_per_step(self) -> int:
+        # fwd: read x, write y; bwd: read x, dy, write dx; + w read twice, dw write (fp32)
+        n = self.ROWS * self.H * 2
+        return 5 * n + 3 * self.H * 4
+
+    def config(self):
+        return {"workload": "RMSNorm fwd+bwd, x[4,4096,4096] bf16, weight fp32, eps 1e-5",
+                "rows": self.ROWS, "hidden": self.H, "per_rank": "full workload per GPU (replicas)",
+                "l2": "inputs larger than L2 (x and dy 134 MB each)"}
+
+    def setup(self):
+        t = self.torch
+        from ats_v2_b200.norm import RMSNorm
+        g = t.Generator(device="cuda").manual_seed(self.rank)
+        self.x = t.randn(self.ROWS, self.H, device="cuda", generator=g).bfloat16().requires_grad_()
+        self.dy = t.randn(self.ROWS, self.H, device="cuda", generator=g).bfloat16()
+        self.mod = RMSNorm(self.H, eps=1e-5).cuda()
+        with t.no_grad():
+            self.mod.weight.copy_(1 + 0.02 * t.randn(self.H, device="cuda", generator=g))
+
+    def step(self, evs):
+        y = self.mod(self.x)
+        self.x.grad = None
+        self.mod.weight.grad = None
+        if evs:
+            evs[0].record()
+        y.backward(self.dy)
+        if evs:
+            evs[1].record()
+
+    def dominant(self):
+        # rmsnorm_bwd_kernel (+ the tiny dw reduce): reads x, dy, writes dx
+        return {"kernel": "rmsnorm_bwd_kernel<bf16,float>", "bytes": 3 * self.ROWS * self.H * 2 + 2 * self.H * 4,
+                "bound": "hbm"}
+
+    # e2e through the public module with pinned host buffers
+    def e2e_setup(self):
+        t = self.torch
+        self.hx = self.x.detach().cpu().pin_memory()
+        self.hdy = self.dy.cpu().pin_memory()
+        self.hy = t.empty_like(self.hx).pin_memory()
+        self.hdx = t.empty_like(self.hx).pin_memory()
+        self.hdw = t.empty(self.H, dtype=t.float32).pin_memory()
+        self.dx_in = t.empty_like(self.x.detach())
+        self.ddy = t.empty_like(self.dy)
+        self.h2d = self.hx.numel() * 2 + self.hdy.numel() * 2
+        self.d2h = self.hy.numel() * 2 + self.hdx.numel() * 2 + self.H * 4
+
+    def e2e_step(self):
+        self.dx_in.copy_(self.hx, non_blocking=True)
+        self.ddy.copy_(self.hdy, non_blocking=True)
+        x = self.dx_in.requires_grad_()
+        self.mod.weight.grad = None
+        y = self.mod(x)
+        y.backward(self.ddy)
+        self.hy.copy_(y.detach(), non_blocking=True)
+        self.hdx.copy_(x.grad, non_blocking=True)
+        self.hdw.copy_(self.mod.weight.grad, non_blocking=True)
+        x.grad = None
+        x.requires_grad_(False)
+
+    def units_to_value(self, steps, ms):  # GB/s over all work
+        return self.bytes_per_step() * steps / (ms * 1e-3) / 1e9
+
+    # CPU restatement timed on host cores (bounded sample of rows)
+    def cpu_baseline(self, seconds: float):
+        from oracle import norm as onorm
+        from oracle.bf16 import round_bf16
+        threads = cpu_threads()
+        rows = 64 * threads
+        rng = np.random.default_rng(0)
+        x = round_bf16(rng.standard_normal((rows, self.H)).astype(np.float32))
+        dy = round_bf16(rng.standard_normal((rows, self.H)).astype(np.float32))
+        w = (1 + 0.02 * rng.standard_normal(self.H)).astype(np.float32)
+        parts = np.array_split(np.arange(rows), threads)
+
+        def work(ix):
+            onorm.rmsnorm_fwd(x[ix], w, 1e-5, "bf16")
+            onorm.rmsnorm_bwd(dy[ix], x[ix], w, 1e-5, "bf16", "f32")
+
+        t0 = time.perf_counter()
+        n = 0
+        while True:
+            run_threads(work, parts, threads)
+            n += 1
+            if time.perf_counter() - t0 >= seconds:
+                break
+        dt = time.perf_counter() - t0
+        bytes_ = (5 * rows * self.H * 2 + 3 * self.H * 4) * n
+        return {"value": bytes_ / dt / 1e9, "unit": self.unit, "cores": threads, "kind": "port",
+                "sample": f"{rows} of {self.ROWS} rows per pass, {n} passes in {dt:.1f} s (numpy oracle, "
+                          f"{threads} threads)"}
+
+
+class RopeWorkload(Workload):
+    name = "rope"
+    metric = "rope_qk_fwd_bwd_hbm_gbs"
+    unit = "GB/s"
+    B, S, HQ, HK, D = 4, 4096, 32, 8, 128
+
+    def bytes_per_step(self) -> int:
+        n = self.B * self.S * (self.HQ + self.HK) * self.D * 2
+        return 4 * n  # fwd read+write, bwd read+write
+
+    def config(self):
+        return {"workload": "q/k RoPE fwd+bwd, q[4,4096,32,128] k[4,4096,8,128] bf16 BSHD views, theta 5e5",
+                "per_rank": "full workload per GPU (replicas)", "l2": "inputs larger than L2 (q 134 MB)"}
+
+    def setup(self):
+        t = self.torch
+        from ats_v2_b200.rope import RotaryEmbedding, apply_rotary_pos_emb
+        self.apply = apply_rotary_pos_emb
+        g = t.Generator(device="cuda").manual_seed(self.rank)
+        self.qm = t.randn(self.B, self.S, self.HQ, self.D, device="cuda", generator=g).bfloat16()
+        self.km = t.randn(self.B, self.S, self.HK, self.D, device="cuda", generator=g).bfloat16()
+        self.gq = t.randn(self.B, self.HQ, self.S, self.D, device="cuda", generator=g).bfloat16()
+        self.gk = t.randn(self.B, self.HK, self.S, self.D, device="cuda", generator=g).bfloat16()
+        self.rope = RotaryEmbedding(self.D, self.S, 500000.0).cuda()
+
+    def step(self, evs):
+        t = self.torch
+        q = self.qm.transpose(1, 2).requires_grad_()
+        k = self.km.transpose(1, 2).requires_grad_()
+        cos, sin = self.rope(self.S, self.qm.device, t.bfloat16)
+        if evs:
+            evs[0].record()
+        qo, ko = self.apply(q, k, cos, sin)
+        if evs:
+            evs[1].record()
+        t.autograd.backward([qo, ko], [self.gq, self.gk])
+
+    def dominant(self):
+        return {"kernel": "rope_vec_kernel<bf16> (forward launch)", "bytes": self.bytes_per_step() // 2,
+                "bound": "hbm"}
+
+    def e2e_setup(self):
+        t = self.torch
+        self.hq = self.qm.cpu().pin_memory()
+        self.hk = self.km.cpu().pin_memory()
+        self.hgq = self.gq.cpu().pin_memory()
+        self.hgk = self.gk.cpu().pin_memory()
+        self.hqo = t.empty(self.gq.shape, dtype=t.bfloat16).pin_memory()
+        self.hko = t.empty(self.gk.shape, dtype=t.bfloat16).pin_memory()
+        self.hdq = t.empty_like(self.hq).pin_memory()
+        self.hdk = t.empty_like(self.hk).pin_memory()
+        self.dq_in, self.dk_in = t.empty_like(self.qm), t.empty_like(self.km)
+        self.dgq, self.dgk = t.empty_like(self.gq), t.empty_like(self.gk)
+        n = (self.hq.numel() + self.hk.numel()) * 2
+        self.h2d = 2 * n
+        self.d2h = 2 * n
+
+    def e2e_step(self):
+        t = self.torch
+        for dst, src in ((self.dq_in, self.hq), (self.dk_in, self.hk), (self.dgq, self.hgq), (self.dgk, self.hgk)):
+            dst.copy_(src, non_blocking=True)
+        q = self.dq_in.transpose(1, 2).requires_grad_()
+        k = self.dk_in.transpose(1, 2).requires_grad_()
+        cos, sin = self.rope(self.S, self.qm.device, t.bfloat16)
+        qo, ko = self.apply(q, k, cos, sin)
+        t.autograd.backward([qo, ko], [self.dgq, self.dgk])
+        self.hqo.copy_(qo.detach(), non_blocking=True)
+        self.hko.copy_(ko.detach(), non_blocking=True)
+        self.hdq.copy_(q.grad.transpose(1, 2), non_blocking=True)
+        self.hdk.copy_(k.grad.transpose(1, 2), non_blocking=True)
+
+    def units_to_value(self, steps, ms):
+        return self.bytes_per_step() * steps / (ms * 1e-3) / 1e9
+
+    def cpu_baseline(self, seconds: float):
+        from oracle import rope as orope
+        from oracle.bf16 import round_bf16
+        threads = cpu_threads()
+        pos = 8 * threads
+        rng = np.random.default_rng(0)
+        q = round_bf16(rng.standard_normal((1, self.HQ, pos, self.D)).astype(np.float32))
+        k = round_bf16(rng.standard_normal((1, self.HK, pos, self.D)).astype(np.float32))
+        cos, sin = orope.cos_sin_cache(pos, self.D, 500000.0, "bf16")
+        parts = np.array_split(np.arange(pos), threads)
+
+        def work(ix):
+            for x in (q[:, :, ix], k[:, :, ix]):
+                y = orope.rope_fwd(x, cos[ix], sin[ix], "bf16")
+                orope.rope_bwd(y, cos[ix], sin[ix], "bf16")
+
+        t0 = time.perf_counter()
+        n = 0
+        while True:
+            run_threads(work, parts, threads)
+            n += 1
+            if time.perf_counter() - t0 >= seconds:
+                break
+        dt = time.perf_counter() - t0
+        bytes_ = 4 * pos * (self.HQ + self.HK) * self.D * 2 * n
+        return {"value": bytes_ / dt / 1e9, "unit": self.unit, "cores": threads, "kind": "port",
+                "sample": f"{pos} of {self.B * self.S} (batch, position) rows of q and k per pass, {n} passes "
+                          f"in {dt:.1f} s (numpy oracle, {threads} threads)"}
+
+
+class MoEWorkload(Workload):
+    name = "moe"
+    metric = "moe_layer_fwd_bwd_tokens_per_s"
+    unit = "tokens/s"
+    T, H, F, E, K = 8192, 2048, 5632, 8, 2
+
+    def flops_per_step(self) -> int:
+        return 3 * 6 * self.T * self.K * self.H * self.F  # expert GEMMs, fwd + bwd
+
+    def config(self):
+        return {"workload": "MoE layer fwd+bwd, 8192 tokens, hidden 2048, 8 experts top-2, ffn 5632, bf16, "
+                            "fp32 router, capacity factor E/k (no drop)",
+                "per_rank": "full workload per GPU (replicas)",
+                "l2": "inputs larger than L2 (expert weights 553 MB)"}
+
+    def setup(self):
+        t = self.torch
+        from ats_v2_b200.moe import MoELayer
+        t.manual_seed(1000 + self.rank)
+        layer = MoELayer(self.H, self.F, self.E, num_layers=2, top_k=self.K, capacity_factor=self.E / self.K)
+        with t.no_grad():
+            layer.moe.gate.weight.normal_(0, 0.02)
+            for ex in layer.moe.experts:
+                ex.gate_up_proj.weight.normal_(0, 0.02)
+                ex.down_proj.weight.normal_(0, 0.02)
+        self.layer = layer.cuda()
+        self.layer.moe.experts.to(t.bfloat16)
+        g = t.Generator(device="cuda").manual_seed(self.rank)
+        self.x = t.randn(1, self.T, self.H, device="cuda", generator=g).bfloat16().requires_grad_()
+        self.dy = t.randn(1, self.T, self.H, device="cuda", generator=g).bfloat16()
+        self.one = t.ones((), device="cuda")
+
+    def _zero(self):
+        for p in self.layer.parameters():
+            p.grad = None
+
+    def step(self, evs):
+        t = self.torch
+        self._zero()
+        self.x.grad = None
+        if evs:
+            evs[0].record()
+        out, aux = self.layer(self.x)
+        t.autograd.backward([out, aux], [self.dy, self.one])
+        if evs:
+            evs[1].record()
+
+    def dominant(self):
+        return {"kernel": "expert grouped GEMMs (whole layer fwd+bwd timed)", "flops": self.flops_per_step(),
+                "bound": "tensor"}
+
+    def e2e_setup(self):
+        t = self.torch
+        self.hx = self.x.detach().cpu().pin_memory()
+        self.hdy = self.dy.cpu().pin_memory()
+        self.hout = t.empty_like(self.hx).pin_memory()
+        self.hdx = t.empty_like(self.hx).pin_memory()
+        self.haux = t.empty((), dtype=t.float32).pin_memory()
+        self.dx_in = t.empty_like(self.x.detach())
+        self.ddy = t.empty_like(self.dy)
+        self.h2d = 2 * self.hx.numel() * 2
+        self.d2h = 2 * self.hx.numel() * 2 + 4
+
+    def e2e_step(self):
+        t = self.torch
+        self.dx_in.copy_(self.hx, non_blocking=True)
+        self.ddy.copy_(self.hdy, non_blocking=True)
+        x = self.dx_in.requires_grad_()
+        self._zero()
+        out, aux = self.layer(x)
+        t.autograd.backward([out, aux], [self.ddy, self.one])
+        self.hout.copy_(out.detach(), non_blocking=True)
+        self.hdx.copy_(x.grad, non_blocking=True)
+        self.haux.copy_(aux.detach(), non_blocking=True)
+        x.grad = None
+        x.requires_grad_(False)
+
+    def units_to_value(self, steps, ms):
+        return self.T * steps / (ms * 1e-3)
+
+    def cpu_baseline(self, seconds: float):
+        from oracle import moe as omoe
+        from oracle.bf16 import round_bf16
+        threads = cpu_threads()
+        T = 256
+        rng = np.random.default_rng(0)
+        x = round_bf16(rng.standard_normal((T, self.H)).astype(np.float32))
+        wg = (0.02 * rng.standard_normal((self.E, self.H))).astype(np.float32)
+        wgu = round_bf16((0.02 * rng.standard_normal((self.E, 2 * self.F, self.H))).astype(np.float32))
+        wd = round_bf16((0.02 * rng.standard_normal((self.E, self.H, self.F))).astype(np.float32))
+        dy = round_bf16(rng.standard_normal((T, self.H)).astype(np.float32))
+        t0 = time.perf_counter()
+        n = 0
+        while True:
+            logits = omoe.router_logits(x, wg)
+            fwd = omoe.moe_forward(x, logits, wgu, wd, self.K, self.E / self.K, 0.01, "bf16")
+            omoe.moe_layer_backward_full(dy, fwd, x, wg, wgu, wd, 0.01, "bf16")
+            n += 1
+            if time.perf_counter() - t0 >= seconds:
+                break
+        dt = time.perf_counter() - t0
+        return {"value": T * n / dt, "unit": self.unit, "cores": threads, "kind": "port",
+                "sample": f"{T} of {self.T} tokens per pass (full expert weights), {n} passes in {dt:.1f} s "
+                          f"(numpy oracle, BLAS on {threads} threads)"}
+
+
+WORKLOADS = {"rmsnorm": RMSNormWorkload, "rope": RopeWorkload, "moe": MoEWorkload}
+
+
+# ---------------------------------------------------------------- timing
+def timed(torch, dist, fn, steps: int, warmup: int, probe: bool = False):
+    """Run warmup then `steps` calls of fn(evs); returns (max-over-ranks ms,
+    mean probe ms).  With probe=True each timed call gets its own CUDA event
+    pair, recorded on the launching (current) stream around the probed call."""
+    for _ in range(warmup):
+        fn(None)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+             for _ in range(steps)] if probe else [None] * steps
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(steps):
+        fn(pairs[i])
+    e.record()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e)
+    pms = statistics.mean(a.elapsed_time(b) for a, b in pairs) if probe else None
+    if dist is not None:
+        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms, pms
+
+
+def measure(torch, dist, wl: Workload, steps: int, warmup: int, world: int, with_cpu: bool, cpu_seconds: float,
+            gpu_index: int, lib) -> dict:
+    wl.setup()
+    for _ in range(warmup):
+        wl.step(None)
+    torch.cuda.synchronize()
+    with ClockSampler(gpu_index) as clk:
+        launches0 = lib.ats_kernel_launches()
+        ms, kms = timed(torch, dist, wl.step, steps, 0, probe=True)
+        launches = lib.ats_kernel_launches() - launches0
+    clocks = clk.summary
+    value = wl.units_to_value(steps, ms) * world
+    res = {"metric": wl.metric, "value": value, "unit": wl.unit, "ms_per_step": ms / steps,
+           "higher_is_better": True, "dtype": wl.dtype, "config": wl.config(), "clocks": clocks,
+           "gpu_launches": int(launches)}
+    dom = wl.dominant()
+    if kms:
+        if dom["bound"] == "hbm":
+            ach = dom["bytes"] / (kms * 1e-3) / 1e9
+            peak = wl.peaks["hbm_gbs"]
+            res["roofline"] = {"bound": "hbm", "kernel": dom["kernel"], "achieved": ach, "peak": peak,
+                               "unit": "GB/s", "frac": ach / peak, "peak_source": wl.peaks_kind,
+                               "traffic": None, "algorithmic_bytes": dom["bytes"], "kernel_ms": kms}
+        else:
+            ach = dom["flops"] / (kms * 1e-3) / 1e12
+            peak = wl.peaks.get("bf16_tflops_sustained", wl.peaks["bf16_tflops"])
+            res["roofline"] = {"bound": "tensor", "kernel": dom["kernel"], "achieved": ach, "peak": peak,
+                               "unit": "TFLOP/s", "frac": ach / peak, "peak_source": wl.peaks_kind + " sustained",
+                               "traffic": None, "algorithmic_flops": dom["flops"], "kernel_ms": kms}
+    # end to end through the public module with host buffers
+    wl.e2e_setup()
+    e2e_steps = max(3, min(steps, 10))
+    ems, _ = timed(torch, dist, lambda evs: wl.e2e_step(), e2e_steps, 2)
+    res["e2e"] = {"value": wl.units_to_value(e2e_steps, ems) * world, "unit": wl.unit,
+                  "h2d_bytes_per_step": int(wl.h2d), "d2h_bytes_per_step": int(wl.d2h),
+                  "ms_per_step": ems / e2e_steps}
+    if with_cpu:
+        try:
+            res["cpu_baseline"] = wl.cpu_baseline(cpu_seconds)
+        except Exception as exc:  # a baseline failure must not hide the GPU number
+            res["cpu_baseline"] = {"error": repr(exc)[:300]}
+    return res
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser(description="ats-v2 hot path benchmark on B200")
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="rmsnorm", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-extras", action="store_true", help="only the selected workload")
+    ap.add_argument("--cpu-seconds", type=float, default=8.0)
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+    world, rank, local = dist_env()
+    peaks, pk = load_peaks()
+
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        return reference_arm(args, world, peaks, pk)
+
+    import torch
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as tdist
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                 device_id=torch.device("cuda", local))
+        dist = tdist
+    from ats_v2_b200 import _lib
+    lib = _lib.load()
+    gpu_index = int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local]) \
+        if os.environ.get("CUDA_VISIBLE_DEVICES") else local
+    main_wl = WORKLOADS[args.workload](torch, rank, world, peaks, pk)
+    with_cpu = (world == 1 and rank == 0)
+    res = measure(torch, dist, main_wl, args.steps, args.warmup, world, with_cpu, args.cpu_seconds, gpu_index, lib)
+    line = {"metric": res["metric"], "value": res["value"], "unit": res["unit"], "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_per_step"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": res["dtype"],
+            "data": "synthetic (seeded normal inputs of the config's shapes)", "config": res["config"],
+            "e2e": res["e2e"], "roofline": res.get("roofline"), "clocks": res["clocks"],
+            "gpu_launches": res["gpu_launches"]}
+    if "cpu_baseline" in res:
+        line["cpu_baseline"] = res["cpu_baseline"]
+    if not args.no_extras:
+        extras = {}
+        for name, cls in WORKLOADS.items():
+            if name == args.workload:
+                continue
+            try:
+                wl = cls(torch, rank, world, peaks, pk)
+                extras[name] = measure(torch, dist, wl, args.steps, args.warmup, world, with_cpu,
+                                       args.cpu_seconds, gpu_index, lib)
+                del wl
+                torch.cuda.empty_cache()
+            except Exception as exc:
+                extras[name] = {"error": repr(exc)[:400]}
+        line["extras"] = extras
+    if rank == 0:
+        print(json.dumps(line))
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def reference_arm(args, world: int, peaks: dict, pk: str) -> int:
+    """The reference's algorithm (numpy oracle port) on the host cores, same metric/config."""
+    wl = WORKLOADS[args.workload](None, 0, 1, peaks, pk)
+    per_step = max(1.0, min(10.0, 150.0 / max(1, args.steps + args.warmup)))
+    for _ in range(args.warmup):
+        wl.cpu_baseline(per_step * 0.25)
+    vals = [wl.cpu_baseline(per_step) for _ in range(args.steps)]
+    v = statistics.mean(x["value"] for x in vals)
+    base = dict(vals[-1])
+    base["value"] = v
+    line = {"impl": "reference", "metric": wl.metric, "value": v, "unit": wl.unit, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic (seeded normal inputs of the config's shapes)",
+            "config": wl.config(), "cpu_baseline": base,
+            "e2e": {"value": v, "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

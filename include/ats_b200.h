@@ -1,0 +1,202 @@
+/*
+ * ats_b200 -- C ABI of the B200 (sm_100a) kernels for the ats-v2 hot path:
+ * RMSNorm, rotary embedding and the MoE layer (router, permutation, grouped
+ * SwiGLU experts, combine), forward and backward.
+ *
+ * Conventions
+ *   - Every function returns an int status: ATS_OK (0) or a negative ATS_E*
+ *     code; ats_last_error_message() gives the detail for this host thread.
+ *   - All tensor pointers are device pointers.  The caller allocates every
+ *     output and workspace buffer (sizes from the *_workspace_bytes queries);
+ *     the library allocates nothing, frees nothing and never synchronises.
+ *   - `stream` is a cudaStream_t passed as void*; NULL is the legacy stream.
+ *     All work is enqueued on it; calls are re-entrant.
+ *   - Arguments are validated on the host before any launch; a bad argument
+ *     returns ATS_EBADARG and launches nothing.
+ *   - Shapes follow the reference: rows x hidden for norms, [B,H,S,D] views for
+ *     RoPE (strides in elements, last dim contiguous), [T,E] router logits.
+ *
+ * Each entry point names the reference interface (file:line within the
+ * ats-v2 project) whose computation it performs.
+ */
+#ifndef ATS_B200_H
+#define ATS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ATS_OK 0
+#define ATS_EBADARG (-1)      /* invalid shape, stride, dtype or pointer */
+#define ATS_EUNSUPPORTED (-2) /* valid request this build does not implement */
+#define ATS_ECUDA (-3)        /* a CUDA launch or runtime call failed */
+#define ATS_ETIMEOUT (-4)     /* a bounded device-side wait gave up */
+
+#define ATS_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define ATS_API __attribute__((visibility("default")))
+#else
+#define ATS_API
+#endif
+
+typedef enum ats_dtype { ATS_F32 = 0, ATS_BF16 = 1 } ats_dtype;
+
+ATS_API int ats_abi_version(void);
+ATS_API const char* ats_strerror(int status);
+ATS_API const char* ats_last_error_message(void);
+/* Number of kernels this library has launched in this process (all devices,
+ * all threads); a benchmark reads it before and after a timed region. */
+ATS_API uint64_t ats_kernel_launches(void);
+
+/* ------------------------------------------------------------------ RMSNorm
+ * y = round(x * rsqrt(mean(x^2) + eps) * w), float32 arithmetic, one rounding
+ * to x's dtype.  Replaces RMSNorm.forward, ats/model/norm.py:23-31 (F.rms_norm).
+ * x, y: rows x hidden with row strides in elements; w: [hidden] in w_dtype.
+ * rstd: optional [rows] float32 output (may be NULL). */
+ATS_API int ats_rmsnorm_fwd(const void* x, int64_t x_row_stride, ats_dtype x_dtype,
+                    const void* w, ats_dtype w_dtype,
+                    void* y, int64_t y_row_stride,
+                    float* rstd, int64_t rows, int64_t hidden, float eps, void* stream);
+
+/* Backward of ats_rmsnorm_fwd (autograd of ats/model/norm.py:31):
+ *   dx = r*dy*w - x*r^3/H*sum(dy*w*x)   (rounded to x dtype)
+ *   dw = sum_rows dy*x*r                 (float32 accumulate, rounded to w dtype)
+ * rstd is recomputed from x.  Needs ats_rmsnorm_bwd_workspace_bytes() of
+ * workspace (per-block dw partial sums, reduced in a fixed order, so dw is
+ * deterministic). */
+ATS_API size_t ats_rmsnorm_bwd_workspace_bytes(int64_t rows, int64_t hidden);
+ATS_API int ats_rmsnorm_bwd(const void* dy, const void* x, ats_dtype x_dtype,
+                    const void* w, ats_dtype w_dtype,
+                    void* dx, void* dw,
+                    void* workspace, size_t workspace_bytes,
+                    int64_t rows, int64_t hidden, float eps, void* stream);
+
+/* ------------------------------------------------------ RMSNorm + residual
+ * out = residual + (x*rsqrt(mean(x^2)+eps)).to(x.dtype) * w with torch type
+ * promotion at each step.  Replaces fused_rmsnorm_residual,
+ * ats/model/norm_triton.py:101-123 (math of _pytorch_rmsnorm_residual :88-98).
+ * x and residual are contiguous rows x hidden of x_dtype; out has dtype
+ * promote(x_dtype, w_dtype). */
+ATS_API int ats_rmsnorm_residual_fwd(const void* x, const void* residual, ats_dtype x_dtype,
+                             const void* w, ats_dtype w_dtype, void* out,
+                             int64_t rows, int64_t hidden, float eps, void* stream);
+
+/* Backward: dx (x dtype), dresidual (x dtype), dw (w dtype). dout has dtype
+ * promote(x_dtype, w_dtype).  Workspace as ats_rmsnorm_bwd. */
+ATS_API int ats_rmsnorm_residual_bwd(const void* dout, const void* x, ats_dtype x_dtype,
+                             const void* w, ats_dtype w_dtype,
+                             void* dx, void* dresidual, void* dw,
+                             void* workspace, size_t workspace_bytes,
+                             int64_t rows, int64_t hidden, float eps, void* stream);
+
+/* ------------------------------------------------------------------- RoPE
+ * Rotate-half RoPE on q [B,Hq,S,D] and k [B,Hk,S,D] in one launch:
+ *   out = round(round(x*cos) + round(rotate_half(x)*sin)),
+ * cos/sin [S,D] tables (row stride cs_row_stride; 0 broadcasts one row to all
+ * positions).  backward != 0 applies the
+ * adjoint (the gradient w.r.t. x for upstream gradients in *_in).
+ * Replaces apply_rotary_pos_emb, ats/model/rope.py:71-87, and fused_apply_rope,
+ * ats/model/rope_triton.py:195-215 (k may be NULL, Hk ignored).
+ * Strides are in elements for the (b, h, s) dims; D must be contiguous.
+ * x_dtype is the dtype of q/k and of cos/sin; outputs have the same dtype. */
+ATS_API int ats_rope_apply(const void* q_in, void* q_out, int64_t Hq,
+                   const int64_t q_in_strides[3], const int64_t q_out_strides[3],
+                   const void* k_in, void* k_out, int64_t Hk,
+                   const int64_t k_in_strides[3], const int64_t k_out_strides[3],
+                   const void* cos, const void* sin, int64_t cs_row_stride,
+                   int64_t B, int64_t S, int64_t D, ats_dtype x_dtype,
+                   int backward, void* stream);
+
+/* --------------------------------------------------------------- MoE router
+ * Softmax over E experts in float32, top-k (descending; exact ties -> lower
+ * expert index), renormalised gates.  Replaces fused_moe_routing,
+ * ats/model/moe_triton.py:130-146 (math of _pytorch_moe_routing :121-127) and
+ * _PyTorchMoEFallback.compute_routing, ats/model/moe.py:76-90.
+ * logits [T,E] float32 contiguous; gates [T,k] float32; idx [T,k] int64;
+ * probs: optional [T,E] float32 softmax output (may be NULL). 1 <= k <= E <= 1024, k <= 16. */
+ATS_API int ats_moe_topk(const float* logits, int64_t T, int E, int k,
+                 float* gates, int64_t* idx, float* probs, void* stream);
+
+/* ------------------------------------------------------- MoE layer (plan)
+ * The MoE layer of ats/model/moe.py:92-164 split into device stages that need
+ * no host synchronisation.  One workspace (ats_moe_workspace_bytes) carries
+ * the routing plan between the stages of a forward and its backward.
+ *
+ * Permuted ("expert-major") row space: expert e owns rows
+ * [seg_start[e], seg_start[e] + kept_e) with kept_e = min(count_e, capacity),
+ * followed by zero padding up to a multiple of 128 rows; tokens inside a
+ * segment are in ascending token order (moe.py:109-116).  The number of
+ * permuted rows is at most ats_moe_max_rows(). */
+ATS_API int64_t ats_moe_max_rows(int64_t T, int E, int k, int64_t capacity);
+ATS_API size_t ats_moe_workspace_bytes(int64_t T, int E, int k, int64_t capacity);
+
+/* Stage 1: route + plan + permutation (moe.py:101-116, :136-162).
+ * Writes gates/idx like ats_moe_topk, the workspace plan, and
+ *   aux_loss[1]   = E * sum_e mean_t(p[t,e]) * count_e/T * lbw   (float32)
+ *   utilization[E] = count_e / max(sum count, 1e-8)               (float32)
+ *   counts[E]     = pre-capacity dispatch counts                  (int32) */
+ATS_API int ats_moe_route_plan(const float* logits, int64_t T, int E, int k, int64_t capacity,
+                       float lbw, float* gates, int64_t* idx,
+                       float* aux_loss, float* utilization, int32_t* counts,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
+/* Stage 2: xp[row] = x[token(row)], zero for padding rows.  x [T,H]; xp [max_rows,H]. */
+ATS_API int ats_moe_gather(const void* x, void* xp, ats_dtype dtype, int64_t T, int64_t H,
+                   int E, int k, int64_t capacity,
+                   const void* workspace, size_t workspace_bytes, void* stream);
+
+/* Stage 3: the grouped SwiGLU experts (ats/model/ffn.py:37-45 per expert):
+ *   h = round(xp Wgu_e^T) [rows,2F] (gate | up), a = round(round(silu(g))*u) [rows,F],
+ *   y = round(a Wd_e^T) [rows,H].
+ * w_gate_up [E,2F,H] and w_down [E,H,F] contiguous.  bf16 runs on tcgen05
+ * tensor cores (float32 accumulate); f32 runs on CUDA cores in float32. */
+ATS_API int ats_moe_experts_fwd(const void* xp, const void* w_gate_up, const void* w_down,
+                        void* h, void* a, void* y, ats_dtype dtype,
+                        int64_t T, int E, int k, int64_t capacity, int64_t H, int64_t F,
+                        const void* workspace, size_t workspace_bytes, void* stream);
+
+/* Stage 4: out[t] = sum over kept (t,e), ascending e, of round(y[row]*gate)
+ * accumulated in the token dtype (moe.py:119-122 index_add_).  out [T,H]. */
+ATS_API int ats_moe_combine(const void* y, void* out, ats_dtype dtype, int64_t T, int64_t H,
+                    int E, int k, int64_t capacity,
+                    const void* workspace, size_t workspace_bytes, void* stream);
+
+/* Backward stage 4: dy[row] = round(dout[token]*gate[row]) (zero on padding),
+ * dgate_row[row] = sum_h dout[token,h]*y[row,h] (float32). */
+ATS_API int ats_moe_combine_bwd(const void* dout, const void* y, void* dy, float* dgate_row,
+                        ats_dtype dtype, int64_t T, int64_t H, int E, int k, int64_t capacity,
+                        const void* workspace, size_t workspace_bytes, void* stream);
+
+/* Backward stage 3: with dh [rows,2F] as caller scratch,
+ *   da = round(dy Wd_e); ds = round(da*u); du = round(da*s); dg = round(ds*silu'(g));
+ *   dxp = round(dh Wgu_e); dWd_e = round(dy_e^T a_e); dWgu_e = round(dh_e^T xp_e). */
+ATS_API int ats_moe_experts_bwd(const void* dy, const void* xp, const void* h, const void* a,
+                        const void* w_gate_up, const void* w_down,
+                        void* dh, void* dxp, void* dw_gate_up, void* dw_down, ats_dtype dtype,
+                        int64_t T, int E, int k, int64_t capacity, int64_t H, int64_t F,
+                        const void* workspace, size_t workspace_bytes, void* stream);
+
+/* Backward stage 2: dx[t] = round(sum over kept rows of token t of dxp[row]),
+ * summed in float32 in ascending expert order; zero for tokens with no kept row. */
+ATS_API int ats_moe_scatter_grad(const void* dxp, void* dx, ats_dtype dtype, int64_t T, int64_t H,
+                         int E, int k, int64_t capacity,
+                         const void* workspace, size_t workspace_bytes, void* stream);
+
+/* Backward stage 1: d(logits) [T,E] float32 from the per-row gate gradients
+ * (dgate_row from ats_moe_combine_bwd) through the renormalisation and the
+ * softmax, plus the aux-loss term daux * d(aux)/d(probs).  daux is a device
+ * pointer to one float32 (the upstream gradient of aux_loss), or NULL for 0. */
+ATS_API int ats_moe_route_bwd(const float* logits, const float* gates, const int64_t* idx,
+                      const float* dgate_row, const float* daux, float* dlogits,
+                      int64_t T, int E, int k, int64_t capacity, float lbw,
+                      const void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ATS_B200_H */

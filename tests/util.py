@@ -1,0 +1,42 @@
+"""Helpers shared by the GPU parity tests."""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+# north-star tolerances
+F32 = dict(rtol=1e-5, atol=1e-6)
+BF16 = dict(rtol=2e-2, atol=1e-2)
+
+
+def np32(t: torch.Tensor) -> np.ndarray:
+    return t.detach().float().cpu().numpy()
+
+
+def dev(a, dtype=torch.float32, requires_grad: bool = False) -> torch.Tensor:
+    """numpy float32 (bf16-exact values for bf16) -> CUDA tensor of dtype (exact)."""
+    t = torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to("cuda").to(dtype)
+    return t.requires_grad_(requires_grad)
+
+
+def exact_fraction(a: np.ndarray, b: np.ndarray) -> float:
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    b = np.ascontiguousarray(b, dtype=np.float32)
+    return float(np.mean(a.view(np.uint32) == b.view(np.uint32)))
+
+
+def close(actual, expected, dtype: str, min_exact: float | None = None, **tol) -> None:
+    a = np32(actual) if isinstance(actual, torch.Tensor) else np.asarray(actual, np.float32)
+    b = np.asarray(expected, np.float32)
+    kw = dict(F32 if dtype == "f32" else BF16)
+    kw.update(tol)
+    np.testing.assert_allclose(a, b, **kw)
+    if min_exact is not None:
+        fr = exact_fraction(a, b)
+        assert fr >= min_exact, f"only {fr:.5f} bit-identical (need {min_exact})"
+
+
+def seeded_normal(shape, seed: int, scale: float = 1.0, shift: float = 0.0) -> np.ndarray:
+    rng = np.random.default_rng(seed)
+    return (shift + scale * rng.standard_normal(shape)).astype(np.float32)
