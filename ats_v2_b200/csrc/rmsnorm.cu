@@ -161,6 +161,9 @@ __global__ void __launch_bounds__(256) rmsnorm_fwd_stream_kernel(
 // RESID=false: TD = TX; g = dy*w; dx = r*g - x*r^3/H*sum(g*x); dw += dy*x*r.
 // RESID=true : TD = promote(X,W); dres = round_X(dout); dn1 = round_X(dout*w);
 //              dx = r*dn1 - x*r^3/H*sum(dn1*x); dw += dout*round_X(x*r).
+// The per-warp dw slice is lane-interleaved: value i of the lane's j-th chunk
+// lives at acc[(j*N + i)*32 + lane], so every shared-memory access of a warp
+// touches 32 consecutive words (no bank conflicts).
 template <typename TX, typename TW, bool RESID, int NCH>
 __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(
     const void* __restrict__ dyv, const TX* __restrict__ x, const TW* __restrict__ w,
@@ -168,11 +171,12 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(
     int64_t rows, int H, float eps) {
   typedef typename std::conditional<RESID, typename Promote<TX, TW>::type, TX>::type TD;
   constexpr int N = Chunk<TX>::N;
+  constexpr int SLICE = NCH * N * 32;
   extern __shared__ float acc_smem[];
   const int warps = blockDim.x >> 5;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float* acc = acc_smem + (size_t)warp * H;
-  for (int i = lane; i < H; i += 32) acc[i] = 0.f;
+  float* acc = acc_smem + (size_t)warp * SLICE;
+  for (int i = lane; i < SLICE; i += 32) acc[i] = 0.f;
   const int nch = H / N;
   const TD* dy = reinterpret_cast<const TD*>(dyv);
   const float invH = 1.0f / (float)H;
@@ -223,16 +227,16 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(
         unpack<TX>(xraw[j], v);
         unpack_span<TD, N, DQ>(draw[j], d);
         load_vals<TW, N>(w + (int64_t)ch * N, wv);
-        float* a = acc + ch * N;
+        float* a = acc + (j * N) * 32 + lane;
 #pragma unroll
         for (int i = 0; i < N; ++i) {
           float g;
           if constexpr (!RESID) {
             g = d[i] * wv[i];
-            a[i] = fmaf(d[i], v[i] * r, a[i]);
+            a[i * 32] = fmaf(d[i], v[i] * r, a[i * 32]);
           } else {
             g = round_to<TX>(d[i] * wv[i]);
-            a[i] = fmaf(d[i], round_to<TX>(v[i] * r), a[i]);
+            a[i * 32] = fmaf(d[i], round_to<TX>(v[i] * r), a[i * 32]);
           }
           o[i] = r * g - v[i] * k2;
         }
@@ -242,10 +246,12 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(
     }
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+  for (int c = threadIdx.x; c < H; c += blockDim.x) {
+    const int ch = c / N, i = c - ch * N;
+    const int idx = ((ch >> 5) * N + i) * 32 + (ch & 31);
     float s = 0.f;
-    for (int q = 0; q < warps; ++q) s += acc_smem[(size_t)q * H + i];
-    partial[(size_t)blockIdx.x * H + i] = s;
+    for (int q = 0; q < warps; ++q) s += acc_smem[(size_t)q * SLICE + idx];
+    partial[(size_t)blockIdx.x * H + c] = s;
   }
 }
 
@@ -371,18 +377,20 @@ int launch_fwd(const void* x, int64_t xs, const void* res, const void* w, void* 
 template <typename TX, typename TW, bool RESID>
 int launch_bwd(const void* dy, const void* x, const void* w, void* dx, void* dres, void* dw,
                void* ws, int64_t rows, int64_t H, float eps, cudaStream_t st) {
-  const int warps = bwd_warps(H);
-  const int blocks = bwd_blocks(rows, H);
-  const size_t smem = (size_t)warps * H * 4;
+  constexpr int N = Chunk<TX>::N;
+  const int nch = chunks_per_lane(H, N);
+  const int ncht = nch <= 1 ? 1 : nch <= 2 ? 2 : nch <= 4 ? 4 : nch <= 8 ? 8 : 16;
+  const bool vec = vec_ok<TX>(x, H, H) && aligned16(dy) && aligned16(dx) && aligned16(w) &&
+                   (!RESID || aligned16(dres)) && nch <= kMaxChunksPerLane;
+  const int64_t slice = vec ? (int64_t)ncht * N * 32 : H;  // floats of one warp's dw slice
+  const int warps = bwd_warps(slice);
+  const int blocks = bwd_blocks(rows, slice);
+  const size_t smem = (size_t)warps * slice * 4;
   float* partial = static_cast<float*>(ws);
   const TX* xp = static_cast<const TX*>(x);
   const TW* wp = static_cast<const TW*>(w);
-  constexpr int N = Chunk<TX>::N;
-  const bool vec = vec_ok<TX>(x, H, H) && aligned16(dy) && aligned16(dx) && aligned16(w) &&
-                   (!RESID || aligned16(dres));
-  const int nch = chunks_per_lane(H, N);
   if (rows > 0) {
-    if (vec && nch <= kMaxChunksPerLane) {
+    if (vec) {
 #define ATS_BWD(NC)                                                                                        \
   do {                                                                                                     \
     auto kfn = rmsnorm_bwd_kernel<TX, TW, RESID, NC>;                                                     \

@@ -102,6 +102,7 @@ def _launch(q_in, q_out, k_in, k_out, cos, sin, cs_stride, backward: bool) -> No
 class _RopeFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, cos, sin, cs_stride):
+        ctx.set_materialize_grads(False)  # an unused output's gradient arrives as None, not zeros
         q_out = torch.empty_like(q)
         k_out = torch.empty_like(k) if k is not None else None
         _launch(q, q_out, k, k_out, cos, sin, cs_stride, False)

@@ -102,7 +102,9 @@ def test_layer_golden(case, dn):
     (out.float() * dev(g["g"]).view(1, T, H)).sum().add(aux).backward()
     gtol = dict(rtol=1e-4, atol=1e-6) if dn == "f32" else {}
     close(x.grad.view(T, H), g["dx"], dn, **gtol)
-    close(layer.moe.gate.weight.grad, g["dwg"], "f32", rtol=1e-3, atol=1e-5)
+    scale = float(np.abs(g["dwg"]).max())
+    r = 1e-3 if dn == "f32" else 2e-2
+    close(layer.moe.gate.weight.grad, g["dwg"], "f32", rtol=r, atol=r * scale)
     for e, ex in enumerate(layer.moe.experts):
         close(ex.gate_up_proj.weight.grad, g["dwgu"][e], dn, **gtol)
         close(ex.down_proj.weight.grad, g["dwd"][e], dn, **gtol)
@@ -133,7 +135,11 @@ def _oracle_layer_check(T, H, F, E, k, cf, lbw, dn, seed, sample_tokens=None):
     b = omoe.moe_layer_backward_full(np32(gout.view(T, H)), fwd, xs, np32(layer.moe.gate.weight), wgu, wd,
                                      lbw, dn)
     close(x.grad.view(T, H), b["dx"], dn, **tol)
-    close(layer.moe.gate.weight.grad, b["dwg"], "f32", rtol=1e-3, atol=1e-5)
+    # the router-weight gradient sums T products of d(logits) that inherit the
+    # experts' rounding; its error is judged against the tensor's own scale
+    scale = float(np.abs(b["dwg"]).max())
+    r = 1e-3 if dn == "f32" else 2e-2
+    close(layer.moe.gate.weight.grad, b["dwg"], "f32", rtol=r, atol=r * scale)
     for e, ex in enumerate(layer.moe.experts):
         close(ex.gate_up_proj.weight.grad, b["dwgu"][e], dn, **tol)
         close(ex.down_proj.weight.grad, b["dwd"][e], dn, **tol)
