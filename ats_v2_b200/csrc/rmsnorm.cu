@@ -18,6 +18,7 @@
 // from L1/L2).
 #include "common.cuh"
 
+#include <mutex>
 #include <type_traits>
 
 namespace ats {
@@ -500,3 +501,64 @@ int ats_rmsnorm_residual_bwd(const void* dout, const void* x, ats_dtype x_dtype,
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------ no-alloc variant
+// ats_rmsnorm_bwd_noalloc: the same backward kernels, with the per-block dw
+// partial sums kept in a fixed device array of this file instead of a
+// caller-supplied workspace.  See include/ats_b200.h for the contract.
+namespace ats {
+namespace {
+constexpr int64_t kNoAllocMaxHidden = 8192;
+constexpr size_t kNoAllocScratchFloats = (size_t)kBwdMaxBlocks * (size_t)kNoAllocMaxHidden;  // 5 MiB
+}  // namespace
+}  // namespace ats
+
+// One copy per GPU that loads this library, alive until the process exits.
+static __device__ __align__(256) float g_rmsnorm_bwd_scratch[ats::kNoAllocScratchFloats];
+
+namespace ats {
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+float* g_scratch_ptr[kMaxDevices] = {};
+
+// Device address of g_rmsnorm_bwd_scratch on the current device, looked up
+// once per device (the host-side name of the array is not a device address).
+int scratch_for_current_device(float** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(ATS_ECUDA, "rmsnorm_bwd_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return fail(ATS_EUNSUPPORTED, "rmsnorm_bwd_noalloc: device %d", dev);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_rmsnorm_bwd_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(ATS_ECUDA, "rmsnorm_bwd_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    g_scratch_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_scratch_ptr[dev];
+  return ATS_OK;
+}
+}  // namespace
+}  // namespace ats
+
+extern "C" int ats_rmsnorm_bwd_noalloc(const void* dy, const void* x, ats_dtype x_dtype, const void* w,
+                                       ats_dtype w_dtype, void* dx, void* dw, int64_t rows, int64_t hidden,
+                                       float eps, void* stream) {
+  ATS_TRY(check_common(x, x_dtype, w, w_dtype, rows, hidden));
+  if (hidden > kNoAllocMaxHidden)
+    return fail(ATS_EUNSUPPORTED,
+                "rmsnorm_bwd_noalloc: hidden=%lld exceeds the fixed scratch limit of %lld; "
+                "use ats_rmsnorm_bwd with a caller workspace",
+                (long long)hidden, (long long)kNoAllocMaxHidden);
+  if (dw == nullptr || (rows > 0 && (dy == nullptr || dx == nullptr)))
+    return fail(ATS_EBADARG, "rmsnorm_bwd_noalloc: null pointer");
+  float* scratch = nullptr;
+  ATS_TRY(scratch_for_current_device(&scratch));
+  // kBwdMaxBlocks partial rows of `hidden` floats fit: hidden <= kNoAllocMaxHidden.
+  // Every block that runs writes its whole partial row before the reduce reads
+  // it, and the reduce reads only those rows, so nothing needs clearing.
+  auto fn = ATS_DISPATCH2(x_dtype, w_dtype, launch_bwd, false);
+  return fn(dy, x, w, dx, nullptr, dw, scratch, rows, hidden, eps, (cudaStream_t)stream);
+}

@@ -75,6 +75,28 @@ ATS_API int ats_rmsnorm_bwd(const void* dy, const void* x, ats_dtype x_dtype,
                     void* workspace, size_t workspace_bytes,
                     int64_t rows, int64_t hidden, float eps, void* stream);
 
+/* Allocation-free variant of ats_rmsnorm_bwd (no counterpart in the
+ * reference).  It is meant for callers that cannot allocate device memory
+ * around the call: a host runtime that reaches this library through a bare C
+ * FFI (cgo, JNI, ctypes) and has no caching allocator of its own, where a
+ * cudaMalloc/cudaFree per backward call would stall the device and fragment
+ * memory, or a process that runs inside a fixed, pre-reserved memory budget.
+ * The caller still passes every input and output; the dw partial sums live
+ * in a fixed device array of this library (5 MiB, held by every GPU that
+ * loads the library until the process exits).
+ *   - hidden must be <= 8192; larger sizes return ATS_EUNSUPPORTED and launch
+ *     nothing (use ats_rmsnorm_bwd with a workspace instead).
+ *   - The first call on a device looks up that device's address of the array
+ *     (cudaGetSymbolAddress with the device current); make that first call
+ *     before any stream capture.
+ *   - All calls share the one array: calls that overlap on the GPU (different
+ *     streams, or other threads, without ordering between them) race on it.
+ *     Each call overwrites the part it reads, so no clearing is needed.
+ *   - Results equal ats_rmsnorm_bwd's. */
+ATS_API int ats_rmsnorm_bwd_noalloc(const void* dy, const void* x, ats_dtype x_dtype,
+                            const void* w, ats_dtype w_dtype, void* dx, void* dw,
+                            int64_t rows, int64_t hidden, float eps, void* stream);
+
 /* ------------------------------------------------------ RMSNorm + residual
  * out = residual + (x*rsqrt(mean(x^2)+eps)).to(x.dtype) * w with torch type
  * promotion at each step.  Replaces fused_rmsnorm_residual,
