@@ -106,8 +106,9 @@ def test_layer_golden(case, dn):
     r = 1e-3 if dn == "f32" else 2e-2
     close(layer.moe.gate.weight.grad, g["dwg"], "f32", rtol=r, atol=r * scale)
     for e, ex in enumerate(layer.moe.experts):
-        close(ex.gate_up_proj.weight.grad, g["dwgu"][e], dn, **gtol)
-        close(ex.down_proj.weight.grad, g["dwd"][e], dn, **gtol)
+        for got, ref in ((ex.gate_up_proj.weight.grad, g["dwgu"][e]), (ex.down_proj.weight.grad, g["dwd"][e])):
+            wt = dict(rtol=1e-4, atol=1e-4 * float(np.abs(ref).max())) if dn == "f32" else {}
+            close(got, ref, dn, **wt)
 
 
 def _oracle_layer_check(T, H, F, E, k, cf, lbw, dn, seed, sample_tokens=None):
@@ -140,9 +141,12 @@ def _oracle_layer_check(T, H, F, E, k, cf, lbw, dn, seed, sample_tokens=None):
     scale = float(np.abs(b["dwg"]).max())
     r = 1e-3 if dn == "f32" else 2e-2
     close(layer.moe.gate.weight.grad, b["dwg"], "f32", rtol=r, atol=r * scale)
+    # weight gradients sum hundreds of products: float32 results are judged
+    # against each tensor's scale (1e-4 of its largest magnitude)
     for e, ex in enumerate(layer.moe.experts):
-        close(ex.gate_up_proj.weight.grad, b["dwgu"][e], dn, **tol)
-        close(ex.down_proj.weight.grad, b["dwd"][e], dn, **tol)
+        for got, ref in ((ex.gate_up_proj.weight.grad, b["dwgu"][e]), (ex.down_proj.weight.grad, b["dwd"][e])):
+            wt = dict(rtol=1e-4, atol=1e-4 * float(np.abs(ref).max())) if dn == "f32" else {}
+            close(got, ref, dn, **wt)
     return fwd
 
 
