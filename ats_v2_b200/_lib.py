@@ -48,6 +48,10 @@ SIGNATURES: dict[str, tuple] = {
     "ats_rope_apply": (c_int, [c_void_p, c_void_p, c_int64, POINTER(c_int64), POINTER(c_int64),
                                c_void_p, c_void_p, c_int64, POINTER(c_int64), POINTER(c_int64),
                                c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int, c_int, c_void_p]),
+    "ats_moe_status": (c_int, [c_void_p, c_size_t, c_int64, c_int, c_int, c_int64, POINTER(c_int)]),
+    "ats_moe_plan_export": (c_int, [c_void_p, c_size_t, c_int64, c_int, c_int, c_int64, c_void_p, c_void_p,
+                                    c_void_p]),
+    "ats_moe_uses_tensor_cores": (c_int, [c_int, c_int64, c_int64]),
     "ats_moe_topk": (c_int, [c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
     "ats_moe_max_rows": (c_int64, [c_int64, c_int, c_int, c_int64]),
     "ats_moe_workspace_bytes": (c_size_t, [c_int64, c_int, c_int, c_int64]),

@@ -183,6 +183,10 @@ using namespace ats;
 
 extern "C" {
 
+int ats_moe_uses_tensor_cores(ats_dtype dtype, int64_t H, int64_t F) {
+  return dtype == ATS_BF16 && tc_shape_supported(H, F) ? 1 : 0;
+}
+
 int ats_moe_experts_fwd(const void* xp, const void* w_gate_up, const void* w_down, void* h, void* a, void* y,
                         ats_dtype dtype, int64_t T, int E, int k, int64_t capacity, int64_t H, int64_t F,
                         const void* workspace, size_t workspace_bytes, void* stream) {

@@ -26,6 +26,11 @@ __device__ __forceinline__ void swiglu_grad(float g, float u, float da, float& d
   dg = round_to<T>((ds * sig) * (1.0f + g * (1.0f - sig)));
 }
 
+// Shapes the tcgen05 tiling covers: hidden and ffn multiples of 128.
+inline bool tc_shape_supported(int64_t H, int64_t F) {
+  return H % 128 == 0 && F % 128 == 0 && H >= 128 && F >= 128;
+}
+
 // tcgen05 tensor-core expert GEMMs (bf16).  Return ATS_EUNSUPPORTED for shapes
 // the tensor-core tiling does not cover; the caller then uses the CUDA-core path.
 int tc_experts_fwd(const void* xp, const void* wgu, const void* wd, void* h, void* a, void* y, int E, int64_t H,

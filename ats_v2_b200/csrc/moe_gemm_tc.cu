@@ -1,16 +1,547 @@
 // tcgen05 / TMEM grouped GEMMs for the bf16 SwiGLU experts (sm_100a).
+//
+// One persistent CTA per SM walks a static list of 128 x BN output tiles.
+// Warp roles:
+//   warp 0    TMA producer: 2-D tiled loads (128-byte swizzle) of the A and B
+//             tiles into a 4-stage shared-memory ring, completion counted on
+//             an mbarrier per stage.
+//   warp 1    allocates 2*BN TMEM columns (two accumulators) and one thread
+//             issues tcgen05.mma (M=128, N=BN, K=16, bf16 in, f32 accumulate)
+//             four per 64-wide K block; tcgen05.commit frees each ring stage
+//             and, after the last K block, hands the accumulator to the
+//             epilogue.
+//   warps 2-5 epilogue: tcgen05.ld of their 32 TMEM lanes (= 32 tile rows),
+//             fused SwiGLU forward / plain bf16 store / SwiGLU backward,
+//             vector stores to global; then release the accumulator, so the
+//             next tile's MMAs overlap this tile's epilogue.
+// Operands may be K-major or MN-major in shared memory (the tcgen05 descriptor
+// says which), so every forward and backward GEMM of the experts reads its
+// operands in place, without transposed copies:
+//   M-grouped (forward, data gradients): tile rows are permuted token rows of
+//     one expert segment; B is that expert's slice of the stacked weights.
+//   K-grouped (weight gradients): the reduction runs over the expert's
+//     segment rows; the output is that expert's weight gradient.
+// Every wait is bounded (SM clock budget); a role that gives up records an
+// error code in the plan's status word and raises a CTA-wide abort flag, the
+// other roles stop, in-flight TMA loads and MMAs are drained, and TMEM is
+// freed before the CTA exits.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
 #include "moe_gemm.cuh"
+#include "tc_ptx.cuh"
 
 namespace ats {
+namespace {
 
-int tc_experts_fwd(const void*, const void*, const void*, void*, void*, void*, int, int64_t, int64_t,
-                   const MoePlan&, cudaStream_t) {
-  return ATS_EUNSUPPORTED;
+constexpr int BM = 128, BK = 64, STAGES = 4;
+constexpr int kThreads = 192;
+constexpr long long kWaitBudget = 4000000000LL;  // SM cycles, about 2 s
+
+enum Epi { EPI_STORE = 0, EPI_SWIGLU_FWD = 1, EPI_SWIGLU_BWD = 2 };
+enum Base { BASE_SEG = 0, BASE_EXPERT = 1 };
+
+struct OpSpec {
+  int base;        // BASE_SEG: outer coordinate starts at seg_start[g]; BASE_EXPERT: at g*group_rows
+  int group_rows;  // rows of one expert in a stacked weight
+  int sub_offset;  // K-major B loaded as two halves, the second `sub_offset` rows further (0: one load)
+};
+
+struct GemmArgs {
+  const int* seg_start;  // [E+1] padded segment starts of the permuted rows
+  int E;
+  int M, N, K;  // M-grouped: N, K fixed; K-grouped: M, N fixed
+  OpSpec a, b;
+  bf16* out;  // output (bf16)
+  int64_t ldo;
+  int64_t out_group;  // K-grouped: elements between consecutive experts' outputs
+  const bf16* h;      // SWIGLU_BWD: [rows, 2F] gate|up pre-activations
+  bf16* h_out;        // SWIGLU_FWD: [rows, 2F]
+  bf16* a_out;        // SWIGLU_FWD: [rows, F]
+  int F;
+  int* err;
+};
+
+// tile -> (group, m tile, n tile, k blocks); groups scanned linearly (E is small)
+struct TileInfo {
+  int g, mt, nt, kb;
+};
+
+template <int BN, bool KGROUP, int EPI>
+__device__ __forceinline__ int n_tiles(const GemmArgs& p) {
+  return EPI == EPI_SWIGLU_FWD ? p.F / (BN / 2) : p.N / BN;
 }
 
-int tc_experts_bwd(const void*, const void*, const void*, const void*, const void*, const void*, void*, void*,
-                   void*, void*, int, int64_t, int64_t, const MoePlan&, cudaStream_t) {
-  return ATS_EUNSUPPORTED;
+template <int BN, bool KGROUP, int EPI>
+__device__ __forceinline__ bool decode_tile(const GemmArgs& p, const int* tiles_before, int t, TileInfo& ti) {
+  const int NT = n_tiles<BN, KGROUP, EPI>(p);
+  for (int g = 0; g < p.E; ++g) {
+    if (t < tiles_before[g + 1]) {
+      const int q = t - tiles_before[g];
+      ti.g = g;
+      ti.mt = q / NT;
+      ti.nt = q - ti.mt * NT;
+      if (KGROUP)
+        ti.kb = (p.seg_start[g + 1] - p.seg_start[g]) / BK;
+      else
+        ti.kb = p.K / BK;
+      return true;
+    }
+  }
+  return false;
+}
+
+__device__ __forceinline__ int op_base(const OpSpec& o, const int* seg, int g) {
+  return o.base == BASE_SEG ? seg[g] : g * o.group_rows;
+}
+
+__device__ __forceinline__ void fail_abort(int* err, volatile int* abort, int code) {
+  if (*abort == 0) {
+    *abort = 1;
+    atomicCAS(err, 0, code);
+  }
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// Store 32 floats as bf16 (64 contiguous bytes, 16-byte aligned).
+__device__ __forceinline__ void store32(bf16* dst, const float (&v)[32]) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 w;
+    w.x = pack_bf16(v[q * 8 + 0], v[q * 8 + 1]);
+    w.y = pack_bf16(v[q * 8 + 2], v[q * 8 + 3]);
+    w.z = pack_bf16(v[q * 8 + 4], v[q * 8 + 5]);
+    w.w = pack_bf16(v[q * 8 + 6], v[q * 8 + 7]);
+    d[q] = w;
+  }
+}
+
+__device__ __forceinline__ void load32(const bf16* src, float (&v)[32]) {
+  const uint4* s = reinterpret_cast<const uint4*>(src);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 w = s[q];
+    const bf16* e = reinterpret_cast<const bf16*>(&w);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[q * 8 + i] = __bfloat162float(e[i]);
+  }
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI, bool KGROUP>
+__global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
+                                                              const __grid_constant__ CUtensorMap tmB,
+                                                              GemmArgs p) {
+  constexpr uint32_t A_BYTES = BM * BK * 2;
+  constexpr uint32_t B_BYTES = BN * BK * 2;
+  constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  constexpr uint32_t IDESC = tc::idesc_bf16(BM, BN, A_MN, B_MN);
+  extern __shared__ uint8_t smem_raw[];
+  // 1024-byte aligned ring (the 128-byte swizzle atom spans 1024 bytes)
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t full_bar[STAGES], empty_bar[STAGES], tfull_bar[2], tempty_bar[2], done_bar;
+  __shared__ uint32_t tmem_base_s;
+  __shared__ int tiles_before[kMaxExperts + 1];
+  __shared__ volatile int abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      tc::mbar_init(&full_bar[s], 1);
+      tc::mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      tc::mbar_init(&tfull_bar[a], 1);
+      tc::mbar_init(&tempty_bar[a], 4);
+    }
+    tc::mbar_init(&done_bar, 1);
+    tc::fence_barrier_init();
+    tc::fence_proxy_async_smem();
+    abort_flag = 0;
+    // tiles per group, prefix-summed
+    const int NT = n_tiles<BN, KGROUP, EPI>(p);
+    int acc = 0;
+    tiles_before[0] = 0;
+    for (int g = 0; g < p.E; ++g) {
+      const int mt = KGROUP ? p.M / BM : (p.seg_start[g + 1] - p.seg_start[g]) / BM;
+      acc += mt * NT;
+      tiles_before[g + 1] = acc;
+    }
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(&tmem_base_s, 2 * BN);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem_base = tmem_base_s;
+  const int total = tiles_before[p.E];
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tc::prefetch_tensormap(&tmA);
+      tc::prefetch_tensormap(&tmB);
+      int stage = 0;
+      uint32_t phase = 0;
+      int last_parity[STAGES];
+#pragma unroll
+      for (int s = 0; s < STAGES; ++s) last_parity[s] = -1;
+      for (int t = blockIdx.x; t < total && !abort_flag; t += gridDim.x) {
+        TileInfo ti;
+        decode_tile<BN, KGROUP, EPI>(p, tiles_before, t, ti);
+        const int abase = op_base(p.a, p.seg_start, ti.g);
+        const int bbase = op_base(p.b, p.seg_start, ti.g);
+        const int m0 = ti.mt * BM;
+        const int n0 = EPI == EPI_SWIGLU_FWD ? ti.nt * (BN / 2) : ti.nt * BN;
+        for (int kb = 0; kb < ti.kb; ++kb) {
+          if (!tc::mbar_wait(&empty_bar[stage], phase ^ 1u, &abort_flag, kWaitBudget)) {
+            fail_abort(p.err, &abort_flag, 1);
+            break;
+          }
+          uint8_t* sa = ring + stage * STAGE_BYTES;
+          uint8_t* sb = sa + A_BYTES;
+          tc::mbar_arrive_expect_tx(&full_bar[stage], STAGE_BYTES);
+          if (!A_MN) {
+            tc::tma_load_2d(sa, &tmA, kb * BK, abase + m0, &full_bar[stage]);
+          } else {
+            tc::tma_load_2d(sa, &tmA, m0, abase + kb * BK, &full_bar[stage]);
+            tc::tma_load_2d(sa + 8192, &tmA, m0 + 64, abase + kb * BK, &full_bar[stage]);
+          }
+          if (!B_MN) {
+            if (p.b.sub_offset) {
+              tc::tma_load_2d(sb, &tmB, kb * BK, bbase + n0, &full_bar[stage]);
+              tc::tma_load_2d(sb + (BN / 2) * 128, &tmB, kb * BK, bbase + p.b.sub_offset + n0, &full_bar[stage]);
+            } else {
+              tc::tma_load_2d(sb, &tmB, kb * BK, bbase + n0, &full_bar[stage]);
+            }
+          } else {
+#pragma unroll
+            for (int b = 0; b < BN / 64; ++b)
+              tc::tma_load_2d(sb + b * 8192, &tmB, n0 + b * 64, bbase + kb * BK, &full_bar[stage]);
+          }
+          last_parity[stage] = (int)phase;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // drain: every issued load lands before the CTA may exit
+      for (int s = 0; s < STAGES; ++s)
+        if (last_parity[s] >= 0 && !tc::mbar_wait(&full_bar[s], (uint32_t)last_parity[s], nullptr, kWaitBudget))
+          atomicCAS(p.err, 0, 11);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int i = 0;
+      bool issued = false;
+      const uint32_t a_lbo = A_MN ? 8192u : 16u, b_lbo = B_MN ? 8192u : 16u;
+      const uint32_t a_step = A_MN ? 2048u : 32u, b_step = B_MN ? 2048u : 32u;
+      for (int t = blockIdx.x; t < total && !abort_flag; t += gridDim.x, ++i) {
+        TileInfo ti;
+        decode_tile<BN, KGROUP, EPI>(p, tiles_before, t, ti);
+        const int acc = i & 1;
+        const uint32_t acc_phase = (uint32_t)(i >> 1) & 1u;
+        if (!tc::mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, &abort_flag, kWaitBudget)) {
+          fail_abort(p.err, &abort_flag, 2);
+          break;
+        }
+        tc::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        bool ok = true;
+        for (int kb = 0; kb < ti.kb; ++kb) {
+          if (!tc::mbar_wait(&full_bar[stage], phase, &abort_flag, kWaitBudget)) {
+            fail_abort(p.err, &abort_flag, 3);
+            ok = false;
+            break;
+          }
+          tc::tc_fence_after();
+          const uint32_t sa = tc::smem_u32(ring + stage * STAGE_BYTES);
+          const uint32_t sb = sa + A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = tc::smem_desc(sa + k * a_step, a_lbo, 1024u, tc::kLayoutSW128);
+            const uint64_t bd = tc::smem_desc(sb + k * b_step, b_lbo, 1024u, tc::kLayoutSW128);
+            tc::mma_bf16(d_tmem, ad, bd, IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          tc::mma_commit(&empty_bar[stage]);
+          issued = true;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        if (ti.kb > 0)
+          tc::mma_commit(&tfull_bar[acc]);
+        else
+          tc::mbar_arrive(&tfull_bar[acc]);
+      }
+      // drain: all issued MMAs complete before TMEM may be freed
+      if (issued) {
+        tc::mma_commit(&done_bar);
+        if (!tc::mbar_wait(&done_bar, 0u, nullptr, kWaitBudget)) atomicCAS(p.err, 0, 12);
+      }
+    }
+  } else {
+    // ----------------------------------------------------------- epilogue
+    const int quad = warp & 3;  // TMEM lanes [32*quad, 32*quad + 32)
+    const int row_in_tile = quad * 32 + lane;
+    int i = 0;
+    for (int t = blockIdx.x; t < total && !abort_flag; t += gridDim.x, ++i) {
+      TileInfo ti;
+      decode_tile<BN, KGROUP, EPI>(p, tiles_before, t, ti);
+      const int acc = i & 1;
+      const uint32_t acc_phase = (uint32_t)(i >> 1) & 1u;
+      if (!tc::mbar_wait(&tfull_bar[acc], acc_phase, &abort_flag, kWaitBudget)) {
+        fail_abort(p.err, &abort_flag, 4);
+        break;
+      }
+      tc::tc_fence_after();
+      const uint32_t t_row = tmem_base + (uint32_t)(acc * BN) + ((uint32_t)(quad * 32) << 16);
+      const bool zero = ti.kb == 0;
+      if constexpr (EPI == EPI_SWIGLU_FWD) {
+        const int64_t row = (int64_t)p.seg_start[ti.g] + ti.mt * BM + row_in_tile;
+        const int n0 = ti.nt * (BN / 2);
+#pragma unroll 1
+        for (int c = 0; c < BN / 2; c += 32) {
+          float gv[32], uv[32], av[32];
+          tc::tmem_ld32(t_row + c, gv);
+          tc::tmem_ld32(t_row + BN / 2 + c, uv);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            gv[j] = round_to<bf16>(gv[j]);
+            uv[j] = round_to<bf16>(uv[j]);
+            av[j] = silu_mul<bf16>(gv[j], uv[j]);
+          }
+          store32(p.h_out + row * (2 * (int64_t)p.F) + n0 + c, gv);
+          store32(p.h_out + row * (2 * (int64_t)p.F) + p.F + n0 + c, uv);
+          store32(p.a_out + row * (int64_t)p.F + n0 + c, av);
+        }
+      } else if constexpr (EPI == EPI_SWIGLU_BWD) {
+        const int64_t row = (int64_t)p.seg_start[ti.g] + ti.mt * BM + row_in_tile;
+        const int n0 = ti.nt * BN;
+        const int64_t F2 = 2 * (int64_t)p.F;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          float dv[32], gv[32], uv[32];
+          tc::tmem_ld32(t_row + c, dv);
+          load32(p.h + row * F2 + n0 + c, gv);
+          load32(p.h + row * F2 + p.F + n0 + c, uv);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float dg, du;
+            swiglu_grad<bf16>(gv[j], uv[j], round_to<bf16>(dv[j]), dg, du);
+            gv[j] = dg;
+            uv[j] = du;
+          }
+          store32(p.out + row * F2 + n0 + c, gv);
+          store32(p.out + row * F2 + p.F + n0 + c, uv);
+        }
+      } else {
+        const int64_t row = KGROUP ? (int64_t)ti.mt * BM + row_in_tile
+                                   : (int64_t)p.seg_start[ti.g] + ti.mt * BM + row_in_tile;
+        bf16* outp = p.out + (KGROUP ? (int64_t)ti.g * p.out_group : 0) + row * p.ldo + (int64_t)ti.nt * BN;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          float v[32];
+          if (!zero) {
+            tc::tmem_ld32(t_row + c, v);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = 0.f;
+          }
+          store32(outp + c, v);
+        }
+      }
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&tempty_bar[acc]);
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem_base, 2 * BN);
+  }
+}
+
+// ------------------------------------------------------------------- host
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+int encode_fn(PFN_cuTensorMapEncodeTiled_v12000* out) {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  if (g_encode == nullptr) return fail(ATS_ECUDA, "moe_gemm: cuTensorMapEncodeTiled unavailable");
+  *out = g_encode;
+  return ATS_OK;
+}
+
+// 2-D bf16 tensor map, inner dim contiguous, 128-byte swizzle, box {64, box_outer}.
+int make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+             uint32_t box_outer) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc;
+  ATS_TRY(encode_fn(&enc));
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (row_bytes & 15) || inner < 64 || outer < box_outer)
+    return fail(ATS_EBADARG, "moe_gemm: operand not TMA-compatible (base %p, row %llu B, %llu x %llu)", base,
+                (unsigned long long)row_bytes, (unsigned long long)inner, (unsigned long long)outer);
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {64, box_outer};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(ATS_ECUDA, "moe_gemm: cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return ATS_OK;
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI, bool KGROUP>
+int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& p, int64_t max_tiles,
+              cudaStream_t st) {
+  auto kfn = tc_gemm_kernel<BN, A_MN, B_MN, EPI, KGROUP>;
+  const int smem = STAGES * (BM * BK * 2 + BN * BK * 2) + 1024;
+  cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return fail(ATS_ECUDA, "moe_gemm: smem attribute: %s", cudaGetErrorString(e));
+  int grid = num_sms();
+  if (max_tiles < grid) grid = (int)(max_tiles > 0 ? max_tiles : 1);
+  kfn<<<grid, kThreads, smem, st>>>(ta, tb, p);
+  return check_launch("moe_tc_gemm");
+}
+
+
+int pick_bn(int64_t n) { return n % 256 == 0 ? 256 : 128; }
+
+}  // namespace
+
+int tc_experts_fwd(const void* xp, const void* wgu, const void* wd, void* h, void* a, void* y, int E, int64_t H,
+                   int64_t F, const MoePlan& plan, cudaStream_t st) {
+  if (!tc_shape_supported(H, F)) return ATS_EUNSUPPORTED;
+  const int64_t R = plan.max_rows;
+  CUtensorMap ma, mb;
+  GemmArgs p{};
+  p.seg_start = plan.seg_start;
+  p.E = E;
+  p.err = plan.dev_err;
+  p.F = (int)F;
+  // h = xp Wgu_e^T with the SwiGLU epilogue: tile N = 128 gate + 128 up columns
+  ATS_TRY(make_map(&ma, xp, H, R, H * 2, 128));
+  ATS_TRY(make_map(&mb, wgu, H, (uint64_t)E * 2 * F, H * 2, 128));
+  p.M = 0;
+  p.N = (int)F;
+  p.K = (int)H;
+  p.a = OpSpec{BASE_SEG, 0, 0};
+  p.b = OpSpec{BASE_EXPERT, (int)(2 * F), (int)F};
+  p.h_out = static_cast<bf16*>(h);
+  p.a_out = static_cast<bf16*>(a);
+  ATS_TRY((launch_tc<256, false, false, EPI_SWIGLU_FWD, false>(ma, mb, p, (R / BM) * (F / 128), st)));
+  // y = a Wd_e^T
+  const int bn = pick_bn(H);
+  ATS_TRY(make_map(&ma, a, F, R, F * 2, 128));
+  ATS_TRY(make_map(&mb, wd, F, (uint64_t)E * H, F * 2, bn));
+  p.N = (int)H;
+  p.K = (int)F;
+  p.a = OpSpec{BASE_SEG, 0, 0};
+  p.b = OpSpec{BASE_EXPERT, (int)H, 0};
+  p.out = static_cast<bf16*>(y);
+  p.ldo = H;
+  if (bn == 256) return launch_tc<256, false, false, EPI_STORE, false>(ma, mb, p, (R / BM) * (H / 256), st);
+  return launch_tc<128, false, false, EPI_STORE, false>(ma, mb, p, (R / BM) * (H / 128), st);
+}
+
+int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a, const void* wgu, const void* wd,
+                   void* dh, void* dxp, void* dwgu, void* dwd, int E, int64_t H, int64_t F, const MoePlan& plan,
+                   cudaStream_t st) {
+  if (!tc_shape_supported(H, F)) return ATS_EUNSUPPORTED;
+  const int64_t R = plan.max_rows;
+  CUtensorMap ma, mb;
+  GemmArgs p{};
+  p.seg_start = plan.seg_start;
+  p.E = E;
+  p.err = plan.dev_err;
+  p.F = (int)F;
+  // da = dy Wd_e (B N-major: Wd_e[h][f]) with the SwiGLU backward epilogue -> dh
+  {
+    const int bn = pick_bn(F);
+    ATS_TRY(make_map(&ma, dy, H, R, H * 2, 128));
+    ATS_TRY(make_map(&mb, wd, F, (uint64_t)E * H, F * 2, 64));
+    p.N = (int)F;
+    p.K = (int)H;
+    p.a = OpSpec{BASE_SEG, 0, 0};
+    p.b = OpSpec{BASE_EXPERT, (int)H, 0};
+    p.h = static_cast<const bf16*>(h);
+    p.out = static_cast<bf16*>(dh);
+    if (bn == 256)
+      ATS_TRY((launch_tc<256, false, true, EPI_SWIGLU_BWD, false>(ma, mb, p, (R / BM) * (F / 256), st)));
+    else
+      ATS_TRY((launch_tc<128, false, true, EPI_SWIGLU_BWD, false>(ma, mb, p, (R / BM) * (F / 128), st)));
+  }
+  // dxp = dh Wgu_e (B N-major: Wgu_e[j][h])
+  {
+    const int bn = pick_bn(H);
+    ATS_TRY(make_map(&ma, dh, 2 * F, R, 2 * F * 2, 128));
+    ATS_TRY(make_map(&mb, wgu, H, (uint64_t)E * 2 * F, H * 2, 64));
+    p.N = (int)H;
+    p.K = (int)(2 * F);
+    p.a = OpSpec{BASE_SEG, 0, 0};
+    p.b = OpSpec{BASE_EXPERT, (int)(2 * F), 0};
+    p.out = static_cast<bf16*>(dxp);
+    p.ldo = H;
+    if (bn == 256)
+      ATS_TRY((launch_tc<256, false, true, EPI_STORE, false>(ma, mb, p, (R / BM) * (H / 256), st)));
+    else
+      ATS_TRY((launch_tc<128, false, true, EPI_STORE, false>(ma, mb, p, (R / BM) * (H / 128), st)));
+  }
+  // dWd_e[h][f] = sum_r dy[r][h] a[r][f]   (A M-major, B N-major, K = segment rows)
+  {
+    const int bn = pick_bn(F);
+    ATS_TRY(make_map(&ma, dy, H, R, H * 2, 64));
+    ATS_TRY(make_map(&mb, a, F, R, F * 2, 64));
+    p.M = (int)H;
+    p.N = (int)F;
+    p.K = 0;
+    p.a = OpSpec{BASE_SEG, 0, 0};
+    p.b = OpSpec{BASE_SEG, 0, 0};
+    p.out = static_cast<bf16*>(dwd);
+    p.ldo = F;
+    p.out_group = H * F;
+    const int64_t tiles = (int64_t)E * (H / BM) * (F / bn);
+    if (bn == 256)
+      ATS_TRY((launch_tc<256, true, true, EPI_STORE, true>(ma, mb, p, tiles, st)));
+    else
+      ATS_TRY((launch_tc<128, true, true, EPI_STORE, true>(ma, mb, p, tiles, st)));
+  }
+  // dWgu_e[j][h] = sum_r dh[r][j] xp[r][h]
+  {
+    const int bn = pick_bn(H);
+    ATS_TRY(make_map(&ma, dh, 2 * F, R, 2 * F * 2, 64));
+    ATS_TRY(make_map(&mb, xp, H, R, H * 2, 64));
+    p.M = (int)(2 * F);
+    p.N = (int)H;
+    p.out = static_cast<bf16*>(dwgu);
+    p.ldo = H;
+    p.out_group = 2 * F * H;
+    const int64_t tiles = (int64_t)E * (2 * F / BM) * (H / bn);
+    if (bn == 256) return launch_tc<256, true, true, EPI_STORE, true>(ma, mb, p, tiles, st);
+    return launch_tc<128, true, true, EPI_STORE, true>(ma, mb, p, tiles, st);
+  }
 }
 
 }  // namespace ats

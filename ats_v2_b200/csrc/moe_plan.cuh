@@ -27,6 +27,7 @@ struct MoePlan {
   int* row_token;       // [max_rows] token of a permuted row, -1 = padding
   float* row_gate;      // [max_rows] gate weight of the row
   int* tok_row;         // [T*k] permuted row of (token, slot), -1 = dropped
+  int* dev_err;         // [1] device status: 0, or the code of a bounded wait that gave up
 };
 
 inline int64_t moe_cap_rows(int64_t T, int E, int k, int64_t C) {
@@ -61,6 +62,7 @@ inline size_t moe_plan_carve(void* ws, int64_t T, int E, int k, int64_t C, MoePl
   q.row_token = (int*)take((size_t)mr * 4);
   q.row_gate = (float*)take((size_t)mr * 4);
   q.tok_row = (int*)take((size_t)T * k * 4);
+  q.dev_err = (int*)take(4);
   if (p) *p = q;
   return off;
 }

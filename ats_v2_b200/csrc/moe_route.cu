@@ -179,6 +179,7 @@ __global__ void __launch_bounds__(1024) plan_kernel(MoePlan plan, float lbw, flo
   }
   __syncthreads();
   if (threadIdx.x == 0) {
+    plan.dev_err[0] = 0;
     int acc = 0;
     float a = 0.f, fs = 0.f;
     for (int e = 0; e < E; ++e) {
@@ -467,6 +468,31 @@ int64_t ats_moe_max_rows(int64_t T, int E, int k, int64_t capacity) {
 size_t ats_moe_workspace_bytes(int64_t T, int E, int k, int64_t capacity) {
   if (moe_check(T, E, k, capacity) != ATS_OK) return 0;
   return moe_plan_carve(nullptr, T, E, k, capacity, nullptr);
+}
+
+int ats_moe_status(const void* workspace, size_t workspace_bytes, int64_t T, int E, int k, int64_t capacity,
+                   int* status) {
+  MoePlan plan;
+  ATS_TRY(moe_plan_from_ws(workspace, workspace_bytes, T, E, k, capacity, &plan));
+  if (status == nullptr) return fail(ATS_EBADARG, "moe_status: null output");
+  cudaError_t e = cudaMemcpy(status, plan.dev_err, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return fail(ATS_ECUDA, "moe_status: %s", cudaGetErrorString(e));
+  return *status == 0 ? ATS_OK : fail(ATS_ETIMEOUT, "moe: a bounded device wait gave up (code %d)", *status);
+}
+
+int ats_moe_plan_export(const void* workspace, size_t workspace_bytes, int64_t T, int E, int k, int64_t capacity,
+                        int32_t* seg_start, int32_t* row_token, void* stream) {
+  MoePlan plan;
+  ATS_TRY(moe_plan_from_ws(workspace, workspace_bytes, T, E, k, capacity, &plan));
+  cudaStream_t st = (cudaStream_t)stream;
+  if (seg_start != nullptr &&
+      cudaMemcpyAsync(seg_start, plan.seg_start, (size_t)(E + 1) * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+    return fail(ATS_ECUDA, "moe_plan_export: copy failed");
+  if (row_token != nullptr &&
+      cudaMemcpyAsync(row_token, plan.row_token, (size_t)plan.max_rows * 4, cudaMemcpyDeviceToDevice, st) !=
+          cudaSuccess)
+    return fail(ATS_ECUDA, "moe_plan_export: copy failed");
+  return ATS_OK;
 }
 
 int ats_moe_topk(const float* logits, int64_t T, int E, int k, float* gates, int64_t* idx, float* probs,

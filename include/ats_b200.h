@@ -156,6 +156,23 @@ ATS_API int ats_moe_topk(const float* logits, int64_t T, int E, int k,
 ATS_API int64_t ats_moe_max_rows(int64_t T, int E, int k, int64_t capacity);
 ATS_API size_t ats_moe_workspace_bytes(int64_t T, int E, int k, int64_t capacity);
 
+/* Device status of the MoE stages that ran with this workspace since the last
+ * ats_moe_route_plan: writes 0 to *status and returns ATS_OK when every
+ * bounded device-side wait completed, else the wait's code and ATS_ETIMEOUT.
+ * Synchronous (copies one int from the device); for diagnostics, not the step. */
+ATS_API int ats_moe_status(const void* workspace, size_t workspace_bytes, int64_t T, int E, int k,
+                   int64_t capacity, int* status);
+
+/* Copies the plan's padded segment starts [E+1] and the token of every
+ * permuted row [max_rows] (-1 = padding) into caller device buffers (either
+ * may be NULL), stream-ordered. */
+ATS_API int ats_moe_plan_export(const void* workspace, size_t workspace_bytes, int64_t T, int E, int k,
+                        int64_t capacity, int32_t* seg_start, int32_t* row_token, void* stream);
+
+/* 1 when ats_moe_experts_fwd/bwd run this dtype and shape on tcgen05 tensor
+ * cores (bf16, hidden and ffn multiples of 128), 0 when on CUDA cores. */
+ATS_API int ats_moe_uses_tensor_cores(ats_dtype dtype, int64_t H, int64_t F);
+
 /* Stage 1: route + plan + permutation (moe.py:101-116, :136-162).
  * Writes gates/idx like ats_moe_topk, the workspace plan, and
  *   aux_loss[1]   = E * sum_e mean_t(p[t,e]) * count_e/T * lbw   (float32)
