@@ -39,6 +39,7 @@ SIGNATURES: dict[str, tuple] = {
     "ats_rmsnorm_bwd_workspace_bytes": (c_size_t, [c_int64, c_int64]),
     "ats_rmsnorm_bwd": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_void_p,
                                 c_size_t, c_int64, c_int64, c_float, c_void_p]),
+    "ats_rmsnorm_status": (c_int, [POINTER(c_int)]),
     "ats_rmsnorm_bwd_noalloc": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p,
                                         c_int64, c_int64, c_float, c_void_p]),
     "ats_rmsnorm_residual_fwd": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int64,

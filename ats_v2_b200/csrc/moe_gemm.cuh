@@ -26,6 +26,23 @@ __device__ __forceinline__ void swiglu_grad(float g, float u, float da, float& d
   dg = round_to<T>((ds * sig) * (1.0f + g * (1.0f - sig)));
 }
 
+// Epilogue forms of the two functions above for bf16 results: the
+// exponential and reciprocal use the SFU (__expf, __frcp_rn); their float32
+// error (a few ulp) is far below half a bf16 ulp, so the rounded results
+// match the accurate forms except at rare exact ties.
+__device__ __forceinline__ float silu_mul_fast_bf16(float g, float u) {
+  const float s = round_to<bf16>(g * __frcp_rn(1.0f + __expf(-g)));
+  return round_to<bf16>(s * u);
+}
+
+__device__ __forceinline__ void swiglu_grad_fast_bf16(float g, float u, float da, float& dg, float& du) {
+  const float sig = __frcp_rn(1.0f + __expf(-g));
+  const float s = round_to<bf16>(g * sig);
+  du = round_to<bf16>(da * s);
+  const float ds = round_to<bf16>(da * u);
+  dg = round_to<bf16>((ds * sig) * (1.0f + g * (1.0f - sig)));
+}
+
 // Shapes the tcgen05 tiling covers: hidden and ffn multiples of 128.
 inline bool tc_shape_supported(int64_t H, int64_t F) {
   return H % 128 == 0 && F % 128 == 0 && H >= 128 && F >= 128;

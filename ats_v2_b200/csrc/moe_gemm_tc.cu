@@ -10,10 +10,12 @@
 //             four per 64-wide K block; tcgen05.commit frees each ring stage
 //             and, after the last K block, hands the accumulator to the
 //             epilogue.
-//   warps 2-5 epilogue: tcgen05.ld of their 32 TMEM lanes (= 32 tile rows),
-//             fused SwiGLU forward / plain bf16 store / SwiGLU backward,
-//             vector stores to global; then release the accumulator, so the
-//             next tile's MMAs overlap this tile's epilogue.
+//   warps 2-9 epilogue: two warps per 32-lane TMEM quadrant (= 32 tile rows),
+//             each owning half of the tile's columns: tcgen05.ld, fused SwiGLU
+//             forward / plain bf16 store / SwiGLU backward (whose pre-activation
+//             loads are prefetched one 32-column chunk ahead), vector stores to
+//             global; then release the accumulator, so the next tile's MMAs
+//             overlap this tile's epilogue.
 // Operands may be K-major or MN-major in shared memory (the tcgen05 descriptor
 // says which), so every forward and backward GEMM of the experts reads its
 // operands in place, without transposed copies:
@@ -36,7 +38,8 @@ namespace ats {
 namespace {
 
 constexpr int BM = 128, BK = 64, STAGES = 4;
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;  // two per TMEM lane quadrant, each owning half of the tile's columns
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr long long kWaitBudget = 4000000000LL;  // SM cycles, about 2 s
 
 enum Epi { EPI_STORE = 0, EPI_SWIGLU_FWD = 1, EPI_SWIGLU_BWD = 2 };
@@ -157,7 +160,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
     }
     for (int a = 0; a < 2; ++a) {
       tc::mbar_init(&tfull_bar[a], 1);
-      tc::mbar_init(&tempty_bar[a], 4);
+      tc::mbar_init(&tempty_bar[a], kEpiWarps);
     }
     tc::mbar_init(&done_bar, 1);
     tc::fence_barrier_init();
@@ -295,7 +298,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
     }
   } else {
     // ----------------------------------------------------------- epilogue
-    const int quad = warp & 3;  // TMEM lanes [32*quad, 32*quad + 32)
+    const int quad = warp & 3;         // TMEM lanes [32*quad, 32*quad + 32)
+    const int chalf = (warp - 2) >> 2;  // which half of the tile's columns
     const int row_in_tile = quad * 32 + lane;
     int i = 0;
     for (int t = blockIdx.x; t < total && !abort_flag; t += gridDim.x, ++i) {
@@ -303,65 +307,100 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
       decode_tile<BN, KGROUP, EPI>(p, tiles_before, t, ti);
       const int acc = i & 1;
       const uint32_t acc_phase = (uint32_t)(i >> 1) & 1u;
-      if (!tc::mbar_wait(&tfull_bar[acc], acc_phase, &abort_flag, kWaitBudget)) {
-        fail_abort(p.err, &abort_flag, 4);
-        break;
-      }
-      tc::tc_fence_after();
-      const uint32_t t_row = tmem_base + (uint32_t)(acc * BN) + ((uint32_t)(quad * 32) << 16);
-      const bool zero = ti.kb == 0;
-      if constexpr (EPI == EPI_SWIGLU_FWD) {
+      if constexpr (EPI == EPI_SWIGLU_BWD) {
+        // the pre-activations do not depend on the accumulator: start loading them now
         const int64_t row = (int64_t)p.seg_start[ti.g] + ti.mt * BM + row_in_tile;
-        const int n0 = ti.nt * (BN / 2);
+        const int64_t F2 = 2 * (int64_t)p.F;
+        const int c0 = chalf * (BN / 2);
+        const bf16* hg = p.h + row * F2 + ti.nt * BN + c0;
+        const bf16* hu = hg + p.F;
+        uint4 gq[4], uq[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          gq[q] = reinterpret_cast<const uint4*>(hg)[q];
+          uq[q] = reinterpret_cast<const uint4*>(hu)[q];
+        }
+        if (!tc::mbar_wait(&tfull_bar[acc], acc_phase, &abort_flag, kWaitBudget)) {
+          fail_abort(p.err, &abort_flag, 4);
+          break;
+        }
+        tc::tc_fence_after();
+        const uint32_t t_row = tmem_base + (uint32_t)(acc * BN + c0) + ((uint32_t)(quad * 32) << 16);
+        bf16* dg_out = p.out + row * F2 + ti.nt * BN + c0;
 #pragma unroll 1
         for (int c = 0; c < BN / 2; c += 32) {
-          float gv[32], uv[32], av[32];
-          tc::tmem_ld32(t_row + c, gv);
-          tc::tmem_ld32(t_row + BN / 2 + c, uv);
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            gv[j] = round_to<bf16>(gv[j]);
-            uv[j] = round_to<bf16>(uv[j]);
-            av[j] = silu_mul<bf16>(gv[j], uv[j]);
-          }
-          store32(p.h_out + row * (2 * (int64_t)p.F) + n0 + c, gv);
-          store32(p.h_out + row * (2 * (int64_t)p.F) + p.F + n0 + c, uv);
-          store32(p.a_out + row * (int64_t)p.F + n0 + c, av);
-        }
-      } else if constexpr (EPI == EPI_SWIGLU_BWD) {
-        const int64_t row = (int64_t)p.seg_start[ti.g] + ti.mt * BM + row_in_tile;
-        const int n0 = ti.nt * BN;
-        const int64_t F2 = 2 * (int64_t)p.F;
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
           float dv[32], gv[32], uv[32];
           tc::tmem_ld32(t_row + c, dv);
-          load32(p.h + row * F2 + n0 + c, gv);
-          load32(p.h + row * F2 + p.F + n0 + c, uv);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const bf16* ge = reinterpret_cast<const bf16*>(&gq[q]);
+            const bf16* ue = reinterpret_cast<const bf16*>(&uq[q]);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              gv[q * 8 + e] = __bfloat162float(ge[e]);
+              uv[q * 8 + e] = __bfloat162float(ue[e]);
+            }
+          }
+          if (c + 32 < BN / 2) {  // prefetch the next chunk while this one computes
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              gq[q] = reinterpret_cast<const uint4*>(hg + c + 32)[q];
+              uq[q] = reinterpret_cast<const uint4*>(hu + c + 32)[q];
+            }
+          }
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             float dg, du;
-            swiglu_grad<bf16>(gv[j], uv[j], round_to<bf16>(dv[j]), dg, du);
+            swiglu_grad_fast_bf16(gv[j], uv[j], round_to<bf16>(dv[j]), dg, du);
             gv[j] = dg;
             uv[j] = du;
           }
-          store32(p.out + row * F2 + n0 + c, gv);
-          store32(p.out + row * F2 + p.F + n0 + c, uv);
+          store32(dg_out + c, gv);
+          store32(dg_out + p.F + c, uv);
         }
       } else {
-        const int64_t row = KGROUP ? (int64_t)ti.mt * BM + row_in_tile
-                                   : (int64_t)p.seg_start[ti.g] + ti.mt * BM + row_in_tile;
-        bf16* outp = p.out + (KGROUP ? (int64_t)ti.g * p.out_group : 0) + row * p.ldo + (int64_t)ti.nt * BN;
+        if (!tc::mbar_wait(&tfull_bar[acc], acc_phase, &abort_flag, kWaitBudget)) {
+          fail_abort(p.err, &abort_flag, 4);
+          break;
+        }
+        tc::tc_fence_after();
+        const uint32_t t_row = tmem_base + (uint32_t)(acc * BN) + ((uint32_t)(quad * 32) << 16);
+        if constexpr (EPI == EPI_SWIGLU_FWD) {
+          const int64_t row = (int64_t)p.seg_start[ti.g] + ti.mt * BM + row_in_tile;
+          const int c0 = chalf * (BN / 4);
+          const int n0 = ti.nt * (BN / 2) + c0;
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
-          float v[32];
-          if (!zero) {
-            tc::tmem_ld32(t_row + c, v);
-          } else {
+          for (int c = 0; c < BN / 4; c += 32) {
+            float gv[32], uv[32], av[32];
+            tc::tmem_ld32(t_row + c0 + c, gv);
+            tc::tmem_ld32(t_row + BN / 2 + c0 + c, uv);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = 0.f;
+            for (int j = 0; j < 32; ++j) {
+              gv[j] = round_to<bf16>(gv[j]);
+              uv[j] = round_to<bf16>(uv[j]);
+              av[j] = silu_mul_fast_bf16(gv[j], uv[j]);
+            }
+            store32(p.h_out + row * (2 * (int64_t)p.F) + n0 + c, gv);
+            store32(p.h_out + row * (2 * (int64_t)p.F) + p.F + n0 + c, uv);
+            store32(p.a_out + row * (int64_t)p.F + n0 + c, av);
           }
-          store32(outp + c, v);
+        } else {
+          const bool zero = ti.kb == 0;
+          const int c0 = chalf * (BN / 2);
+          const int64_t row = KGROUP ? (int64_t)ti.mt * BM + row_in_tile
+                                     : (int64_t)p.seg_start[ti.g] + ti.mt * BM + row_in_tile;
+          bf16* outp = p.out + (KGROUP ? (int64_t)ti.g * p.out_group : 0) + row * p.ldo + (int64_t)ti.nt * BN + c0;
+#pragma unroll 1
+          for (int c = 0; c < BN / 2; c += 32) {
+            float v[32];
+            if (!zero) {
+              tc::tmem_ld32(t_row + c0 + c, v);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = 0.f;
+            }
+            store32(outp + c, v);
+          }
         }
       }
       tc::tc_fence_before();

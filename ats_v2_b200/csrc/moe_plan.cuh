@@ -5,7 +5,7 @@
 
 namespace ats {
 
-constexpr int kRouteTokensPerBlock = 256;  // tokens per route/permute block (8 warps x 32)
+constexpr int kRouteTokensPerBlock = 64;  // tokens per route/permute block (route: 8 warps x 8 tokens)
 constexpr int kSegAlign = 128;             // expert segments padded to this many rows
 constexpr int kMaxExperts = 1024;
 constexpr int kMaxTopK = 16;

@@ -1,6 +1,6 @@
 // MoE routing and token permutation without host synchronisation.
 //
-//   route    : one warp per token.  Lane l holds logits l, l+32, ...; max and
+//   route    : one warp per token (blocks of 64 tokens, 8 warps).  Lane l holds logits l, l+32, ...; max and
 //              sum are warp reductions, the softmax is float32, top-k is k
 //              rounds of a warp arg-max on the logits (softmax is monotone, so
 //              this is the probability order; exact ties go to the lower
@@ -20,7 +20,8 @@
 namespace ats {
 namespace {
 
-constexpr int kWarps = kRouteTokensPerBlock / 32;
+constexpr int kWarps = 8;                                    // route block: 8 warps
+constexpr int kTokPerWarp = kRouteTokensPerBlock / kWarps;  // tokens per route warp
 
 // (value, index) arg-max across the warp: larger value wins, ties -> lower index.
 __device__ __forceinline__ void warp_argmax(float& v, int& i, float& pay) {
@@ -69,7 +70,7 @@ __device__ __forceinline__ void token_softmax(const float* __restrict__ lrow, in
 }
 
 template <int EPL, bool PLAN>
-__global__ void __launch_bounds__(kRouteTokensPerBlock) route_kernel(const float* __restrict__ logits, int64_t T,
+__global__ void __launch_bounds__(32 * kWarps) route_kernel(const float* __restrict__ logits, int64_t T,
                                                                      int E, int k, float* __restrict__ gates,
                                                                      int64_t* __restrict__ idx,
                                                                      float* __restrict__ probs, MoePlan plan) {
@@ -90,8 +91,8 @@ __global__ void __launch_bounds__(kRouteTokensPerBlock) route_kernel(const float
   float psum[EPL];
 #pragma unroll
   for (int j = 0; j < EPL; ++j) psum[j] = 0.f;
-  const int64_t t0 = (int64_t)blockIdx.x * kRouteTokensPerBlock + warp * 32;
-  for (int q = 0; q < 32; ++q) {
+  const int64_t t0 = (int64_t)blockIdx.x * kRouteTokensPerBlock + warp * kTokPerWarp;
+  for (int q = 0; q < kTokPerWarp; ++q) {
     const int64_t t = t0 + q;
     if (t >= T) break;
     float l[EPL], p[EPL], m, s;
@@ -435,7 +436,7 @@ int launch_route(const float* logits, int64_t T, int E, int k, float* gates, int
   do {                                                                                             \
     auto kfn = route_kernel<EP, PLAN>;                                                             \
     if (smem > 48 * 1024) cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
-    kfn<<<nb, kRouteTokensPerBlock, smem, st>>>(logits, T, E, k, gates, idx, probs, plan);         \
+    kfn<<<nb, 32 * kWarps, smem, st>>>(logits, T, E, k, gates, idx, probs, plan);         \
   } while (0)
   switch (epl) {
     case 1: ATS_ROUTE(1); break;

@@ -16,10 +16,21 @@
 // Rows longer than the register budget (more than 16 chunks per lane) take
 // a streaming variant that reads the row twice (the second read is served
 // from L1/L2).
+//
+// Plain RMSNorm on rows of at most 8 KB (bf16 hidden <= 4096, fp32 <= 2048)
+// runs on the TMA ring kernels instead: a persistent CTA per SM in which one
+// thread streams whole rows into a shared-memory ring with 1-D bulk copies
+// (cp.async.bulk, completion on an mbarrier per slot) while four independent
+// groups of two consumer warps each process a row.  The producer keeps 128 KB
+// of rows in flight per SM whatever the consumers are doing, which is what
+// saturates HBM; every consumer thread owns fixed columns, so (backward) the
+// dw accumulators stay in registers.
 #include "common.cuh"
 
 #include <mutex>
 #include <type_traits>
+
+#include "tc_ptx.cuh"
 
 namespace ats {
 namespace {
@@ -320,6 +331,308 @@ __global__ void dw_reduce_kernel(const float* __restrict__ partial, int nblk, in
   dw[i] = Cvt<TW>::from_f(s);
 }
 
+// ---------------------------------------------------------- TMA ring kernels
+// One producer thread streams rows into a shared-memory ring with 1-D bulk
+// copies.  Eight consumer warps form four independent groups of two warps;
+// group g processes rows g, g+4, g+8, ... so four rows are in flight in the
+// consumers at any time and their latency chains overlap.  Group thread gt
+// owns the 16-byte chunks gt + 64*j of every row; the weight sits in shared
+// memory interleaved by gt (conflict-free reads) and the backward's dw
+// accumulators stay in registers.  A row's partial sums meet through a small
+// shared buffer and one named barrier per group and row (bar.red.and, which
+// also makes every member take the same decision when a bounded wait gives
+// up, so none is left waiting at the barrier).
+constexpr int kGroups = 4;
+constexpr int kGroupWarps = 2;
+constexpr int kGroupThreads = 32 * kGroupWarps;
+constexpr int kConsumerThreads = kGroups * kGroupThreads;
+constexpr int kRingThreads = 32 + kConsumerThreads;
+constexpr int kSlotsFwd = 16, kSlotsBwd = 8;
+constexpr long long kRingBudget = 4000000000LL;  // SM cycles, about 2 s
+constexpr int kRingMaxRowBytes = 8192;
+
+// First bounded wait of a ring kernel that gave up (diagnostics; 0 = none).
+__device__ int g_ring_status;
+
+__device__ __forceinline__ void ring_fail(volatile int* abort, int code) {
+  if (*abort == 0) {
+    *abort = 1;
+    atomicCAS(&g_ring_status, 0, code);
+  }
+}
+
+// Named barrier `id` over `count` threads; true only if `ok` held in all of them.
+__device__ __forceinline__ bool bar_and(bool ok, int id, int count) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)ok), "r"(id), "r"(count)
+      : "memory");
+  return r != 0;
+}
+
+// w staged as float32, interleaved by group thread: value e of chunk gt+64*j
+// at ws[(j*N + e)*64 + gt].
+template <typename TW, int NPL, int N>
+__device__ __forceinline__ void stage_weight(float* ws, const TW* __restrict__ w, int H, int tid, int nthreads) {
+  for (int idx = tid; idx < NPL * N * kGroupThreads; idx += nthreads) {
+    const int gt = idx % kGroupThreads, je = idx / kGroupThreads, e = je % N, j = je / N;
+    const int col = (gt + kGroupThreads * j) * N + e;
+    ws[idx] = col < H ? Cvt<TW>::to_f(w[col]) : 0.f;
+  }
+}
+
+// The producer: rows blockIdx.x + i*gridDim.x, i < my_rows, into slot i % S.
+// `nbytes` per tensor; `second` (may be null) goes to the slot's second half.
+template <int S>
+__device__ __forceinline__ void ring_produce(uint8_t* ring, uint32_t slot_bytes, uint32_t half_bytes,
+                                             const uint8_t* first, const uint8_t* second, int64_t row_stride_bytes,
+                                             uint32_t nbytes, int64_t my_rows, uint64_t* full_bar,
+                                             uint64_t* empty_bar, volatile int* abort_flag, int code) {
+  int last_par[S];
+#pragma unroll
+  for (int q = 0; q < S; ++q) last_par[q] = -1;
+  const uint32_t tx = second ? 2 * nbytes : nbytes;
+  for (int64_t i = 0; i < my_rows && !*abort_flag; ++i) {
+    const int slot = (int)(i % S);
+    const uint32_t par = (uint32_t)((i / S) & 1);
+    if (!tc::mbar_wait(&empty_bar[slot], par ^ 1u, abort_flag, kRingBudget)) {
+      ring_fail(abort_flag, code);
+      break;
+    }
+    const int64_t off = (blockIdx.x + i * gridDim.x) * row_stride_bytes;
+    tc::mbar_arrive_expect_tx(&full_bar[slot], tx);
+    tc::bulk_load(ring + slot * slot_bytes, first + off, nbytes, &full_bar[slot]);
+    if (second) tc::bulk_load(ring + slot * slot_bytes + half_bytes, second + off, nbytes, &full_bar[slot]);
+    last_par[slot] = (int)par;
+  }
+  for (int q = 0; q < S; ++q)  // every issued copy lands before the CTA exits
+    if (last_par[q] >= 0 && !tc::mbar_wait(&full_bar[q], (uint32_t)last_par[q], nullptr, kRingBudget))
+      atomicCAS(&g_ring_status, 0, code + 10);
+}
+
+template <typename TX, typename TW, int NPL>
+__global__ void __launch_bounds__(kRingThreads, 1) rmsnorm_fwd_ring_kernel(
+    const TX* __restrict__ x, int64_t xs, const TW* __restrict__ w, TX* __restrict__ y, int64_t ys,
+    float* __restrict__ rstd, int64_t rows, int H, float eps) {
+  constexpr int N = Chunk<TX>::N;
+  constexpr int S = kSlotsFwd;
+  constexpr int WSF = NPL * N * kGroupThreads;  // floats of the staged weight
+  extern __shared__ __align__(128) uint8_t smem_ring[];
+  __shared__ __align__(8) uint64_t full_bar[S], empty_bar[S];
+  __shared__ float red[kGroups][2][kGroupWarps];
+  __shared__ volatile int abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nch = H / N;
+  const uint32_t row_bytes = (uint32_t)H * sizeof(TX);
+  const uint32_t slot_bytes = (row_bytes + 127u) & ~127u;
+  float* ws = reinterpret_cast<float*>(smem_ring);
+  uint8_t* ring = smem_ring + WSF * 4;
+  if (threadIdx.x == 0) {
+    for (int q = 0; q < S; ++q) {
+      tc::mbar_init(&full_bar[q], 1);
+      tc::mbar_init(&empty_bar[q], 1);
+    }
+    tc::fence_barrier_init();
+    tc::fence_proxy_async_smem();
+    abort_flag = 0;
+  }
+  stage_weight<TW, NPL, N>(ws, w, H, threadIdx.x, blockDim.x);
+  __syncthreads();
+  const int64_t my_rows = (rows - blockIdx.x + gridDim.x - 1) / gridDim.x;
+  if (warp == 0) {
+    if (lane == 0)
+      ring_produce<S>(ring, slot_bytes, 0, reinterpret_cast<const uint8_t*>(x), nullptr,
+                      xs * (int64_t)sizeof(TX), row_bytes, my_rows, full_bar, empty_bar, &abort_flag, 1);
+    return;
+  }
+  const int ct = threadIdx.x - 32;
+  const int grp = ct / kGroupThreads, gt = ct % kGroupThreads, gw = gt >> 5;
+  for (int64_t i = grp; i < my_rows; i += kGroups) {
+    const int slot = (int)(i % S);
+    const bool ok = tc::mbar_wait(&full_bar[slot], (uint32_t)((i / S) & 1), &abort_flag, kRingBudget);
+    const uint4* src = reinterpret_cast<const uint4*>(ring + slot * slot_bytes);
+    uint4 raw[NPL];
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < NPL; ++j) {
+      const int c = gt + kGroupThreads * j;
+      if (ok && c < nch) {
+        raw[j] = src[c];
+        float v[N];
+        unpack<TX>(raw[j], v);
+#pragma unroll
+        for (int e = 0; e < N; ++e) ss = fmaf(v[e], v[e], ss);
+      }
+    }
+    ss = warp_sum(ss);
+    const int rb = (int)((i / kGroups) & 1);
+    if (lane == 0) red[grp][rb][gw] = ss;
+    if (!bar_and(ok, 1 + grp, kGroupThreads)) {
+      if (gt == 0) ring_fail(&abort_flag, 2);
+      break;
+    }
+    if (gt == 0) tc::mbar_arrive(&empty_bar[slot]);  // the group holds its chunks: free the slot
+    float tot = 0.f;
+#pragma unroll
+    for (int q = 0; q < kGroupWarps; ++q) tot += red[grp][rb][q];
+    const float r = 1.0f / sqrtf(tot / (float)H + eps);
+    const int64_t row = blockIdx.x + i * gridDim.x;
+    if (rstd != nullptr && gt == 0) rstd[row] = r;
+    TX* yr = y + row * ys;
+#pragma unroll
+    for (int j = 0; j < NPL; ++j) {
+      const int c = gt + kGroupThreads * j;
+      if (c < nch) {
+        float v[N], o[N];
+        unpack<TX>(raw[j], v);
+#pragma unroll
+        for (int e = 0; e < N; ++e) o[e] = (v[e] * r) * ws[(j * N + e) * kGroupThreads + gt];
+        store_chunk<TX>(yr + (int64_t)c * N, o);
+      }
+    }
+  }
+}
+
+template <typename TX, typename TW, int NPL>
+__global__ void __launch_bounds__(kRingThreads, 1) rmsnorm_bwd_ring_kernel(
+    const TX* __restrict__ dy, const TX* __restrict__ x, const TW* __restrict__ w, TX* __restrict__ dx,
+    float* __restrict__ partial, int64_t rows, int H, float eps) {
+  constexpr int N = Chunk<TX>::N;
+  constexpr int S = kSlotsBwd;
+  constexpr int WSF = NPL * N * kGroupThreads;  // floats of the staged weight / of one group's dw fold
+  extern __shared__ __align__(128) uint8_t smem_ring[];
+  __shared__ __align__(8) uint64_t full_bar[S], empty_bar[S];
+  __shared__ float2 red[kGroups][2][kGroupWarps];
+  __shared__ volatile int abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nch = H / N;
+  const uint32_t row_bytes = (uint32_t)H * sizeof(TX);
+  const uint32_t half_bytes = (row_bytes + 127u) & ~127u;
+  const uint32_t slot_bytes = 2 * half_bytes;  // x row, then dy row
+  float* ws = reinterpret_cast<float*>(smem_ring);
+  uint8_t* ring = smem_ring + WSF * 4;
+  if (threadIdx.x == 0) {
+    for (int q = 0; q < S; ++q) {
+      tc::mbar_init(&full_bar[q], 1);
+      tc::mbar_init(&empty_bar[q], 1);
+    }
+    tc::fence_barrier_init();
+    tc::fence_proxy_async_smem();
+    abort_flag = 0;
+  }
+  stage_weight<TW, NPL, N>(ws, w, H, threadIdx.x, blockDim.x);
+  __syncthreads();
+  const int64_t my_rows = (rows - blockIdx.x + gridDim.x - 1) / gridDim.x;
+  if (warp == 0) {
+    if (lane == 0)
+      ring_produce<S>(ring, slot_bytes, half_bytes, reinterpret_cast<const uint8_t*>(x),
+                      reinterpret_cast<const uint8_t*>(dy), (int64_t)H * sizeof(TX), row_bytes, my_rows, full_bar,
+                      empty_bar, &abort_flag, 3);
+    return;
+  }
+  const int ct = threadIdx.x - 32;
+  const int grp = ct / kGroupThreads, gt = ct % kGroupThreads, gw = gt >> 5;
+  const float invH = 1.0f / (float)H;
+  float acc[NPL][N];
+#pragma unroll
+  for (int j = 0; j < NPL; ++j)
+#pragma unroll
+    for (int e = 0; e < N; ++e) acc[j][e] = 0.f;
+  for (int64_t i = grp; i < my_rows; i += kGroups) {
+    const int slot = (int)(i % S);
+    const bool ok = tc::mbar_wait(&full_bar[slot], (uint32_t)((i / S) & 1), &abort_flag, kRingBudget);
+    const uint4* sx = reinterpret_cast<const uint4*>(ring + slot * slot_bytes);
+    const uint4* sd = reinterpret_cast<const uint4*>(ring + slot * slot_bytes + half_bytes);
+    uint4 xr[NPL], dr[NPL];
+    float ss = 0.f, cc = 0.f;
+#pragma unroll
+    for (int j = 0; j < NPL; ++j) {
+      const int c = gt + kGroupThreads * j;
+      if (ok && c < nch) {
+        xr[j] = sx[c];
+        dr[j] = sd[c];
+        float v[N], d[N];
+        unpack<TX>(xr[j], v);
+        unpack<TX>(dr[j], d);
+#pragma unroll
+        for (int e = 0; e < N; ++e) {
+          ss = fmaf(v[e], v[e], ss);
+          cc = fmaf(d[e] * ws[(j * N + e) * kGroupThreads + gt], v[e], cc);
+        }
+      }
+    }
+    ss = warp_sum(ss);
+    cc = warp_sum(cc);
+    const int rb = (int)((i / kGroups) & 1);
+    if (lane == 0) red[grp][rb][gw] = make_float2(ss, cc);
+    if (!bar_and(ok, 1 + grp, kGroupThreads)) {
+      if (gt == 0) ring_fail(&abort_flag, 4);
+      break;
+    }
+    if (gt == 0) tc::mbar_arrive(&empty_bar[slot]);
+    float tss = 0.f, tcc = 0.f;
+#pragma unroll
+    for (int q = 0; q < kGroupWarps; ++q) {
+      const float2 t = red[grp][rb][q];
+      tss += t.x;
+      tcc += t.y;
+    }
+    const float r = 1.0f / sqrtf(tss * invH + eps);
+    const float k2 = r * r * r * tcc * invH;
+    TX* dxr = dx + (blockIdx.x + i * gridDim.x) * (int64_t)H;
+#pragma unroll
+    for (int j = 0; j < NPL; ++j) {
+      const int c = gt + kGroupThreads * j;
+      if (c < nch) {
+        float v[N], d[N], o[N];
+        unpack<TX>(xr[j], v);
+        unpack<TX>(dr[j], d);
+#pragma unroll
+        for (int e = 0; e < N; ++e) {
+          const float g = d[e] * ws[(j * N + e) * kGroupThreads + gt];
+          acc[j][e] = fmaf(d[e], v[e] * r, acc[j][e]);
+          o[e] = r * g - v[e] * k2;
+        }
+        store_chunk<TX>(dxr + (int64_t)c * N, o);
+      }
+    }
+  }
+  // fold the four groups' dw in the (now idle) ring, then write this block's partial row
+  bar_and(true, 5, kConsumerThreads);
+  float* fold = reinterpret_cast<float*>(ring);
+#pragma unroll
+  for (int j = 0; j < NPL; ++j)
+#pragma unroll
+    for (int e = 0; e < N; ++e) fold[(size_t)grp * WSF + (j * N + e) * kGroupThreads + gt] = acc[j][e];
+  bar_and(true, 5, kConsumerThreads);
+  for (int c = ct; c < H; c += kConsumerThreads) {
+    const int ch = c / N, e = c - ch * N;
+    const int idx = ((ch / kGroupThreads) * N + e) * kGroupThreads + (ch % kGroupThreads);
+    float s2 = 0.f;
+#pragma unroll
+    for (int q = 0; q < kGroups; ++q) s2 += fold[(size_t)q * WSF + idx];
+    partial[(size_t)blockIdx.x * H + c] = s2;
+  }
+}
+
+template <typename TX>
+bool ring_ok(const void* x, int64_t xs, const void* out, int64_t os, int64_t H, int64_t rows) {
+  constexpr int N = Chunk<TX>::N;
+  return rows > 0 && (H % N) == 0 && H * (int64_t)sizeof(TX) <= kRingMaxRowBytes && aligned16(x) && aligned16(out) &&
+         (xs % N) == 0 && (os % N) == 0;
+}
+
+// 16-byte chunks per group thread (1..8 for rows of at most 8 KB).
+int ring_npl(int64_t H, int N) {
+  const int64_t per = (H / N + kGroupThreads - 1) / kGroupThreads;
+  return per <= 1 ? 1 : per <= 2 ? 2 : per <= 4 ? 4 : 8;
+}
+
 // ----------------------------------------------------------------- launchers
 constexpr int kBwdMaxBlocks = 160;  // upper bound on persistent blocks (>= B200's 148 SMs)
 constexpr size_t kBwdSmemBudget = 160 * 1024;
@@ -361,6 +674,21 @@ int launch_fwd(const void* x, int64_t xs, const void* res, const void* w, void* 
   const bool vec = vec_ok<TX>(x, xs, H) && aligned16(y) && (ys % N) == 0 &&
                    (!RESID || aligned16(res)) && aligned16(w);
   const int nch = chunks_per_lane(H, N);
+  if (!RESID && vec && ring_ok<TX>(x, xs, y, ys, H, rows)) {
+    const int npl = ring_npl(H, N);
+    const int slot = (int)((H * (int64_t)sizeof(TX) + 127) & ~(int64_t)127);
+    const int smem = npl * N * kGroupThreads * 4 + kSlotsFwd * slot;
+    int grid = num_sms();
+    if (rows < grid) grid = (int)rows;
+    TX* yo = static_cast<TX*>(y);
+    auto kfn = npl == 1 ? rmsnorm_fwd_ring_kernel<TX, TW, 1>
+             : npl == 2 ? rmsnorm_fwd_ring_kernel<TX, TW, 2>
+             : npl == 4 ? rmsnorm_fwd_ring_kernel<TX, TW, 4>
+                        : rmsnorm_fwd_ring_kernel<TX, TW, 8>;
+    cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    kfn<<<grid, kRingThreads, smem, st>>>(xp, xs, wp, yo, ys, rstd, rows, (int)H, eps);
+    return check_launch("rmsnorm_fwd_ring");
+  }
   if (vec && nch <= kMaxChunksPerLane) {
 #define ATS_FWD(NC) rmsnorm_fwd_kernel<TX, TW, RESID, NC><<<grid, block, 0, st>>>(xp, xs, rp, wp, y, ys, rstd, rows, (int)H, eps)
     if (nch <= 1) ATS_FWD(1);
@@ -390,6 +718,27 @@ int launch_bwd(const void* dy, const void* x, const void* w, void* dx, void* dre
   float* partial = static_cast<float*>(ws);
   const TX* xp = static_cast<const TX*>(x);
   const TW* wp = static_cast<const TW*>(w);
+  if (!RESID && vec && ring_ok<TX>(x, H, dx, H, H, rows) && aligned16(dy)) {
+    const int npl = ring_npl(H, N);
+    const int64_t half = (H * (int64_t)sizeof(TX) + 127) & ~(int64_t)127;
+    // the ring region also holds the final dw fold of the four consumer groups
+    const int64_t ring_bytes = kSlotsBwd * 2 * half;
+    const int64_t fold_bytes = (int64_t)kGroups * npl * N * kGroupThreads * 4;
+    const int smem = npl * N * kGroupThreads * 4 + (int)(ring_bytes > fold_bytes ? ring_bytes : fold_bytes);
+    int grid = num_sms() < kBwdMaxBlocks ? num_sms() : kBwdMaxBlocks;
+    if (rows < grid) grid = (int)rows;
+    const TX* dyp = static_cast<const TX*>(dy);
+    TX* dxo = static_cast<TX*>(dx);
+    auto kfn = npl == 1 ? rmsnorm_bwd_ring_kernel<TX, TW, 1>
+             : npl == 2 ? rmsnorm_bwd_ring_kernel<TX, TW, 2>
+             : npl == 4 ? rmsnorm_bwd_ring_kernel<TX, TW, 4>
+                        : rmsnorm_bwd_ring_kernel<TX, TW, 8>;
+    cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    kfn<<<grid, kRingThreads, smem, st>>>(dyp, xp, wp, dxo, partial, rows, (int)H, eps);
+    ATS_TRY(check_launch("rmsnorm_bwd_ring"));
+    dw_reduce_kernel<TW><<<(unsigned)((H + 255) / 256), 256, 0, st>>>(partial, grid, (int)H, static_cast<TW*>(dw));
+    return check_launch("rmsnorm_dw_reduce");
+  }
   if (rows > 0) {
     if (vec) {
 #define ATS_BWD(NC)                                                                                        \
@@ -445,6 +794,13 @@ using namespace ats;
                     : ((wd) == ATS_BF16 ? FN<float, bf16, R> : FN<float, float, R>))
 
 extern "C" {
+
+int ats_rmsnorm_status(int* status) {
+  if (status == nullptr) return fail(ATS_EBADARG, "rmsnorm_status: null output");
+  cudaError_t e = cudaMemcpyFromSymbol(status, g_ring_status, sizeof(int));
+  if (e != cudaSuccess) return fail(ATS_ECUDA, "rmsnorm_status: %s", cudaGetErrorString(e));
+  return *status == 0 ? ATS_OK : fail(ATS_ETIMEOUT, "rmsnorm: a bounded device wait gave up (code %d)", *status);
+}
 
 size_t ats_rmsnorm_bwd_workspace_bytes(int64_t rows, int64_t hidden) {
   (void)rows;

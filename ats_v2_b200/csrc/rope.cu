@@ -1,13 +1,13 @@
 // Rotate-half rotary embedding for q and k in one launch, forward and adjoint.
 //
-// Work item = (token, head, chunk pair): a thread loads the 16-byte chunk at
-// column j of the first half of a head row and the matching chunk at j+D/2,
-// plus the cos/sin chunks of the token's position, and writes both output
-// chunks.  Items are ordered token-major, then head, then chunk, so for the
-// attention layout (BSHD memory viewed as [B,H,S,D]) consecutive threads
-// stream consecutive memory, and the 4*D bytes of cos/sin for a position are
-// reused from L1 by all Hq+Hk heads of that token.  q/k are read once and
-// written once: one HBM pass in each direction.
+// A thread owns one (token, 16-byte chunk pair): the chunk at column j of
+// the first half of a head row and the matching chunk at j+D/2.  It loads the
+// token's cos/sin chunks once, keeps them in registers, and rotates that
+// chunk pair in all Hq+Hk heads of the token, several heads per step so
+// many loads are in flight.  Consecutive threads take consecutive chunks of
+// a head row, so for the attention layout (BSHD memory viewed as [B,H,S,D])
+// every warp load is whole 128-byte lines.  q/k are read once and written
+// once: one HBM pass in each direction.
 //
 // Rounding mirrors the reference's torch ops (rope.py:85-86), each of which
 // rounds to the tensor dtype:
@@ -41,50 +41,110 @@ __device__ __forceinline__ void rot_pair(float x1, float x2, float c1, float c2,
   }
 }
 
-// Vectorised: D/2 a multiple of the chunk size, strides and pointers aligned.
-// Block b handles tokens [b*TPB, b*TPB+TPB); within it, item i decomposes
-// (32-bit) into (token, head, chunk pair).
-constexpr int kTokensPerBlock = 4;
+// Packed bf16x2 arithmetic (sm_90+): each op rounds its exact result once
+// to bf16, which is what torch's bf16 mul/add/sub produce (the float32
+// intermediate of two bf16 operands cannot double-round differently).
+__device__ __forceinline__ uint32_t bmul2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t badd2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t bsub2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
 
-template <typename T>
-__global__ void __launch_bounds__(256) rope_vec_kernel(RopeTensor q, RopeTensor k, const T* __restrict__ cosp,
+// Rotate one 16-byte chunk pair (x1 at column j, x2 at j+D/2).
+template <typename T, bool adj>
+__device__ __forceinline__ void rot_chunk(const uint4& x1, const uint4& x2, const uint4& c1, const uint4& c2,
+                                          const uint4& s1, const uint4& s2, uint4& o1, uint4& o2) {
+  if constexpr (sizeof(T) == 2) {
+    const uint32_t* a = &x1.x;
+    const uint32_t* bq = &x2.x;
+    const uint32_t* C1 = &c1.x;
+    const uint32_t* C2 = &c2.x;
+    const uint32_t* S1 = &s1.x;
+    const uint32_t* S2 = &s2.x;
+    uint32_t* p1 = &o1.x;
+    uint32_t* p2 = &o2.x;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      if (!adj) {
+        p1[q] = bsub2(bmul2(a[q], C1[q]), bmul2(bq[q], S1[q]));
+        p2[q] = badd2(bmul2(bq[q], C2[q]), bmul2(a[q], S2[q]));
+      } else {
+        p1[q] = badd2(bmul2(a[q], C1[q]), bmul2(bq[q], S2[q]));
+        p2[q] = bsub2(bmul2(bq[q], C2[q]), bmul2(a[q], S1[q]));
+      }
+    }
+  } else {
+    const float* a = reinterpret_cast<const float*>(&x1);
+    const float* bq = reinterpret_cast<const float*>(&x2);
+    const float* C1 = reinterpret_cast<const float*>(&c1);
+    const float* C2 = reinterpret_cast<const float*>(&c2);
+    const float* S1 = reinterpret_cast<const float*>(&s1);
+    const float* S2 = reinterpret_cast<const float*>(&s2);
+    float* p1 = reinterpret_cast<float*>(&o1);
+    float* p2 = reinterpret_cast<float*>(&o2);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) rot_pair<float>(a[q], bq[q], C1[q], C2[q], S1[q], S2[q], adj, p1[q], p2[q]);
+  }
+}
+
+// Vectorised: one thread per (token, 16-byte chunk pair).  The thread loads
+// its four cos/sin chunks once and rotates that chunk pair in every q and k
+// head of the token, UH heads per step so 2*UH loads are in flight.
+constexpr int kUH = 4;
+
+template <typename T, bool adj>
+__global__ void __launch_bounds__(256, 3) rope_vec_kernel(RopeTensor q, RopeTensor k, const T* __restrict__ cosp,
                                                         const T* __restrict__ sinp, int64_t cs_stride, int64_t S,
-                                                        int64_t D, int64_t n_tokens, bool adj) {
+                                                        int64_t D, int64_t n_tokens) {
   constexpr int N = Chunk<T>::N;
   const int half = (int)(D / 2);
   const int cph = half / N;  // chunk pairs per head row
-  const int heads = (int)(q.heads + k.heads);
-  const int per_tok = heads * cph;
-  const int64_t tok0 = (int64_t)blockIdx.x * kTokensPerBlock;
-  int64_t ntok = n_tokens - tok0;
-  if (ntok > kTokensPerBlock) ntok = kTokensPerBlock;
-  const int items = (int)ntok * per_tok;
-  for (int i = threadIdx.x; i < items; i += blockDim.x) {
-    const int tl = i / per_tok;
-    const int r = i - tl * per_tok;
-    const int hh = r / cph;
-    const int cp = r - hh * cph;
-    const int64_t tok = tok0 + tl;
-    const int64_t b = tok / S, s = tok - b * S;
-    const bool isq = hh < q.heads;
-    const RopeTensor& t = isq ? q : k;
-    const int64_t h = isq ? hh : hh - q.heads;
-    const int j = cp * N;
-    const T* src = static_cast<const T*>(t.in) + b * t.is_b + h * t.is_h + s * t.is_s;
-    T* dst = static_cast<T*>(t.out) + b * t.os_b + h * t.os_h + s * t.os_s;
-    float x1[N], x2[N], c1[N], c2[N], s1[N], s2[N], o1[N], o2[N];
-    load_chunk<T>(src + j, x1);
-    load_chunk<T>(src + j + half, x2);
-    const T* cr = cosp + s * cs_stride;
-    const T* sr = sinp + s * cs_stride;
-    load_chunk<T>(cr + j, c1);
-    load_chunk<T>(cr + j + half, c2);
-    load_chunk<T>(sr + j, s1);
-    load_chunk<T>(sr + j + half, s2);
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t tok = idx / cph;
+  if (tok >= n_tokens) return;
+  const int j = (int)(idx - tok * cph) * N;
+  const int64_t b = tok / S, s = tok - b * S;
+  const uint4* cr = reinterpret_cast<const uint4*>(cosp + s * cs_stride + j);
+  const uint4* sr = reinterpret_cast<const uint4*>(sinp + s * cs_stride + j);
+  const uint4 c1 = cr[0], s1 = sr[0];
+  const uint4 c2 = *reinterpret_cast<const uint4*>(cosp + s * cs_stride + j + half);
+  const uint4 s2 = *reinterpret_cast<const uint4*>(sinp + s * cs_stride + j + half);
+#pragma unroll 1
+  for (int which = 0; which < 2; ++which) {
+    const RopeTensor& t = which == 0 ? q : k;
+    const T* src0 = static_cast<const T*>(t.in) + b * t.is_b + s * t.is_s + j;
+    T* dst0 = static_cast<T*>(t.out) + b * t.os_b + s * t.os_s + j;
+    for (int64_t h0 = 0; h0 < t.heads; h0 += kUH) {
+      uint4 x1[kUH], x2[kUH];
 #pragma unroll
-    for (int e = 0; e < N; ++e) rot_pair<T>(x1[e], x2[e], c1[e], c2[e], s1[e], s2[e], adj, o1[e], o2[e]);
-    store_chunk<T>(dst + j, o1);
-    store_chunk<T>(dst + j + half, o2);
+      for (int u = 0; u < kUH; ++u) {
+        if (h0 + u < t.heads) {
+          const T* src = src0 + (h0 + u) * t.is_h;
+          x1[u] = *reinterpret_cast<const uint4*>(src);
+          x2[u] = *reinterpret_cast<const uint4*>(src + half);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kUH; ++u) {
+        if (h0 + u < t.heads) {
+          uint4 o1, o2;
+          rot_chunk<T, adj>(x1[u], x2[u], c1, c2, s1, s2, o1, o2);
+          T* dst = dst0 + (h0 + u) * t.os_h;
+          *reinterpret_cast<uint4*>(dst) = o1;
+          *reinterpret_cast<uint4*>(dst + half) = o2;
+        }
+      }
+    }
   }
 }
 
@@ -132,12 +192,18 @@ int launch(const RopeTensor& q, const RopeTensor& k, const void* cosp, const voi
                    aligned16(sinp) && (cs_stride % N) == 0;
   const int64_t n_tokens = B * S;
   if (n_tokens * heads == 0) return ATS_OK;
-  if (vec && heads * (D / 2) / N < (int64_t)1 << 28) {
-    const int64_t blocks = (n_tokens + kTokensPerBlock - 1) / kTokensPerBlock;
+  if (vec) {
+    const int64_t threads = n_tokens * ((D / 2) / N);
+    const int64_t blocks = (threads + 255) / 256;
     if (blocks >= ((int64_t)1 << 31)) return fail(ATS_EUNSUPPORTED, "rope_apply: too many tokens");
-    rope_vec_kernel<T><<<(unsigned)blocks, 256, 0, st>>>(q, k, static_cast<const T*>(cosp),
-                                                           static_cast<const T*>(sinp), cs_stride, S, D, n_tokens,
-                                                           adj);
+    if (adj)
+      rope_vec_kernel<T, true><<<(unsigned)blocks, 256, 0, st>>>(q, k, static_cast<const T*>(cosp),
+                                                                   static_cast<const T*>(sinp), cs_stride, S, D,
+                                                                   n_tokens);
+    else
+      rope_vec_kernel<T, false><<<(unsigned)blocks, 256, 0, st>>>(q, k, static_cast<const T*>(cosp),
+                                                                    static_cast<const T*>(sinp), cs_stride, S, D,
+                                                                    n_tokens);
   } else {
     const int64_t n_items = n_tokens * heads * (D / 2);
     const int64_t cap = (int64_t)num_sms() * 16;

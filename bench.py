@@ -265,8 +265,9 @@ class RopeWorkload(Workload):
         g = t.Generator(device="cuda").manual_seed(self.rank)
         self.qm = t.randn(self.B, self.S, self.HQ, self.D, device="cuda", generator=g).bfloat16()
         self.km = t.randn(self.B, self.S, self.HK, self.D, device="cuda", generator=g).bfloat16()
-        self.gq = t.randn(self.B, self.HQ, self.S, self.D, device="cuda", generator=g).bfloat16()
-        self.gk = t.randn(self.B, self.HK, self.S, self.D, device="cuda", generator=g).bfloat16()
+        # upstream gradients in the layout attention hands back: BSHD memory viewed as [B,H,S,D]
+        self.gq = t.randn(self.B, self.S, self.HQ, self.D, device="cuda", generator=g).bfloat16().transpose(1, 2)
+        self.gk = t.randn(self.B, self.S, self.HK, self.D, device="cuda", generator=g).bfloat16().transpose(1, 2)
         self.rope = RotaryEmbedding(self.D, self.S, 500000.0).cuda()
 
     def step(self, evs):
@@ -289,29 +290,29 @@ class RopeWorkload(Workload):
         t = self.torch
         self.hq = self.qm.cpu().pin_memory()
         self.hk = self.km.cpu().pin_memory()
-        self.hgq = self.gq.cpu().pin_memory()
-        self.hgk = self.gk.cpu().pin_memory()
-        self.hqo = t.empty(self.gq.shape, dtype=t.bfloat16).pin_memory()
-        self.hko = t.empty(self.gk.shape, dtype=t.bfloat16).pin_memory()
+        self.hgq = self.gq.transpose(1, 2).cpu().pin_memory()  # BSHD host buffers
+        self.hgk = self.gk.transpose(1, 2).cpu().pin_memory()
+        self.hqo = t.empty_like(self.hq).pin_memory()
+        self.hko = t.empty_like(self.hk).pin_memory()
         self.hdq = t.empty_like(self.hq).pin_memory()
         self.hdk = t.empty_like(self.hk).pin_memory()
         self.dq_in, self.dk_in = t.empty_like(self.qm), t.empty_like(self.km)
-        self.dgq, self.dgk = t.empty_like(self.gq), t.empty_like(self.gk)
+        self.dgq_m, self.dgk_m = t.empty_like(self.qm), t.empty_like(self.km)
         n = (self.hq.numel() + self.hk.numel()) * 2
         self.h2d = 2 * n
         self.d2h = 2 * n
 
     def e2e_step(self):
         t = self.torch
-        for dst, src in ((self.dq_in, self.hq), (self.dk_in, self.hk), (self.dgq, self.hgq), (self.dgk, self.hgk)):
+        for dst, src in ((self.dq_in, self.hq), (self.dk_in, self.hk), (self.dgq_m, self.hgq), (self.dgk_m, self.hgk)):
             dst.copy_(src, non_blocking=True)
         q = self.dq_in.transpose(1, 2).requires_grad_()
         k = self.dk_in.transpose(1, 2).requires_grad_()
         cos, sin = self.rope(self.S, self.qm.device, t.bfloat16)
         qo, ko = self.apply(q, k, cos, sin)
-        t.autograd.backward([qo, ko], [self.dgq, self.dgk])
-        self.hqo.copy_(qo.detach(), non_blocking=True)
-        self.hko.copy_(ko.detach(), non_blocking=True)
+        t.autograd.backward([qo, ko], [self.dgq_m.transpose(1, 2), self.dgk_m.transpose(1, 2)])
+        self.hqo.copy_(qo.detach().transpose(1, 2), non_blocking=True)
+        self.hko.copy_(ko.detach().transpose(1, 2), non_blocking=True)
         self.hdq.copy_(q.grad.transpose(1, 2), non_blocking=True)
         self.hdk.copy_(k.grad.transpose(1, 2), non_blocking=True)
 

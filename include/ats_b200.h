@@ -75,6 +75,11 @@ ATS_API int ats_rmsnorm_bwd(const void* dy, const void* x, ats_dtype x_dtype,
                     void* workspace, size_t workspace_bytes,
                     int64_t rows, int64_t hidden, float eps, void* stream);
 
+/* Device status of the RMSNorm ring kernels since the library loaded: 0 and
+ * ATS_OK when every bounded device-side wait completed, else the wait's code
+ * and ATS_ETIMEOUT.  Synchronous; for diagnostics. */
+ATS_API int ats_rmsnorm_status(int* status);
+
 /* Allocation-free variant of ats_rmsnorm_bwd (no counterpart in the
  * reference).  It is meant for callers that cannot allocate device memory
  * around the call: a host runtime that reaches this library through a bare C
