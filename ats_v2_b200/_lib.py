@@ -26,6 +26,9 @@ ATS_ETIMEOUT = -4
 ATS_F32 = 0
 ATS_BF16 = 1
 
+ATS_MOE_PACKED = 0
+ATS_MOE_SLOTS = 1
+
 _I64x3 = c_int64 * 3
 
 # name -> (restype, argtypes); mirrors include/ats_b200.h
@@ -49,31 +52,39 @@ SIGNATURES: dict[str, tuple] = {
     "ats_rope_apply": (c_int, [c_void_p, c_void_p, c_int64, POINTER(c_int64), POINTER(c_int64),
                                c_void_p, c_void_p, c_int64, POINTER(c_int64), POINTER(c_int64),
                                c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int, c_int, c_void_p]),
-    "ats_moe_status": (c_int, [c_void_p, c_size_t, c_int64, c_int, c_int, c_int64, POINTER(c_int)]),
-    "ats_moe_plan_export": (c_int, [c_void_p, c_size_t, c_int64, c_int, c_int, c_int64, c_void_p, c_void_p,
-                                    c_void_p]),
+    "ats_moe_status": (c_int, [c_void_p, c_size_t, c_int64, c_int, c_int, c_int64, c_int, POINTER(c_int)]),
+    "ats_moe_plan_export": (c_int, [c_void_p, c_size_t, c_int64, c_int, c_int, c_int64, c_int, c_void_p, c_void_p,
+                                    c_void_p, c_void_p]),
     "ats_moe_uses_tensor_cores": (c_int, [c_int, c_int64, c_int64]),
     "ats_moe_topk": (c_int, [c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
-    "ats_moe_max_rows": (c_int64, [c_int64, c_int, c_int, c_int64]),
-    "ats_moe_workspace_bytes": (c_size_t, [c_int64, c_int, c_int, c_int64]),
-    "ats_moe_route_plan": (c_int, [c_void_p, c_int64, c_int, c_int, c_int64, c_float, c_void_p, c_void_p,
+    "ats_moe_max_rows": (c_int64, [c_int64, c_int, c_int, c_int64, c_int]),
+    "ats_moe_workspace_bytes": (c_size_t, [c_int64, c_int, c_int, c_int64, c_int]),
+    "ats_moe_route_plan": (c_int, [c_void_p, c_int64, c_int, c_int, c_int64, c_int, c_float, c_void_p, c_void_p,
                                    c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
-    "ats_moe_gather": (c_int, [c_void_p, c_void_p, c_int, c_int64, c_int64, c_int, c_int, c_int64,
+    "ats_moe_gather": (c_int, [c_void_p, c_void_p, c_int, c_int64, c_int64, c_int, c_int, c_int64, c_int,
                                c_void_p, c_size_t, c_void_p]),
     "ats_moe_experts_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
-                                    c_int64, c_int, c_int, c_int64, c_int64, c_int64, c_void_p, c_size_t,
+                                    c_int64, c_int, c_int, c_int64, c_int, c_int64, c_int64, c_void_p, c_size_t,
                                     c_void_p]),
-    "ats_moe_combine": (c_int, [c_void_p, c_void_p, c_int, c_int64, c_int64, c_int, c_int, c_int64,
+    "ats_moe_combine": (c_int, [c_void_p, c_void_p, c_int, c_int64, c_int64, c_int, c_int, c_int64, c_int,
                                 c_void_p, c_size_t, c_void_p]),
     "ats_moe_combine_bwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int64, c_int64, c_int,
-                                    c_int, c_int64, c_void_p, c_size_t, c_void_p]),
+                                    c_int, c_int64, c_int, c_void_p, c_size_t, c_void_p]),
     "ats_moe_experts_bwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
-                                    c_void_p, c_void_p, c_void_p, c_int, c_int64, c_int, c_int, c_int64,
+                                    c_void_p, c_void_p, c_void_p, c_int, c_int64, c_int, c_int, c_int64, c_int,
                                     c_int64, c_int64, c_void_p, c_size_t, c_void_p]),
-    "ats_moe_scatter_grad": (c_int, [c_void_p, c_void_p, c_int, c_int64, c_int64, c_int, c_int, c_int64,
+    "ats_moe_scatter_grad": (c_int, [c_void_p, c_void_p, c_int, c_int64, c_int64, c_int, c_int, c_int64, c_int,
                                      c_void_p, c_size_t, c_void_p]),
     "ats_moe_route_bwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64,
-                                  c_int, c_int, c_int64, c_float, c_void_p, c_size_t, c_void_p]),
+                                  c_int, c_int, c_int64, c_int, c_float, c_void_p, c_size_t, c_void_p]),
+    "ats_moe_ep_segments_bytes": (c_size_t, [c_int, c_int]),
+    "ats_moe_ep_segments": (c_int, [c_void_p, c_int, c_int, c_int64, c_void_p, c_size_t, c_void_p]),
+    "ats_moe_ep_experts_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
+                                       c_int, c_int64, c_int64, c_int64, c_void_p, c_size_t, c_void_p]),
+    "ats_moe_ep_experts_bwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                       c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int64, c_int64,
+                                       c_int64, c_void_p, c_size_t, c_void_p]),
+    "ats_moe_ep_status": (c_int, [c_void_p, c_size_t, c_int, c_int, POINTER(c_int)]),
 }
 
 _lib = None

@@ -25,58 +25,65 @@ struct Opnd {
 template <typename TI, typename TO>
 __global__ void __launch_bounds__(256) simt_gemm_kernel(Opnd A, Opnd B, TO* __restrict__ C, int64_t c_si,
                                                         int64_t c_sg, int M, int N, int K, bool kgrouped,
-                                                        const int* __restrict__ seg_start) {
+                                                        SegTable sg) {
   __shared__ float As[kBK][kBM + 4];
   __shared__ float Bs[kBK][kBN + 4];
-  const int e = blockIdx.z;
-  int m0, m1, k0, k1;
-  if (!kgrouped) {  // rows of the group are global rows of A and C
-    m0 = seg_start[e] + blockIdx.y * kBM;
-    m1 = seg_start[e + 1];
+  const int z = blockIdx.z;  // M-grouped: segment; K-grouped: expert
+  int m0, m1, nranges;
+  const TI* Bp = static_cast<const TI*>(B.p);
+  if (!kgrouped) {  // rows of the segment are global rows of A and C
+    m0 = sg.row0[z] + blockIdx.y * kBM;
+    m1 = sg.row0[z] + sg.rows[z];
     if (m0 >= m1) return;
-    k0 = 0;
-    k1 = K;
+    Bp += (int64_t)sg.expert[z] * B.sg;
+    nranges = 1;
   } else {
     m0 = blockIdx.y * kBM;
     m1 = M;
-    k0 = seg_start[e];
-    k1 = seg_start[e + 1];
+    nranges = sg.spe;
   }
+  const TI* Ap = static_cast<const TI*>(A.p);
   const int n0 = blockIdx.x * kBN;
-  const TI* Ap = static_cast<const TI*>(A.p) + (kgrouped ? 0 : 0);
-  const TI* Bp = static_cast<const TI*>(B.p) + (kgrouped ? 0 : (int64_t)e * B.sg);
   const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
   float acc[4][4] = {};
   const bool a_kfast = A.sj == 1, b_nfast = B.sj == 1;
-  for (int kb = k0; kb < k1; kb += kBK) {
-    for (int q = threadIdx.x; q < kBM * kBK; q += 256) {
-      int mm, kk;
-      if (a_kfast) { mm = q / kBK; kk = q % kBK; } else { mm = q % kBM; kk = q / kBM; }
-      const int gm = m0 + mm, gk = kb + kk;
-      As[kk][mm] = (gm < m1 && gk < k1) ? Cvt<TI>::to_f(Ap[(int64_t)gm * A.si + (int64_t)gk * A.sj]) : 0.f;
+  for (int q = 0; q < nranges; ++q) {
+    int k0 = 0, k1 = K;
+    if (kgrouped) {  // the expert's q-th segment of rows
+      const int s = sg.eseg[z * sg.spe + q];
+      k0 = sg.row0[s];
+      k1 = sg.row0[s] + sg.rows[s];
     }
-    for (int q = threadIdx.x; q < kBN * kBK; q += 256) {
-      int nn, kk;
-      if (b_nfast) { nn = q % kBN; kk = q / kBN; } else { nn = q / kBK; kk = q % kBK; }
-      const int gn = n0 + nn, gk = kb + kk;
-      Bs[kk][nn] = (gn < N && gk < k1) ? Cvt<TI>::to_f(Bp[(int64_t)gk * B.si + (int64_t)gn * B.sj]) : 0.f;
+    for (int kb = k0; kb < k1; kb += kBK) {
+      for (int i = threadIdx.x; i < kBM * kBK; i += 256) {
+        int mm, kk;
+        if (a_kfast) { mm = i / kBK; kk = i % kBK; } else { mm = i % kBM; kk = i / kBM; }
+        const int gm = m0 + mm, gk = kb + kk;
+        As[kk][mm] = (gm < m1 && gk < k1) ? Cvt<TI>::to_f(Ap[(int64_t)gm * A.si + (int64_t)gk * A.sj]) : 0.f;
+      }
+      for (int i = threadIdx.x; i < kBN * kBK; i += 256) {
+        int nn, kk;
+        if (b_nfast) { nn = i % kBN; kk = i / kBN; } else { nn = i / kBK; kk = i % kBK; }
+        const int gn = n0 + nn, gk = kb + kk;
+        Bs[kk][nn] = (gn < N && gk < k1) ? Cvt<TI>::to_f(Bp[(int64_t)gk * B.si + (int64_t)gn * B.sj]) : 0.f;
+      }
+      __syncthreads();
+#pragma unroll
+      for (int kk = 0; kk < kBK; ++kk) {
+        float a[4], b[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) a[i] = As[kk][ty * 4 + i];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) b[j] = Bs[kk][tx * 4 + j];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+      }
+      __syncthreads();
     }
-    __syncthreads();
-#pragma unroll
-    for (int kk = 0; kk < kBK; ++kk) {
-      float a[4], b[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) a[i] = As[kk][ty * 4 + i];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) b[j] = Bs[kk][tx * 4 + j];
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
-    }
-    __syncthreads();
   }
-  TO* Cp = C + (kgrouped ? (int64_t)e * c_sg : 0);
+  TO* Cp = C + (kgrouped ? (int64_t)z * c_sg : 0);
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int gm = m0 + ty * 4 + i;
@@ -91,36 +98,35 @@ __global__ void __launch_bounds__(256) simt_gemm_kernel(Opnd A, Opnd B, TO* __re
 
 template <typename T>
 int simt_gemm(Opnd A, Opnd B, T* C, int64_t c_si, int64_t c_sg, int M, int N, int K, bool kgrouped,
-              const int* seg_start, int E, int64_t max_seg_rows, cudaStream_t st) {
-  const int gy = kgrouped ? (M + kBM - 1) / kBM : (int)((max_seg_rows + kBM - 1) / kBM);
-  if (gy == 0 || E == 0) return ATS_OK;
-  dim3 grid((N + kBN - 1) / kBN, gy, E);
-  simt_gemm_kernel<T, T><<<grid, 256, 0, st>>>(A, B, C, c_si, c_sg, M, N, K, kgrouped, seg_start);
+              const SegTable& sg, cudaStream_t st) {
+  const int gy = kgrouped ? (M + kBM - 1) / kBM : (int)((sg.max_seg_rows + kBM - 1) / kBM);
+  const int gz = kgrouped ? sg.E : sg.nseg;
+  if (gy == 0 || gz == 0) return ATS_OK;
+  dim3 grid((N + kBN - 1) / kBN, gy, gz);
+  simt_gemm_kernel<T, T><<<grid, 256, 0, st>>>(A, B, C, c_si, c_sg, M, N, K, kgrouped, sg);
   return check_launch("moe_simt_gemm");
 }
 
-// a = round(round(silu(g)) * u) over the padded rows (h = [g | u], row stride 2F)
+// a = round(round(silu(g)) * u) over every segment's rows (h = [g | u], row stride 2F)
 template <typename T>
-__global__ void swiglu_fwd_kernel(const T* __restrict__ h, T* __restrict__ a, int64_t F,
-                                  const int* __restrict__ seg_start, int E) {
-  const int64_t rows = seg_start[E];
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < rows * F;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / F, f = i - r * F;
+__global__ void swiglu_fwd_kernel(const T* __restrict__ h, T* __restrict__ a, int64_t F, SegTable sg) {
+  const int s = blockIdx.y;
+  const int64_t r0 = sg.row0[s], n = (int64_t)sg.rows[s] * F;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = r0 + i / F, f = i % F;
     const float g = Cvt<T>::to_f(h[r * 2 * F + f]);
     const float u = Cvt<T>::to_f(h[r * 2 * F + F + f]);
-    a[i] = Cvt<T>::from_f(silu_mul<T>(g, u));
+    a[r * F + f] = Cvt<T>::from_f(silu_mul<T>(g, u));
   }
 }
 
 // In place on dh = [dg | du] whose du half holds da on entry.
 template <typename T>
-__global__ void swiglu_bwd_kernel(const T* __restrict__ h, T* __restrict__ dh, int64_t F,
-                                  const int* __restrict__ seg_start, int E) {
-  const int64_t rows = seg_start[E];
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < rows * F;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / F, f = i - r * F;
+__global__ void swiglu_bwd_kernel(const T* __restrict__ h, T* __restrict__ dh, int64_t F, SegTable sg) {
+  const int s = blockIdx.y;
+  const int64_t r0 = sg.row0[s], n = (int64_t)sg.rows[s] * F;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = r0 + i / F, f = i % F;
     const float g = Cvt<T>::to_f(h[r * 2 * F + f]);
     const float u = Cvt<T>::to_f(h[r * 2 * F + F + f]);
     const float da = Cvt<T>::to_f(dh[r * 2 * F + F + f]);
@@ -132,41 +138,129 @@ __global__ void swiglu_bwd_kernel(const T* __restrict__ h, T* __restrict__ dh, i
 }
 
 template <typename T>
-int simt_experts_fwd(const void* xp, const void* wgu, const void* wd, void* h, void* a, void* y, int E, int64_t H,
-                     int64_t F, const MoePlan& plan, cudaStream_t st) {
-  const int64_t msr = align_up((size_t)(plan.C < plan.T ? plan.C : plan.T), kSegAlign);
-  const int* seg = plan.seg_start;
+int simt_experts_fwd(const void* xp, const void* wgu, const void* wd, void* h, void* a, void* y, int64_t H, int64_t F,
+                     const SegTable& sg, cudaStream_t st) {
   // h = xp Wgu_e^T : A(m=row,k=h) = xp[row*H+h], B(k=h,n=j) = Wgu_e[j*H+h]
   ATS_TRY(simt_gemm<T>(Opnd{xp, H, 1, 0}, Opnd{wgu, 1, H, 2 * F * H}, static_cast<T*>(h), 2 * F, 0, 0, (int)(2 * F),
-                       (int)H, false, seg, E, msr, st));
-  swiglu_fwd_kernel<T><<<num_sms() * 8, 256, 0, st>>>(static_cast<const T*>(h), static_cast<T*>(a), F, seg, E);
+                       (int)H, false, sg, st));
+  const dim3 eg((unsigned)(num_sms() * 2), (unsigned)sg.nseg);
+  swiglu_fwd_kernel<T><<<eg, 256, 0, st>>>(static_cast<const T*>(h), static_cast<T*>(a), F, sg);
   ATS_TRY(check_launch("moe_swiglu_fwd"));
   // y = a Wd_e^T : B(k=f,n=h) = Wd_e[h*F+f]
   return simt_gemm<T>(Opnd{a, F, 1, 0}, Opnd{wd, 1, F, H * F}, static_cast<T*>(y), H, 0, 0, (int)H, (int)F, false,
-                      seg, E, msr, st);
+                      sg, st);
 }
 
 template <typename T>
 int simt_experts_bwd(const void* dy, const void* xp, const void* h, const void* a, const void* wgu, const void* wd,
-                     void* dh, void* dxp, void* dwgu, void* dwd, int E, int64_t H, int64_t F, const MoePlan& plan,
+                     void* dh, void* dxp, void* dwgu, void* dwd, int64_t H, int64_t F, const SegTable& sg,
                      cudaStream_t st) {
-  const int64_t msr = align_up((size_t)(plan.C < plan.T ? plan.C : plan.T), kSegAlign);
-  const int* seg = plan.seg_start;
   T* dhp = static_cast<T*>(dh);
   // da = dy Wd_e into the du half of dh : B(k=h,n=f) = Wd_e[h*F+f]
-  ATS_TRY(simt_gemm<T>(Opnd{dy, H, 1, 0}, Opnd{wd, F, 1, H * F}, dhp + F, 2 * F, 0, 0, (int)F, (int)H, false, seg, E,
-                       msr, st));
-  swiglu_bwd_kernel<T><<<num_sms() * 8, 256, 0, st>>>(static_cast<const T*>(h), dhp, F, seg, E);
+  ATS_TRY(simt_gemm<T>(Opnd{dy, H, 1, 0}, Opnd{wd, F, 1, H * F}, dhp + F, 2 * F, 0, 0, (int)F, (int)H, false, sg,
+                       st));
+  const dim3 eg((unsigned)(num_sms() * 2), (unsigned)sg.nseg);
+  swiglu_bwd_kernel<T><<<eg, 256, 0, st>>>(static_cast<const T*>(h), dhp, F, sg);
   ATS_TRY(check_launch("moe_swiglu_bwd"));
-  // dWd_e[h,f] = sum_r dy[r,h] a[r,f]
+  // dWd_e[h,f] = sum over the expert's rows r of dy[r,h] a[r,f]
   ATS_TRY(simt_gemm<T>(Opnd{dy, 1, H, 0}, Opnd{a, F, 1, 0}, static_cast<T*>(dwd), F, H * F, (int)H, (int)F, 0, true,
-                       seg, E, msr, st));
+                       sg, st));
   // dxp = dh Wgu_e : B(k=j,n=h) = Wgu_e[j*H+h]
   ATS_TRY(simt_gemm<T>(Opnd{dh, 2 * F, 1, 0}, Opnd{wgu, H, 1, 2 * F * H}, static_cast<T*>(dxp), H, 0, 0, (int)H,
-                       (int)(2 * F), false, seg, E, msr, st));
-  // dWgu_e[j,h] = sum_r dh[r,j] xp[r,h]
+                       (int)(2 * F), false, sg, st));
+  // dWgu_e[j,h] = sum over the expert's rows r of dh[r,j] xp[r,h]
   return simt_gemm<T>(Opnd{dh, 1, 2 * F, 0}, Opnd{xp, H, 1, 0}, static_cast<T*>(dwgu), H, 2 * F * H, (int)(2 * F),
-                      (int)H, 0, true, seg, E, msr, st);
+                      (int)H, 0, true, sg, st);
+}
+
+int experts_fwd(const void* xp, const void* wgu, const void* wd, void* h, void* a, void* y, ats_dtype dtype, int E,
+                int64_t H, int64_t F, const SegTable& sg, cudaStream_t st) {
+  if (dtype == ATS_BF16) {
+    const int r = tc_experts_fwd(xp, wgu, wd, h, a, y, E, H, F, sg, st);
+    if (r != ATS_EUNSUPPORTED) return r;
+    return simt_experts_fwd<bf16>(xp, wgu, wd, h, a, y, H, F, sg, st);
+  }
+  return simt_experts_fwd<float>(xp, wgu, wd, h, a, y, H, F, sg, st);
+}
+
+int experts_bwd(const void* dy, const void* xp, const void* h, const void* a, const void* wgu, const void* wd,
+                void* dh, void* dxp, void* dwgu, void* dwd, ats_dtype dtype, int E, int64_t H, int64_t F,
+                const SegTable& sg, cudaStream_t st) {
+  if (dtype == ATS_BF16) {
+    const int r = tc_experts_bwd(dy, xp, h, a, wgu, wd, dh, dxp, dwgu, dwd, E, H, F, sg, st);
+    if (r != ATS_EUNSUPPORTED) return r;
+    return simt_experts_bwd<bf16>(dy, xp, h, a, wgu, wd, dh, dxp, dwgu, dwd, H, F, sg, st);
+  }
+  return simt_experts_bwd<float>(dy, xp, h, a, wgu, wd, dh, dxp, dwgu, dwd, H, F, sg, st);
+}
+
+// ---------------------------------------------------------- EP segment table
+struct EpSegs {
+  int* row0;
+  int* rows;
+  int* expert;
+  int* eseg;
+  int* err;
+};
+
+size_t ep_carve(void* ws, int W, int El, EpSegs* o) {
+  const size_t n = (size_t)W * El;
+  size_t off = 0;
+  char* base = static_cast<char*>(ws);
+  auto take = [&](size_t bytes) -> void* {
+    void* r = base ? base + off : nullptr;
+    off = align_up(off + bytes, 256);
+    return r;
+  };
+  EpSegs q;
+  q.row0 = (int*)take(n * 4);
+  q.rows = (int*)take(n * 4);
+  q.expert = (int*)take(n * 4);
+  q.eseg = (int*)take(n * 4);
+  q.err = (int*)take(4);
+  if (o) *o = q;
+  return off;
+}
+
+int ep_check(int W, int El, int64_t C) {
+  if (W < 1 || El < 1 || (int64_t)W * El > kMaxExperts || C < 1)
+    return fail(ATS_EBADARG, "moe_ep: bad sizes W=%d E_local=%d capacity=%lld", W, El, (long long)C);
+  if ((int64_t)W * El * slot_rows(C) >= ((int64_t)1 << 31)) return fail(ATS_EUNSUPPORTED, "moe_ep: rows above 2^31");
+  return ATS_OK;
+}
+
+int ep_table(const void* ws, size_t bytes, int W, int El, int64_t C, SegTable* sg) {
+  ATS_TRY(ep_check(W, El, C));
+  if (ws == nullptr || bytes < ep_carve(nullptr, W, El, nullptr))
+    return fail(ATS_EBADARG, "moe_ep: segment workspace too small");
+  EpSegs q;
+  ep_carve(const_cast<void*>(ws), W, El, &q);
+  sg->row0 = q.row0;
+  sg->rows = q.rows;
+  sg->expert = q.expert;
+  sg->eseg = q.eseg;
+  sg->nseg = W * El;
+  sg->spe = W;
+  sg->E = El;
+  sg->max_rows = (int64_t)W * El * slot_rows(C);
+  sg->max_seg_rows = slot_rows(C);
+  sg->err = q.err;
+  return ATS_OK;
+}
+
+// Segment s = source rank * E_local + local expert, at rows s*Cp.
+__global__ void ep_segments_kernel(const int* __restrict__ recv_kept, int W, int El, int Cp, EpSegs q) {
+  const int n = W * El;
+  for (int s = threadIdx.x; s < n; s += blockDim.x) {
+    const int src = s / El, el = s - src * El;
+    int kept = recv_kept[s];
+    kept = kept < 0 ? 0 : (kept > Cp ? Cp : kept);
+    q.row0[s] = s * Cp;
+    q.rows[s] = (kept + kSegAlign - 1) / kSegAlign * kSegAlign;
+    q.expert[s] = el;
+    q.eseg[el * W + src] = s;
+  }
+  if (threadIdx.x == 0) q.err[0] = 0;
 }
 
 int check_experts(const void* p0, const void* p1, int64_t H, int64_t F, ats_dtype dt) {
@@ -188,38 +282,76 @@ int ats_moe_uses_tensor_cores(ats_dtype dtype, int64_t H, int64_t F) {
 }
 
 int ats_moe_experts_fwd(const void* xp, const void* w_gate_up, const void* w_down, void* h, void* a, void* y,
-                        ats_dtype dtype, int64_t T, int E, int k, int64_t capacity, int64_t H, int64_t F,
+                        ats_dtype dtype, int64_t T, int E, int k, int64_t capacity, int layout, int64_t H, int64_t F,
                         const void* workspace, size_t workspace_bytes, void* stream) {
   MoePlan plan;
-  ATS_TRY(moe_plan_from_ws(workspace, workspace_bytes, T, E, k, capacity, &plan));
+  ATS_TRY(moe_plan_from_ws(workspace, workspace_bytes, T, E, k, capacity, layout, &plan));
   ATS_TRY(check_experts(w_gate_up, w_down, H, F, dtype));
   if (xp == nullptr || h == nullptr || a == nullptr || y == nullptr) return fail(ATS_EBADARG, "moe_experts_fwd: null");
-  cudaStream_t st = (cudaStream_t)stream;
-  if (dtype == ATS_BF16) {
-    const int r = tc_experts_fwd(xp, w_gate_up, w_down, h, a, y, E, H, F, plan, st);
-    if (r != ATS_EUNSUPPORTED) return r;
-    return simt_experts_fwd<bf16>(xp, w_gate_up, w_down, h, a, y, E, H, F, plan, st);
-  }
-  return simt_experts_fwd<float>(xp, w_gate_up, w_down, h, a, y, E, H, F, plan, st);
+  return experts_fwd(xp, w_gate_up, w_down, h, a, y, dtype, E, H, F, plan_segments(plan), (cudaStream_t)stream);
 }
 
 int ats_moe_experts_bwd(const void* dy, const void* xp, const void* h, const void* a, const void* w_gate_up,
                         const void* w_down, void* dh, void* dxp, void* dw_gate_up, void* dw_down, ats_dtype dtype,
-                        int64_t T, int E, int k, int64_t capacity, int64_t H, int64_t F, const void* workspace,
-                        size_t workspace_bytes, void* stream) {
+                        int64_t T, int E, int k, int64_t capacity, int layout, int64_t H, int64_t F,
+                        const void* workspace, size_t workspace_bytes, void* stream) {
   MoePlan plan;
-  ATS_TRY(moe_plan_from_ws(workspace, workspace_bytes, T, E, k, capacity, &plan));
+  ATS_TRY(moe_plan_from_ws(workspace, workspace_bytes, T, E, k, capacity, layout, &plan));
   ATS_TRY(check_experts(w_gate_up, w_down, H, F, dtype));
   if (dy == nullptr || xp == nullptr || h == nullptr || a == nullptr || dh == nullptr || dxp == nullptr ||
       dw_gate_up == nullptr || dw_down == nullptr)
     return fail(ATS_EBADARG, "moe_experts_bwd: null");
-  cudaStream_t st = (cudaStream_t)stream;
-  if (dtype == ATS_BF16) {
-    const int r = tc_experts_bwd(dy, xp, h, a, w_gate_up, w_down, dh, dxp, dw_gate_up, dw_down, E, H, F, plan, st);
-    if (r != ATS_EUNSUPPORTED) return r;
-    return simt_experts_bwd<bf16>(dy, xp, h, a, w_gate_up, w_down, dh, dxp, dw_gate_up, dw_down, E, H, F, plan, st);
-  }
-  return simt_experts_bwd<float>(dy, xp, h, a, w_gate_up, w_down, dh, dxp, dw_gate_up, dw_down, E, H, F, plan, st);
+  return experts_bwd(dy, xp, h, a, w_gate_up, w_down, dh, dxp, dw_gate_up, dw_down, dtype, E, H, F,
+                     plan_segments(plan), (cudaStream_t)stream);
+}
+
+size_t ats_moe_ep_segments_bytes(int W, int E_local) {
+  if (W < 1 || E_local < 1) return 0;
+  return ep_carve(nullptr, W, E_local, nullptr);
+}
+
+int ats_moe_ep_segments(const int32_t* recv_kept, int W, int E_local, int64_t capacity, void* seg_workspace,
+                        size_t seg_workspace_bytes, void* stream) {
+  SegTable sg;
+  ATS_TRY(ep_table(seg_workspace, seg_workspace_bytes, W, E_local, capacity, &sg));
+  if (recv_kept == nullptr) return fail(ATS_EBADARG, "moe_ep_segments: null counts");
+  EpSegs q;
+  ep_carve(seg_workspace, W, E_local, &q);
+  ep_segments_kernel<<<1, 256, 0, (cudaStream_t)stream>>>(recv_kept, W, E_local, (int)slot_rows(capacity), q);
+  return check_launch("moe_ep_segments");
+}
+
+int ats_moe_ep_experts_fwd(const void* xr, const void* w_gate_up, const void* w_down, void* h, void* a, void* y,
+                           ats_dtype dtype, int W, int E_local, int64_t capacity, int64_t H, int64_t F,
+                           const void* seg_workspace, size_t seg_workspace_bytes, void* stream) {
+  SegTable sg;
+  ATS_TRY(ep_table(seg_workspace, seg_workspace_bytes, W, E_local, capacity, &sg));
+  ATS_TRY(check_experts(w_gate_up, w_down, H, F, dtype));
+  if (xr == nullptr || h == nullptr || a == nullptr || y == nullptr) return fail(ATS_EBADARG, "moe_ep_experts_fwd: null");
+  return experts_fwd(xr, w_gate_up, w_down, h, a, y, dtype, E_local, H, F, sg, (cudaStream_t)stream);
+}
+
+int ats_moe_ep_experts_bwd(const void* dy, const void* xr, const void* h, const void* a, const void* w_gate_up,
+                           const void* w_down, void* dh, void* dxr, void* dw_gate_up, void* dw_down, ats_dtype dtype,
+                           int W, int E_local, int64_t capacity, int64_t H, int64_t F, const void* seg_workspace,
+                           size_t seg_workspace_bytes, void* stream) {
+  SegTable sg;
+  ATS_TRY(ep_table(seg_workspace, seg_workspace_bytes, W, E_local, capacity, &sg));
+  ATS_TRY(check_experts(w_gate_up, w_down, H, F, dtype));
+  if (dy == nullptr || xr == nullptr || h == nullptr || a == nullptr || dh == nullptr || dxr == nullptr ||
+      dw_gate_up == nullptr || dw_down == nullptr)
+    return fail(ATS_EBADARG, "moe_ep_experts_bwd: null");
+  return experts_bwd(dy, xr, h, a, w_gate_up, w_down, dh, dxr, dw_gate_up, dw_down, dtype, E_local, H, F, sg,
+                     (cudaStream_t)stream);
+}
+
+int ats_moe_ep_status(const void* seg_workspace, size_t seg_workspace_bytes, int W, int E_local, int* status) {
+  SegTable sg;
+  ATS_TRY(ep_table(seg_workspace, seg_workspace_bytes, W, E_local, 1, &sg));
+  if (status == nullptr) return fail(ATS_EBADARG, "moe_ep_status: null output");
+  cudaError_t e = cudaMemcpy(status, sg.err, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return fail(ATS_ECUDA, "moe_ep_status: %s", cudaGetErrorString(e));
+  return *status == 0 ? ATS_OK : fail(ATS_ETIMEOUT, "moe_ep: a bounded device wait gave up (code %d)", *status);
 }
 
 }  // extern "C"

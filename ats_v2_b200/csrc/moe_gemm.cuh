@@ -51,9 +51,9 @@ inline bool tc_shape_supported(int64_t H, int64_t F) {
 // tcgen05 tensor-core expert GEMMs (bf16).  Return ATS_EUNSUPPORTED for shapes
 // the tensor-core tiling does not cover; the caller then uses the CUDA-core path.
 int tc_experts_fwd(const void* xp, const void* wgu, const void* wd, void* h, void* a, void* y, int E, int64_t H,
-                   int64_t F, const MoePlan& plan, cudaStream_t st);
+                   int64_t F, const SegTable& sg, cudaStream_t st);
 int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a, const void* wgu, const void* wd,
-                   void* dh, void* dxp, void* dwgu, void* dwd, int E, int64_t H, int64_t F, const MoePlan& plan,
+                   void* dh, void* dxp, void* dwgu, void* dwd, int E, int64_t H, int64_t F, const SegTable& sg,
                    cudaStream_t st);
 
 }  // namespace ats

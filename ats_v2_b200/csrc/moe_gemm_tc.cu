@@ -43,19 +43,17 @@ constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr long long kWaitBudget = 4000000000LL;  // SM cycles, about 2 s
 
 enum Epi { EPI_STORE = 0, EPI_SWIGLU_FWD = 1, EPI_SWIGLU_BWD = 2 };
-enum Base { BASE_SEG = 0, BASE_EXPERT = 1 };
 
+// Where B (the stacked expert weights in M-grouped GEMMs) is read.
 struct OpSpec {
-  int base;        // BASE_SEG: outer coordinate starts at seg_start[g]; BASE_EXPERT: at g*group_rows
-  int group_rows;  // rows of one expert in a stacked weight
+  int group_rows;  // rows of one expert in the stacked weight
   int sub_offset;  // K-major B loaded as two halves, the second `sub_offset` rows further (0: one load)
 };
 
 struct GemmArgs {
-  const int* seg_start;  // [E+1] padded segment starts of the permuted rows
-  int E;
-  int M, N, K;  // M-grouped: N, K fixed; K-grouped: M, N fixed
-  OpSpec a, b;
+  SegTable seg;  // segments of the permuted rows and their experts
+  int M, N, K;   // M-grouped: N, K fixed; K-grouped: M, N fixed
+  OpSpec b;
   bf16* out;  // output (bf16)
   int64_t ldo;
   int64_t out_group;  // K-grouped: elements between consecutive experts' outputs
@@ -66,9 +64,10 @@ struct GemmArgs {
   int* err;
 };
 
-// tile -> (group, m tile, n tile, k blocks); groups scanned linearly (E is small)
+// tile -> (group, weight index, m tile, n tile, k blocks).  Groups are the
+// segments (M-grouped) or the experts (K-grouped), scanned linearly.
 struct TileInfo {
-  int g, mt, nt, kb;
+  int g, e, mt, nt, kb;
 };
 
 template <int BN, bool KGROUP, int EPI>
@@ -76,27 +75,34 @@ __device__ __forceinline__ int n_tiles(const GemmArgs& p) {
   return EPI == EPI_SWIGLU_FWD ? p.F / (BN / 2) : p.N / BN;
 }
 
+template <bool KGROUP>
+__device__ __forceinline__ int n_groups(const GemmArgs& p) {
+  return KGROUP ? p.seg.E : p.seg.nseg;
+}
+
 template <int BN, bool KGROUP, int EPI>
 __device__ __forceinline__ bool decode_tile(const GemmArgs& p, const int* tiles_before, int t, TileInfo& ti) {
   const int NT = n_tiles<BN, KGROUP, EPI>(p);
-  for (int g = 0; g < p.E; ++g) {
+  const int G = n_groups<KGROUP>(p);
+  for (int g = 0; g < G; ++g) {
     if (t < tiles_before[g + 1]) {
       const int q = t - tiles_before[g];
       ti.g = g;
       ti.mt = q / NT;
       ti.nt = q - ti.mt * NT;
-      if (KGROUP)
-        ti.kb = (p.seg_start[g + 1] - p.seg_start[g]) / BK;
-      else
+      if (KGROUP) {
+        ti.e = g;
+        int kb = 0;
+        for (int u = 0; u < p.seg.spe; ++u) kb += p.seg.rows[p.seg.eseg[g * p.seg.spe + u]] / BK;
+        ti.kb = kb;
+      } else {
+        ti.e = p.seg.expert[g];
         ti.kb = p.K / BK;
+      }
       return true;
     }
   }
   return false;
-}
-
-__device__ __forceinline__ int op_base(const OpSpec& o, const int* seg, int g) {
-  return o.base == BASE_SEG ? seg[g] : g * o.group_rows;
 }
 
 __device__ __forceinline__ void fail_abort(int* err, volatile int* abort, int code) {
@@ -168,10 +174,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
     abort_flag = 0;
     // tiles per group, prefix-summed
     const int NT = n_tiles<BN, KGROUP, EPI>(p);
+    const int G = n_groups<KGROUP>(p);
     int acc = 0;
     tiles_before[0] = 0;
-    for (int g = 0; g < p.E; ++g) {
-      const int mt = KGROUP ? p.M / BM : (p.seg_start[g + 1] - p.seg_start[g]) / BM;
+    for (int g = 0; g < G; ++g) {
+      const int mt = KGROUP ? p.M / BM : p.seg.rows[g] / BM;
       acc += mt * NT;
       tiles_before[g + 1] = acc;
     }
@@ -184,7 +191,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem_base = tmem_base_s;
-  const int total = tiles_before[p.E];
+  const int total = tiles_before[n_groups<KGROUP>(p)];
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -199,36 +206,43 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
       for (int t = blockIdx.x; t < total && !abort_flag; t += gridDim.x) {
         TileInfo ti;
         decode_tile<BN, KGROUP, EPI>(p, tiles_before, t, ti);
-        const int abase = op_base(p.a, p.seg_start, ti.g);
-        const int bbase = op_base(p.b, p.seg_start, ti.g);
         const int m0 = ti.mt * BM;
         const int n0 = EPI == EPI_SWIGLU_FWD ? ti.nt * (BN / 2) : ti.nt * BN;
+        // K blocks: M-grouped = kb of the fixed K; K-grouped = the expert's segments' rows, in order
+        int u = 0, lkb = 0, seg_s = KGROUP ? p.seg.eseg[ti.g * p.seg.spe] : ti.g;
         for (int kb = 0; kb < ti.kb; ++kb) {
+          if (KGROUP) {
+            while (lkb * BK >= p.seg.rows[seg_s]) {  // next non-empty segment of this expert
+              ++u;
+              lkb = 0;
+              seg_s = p.seg.eseg[ti.g * p.seg.spe + u];
+            }
+          }
           if (!tc::mbar_wait(&empty_bar[stage], phase ^ 1u, &abort_flag, kWaitBudget)) {
-            fail_abort(p.err, &abort_flag, 1);
+            fail_abort(p.seg.err, &abort_flag, 1);
             break;
           }
           uint8_t* sa = ring + stage * STAGE_BYTES;
           uint8_t* sb = sa + A_BYTES;
           tc::mbar_arrive_expect_tx(&full_bar[stage], STAGE_BYTES);
-          if (!A_MN) {
-            tc::tma_load_2d(sa, &tmA, kb * BK, abase + m0, &full_bar[stage]);
-          } else {
-            tc::tma_load_2d(sa, &tmA, m0, abase + kb * BK, &full_bar[stage]);
-            tc::tma_load_2d(sa + 8192, &tmA, m0 + 64, abase + kb * BK, &full_bar[stage]);
+          if (!A_MN) {  // M-grouped A: rows of the tile's segment, K contiguous
+            tc::tma_load_2d(sa, &tmA, kb * BK, p.seg.row0[ti.g] + m0, &full_bar[stage]);
+          } else {      // K-grouped A: M contiguous, K = rows of the current segment
+            const int krow = p.seg.row0[seg_s] + lkb * BK;
+            tc::tma_load_2d(sa, &tmA, m0, krow, &full_bar[stage]);
+            tc::tma_load_2d(sa + 8192, &tmA, m0 + 64, krow, &full_bar[stage]);
           }
-          if (!B_MN) {
-            if (p.b.sub_offset) {
-              tc::tma_load_2d(sb, &tmB, kb * BK, bbase + n0, &full_bar[stage]);
-              tc::tma_load_2d(sb + (BN / 2) * 128, &tmB, kb * BK, bbase + p.b.sub_offset + n0, &full_bar[stage]);
-            } else {
-              tc::tma_load_2d(sb, &tmB, kb * BK, bbase + n0, &full_bar[stage]);
-            }
+          if (!B_MN) {  // stacked weights, K contiguous
+            const int brow = ti.e * p.b.group_rows + n0;
+            tc::tma_load_2d(sb, &tmB, kb * BK, brow, &full_bar[stage]);
+            if (p.b.sub_offset)
+              tc::tma_load_2d(sb + (BN / 2) * 128, &tmB, kb * BK, brow + p.b.sub_offset, &full_bar[stage]);
           } else {
+            const int krow = KGROUP ? p.seg.row0[seg_s] + lkb * BK : ti.e * p.b.group_rows + kb * BK;
 #pragma unroll
-            for (int b = 0; b < BN / 64; ++b)
-              tc::tma_load_2d(sb + b * 8192, &tmB, n0 + b * 64, bbase + kb * BK, &full_bar[stage]);
+            for (int b = 0; b < BN / 64; ++b) tc::tma_load_2d(sb + b * 8192, &tmB, n0 + b * 64, krow, &full_bar[stage]);
           }
+          ++lkb;
           last_parity[stage] = (int)phase;
           if (++stage == STAGES) {
             stage = 0;
@@ -239,7 +253,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
       // drain: every issued load lands before the CTA may exit
       for (int s = 0; s < STAGES; ++s)
         if (last_parity[s] >= 0 && !tc::mbar_wait(&full_bar[s], (uint32_t)last_parity[s], nullptr, kWaitBudget))
-          atomicCAS(p.err, 0, 11);
+          atomicCAS(p.seg.err, 0, 11);
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA
@@ -256,7 +270,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
         const int acc = i & 1;
         const uint32_t acc_phase = (uint32_t)(i >> 1) & 1u;
         if (!tc::mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, &abort_flag, kWaitBudget)) {
-          fail_abort(p.err, &abort_flag, 2);
+          fail_abort(p.seg.err, &abort_flag, 2);
           break;
         }
         tc::tc_fence_after();
@@ -264,7 +278,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
         bool ok = true;
         for (int kb = 0; kb < ti.kb; ++kb) {
           if (!tc::mbar_wait(&full_bar[stage], phase, &abort_flag, kWaitBudget)) {
-            fail_abort(p.err, &abort_flag, 3);
+            fail_abort(p.seg.err, &abort_flag, 3);
             ok = false;
             break;
           }
@@ -293,7 +307,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
       // drain: all issued MMAs complete before TMEM may be freed
       if (issued) {
         tc::mma_commit(&done_bar);
-        if (!tc::mbar_wait(&done_bar, 0u, nullptr, kWaitBudget)) atomicCAS(p.err, 0, 12);
+        if (!tc::mbar_wait(&done_bar, 0u, nullptr, kWaitBudget)) atomicCAS(p.seg.err, 0, 12);
       }
     }
   } else {
@@ -309,7 +323,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
       const uint32_t acc_phase = (uint32_t)(i >> 1) & 1u;
       if constexpr (EPI == EPI_SWIGLU_BWD) {
         // the pre-activations do not depend on the accumulator: start loading them now
-        const int64_t row = (int64_t)p.seg_start[ti.g] + ti.mt * BM + row_in_tile;
+        const int64_t row = (int64_t)p.seg.row0[ti.g] + ti.mt * BM + row_in_tile;
         const int64_t F2 = 2 * (int64_t)p.F;
         const int c0 = chalf * (BN / 2);
         const bf16* hg = p.h + row * F2 + ti.nt * BN + c0;
@@ -321,7 +335,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
           uq[q] = reinterpret_cast<const uint4*>(hu)[q];
         }
         if (!tc::mbar_wait(&tfull_bar[acc], acc_phase, &abort_flag, kWaitBudget)) {
-          fail_abort(p.err, &abort_flag, 4);
+          fail_abort(p.seg.err, &abort_flag, 4);
           break;
         }
         tc::tc_fence_after();
@@ -360,13 +374,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
         }
       } else {
         if (!tc::mbar_wait(&tfull_bar[acc], acc_phase, &abort_flag, kWaitBudget)) {
-          fail_abort(p.err, &abort_flag, 4);
+          fail_abort(p.seg.err, &abort_flag, 4);
           break;
         }
         tc::tc_fence_after();
         const uint32_t t_row = tmem_base + (uint32_t)(acc * BN) + ((uint32_t)(quad * 32) << 16);
         if constexpr (EPI == EPI_SWIGLU_FWD) {
-          const int64_t row = (int64_t)p.seg_start[ti.g] + ti.mt * BM + row_in_tile;
+          const int64_t row = (int64_t)p.seg.row0[ti.g] + ti.mt * BM + row_in_tile;
           const int c0 = chalf * (BN / 4);
           const int n0 = ti.nt * (BN / 2) + c0;
 #pragma unroll 1
@@ -388,8 +402,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
           const bool zero = ti.kb == 0;
           const int c0 = chalf * (BN / 2);
           const int64_t row = KGROUP ? (int64_t)ti.mt * BM + row_in_tile
-                                     : (int64_t)p.seg_start[ti.g] + ti.mt * BM + row_in_tile;
-          bf16* outp = p.out + (KGROUP ? (int64_t)ti.g * p.out_group : 0) + row * p.ldo + (int64_t)ti.nt * BN + c0;
+                                     : (int64_t)p.seg.row0[ti.g] + ti.mt * BM + row_in_tile;
+          bf16* outp = p.out + (KGROUP ? (int64_t)ti.e * p.out_group : 0) + row * p.ldo + (int64_t)ti.nt * BN + c0;
 #pragma unroll 1
           for (int c = 0; c < BN / 2; c += 32) {
             float v[32];
@@ -471,23 +485,19 @@ int pick_bn(int64_t n) { return n % 256 == 0 ? 256 : 128; }
 }  // namespace
 
 int tc_experts_fwd(const void* xp, const void* wgu, const void* wd, void* h, void* a, void* y, int E, int64_t H,
-                   int64_t F, const MoePlan& plan, cudaStream_t st) {
+                   int64_t F, const SegTable& sg, cudaStream_t st) {
   if (!tc_shape_supported(H, F)) return ATS_EUNSUPPORTED;
-  const int64_t R = plan.max_rows;
+  const int64_t R = sg.max_rows;
   CUtensorMap ma, mb;
   GemmArgs p{};
-  p.seg_start = plan.seg_start;
-  p.E = E;
-  p.err = plan.dev_err;
+  p.seg = sg;
   p.F = (int)F;
   // h = xp Wgu_e^T with the SwiGLU epilogue: tile N = 128 gate + 128 up columns
   ATS_TRY(make_map(&ma, xp, H, R, H * 2, 128));
   ATS_TRY(make_map(&mb, wgu, H, (uint64_t)E * 2 * F, H * 2, 128));
-  p.M = 0;
   p.N = (int)F;
   p.K = (int)H;
-  p.a = OpSpec{BASE_SEG, 0, 0};
-  p.b = OpSpec{BASE_EXPERT, (int)(2 * F), (int)F};
+  p.b = OpSpec{(int)(2 * F), (int)F};
   p.h_out = static_cast<bf16*>(h);
   p.a_out = static_cast<bf16*>(a);
   ATS_TRY((launch_tc<256, false, false, EPI_SWIGLU_FWD, false>(ma, mb, p, (R / BM) * (F / 128), st)));
@@ -497,8 +507,7 @@ int tc_experts_fwd(const void* xp, const void* wgu, const void* wd, void* h, voi
   ATS_TRY(make_map(&mb, wd, F, (uint64_t)E * H, F * 2, bn));
   p.N = (int)H;
   p.K = (int)F;
-  p.a = OpSpec{BASE_SEG, 0, 0};
-  p.b = OpSpec{BASE_EXPERT, (int)H, 0};
+  p.b = OpSpec{(int)H, 0};
   p.out = static_cast<bf16*>(y);
   p.ldo = H;
   if (bn == 256) return launch_tc<256, false, false, EPI_STORE, false>(ma, mb, p, (R / BM) * (H / 256), st);
@@ -506,15 +515,13 @@ int tc_experts_fwd(const void* xp, const void* wgu, const void* wd, void* h, voi
 }
 
 int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a, const void* wgu, const void* wd,
-                   void* dh, void* dxp, void* dwgu, void* dwd, int E, int64_t H, int64_t F, const MoePlan& plan,
+                   void* dh, void* dxp, void* dwgu, void* dwd, int E, int64_t H, int64_t F, const SegTable& sg,
                    cudaStream_t st) {
   if (!tc_shape_supported(H, F)) return ATS_EUNSUPPORTED;
-  const int64_t R = plan.max_rows;
+  const int64_t R = sg.max_rows;
   CUtensorMap ma, mb;
   GemmArgs p{};
-  p.seg_start = plan.seg_start;
-  p.E = E;
-  p.err = plan.dev_err;
+  p.seg = sg;
   p.F = (int)F;
   // da = dy Wd_e (B N-major: Wd_e[h][f]) with the SwiGLU backward epilogue -> dh
   {
@@ -523,8 +530,7 @@ int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a,
     ATS_TRY(make_map(&mb, wd, F, (uint64_t)E * H, F * 2, 64));
     p.N = (int)F;
     p.K = (int)H;
-    p.a = OpSpec{BASE_SEG, 0, 0};
-    p.b = OpSpec{BASE_EXPERT, (int)H, 0};
+    p.b = OpSpec{(int)H, 0};
     p.h = static_cast<const bf16*>(h);
     p.out = static_cast<bf16*>(dh);
     if (bn == 256)
@@ -539,8 +545,7 @@ int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a,
     ATS_TRY(make_map(&mb, wgu, H, (uint64_t)E * 2 * F, H * 2, 64));
     p.N = (int)H;
     p.K = (int)(2 * F);
-    p.a = OpSpec{BASE_SEG, 0, 0};
-    p.b = OpSpec{BASE_EXPERT, (int)(2 * F), 0};
+    p.b = OpSpec{(int)(2 * F), 0};
     p.out = static_cast<bf16*>(dxp);
     p.ldo = H;
     if (bn == 256)
@@ -548,7 +553,7 @@ int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a,
     else
       ATS_TRY((launch_tc<128, false, true, EPI_STORE, false>(ma, mb, p, (R / BM) * (H / 128), st)));
   }
-  // dWd_e[h][f] = sum_r dy[r][h] a[r][f]   (A M-major, B N-major, K = segment rows)
+  // dWd_e[h][f] = sum over the expert's rows r of dy[r][h] a[r][f]   (A M-major, B N-major)
   {
     const int bn = pick_bn(F);
     ATS_TRY(make_map(&ma, dy, H, R, H * 2, 64));
@@ -556,18 +561,17 @@ int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a,
     p.M = (int)H;
     p.N = (int)F;
     p.K = 0;
-    p.a = OpSpec{BASE_SEG, 0, 0};
-    p.b = OpSpec{BASE_SEG, 0, 0};
+    p.b = OpSpec{0, 0};
     p.out = static_cast<bf16*>(dwd);
     p.ldo = F;
     p.out_group = H * F;
-    const int64_t tiles = (int64_t)E * (H / BM) * (F / bn);
+    const int64_t tiles = (int64_t)sg.E * (H / BM) * (F / bn);
     if (bn == 256)
       ATS_TRY((launch_tc<256, true, true, EPI_STORE, true>(ma, mb, p, tiles, st)));
     else
       ATS_TRY((launch_tc<128, true, true, EPI_STORE, true>(ma, mb, p, tiles, st)));
   }
-  // dWgu_e[j][h] = sum_r dh[r][j] xp[r][h]
+  // dWgu_e[j][h] = sum over the expert's rows r of dh[r][j] xp[r][h]
   {
     const int bn = pick_bn(H);
     ATS_TRY(make_map(&ma, dh, 2 * F, R, 2 * F * 2, 64));
@@ -577,7 +581,7 @@ int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a,
     p.out = static_cast<bf16*>(dwgu);
     p.ldo = H;
     p.out_group = 2 * F * H;
-    const int64_t tiles = (int64_t)E * (2 * F / BM) * (H / bn);
+    const int64_t tiles = (int64_t)sg.E * (2 * F / BM) * (H / bn);
     if (bn == 256) return launch_tc<256, true, true, EPI_STORE, true>(ma, mb, p, tiles, st);
     return launch_tc<128, true, true, EPI_STORE, true>(ma, mb, p, tiles, st);
   }

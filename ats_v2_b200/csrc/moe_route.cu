@@ -168,9 +168,12 @@ __global__ void __launch_bounds__(1024) plan_kernel(MoePlan plan, float lbw, flo
       ps += plan.prob_partial[(size_t)b * E + e];
     }
     const int kept = (int64_t)run < plan.C ? run : (int)plan.C;
+    const int kept_pad = (kept + kSegAlign - 1) / kSegAlign * kSegAlign;
     plan.counts[e] = run;
     plan.kept[e] = kept;
-    padded[e] = (kept + kSegAlign - 1) / kSegAlign * kSegAlign;
+    plan.seg_rows[e] = kept_pad;
+    plan.seg_expert[e] = e;
+    padded[e] = plan.layout == ATS_MOE_SLOTS ? (int)slot_rows(plan.C) : kept_pad;
     const float fr = plan.T > 0 ? (float)run / Tf : 0.f;
     const float pm = plan.T > 0 ? ps / Tf : 0.f;
     plan.frac[e] = fr;
@@ -461,20 +464,20 @@ using namespace ats;
 
 extern "C" {
 
-int64_t ats_moe_max_rows(int64_t T, int E, int k, int64_t capacity) {
-  if (moe_check(T, E, k, capacity) != ATS_OK) return -1;
-  return moe_cap_rows(T, E, k, capacity);
+int64_t ats_moe_max_rows(int64_t T, int E, int k, int64_t capacity, int layout) {
+  if (moe_check(T, E, k, capacity, layout) != ATS_OK) return -1;
+  return moe_cap_rows(T, E, k, capacity, layout);
 }
 
-size_t ats_moe_workspace_bytes(int64_t T, int E, int k, int64_t capacity) {
-  if (moe_check(T, E, k, capacity) != ATS_OK) return 0;
-  return moe_plan_carve(nullptr, T, E, k, capacity, nullptr);
+size_t ats_moe_workspace_bytes(int64_t T, int E, int k, int64_t capacity, int layout) {
+  if (moe_check(T, E, k, capacity, layout) != ATS_OK) return 0;
+  return moe_plan_carve(nullptr, T, E, k, capacity, layout, nullptr);
 }
 
 int ats_moe_status(const void* workspace, size_t workspace_bytes, int64_t T, int E, int k, int64_t capacity,
-                   int* status) {
+                   int layout, int* status) {
   MoePlan plan;
-  ATS_TRY(moe_plan_from_ws(workspace, workspace_bytes, T, E, k, capacity, &plan));
+  ATS_TRY(moe_plan_from_ws(workspace, workspace_bytes, T, E, k, capacity, layout, &plan));
   if (status == nullptr) return fail(ATS_EBADARG, "moe_status: null output");
   cudaError_t e = cudaMemcpy(status, plan.dev_err, sizeof(int), cudaMemcpyDeviceToHost);
   if (e != cudaSuccess) return fail(ATS_ECUDA, "moe_status: %s", cudaGetErrorString(e));
@@ -482,9 +485,9 @@ int ats_moe_status(const void* workspace, size_t workspace_bytes, int64_t T, int
 }
 
 int ats_moe_plan_export(const void* workspace, size_t workspace_bytes, int64_t T, int E, int k, int64_t capacity,
-                        int32_t* seg_start, int32_t* row_token, void* stream) {
+                        int layout, int32_t* seg_start, int32_t* row_token, int32_t* kept, void* stream) {
   MoePlan plan;
-  ATS_TRY(moe_plan_from_ws(workspace, workspace_bytes, T, E, k, capacity, &plan));
+  ATS_TRY(moe_plan_from_ws(workspace, workspace_bytes, T, E, k, capacity, layout, &plan));
   cudaStream_t st = (cudaStream_t)stream;
   if (seg_start != nullptr &&
       cudaMemcpyAsync(seg_start, plan.seg_start, (size_t)(E + 1) * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
@@ -493,23 +496,27 @@ int ats_moe_plan_export(const void* workspace, size_t workspace_bytes, int64_t T
       cudaMemcpyAsync(row_token, plan.row_token, (size_t)plan.max_rows * 4, cudaMemcpyDeviceToDevice, st) !=
           cudaSuccess)
     return fail(ATS_ECUDA, "moe_plan_export: copy failed");
+  if (kept != nullptr &&
+      cudaMemcpyAsync(kept, plan.kept, (size_t)E * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+    return fail(ATS_ECUDA, "moe_plan_export: copy failed");
   return ATS_OK;
 }
 
 int ats_moe_topk(const float* logits, int64_t T, int E, int k, float* gates, int64_t* idx, float* probs,
                  void* stream) {
-  ATS_TRY(moe_check(T, E, k, 1));
+  ATS_TRY(moe_check(T, E, k, 1, ATS_MOE_PACKED));
   if (T == 0) return ATS_OK;
   if (logits == nullptr || gates == nullptr || idx == nullptr) return fail(ATS_EBADARG, "moe_topk: null pointer");
   MoePlan none{};
   return launch_route<false>(logits, T, E, k, gates, idx, probs, none, (cudaStream_t)stream);
 }
 
-int ats_moe_route_plan(const float* logits, int64_t T, int E, int k, int64_t capacity, float lbw, float* gates,
+int ats_moe_route_plan(const float* logits, int64_t T, int E, int k, int64_t capacity, int layout, float lbw,
+                       float* gates,
                        int64_t* idx, float* aux_loss, float* utilization, int32_t* counts, void* workspace,
                        size_t workspace_bytes, void* stream) {
   MoePlan plan;
-  ATS_TRY(moe_plan_from_ws(workspace, workspace_bytes, T, E, k, capacity, &plan));
+  ATS_TRY(moe_plan_from_ws(workspace, workspace_bytes, T, E, k, capacity, layout, &plan));
   if (T > 0 && (logits == nullptr || gates == nullptr || idx == nullptr))
     return fail(ATS_EBADARG, "moe_route_plan: null pointer");
   cudaStream_t st = (cudaStream_t)stream;
@@ -528,9 +535,9 @@ int ats_moe_route_plan(const float* logits, int64_t T, int E, int k, int64_t cap
 }
 
 int ats_moe_gather(const void* x, void* xp, ats_dtype dtype, int64_t T, int64_t H, int E, int k, int64_t capacity,
-                   const void* workspace, size_t workspace_bytes, void* stream) {
+                   int layout, const void* workspace, size_t workspace_bytes, void* stream) {
   MoePlan plan;
-  ATS_TRY(moe_plan_from_ws(workspace, workspace_bytes, T, E, k, capacity, &plan));
+  ATS_TRY(moe_plan_from_ws(workspace, workspace_bytes, T, E, k, capacity, layout, &plan));
   if (H <= 0 || xp == nullptr || (T > 0 && x == nullptr)) return fail(ATS_EBADARG, "moe_gather: bad arguments");
   const unsigned blocks = (unsigned)((plan.max_rows + 7) / 8);
   cudaStream_t st = (cudaStream_t)stream;
@@ -544,9 +551,9 @@ int ats_moe_gather(const void* x, void* xp, ats_dtype dtype, int64_t T, int64_t 
 }
 
 int ats_moe_combine(const void* y, void* out, ats_dtype dtype, int64_t T, int64_t H, int E, int k,
-                    int64_t capacity, const void* workspace, size_t workspace_bytes, void* stream) {
+                    int64_t capacity, int layout, const void* workspace, size_t workspace_bytes, void* stream) {
   MoePlan plan;
-  ATS_TRY(moe_plan_from_ws(workspace, workspace_bytes, T, E, k, capacity, &plan));
+  ATS_TRY(moe_plan_from_ws(workspace, workspace_bytes, T, E, k, capacity, layout, &plan));
   if (T == 0) return ATS_OK;
   if (H <= 0 || y == nullptr || out == nullptr) return fail(ATS_EBADARG, "moe_combine: bad arguments");
   const unsigned blocks = (unsigned)((T + 7) / 8);
@@ -561,10 +568,10 @@ int ats_moe_combine(const void* y, void* out, ats_dtype dtype, int64_t T, int64_
 }
 
 int ats_moe_combine_bwd(const void* dout, const void* y, void* dy, float* dgate_row, ats_dtype dtype, int64_t T,
-                        int64_t H, int E, int k, int64_t capacity, const void* workspace, size_t workspace_bytes,
+                        int64_t H, int E, int k, int64_t capacity, int layout, const void* workspace, size_t workspace_bytes,
                         void* stream) {
   MoePlan plan;
-  ATS_TRY(moe_plan_from_ws(workspace, workspace_bytes, T, E, k, capacity, &plan));
+  ATS_TRY(moe_plan_from_ws(workspace, workspace_bytes, T, E, k, capacity, layout, &plan));
   if (H <= 0 || y == nullptr || dy == nullptr || dgate_row == nullptr || (T > 0 && dout == nullptr))
     return fail(ATS_EBADARG, "moe_combine_bwd: bad arguments");
   const unsigned blocks = (unsigned)((plan.max_rows + 7) / 8);
@@ -581,9 +588,9 @@ int ats_moe_combine_bwd(const void* dout, const void* y, void* dy, float* dgate_
 }
 
 int ats_moe_scatter_grad(const void* dxp, void* dx, ats_dtype dtype, int64_t T, int64_t H, int E, int k,
-                         int64_t capacity, const void* workspace, size_t workspace_bytes, void* stream) {
+                         int64_t capacity, int layout, const void* workspace, size_t workspace_bytes, void* stream) {
   MoePlan plan;
-  ATS_TRY(moe_plan_from_ws(workspace, workspace_bytes, T, E, k, capacity, &plan));
+  ATS_TRY(moe_plan_from_ws(workspace, workspace_bytes, T, E, k, capacity, layout, &plan));
   if (T == 0) return ATS_OK;
   if (H <= 0 || dxp == nullptr || dx == nullptr) return fail(ATS_EBADARG, "moe_scatter_grad: bad arguments");
   const unsigned blocks = (unsigned)((T + 7) / 8);
@@ -599,10 +606,11 @@ int ats_moe_scatter_grad(const void* dxp, void* dx, ats_dtype dtype, int64_t T, 
 }
 
 int ats_moe_route_bwd(const float* logits, const float* gates, const int64_t* idx, const float* dgate_row,
-                      const float* daux, float* dlogits, int64_t T, int E, int k, int64_t capacity, float lbw,
+                      const float* daux, float* dlogits, int64_t T, int E, int k, int64_t capacity, int layout,
+                      float lbw,
                       const void* workspace, size_t workspace_bytes, void* stream) {
   MoePlan plan;
-  ATS_TRY(moe_plan_from_ws(workspace, workspace_bytes, T, E, k, capacity, &plan));
+  ATS_TRY(moe_plan_from_ws(workspace, workspace_bytes, T, E, k, capacity, layout, &plan));
   if (T == 0) return ATS_OK;
   if (logits == nullptr || gates == nullptr || idx == nullptr || dgate_row == nullptr || dlogits == nullptr)
     return fail(ATS_EBADARG, "moe_route_bwd: null pointer");

@@ -321,14 +321,29 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_stream_kernel(
   }
 }
 
-// dw[i] = round_W(sum_b partial[b][i]), blocks summed in index order.
+// dw[i] = round_W(sum_b partial[b][i]).  A block of 256 threads takes 32
+// columns; thread (c, q) sums the partial rows b = q, q+8, ... of column c
+// (independent loads, so the latency overlaps), and the eight sums are added
+// in q order: a fixed summation order, so dw is deterministic.
 template <typename TW>
-__global__ void dw_reduce_kernel(const float* __restrict__ partial, int nblk, int H, TW* __restrict__ dw) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= H) return;
+__global__ void __launch_bounds__(256) dw_reduce_kernel(const float* __restrict__ partial, int nblk, int H,
+                                                        TW* __restrict__ dw) {
+  __shared__ float part[8][33];
+  const int cx = threadIdx.x & 31, q = threadIdx.x >> 5;
+  const int col = blockIdx.x * 32 + cx;
   float s = 0.f;
-  for (int b = 0; b < nblk; ++b) s += partial[(size_t)b * H + i];
-  dw[i] = Cvt<TW>::from_f(s);
+  if (col < H) {
+#pragma unroll 4
+    for (int b = q; b < nblk; b += 8) s += partial[(size_t)b * H + col];
+  }
+  part[q][cx] = s;
+  __syncthreads();
+  if (q == 0 && col < H) {
+    float t = 0.f;
+#pragma unroll
+    for (int r = 0; r < 8; ++r) t += part[r][cx];
+    dw[col] = Cvt<TW>::from_f(t);
+  }
 }
 
 // ---------------------------------------------------------- TMA ring kernels
@@ -375,14 +390,29 @@ __device__ __forceinline__ bool bar_and(bool ok, int id, int count) {
   return r != 0;
 }
 
-// w staged as float32, interleaved by group thread: value e of chunk gt+64*j
-// at ws[(j*N + e)*64 + gt].
+// w staged as float32 in float4 units interleaved by group thread: values
+// 4q..4q+3 of chunk gt+64*j form the float4 at ws4[(j*N/4 + q)*64 + gt], so a
+// thread reads a chunk's weights with N/4 conflict-free 16-byte loads.
 template <typename TW, int NPL, int N>
 __device__ __forceinline__ void stage_weight(float* ws, const TW* __restrict__ w, int H, int tid, int nthreads) {
   for (int idx = tid; idx < NPL * N * kGroupThreads; idx += nthreads) {
-    const int gt = idx % kGroupThreads, je = idx / kGroupThreads, e = je % N, j = je / N;
-    const int col = (gt + kGroupThreads * j) * N + e;
+    const int e4 = idx & 3, v = idx >> 2;
+    const int gt = v % kGroupThreads, jq = v / kGroupThreads, q = jq % (N / 4), j = jq / (N / 4);
+    const int col = (gt + kGroupThreads * j) * N + q * 4 + e4;
     ws[idx] = col < H ? Cvt<TW>::to_f(w[col]) : 0.f;
+  }
+}
+
+template <int N>
+__device__ __forceinline__ void weight_chunk(const float* ws, int j, int gt, float (&wv)[N]) {
+  const float4* w4 = reinterpret_cast<const float4*>(ws);
+#pragma unroll
+  for (int q = 0; q < N / 4; ++q) {
+    const float4 t = w4[(j * (N / 4) + q) * kGroupThreads + gt];
+    wv[q * 4 + 0] = t.x;
+    wv[q * 4 + 1] = t.y;
+    wv[q * 4 + 2] = t.z;
+    wv[q * 4 + 3] = t.w;
   }
 }
 
@@ -488,10 +518,11 @@ __global__ void __launch_bounds__(kRingThreads, 1) rmsnorm_fwd_ring_kernel(
     for (int j = 0; j < NPL; ++j) {
       const int c = gt + kGroupThreads * j;
       if (c < nch) {
-        float v[N], o[N];
+        float v[N], o[N], wv[N];
         unpack<TX>(raw[j], v);
+        weight_chunk<N>(ws, j, gt, wv);
 #pragma unroll
-        for (int e = 0; e < N; ++e) o[e] = (v[e] * r) * ws[(j * N + e) * kGroupThreads + gt];
+        for (int e = 0; e < N; ++e) o[e] = (v[e] * r) * wv[e];
         store_chunk<TX>(yr + (int64_t)c * N, o);
       }
     }
@@ -556,13 +587,14 @@ __global__ void __launch_bounds__(kRingThreads, 1) rmsnorm_bwd_ring_kernel(
       if (ok && c < nch) {
         xr[j] = sx[c];
         dr[j] = sd[c];
-        float v[N], d[N];
+        float v[N], d[N], wv[N];
         unpack<TX>(xr[j], v);
         unpack<TX>(dr[j], d);
+        weight_chunk<N>(ws, j, gt, wv);
 #pragma unroll
         for (int e = 0; e < N; ++e) {
           ss = fmaf(v[e], v[e], ss);
-          cc = fmaf(d[e] * ws[(j * N + e) * kGroupThreads + gt], v[e], cc);
+          cc = fmaf(d[e] * wv[e], v[e], cc);
         }
       }
     }
@@ -589,12 +621,13 @@ __global__ void __launch_bounds__(kRingThreads, 1) rmsnorm_bwd_ring_kernel(
     for (int j = 0; j < NPL; ++j) {
       const int c = gt + kGroupThreads * j;
       if (c < nch) {
-        float v[N], d[N], o[N];
+        float v[N], d[N], o[N], wv[N];
         unpack<TX>(xr[j], v);
         unpack<TX>(dr[j], d);
+        weight_chunk<N>(ws, j, gt, wv);
 #pragma unroll
         for (int e = 0; e < N; ++e) {
-          const float g = d[e] * ws[(j * N + e) * kGroupThreads + gt];
+          const float g = d[e] * wv[e];
           acc[j][e] = fmaf(d[e], v[e] * r, acc[j][e]);
           o[e] = r * g - v[e] * k2;
         }
@@ -736,7 +769,7 @@ int launch_bwd(const void* dy, const void* x, const void* w, void* dx, void* dre
     cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     kfn<<<grid, kRingThreads, smem, st>>>(dyp, xp, wp, dxo, partial, rows, (int)H, eps);
     ATS_TRY(check_launch("rmsnorm_bwd_ring"));
-    dw_reduce_kernel<TW><<<(unsigned)((H + 255) / 256), 256, 0, st>>>(partial, grid, (int)H, static_cast<TW*>(dw));
+    dw_reduce_kernel<TW><<<(unsigned)((H + 31) / 32), 256, 0, st>>>(partial, grid, (int)H, static_cast<TW*>(dw));
     return check_launch("rmsnorm_dw_reduce");
   }
   if (rows > 0) {
@@ -763,7 +796,7 @@ int launch_bwd(const void* dy, const void* x, const void* w, void* dx, void* dre
     ATS_TRY(check_launch("rmsnorm_bwd"));
   }
   const int nblk = rows > 0 ? blocks : 0;
-  dw_reduce_kernel<TW><<<(unsigned)((H + 255) / 256), 256, 0, st>>>(partial, nblk, (int)H, static_cast<TW*>(dw));
+  dw_reduce_kernel<TW><<<(unsigned)((H + 31) / 32), 256, 0, st>>>(partial, nblk, (int)H, static_cast<TW*>(dw));
   return check_launch("rmsnorm_dw_reduce");
 }
 

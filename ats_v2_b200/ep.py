@@ -1,0 +1,201 @@
+"""Expert-parallel MoE layer over torch.distributed (NCCL over NVLink).
+
+The reference delegates expert parallelism to DeepSpeed's MoE
+(ats/model/moe.py:193-214, ``ep_size`` = number of GPUs from
+ats/cli/train.py:400-402).  Here rank r of a W-rank process group owns the
+E_local = E/W experts [r*E_local, (r+1)*E_local); the router weight is
+replicated.  One forward:
+
+  1. every rank routes its own T tokens (float32 router, capacity
+     ``max(1, int(cf*T*k/E))`` from its own token count, as the fallback and
+     DeepSpeed compute it) into the capacity-slot layout: a [E][Cp] row buffer
+     (Cp = capacity rounded up to 128) that reads as [W][E_local][Cp];
+  2. the kept-row counts [W][E_local] and the row buffer are exchanged with
+     ``all_to_all_single`` on equal splits -- no host synchronisation, no
+     data-dependent sizes;
+  3. the receiving rank runs its local experts on [W][E_local][Cp] through a
+     segment table that covers only the kept rows of every (source, expert)
+     segment (padding costs link bandwidth, not tensor-core time);
+  4. the outputs go back with a second ``all_to_all_single`` and are combined
+     by each source rank in ascending expert order.
+
+The backward sends the expert-output gradients out, runs the expert
+backward (weight gradients reduce over the W segments of each local expert),
+and sends the input gradients back.  Expert weights are rank-local, so their
+gradients need no all-reduce; the replicated router weight's gradient is the
+usual data-parallel all-reduce of the training loop.
+
+The exchange steps (``exchange_counts``, ``exchange_rows``) only move tensors
+and work on any device and backend; the device stages are the library's.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+import torch.nn.functional as F
+from torch import nn
+
+from ats_v2_b200 import _lib
+from ats_v2_b200.ffn import SwiGLU
+from ats_v2_b200.moe import LazyUtilization, capacity_for, init_residual_projection, stacked
+
+SLOTS = _lib.ATS_MOE_SLOTS
+
+
+def slot_rows(capacity: int) -> int:
+    """Rows of one expert's slot: the capacity rounded up to 128."""
+    return (capacity + 127) // 128 * 128
+
+
+def exchange_counts(send_kept: torch.Tensor, group=None) -> torch.Tensor:
+    """send_kept [E] int32 (kept rows per global expert, viewed [W][E_local])
+    -> recv_kept [W*E_local]: row src holds the rows rank src keeps for each of
+    this rank's experts."""
+    recv = torch.empty_like(send_kept)
+    dist.all_to_all_single(recv, send_kept.contiguous(), group=group)
+    return recv
+
+
+def exchange_rows(buf: torch.Tensor, group=None) -> torch.Tensor:
+    """Equal-split all-to-all of a [W*E_local*Cp, H] row buffer: chunk r goes to
+    rank r, chunk src of the result came from rank src.  The same call sends
+    expert inputs out and expert outputs back (the layout is symmetric)."""
+    out = torch.empty_like(buf)
+    dist.all_to_all_single(out, buf.contiguous(), group=group)
+    return out
+
+
+class _EPMoEFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x2, logits, meta, wgu_stack, wd_stack, *local_weights):
+        E, El, k, C, lbw, Fdim, W, group = meta
+        T, H = x2.shape
+        dev = x2.device
+        dt = _lib.dtype_code(x2.dtype)
+        st = _lib.stream_of(x2)
+        Cp = slot_rows(C)
+        wsb = _lib.query("ats_moe_workspace_bytes", T, E, k, C, SLOTS)
+        R = _lib.query("ats_moe_max_rows", T, E, k, C, SLOTS)  # = E*Cp = W*El*Cp
+        ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+        gates = torch.empty((T, k), dtype=torch.float32, device=dev)
+        idx = torch.empty((T, k), dtype=torch.int64, device=dev)
+        aux = torch.empty((), dtype=torch.float32, device=dev)
+        util = torch.empty(E, dtype=torch.float32, device=dev)
+        counts = torch.empty(E, dtype=torch.int32, device=dev)
+        _lib.call("ats_moe_route_plan", logits.data_ptr(), T, E, k, C, SLOTS, float(lbw), gates.data_ptr(),
+                  idx.data_ptr(), aux.data_ptr(), util.data_ptr(), counts.data_ptr(), ws.data_ptr(), wsb, st)
+        kept = torch.empty(E, dtype=torch.int32, device=dev)
+        _lib.call("ats_moe_plan_export", ws.data_ptr(), wsb, T, E, k, C, SLOTS, None, None, kept.data_ptr(), st)
+        xs = torch.empty((R, H), dtype=x2.dtype, device=dev)
+        _lib.call("ats_moe_gather", x2.data_ptr(), xs.data_ptr(), dt, T, H, E, k, C, SLOTS, ws.data_ptr(), wsb, st)
+        recv_kept = exchange_counts(kept, group) if W > 1 else kept
+        xr = exchange_rows(xs, group) if W > 1 else xs
+        segb = _lib.query("ats_moe_ep_segments_bytes", W, El)
+        seg = torch.empty(segb, dtype=torch.uint8, device=dev)
+        _lib.call("ats_moe_ep_segments", recv_kept.data_ptr(), W, El, C, seg.data_ptr(), segb, st)
+        h = torch.empty((R, 2 * Fdim), dtype=x2.dtype, device=dev)
+        a = torch.empty((R, Fdim), dtype=x2.dtype, device=dev)
+        yr = torch.empty((R, H), dtype=x2.dtype, device=dev)
+        _lib.call("ats_moe_ep_experts_fwd", xr.data_ptr(), wgu_stack.data_ptr(), wd_stack.data_ptr(), h.data_ptr(),
+                  a.data_ptr(), yr.data_ptr(), dt, W, El, C, H, Fdim, seg.data_ptr(), segb, st)
+        ys = exchange_rows(yr, group) if W > 1 else yr
+        out = torch.empty((T, H), dtype=x2.dtype, device=dev)
+        _lib.call("ats_moe_combine", ys.data_ptr(), out.data_ptr(), dt, T, H, E, k, C, SLOTS, ws.data_ptr(), wsb, st)
+        ctx.save_for_backward(logits, gates, idx, ws, xr, h, a, ys, seg, wgu_stack, wd_stack)
+        ctx.meta = (E, El, k, C, lbw, Fdim, W, group, T, H, wsb, R, segb)
+        ctx.mark_non_differentiable(util, counts, idx)
+        return out, aux, util, counts, idx
+
+    @staticmethod
+    def backward(ctx, dout, daux, _dutil, _dcounts, _didx):
+        logits, gates, idx, ws, xr, h, a, ys, seg, wgu_stack, wd_stack = ctx.saved_tensors
+        E, El, k, C, lbw, Fdim, W, group, T, H, wsb, R, segb = ctx.meta
+        dev = xr.device
+        dt = _lib.dtype_code(xr.dtype)
+        st = _lib.stream_of(xr)
+        if dout is None:
+            dout = torch.zeros((T, H), dtype=xr.dtype, device=dev)
+        dout = dout.to(xr.dtype).contiguous()
+        dys = torch.empty((R, H), dtype=xr.dtype, device=dev)
+        dgate_row = torch.empty(R, dtype=torch.float32, device=dev)
+        _lib.call("ats_moe_combine_bwd", dout.data_ptr(), ys.data_ptr(), dys.data_ptr(), dgate_row.data_ptr(), dt,
+                  T, H, E, k, C, SLOTS, ws.data_ptr(), wsb, st)
+        dyr = exchange_rows(dys, group) if W > 1 else dys
+        dh = torch.empty((R, 2 * Fdim), dtype=xr.dtype, device=dev)
+        dxr = torch.empty((R, H), dtype=xr.dtype, device=dev)
+        dwgu = torch.empty_like(wgu_stack)
+        dwd = torch.empty_like(wd_stack)
+        _lib.call("ats_moe_ep_experts_bwd", dyr.data_ptr(), xr.data_ptr(), h.data_ptr(), a.data_ptr(),
+                  wgu_stack.data_ptr(), wd_stack.data_ptr(), dh.data_ptr(), dxr.data_ptr(), dwgu.data_ptr(),
+                  dwd.data_ptr(), dt, W, El, C, H, Fdim, seg.data_ptr(), segb, st)
+        dxs = exchange_rows(dxr, group) if W > 1 else dxr
+        dx = torch.empty((T, H), dtype=xr.dtype, device=dev)
+        _lib.call("ats_moe_scatter_grad", dxs.data_ptr(), dx.data_ptr(), dt, T, H, E, k, C, SLOTS, ws.data_ptr(),
+                  wsb, st)
+        dlogits = torch.empty((T, E), dtype=torch.float32, device=dev)
+        daux_t = daux.to(torch.float32).contiguous() if daux is not None else None
+        _lib.call("ats_moe_route_bwd", logits.data_ptr(), gates.data_ptr(), idx.data_ptr(), dgate_row.data_ptr(),
+                  _lib.ptr(daux_t), dlogits.data_ptr(), T, E, k, C, SLOTS, float(lbw), ws.data_ptr(), wsb, st)
+        grads = [dwgu[e] for e in range(El)] + [dwd[e] for e in range(El)]
+        return (dx, dlogits, None, None, None, *grads)
+
+
+class ExpertParallelMoE(nn.Module):
+    """MoE layer with its experts sharded over a process group.
+
+    ``experts[i]`` is global expert ``rank*E_local + i``; ``gate`` is the
+    replicated router (Linear(hidden, num_experts)).  With a world size of 1
+    it is the single-GPU layer on the capacity-slot layout."""
+
+    def __init__(self, hidden_size: int, intermediate_size: int, num_experts: int, num_layers: int,
+                 top_k: int = 2, capacity_factor: float = 1.25, load_balancing_weight: float = 0.01,
+                 group=None) -> None:
+        super().__init__()
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if self.world > 1 else 0
+        if num_experts % self.world != 0:
+            raise ValueError(f"num_experts={num_experts} must be divisible by the expert-parallel size {self.world}")
+        if not 1 <= top_k <= min(num_experts, 16):
+            raise ValueError(f"MoE top_k must be in [1, min(num_experts, 16)], got {top_k}")
+        self.hidden_size = hidden_size
+        self.num_experts = num_experts
+        self.num_local_experts = num_experts // self.world
+        self.top_k = top_k
+        self.capacity_factor = capacity_factor
+        self.load_balancing_weight = load_balancing_weight
+        self.gate = nn.Linear(hidden_size, num_experts, bias=False)
+        self.experts = nn.ModuleList([SwiGLU(hidden_size, intermediate_size) for _ in range(self.num_local_experts)])
+        for ex in self.experts:
+            init_residual_projection(ex.down_proj, num_layers)
+        self.last_expert_utilization: dict[int, float] | None = None
+        self.last_counts: torch.Tensor | None = None
+
+    def router_logits(self, flat_x: torch.Tensor) -> torch.Tensor:
+        return F.linear(flat_x.float(), self.gate.weight.float())
+
+    def forward(self, x: torch.Tensor, logit_bias: torch.Tensor | None = None):
+        """x [B,S,H] -> (out [B,S,H], aux).  ``logit_bias`` [E] is added to the
+        router logits (used to impose a skewed expert load in benchmarks)."""
+        batch, seq, H = x.shape
+        if H != self.hidden_size:
+            raise ValueError(f"MoE expected hidden_size={self.hidden_size}, got {H}.")
+        _lib.require_cuda("ExpertParallelMoE", x)
+        flat = x.reshape(-1, H).contiguous()
+        T = flat.shape[0]
+        cap = capacity_for(T, self.top_k, self.num_experts, self.capacity_factor)
+        logits = self.router_logits(flat)
+        if logit_bias is not None:
+            logits = logits + logit_bias.to(logits.dtype)
+        wgu = [e.gate_up_proj.weight for e in self.experts]
+        wd = [e.down_proj.weight for e in self.experts]
+        if wgu[0].dtype != flat.dtype:
+            raise TypeError(f"MoE: token dtype {flat.dtype} does not match expert weight dtype {wgu[0].dtype}")
+        meta = (self.num_experts, self.num_local_experts, self.top_k, cap, self.load_balancing_weight,
+                wgu[0].shape[0] // 2, self.world, self.group)
+        out, aux, util, counts, _ = _EPMoEFn.apply(flat, logits.contiguous(), meta, stacked(wgu), stacked(wd),
+                                                   *wgu, *wd)
+        self.last_expert_utilization = LazyUtilization(util)
+        self.last_counts = counts
+        return out.view(batch, seq, H), aux

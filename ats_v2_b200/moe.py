@@ -35,7 +35,7 @@ BASE_LINEAR_STD = 0.02
 
 
 def residual_output_std(num_layers: int) -> float:
-    """Depth-scaled std of residual-stream projections (initialization.py:541-546)."""
+    """Depth-scaled std of residual-stream projections (ats/model/initialization.py:52-57)."""
     if num_layers <= 0:
         raise ValueError(f"num_layers must be positive, got {num_layers}.")
     return BASE_LINEAR_STD / math.sqrt(2 * num_layers)
@@ -43,7 +43,7 @@ def residual_output_std(num_layers: int) -> float:
 
 def init_residual_projection(module: nn.Linear, num_layers: int) -> None:
     """N(0, residual_output_std) init, marked so a later blanket init skips it
-    (initialization.py:549-562)."""
+    (ats/model/initialization.py:60-73)."""
     nn.init.normal_(module.weight, mean=0.0, std=residual_output_std(num_layers))
     if module.bias is not None:
         nn.init.zeros_(module.bias)
@@ -137,45 +137,46 @@ class LazyUtilization(dict):
 class _MoEFn(torch.autograd.Function):
     """Device stages of the MoE layer on flattened tokens x2 [T,H].
 
-    Inputs: x2, logits [T,E] f32, meta=(E,k,C,lbw,F), the two weight stacks,
-    then the per-expert weights (only so autograd routes their gradients)."""
+    Inputs: x2, logits [T,E] f32, meta=(E,k,C,lbw,F,layout), the two weight
+    stacks, then the per-expert weights (only so autograd routes their
+    gradients)."""
 
     @staticmethod
     def forward(ctx, x2, logits, meta, wgu_stack, wd_stack, *expert_weights):
-        E, k, C, lbw, Fdim = meta
+        E, k, C, lbw, Fdim, L = meta
         T, H = x2.shape
         dev = x2.device
         dt = _lib.dtype_code(x2.dtype)
         st = _lib.stream_of(x2)
-        ws_bytes = _lib.query("ats_moe_workspace_bytes", T, E, k, C)
-        max_rows = _lib.query("ats_moe_max_rows", T, E, k, C)
+        ws_bytes = _lib.query("ats_moe_workspace_bytes", T, E, k, C, L)
+        max_rows = _lib.query("ats_moe_max_rows", T, E, k, C, L)
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
         gates = torch.empty((T, k), dtype=torch.float32, device=dev)
         idx = torch.empty((T, k), dtype=torch.int64, device=dev)
         aux = torch.empty((), dtype=torch.float32, device=dev)
         util = torch.empty(E, dtype=torch.float32, device=dev)
         counts = torch.empty(E, dtype=torch.int32, device=dev)
-        _lib.call("ats_moe_route_plan", logits.data_ptr(), T, E, k, C, float(lbw), gates.data_ptr(),
+        _lib.call("ats_moe_route_plan", logits.data_ptr(), T, E, k, C, L, float(lbw), gates.data_ptr(),
                   idx.data_ptr(), aux.data_ptr(), util.data_ptr(), counts.data_ptr(), ws.data_ptr(), ws_bytes,
                   st)
         xp = torch.empty((max_rows, H), dtype=x2.dtype, device=dev)
-        _lib.call("ats_moe_gather", x2.data_ptr(), xp.data_ptr(), dt, T, H, E, k, C, ws.data_ptr(), ws_bytes, st)
+        _lib.call("ats_moe_gather", x2.data_ptr(), xp.data_ptr(), dt, T, H, E, k, C, L, ws.data_ptr(), ws_bytes, st)
         h = torch.empty((max_rows, 2 * Fdim), dtype=x2.dtype, device=dev)
         a = torch.empty((max_rows, Fdim), dtype=x2.dtype, device=dev)
         y = torch.empty((max_rows, H), dtype=x2.dtype, device=dev)
         _lib.call("ats_moe_experts_fwd", xp.data_ptr(), wgu_stack.data_ptr(), wd_stack.data_ptr(), h.data_ptr(),
-                  a.data_ptr(), y.data_ptr(), dt, T, E, k, C, H, Fdim, ws.data_ptr(), ws_bytes, st)
+                  a.data_ptr(), y.data_ptr(), dt, T, E, k, C, L, H, Fdim, ws.data_ptr(), ws_bytes, st)
         out = torch.empty((T, H), dtype=x2.dtype, device=dev)
-        _lib.call("ats_moe_combine", y.data_ptr(), out.data_ptr(), dt, T, H, E, k, C, ws.data_ptr(), ws_bytes, st)
+        _lib.call("ats_moe_combine", y.data_ptr(), out.data_ptr(), dt, T, H, E, k, C, L, ws.data_ptr(), ws_bytes, st)
         ctx.save_for_backward(logits, gates, idx, ws, xp, h, a, y, wgu_stack, wd_stack)
-        ctx.meta = (E, k, C, lbw, Fdim, T, H, ws_bytes, max_rows)
+        ctx.meta = (E, k, C, lbw, Fdim, L, T, H, ws_bytes, max_rows)
         ctx.mark_non_differentiable(util, counts, idx)
         return out, aux, util, counts, idx
 
     @staticmethod
     def backward(ctx, dout, daux, _dutil, _dcounts, _didx):
         logits, gates, idx, ws, xp, h, a, y, wgu_stack, wd_stack = ctx.saved_tensors
-        E, k, C, lbw, Fdim, T, H, ws_bytes, max_rows = ctx.meta
+        E, k, C, lbw, Fdim, L, T, H, ws_bytes, max_rows = ctx.meta
         dev = xp.device
         dt = _lib.dtype_code(xp.dtype)
         st = _lib.stream_of(xp)
@@ -185,34 +186,34 @@ class _MoEFn(torch.autograd.Function):
         dy = torch.empty((max_rows, H), dtype=xp.dtype, device=dev)
         dgate_row = torch.empty(max_rows, dtype=torch.float32, device=dev)
         _lib.call("ats_moe_combine_bwd", dout.data_ptr(), y.data_ptr(), dy.data_ptr(), dgate_row.data_ptr(), dt,
-                  T, H, E, k, C, ws.data_ptr(), ws_bytes, st)
+                  T, H, E, k, C, L, ws.data_ptr(), ws_bytes, st)
         dh = torch.empty((max_rows, 2 * Fdim), dtype=xp.dtype, device=dev)
         dxp = torch.empty((max_rows, H), dtype=xp.dtype, device=dev)
         dwgu = torch.empty_like(wgu_stack)
         dwd = torch.empty_like(wd_stack)
         _lib.call("ats_moe_experts_bwd", dy.data_ptr(), xp.data_ptr(), h.data_ptr(), a.data_ptr(),
                   wgu_stack.data_ptr(), wd_stack.data_ptr(), dh.data_ptr(), dxp.data_ptr(), dwgu.data_ptr(),
-                  dwd.data_ptr(), dt, T, E, k, C, H, Fdim, ws.data_ptr(), ws_bytes, st)
+                  dwd.data_ptr(), dt, T, E, k, C, L, H, Fdim, ws.data_ptr(), ws_bytes, st)
         dx = torch.empty((T, H), dtype=xp.dtype, device=dev)
-        _lib.call("ats_moe_scatter_grad", dxp.data_ptr(), dx.data_ptr(), dt, T, H, E, k, C, ws.data_ptr(),
+        _lib.call("ats_moe_scatter_grad", dxp.data_ptr(), dx.data_ptr(), dt, T, H, E, k, C, L, ws.data_ptr(),
                   ws_bytes, st)
         dlogits = torch.empty((T, E), dtype=torch.float32, device=dev)
         daux_t = daux.to(torch.float32).contiguous() if daux is not None else None
         _lib.call("ats_moe_route_bwd", logits.data_ptr(), gates.data_ptr(), idx.data_ptr(), dgate_row.data_ptr(),
-                  _lib.ptr(daux_t), dlogits.data_ptr(), T, E, k, C, float(lbw), ws.data_ptr(), ws_bytes, st)
+                  _lib.ptr(daux_t), dlogits.data_ptr(), T, E, k, C, L, float(lbw), ws.data_ptr(), ws_bytes, st)
         grads = [dwgu[e] for e in range(E)] + [dwd[e] for e in range(E)]
         return (dx, dlogits, None, None, None, *grads)
 
 
 def moe_apply(x2: torch.Tensor, logits: torch.Tensor, wgu: list[torch.Tensor], wd: list[torch.Tensor],
-              top_k: int, capacity: int, lbw: float):
+              top_k: int, capacity: int, lbw: float, layout: int = _lib.ATS_MOE_PACKED):
     """Run the device MoE stages; returns (out [T,H], aux (0-dim), util [E], counts [E], idx [T,k])."""
     E = len(wgu)
     Fdim = wgu[0].shape[0] // 2
     wgu_stack = stacked(wgu)
     wd_stack = stacked(wd)
     logits = logits.float().contiguous()
-    return _MoEFn.apply(x2.contiguous(), logits, (E, top_k, capacity, lbw, Fdim), wgu_stack, wd_stack,
+    return _MoEFn.apply(x2.contiguous(), logits, (E, top_k, capacity, lbw, Fdim, layout), wgu_stack, wd_stack,
                         *wgu, *wd)
 
 

@@ -1,9 +1,9 @@
 """Single-tensor fused RoPE -- mirror of ats/model/rope_triton.py.
 
-``fused_apply_rope(x, cos, sin)`` validates like rope_triton.py:203-212 and
+``fused_apply_rope(x, cos, sin)`` validates like rope_triton.py:115-125 and
 applies the rotate-half rotation of rope.py:83-86 to one [B,H,S,D] tensor in
 one CUDA pass, reading x through its strides (the reference's Triton wrapper
-copied x to contiguous first, rope_triton.py:170).  It is differentiable.
+copied x to contiguous first, rope_triton.py:83).  It is differentiable.
 ``_cuda_apply_rope`` is the kernel call without validation, the counterpart
 of the reference's ``_triton_apply_rope``.
 """

@@ -9,6 +9,9 @@ Workloads (synthetic, seeded; the reference publishes no dataset for this path):
             bf16, theta 5e5 (metric: HBM GB/s)
   moe       MoE layer forward+backward, 8192 tokens, hidden 2048, 8 experts
             top-2, ffn 5632, bf16, fp32 router, no capacity drop (metric: tokens/s)
+  moe_ep    expert-parallel MoE layer forward+backward, 32768 tokens per GPU,
+            hidden 4096, 64 experts top-2 sharded over the GPUs, ffn 1408,
+            capacity factor 1.25, Zipf(1.1) expert skew (metric: tokens/s)
 
 One JSON line is printed by rank 0.  ``value`` is the device-timed throughput
 with inputs resident in HBM (CUDA events on the launching stream, K steps
@@ -18,9 +21,11 @@ inputs copied in and all results copied out inside the timed region;
 ``roofline`` times the dominant kernel with CUDA events inside the timed
 region; ``cpu_baseline`` times the numpy restatement of the reference's
 algorithm (``oracle/``) on the host cores on a bounded sample.  With the
-default workload the line also carries ``extras`` with the other two
+default workload the line also carries ``extras`` with the other
 workloads measured the same way.  Under torchrun every rank runs its own
-shard (weak scaling, no collective on the data path).
+shard (weak scaling): RMSNorm, RoPE and the single-GPU MoE layer have no
+collective on the data path; ``moe_ep`` exchanges expert rows with NCCL
+all-to-all.
 
 ``--impl reference`` times the reference's algorithm on the host CPU (the
 oracle port; the reference itself is Python and is not present here) on the
@@ -455,7 +460,138 @@ class MoEWorkload(Workload):
                           f"(numpy oracle, BLAS on {threads} threads)"}
 
 
-WORKLOADS = {"rmsnorm": RMSNormWorkload, "rope": RopeWorkload, "moe": MoEWorkload}
+def zipf_bias(E: int, s_exp: float = 1.1, seed: int = 1):
+    """Per-expert router-logit bias log(p_pi(e)), p_r ~ r^-s over ranks r=1..E,
+    pi a fixed permutation (generator seed 1), mean-centred."""
+    import torch
+    p = torch.arange(1, E + 1, dtype=torch.float64) ** (-s_exp)
+    p = p / p.sum()
+    perm = torch.randperm(E, generator=torch.Generator().manual_seed(seed))
+    b = torch.log(p[perm])
+    return (b - b.mean()).float()
+
+
+class MoEEPWorkload(Workload):
+    name = "moe_ep"
+    metric = "moe_ep_layer_fwd_bwd_tokens_per_s"
+    unit = "tokens/s"
+    T, H, F, E, K, CF = 32768, 4096, 1408, 64, 2, 1.25
+
+    def config(self):
+        return {"workload": "expert-parallel MoE layer fwd+bwd, 32768 tokens per GPU, hidden 4096, 64 experts "
+                            "top-2, ffn 1408, capacity factor 1.25, Zipf(1.1) router-logit bias, bf16, fp32 router",
+                "experts_per_gpu": self.E // self.world, "exchange": "NCCL all_to_all_single, equal splits "
+                "on capacity slots" if self.world > 1 else "none (all experts local)",
+                "per_rank": "32768 tokens per GPU (weak scaling)", "l2": "inputs larger than L2"}
+
+    def setup(self):
+        t = self.torch
+        from ats_v2_b200.ep import ExpertParallelMoE
+        t.manual_seed(2000 + self.rank)
+        with t.device("cuda"):
+            layer = ExpertParallelMoE(self.H, self.F, self.E, num_layers=2, top_k=self.K, capacity_factor=self.CF)
+        with t.no_grad():
+            # the router weight is replicated: every rank draws the same one
+            layer.gate.weight.copy_(0.02 * t.randn(layer.gate.weight.shape, generator=t.Generator().manual_seed(7)))
+            for ex in layer.experts:
+                ex.gate_up_proj.weight.normal_(0, 0.02)
+                ex.down_proj.weight.normal_(0, 0.02)
+        self.layer = layer
+        self.layer.experts.to(t.bfloat16)
+        self.bias = zipf_bias(self.E).cuda()
+        g = t.Generator(device="cuda").manual_seed(self.rank)
+        self.x = t.randn(1, self.T, self.H, device="cuda", generator=g).bfloat16().requires_grad_()
+        self.dy = t.randn(1, self.T, self.H, device="cuda", generator=g).bfloat16()
+        self.one = t.ones((), device="cuda")
+
+    def _zero(self):
+        for p in self.layer.parameters():
+            p.grad = None
+
+    def step(self, evs):
+        t = self.torch
+        self._zero()
+        self.x.grad = None
+        if evs:
+            evs[0].record()
+        out, aux = self.layer(self.x, logit_bias=self.bias)
+        t.autograd.backward([out, aux], [self.dy, self.one])
+        if evs:
+            evs[1].record()
+
+    def kept_rows(self) -> int:
+        """Expert rows computed per GPU: kept rows of all ranks / ranks."""
+        from ats_v2_b200.moe import capacity_for
+        t = self.torch
+        cap = capacity_for(self.T, self.K, self.E, self.CF)
+        kept = self.layer.last_counts.clamp(max=cap).sum().to(t.float64).reshape(1)
+        if self.world > 1:
+            import torch.distributed as tdist
+            tdist.all_reduce(kept)
+        return int(round(float(kept.item()) / self.world))
+
+    def dominant(self):
+        rows = self.kept_rows()
+        return {"kernel": "whole expert-parallel layer fwd+bwd (expert GEMMs 18*rows*H*F flops)",
+                "flops": 18 * rows * self.H * self.F, "bound": "tensor", "kept_rows": rows}
+
+    def e2e_setup(self):
+        t = self.torch
+        self.hx = self.x.detach().cpu().pin_memory()
+        self.hdy = self.dy.cpu().pin_memory()
+        self.hout = t.empty_like(self.hx).pin_memory()
+        self.hdx = t.empty_like(self.hx).pin_memory()
+        self.haux = t.empty((), dtype=t.float32).pin_memory()
+        self.dx_in = t.empty_like(self.x.detach())
+        self.ddy = t.empty_like(self.dy)
+        self.h2d = 2 * self.hx.numel() * 2
+        self.d2h = 2 * self.hx.numel() * 2 + 4
+
+    def e2e_step(self):
+        t = self.torch
+        self.dx_in.copy_(self.hx, non_blocking=True)
+        self.ddy.copy_(self.hdy, non_blocking=True)
+        x = self.dx_in.requires_grad_()
+        self._zero()
+        out, aux = self.layer(x, logit_bias=self.bias)
+        t.autograd.backward([out, aux], [self.ddy, self.one])
+        self.hout.copy_(out.detach(), non_blocking=True)
+        self.hdx.copy_(x.grad, non_blocking=True)
+        self.haux.copy_(aux.detach(), non_blocking=True)
+        x.grad = None
+        x.requires_grad_(False)
+
+    def units_to_value(self, steps, ms):
+        return self.T * steps / (ms * 1e-3)
+
+    def cpu_baseline(self, seconds: float):
+        # a token's cost is its k experts' FFNs whatever E is: time 256 tokens on 8 of the experts
+        from oracle import moe as omoe
+        from oracle.bf16 import round_bf16
+        threads = cpu_threads()
+        T, E = 256, 8
+        rng = np.random.default_rng(0)
+        x = round_bf16(rng.standard_normal((T, self.H)).astype(np.float32))
+        wg = (0.02 * rng.standard_normal((E, self.H))).astype(np.float32)
+        wgu = round_bf16((0.02 * rng.standard_normal((E, 2 * self.F, self.H))).astype(np.float32))
+        wd = round_bf16((0.02 * rng.standard_normal((E, self.H, self.F))).astype(np.float32))
+        dy = round_bf16(rng.standard_normal((T, self.H)).astype(np.float32))
+        t0 = time.perf_counter()
+        n = 0
+        while True:
+            logits = omoe.router_logits(x, wg)
+            fwd = omoe.moe_forward(x, logits, wgu, wd, self.K, self.CF, 0.01, "bf16")
+            omoe.moe_layer_backward_full(dy, fwd, x, wg, wgu, wd, 0.01, "bf16")
+            n += 1
+            if time.perf_counter() - t0 >= seconds:
+                break
+        dt = time.perf_counter() - t0
+        return {"value": T * n / dt, "unit": self.unit, "cores": threads, "kind": "port",
+                "sample": f"{T} tokens per pass routed over 8 of the experts (a token's cost is its top-2 "
+                          f"experts' FFNs), {n} passes in {dt:.1f} s (numpy oracle, BLAS on {threads} threads)"}
+
+
+WORKLOADS = {"rmsnorm": RMSNormWorkload, "rope": RopeWorkload, "moe": MoEWorkload, "moe_ep": MoEEPWorkload}
 
 
 # ---------------------------------------------------------------- timing
@@ -540,6 +676,8 @@ def measure(torch, dist, wl: Workload, steps: int, warmup: int, world: int, with
             res["roofline"] = {"bound": "tensor", "kernel": dom["kernel"], "achieved": ach, "peak": peak,
                                "unit": "TFLOP/s", "frac": ach / peak, "peak_source": wl.peaks_kind + " sustained",
                                "traffic": None, "algorithmic_flops": dom["flops"], "kernel_ms": kms}
+            if "kept_rows" in dom:
+                res["roofline"]["kept_rows"] = dom["kept_rows"]
     # end to end through the public module with host buffers
     wl.e2e_setup()
     e2e_steps = max(3, min(steps, 10))

@@ -127,7 +127,7 @@ ATS_API int ats_rmsnorm_residual_bwd(const void* dout, const void* x, ats_dtype 
  * positions).  backward != 0 applies the
  * adjoint (the gradient w.r.t. x for upstream gradients in *_in).
  * Replaces apply_rotary_pos_emb, ats/model/rope.py:71-87, and fused_apply_rope,
- * ats/model/rope_triton.py:195-215 (k may be NULL, Hk ignored).
+ * ats/model/rope_triton.py:108-128 (k may be NULL, Hk ignored).
  * Strides are in elements for the (b, h, s) dims; D must be contiguous.
  * x_dtype is the dtype of q/k and of cos/sin; outputs have the same dtype. */
 ATS_API int ats_rope_apply(const void* q_in, void* q_out, int64_t Hq,
@@ -153,44 +153,54 @@ ATS_API int ats_moe_topk(const float* logits, int64_t T, int E, int k,
  * no host synchronisation.  One workspace (ats_moe_workspace_bytes) carries
  * the routing plan between the stages of a forward and its backward.
  *
- * Permuted ("expert-major") row space: expert e owns rows
- * [seg_start[e], seg_start[e] + kept_e) with kept_e = min(count_e, capacity),
- * followed by zero padding up to a multiple of 128 rows; tokens inside a
- * segment are in ascending token order (moe.py:109-116).  The number of
- * permuted rows is at most ats_moe_max_rows(). */
-ATS_API int64_t ats_moe_max_rows(int64_t T, int E, int k, int64_t capacity);
-ATS_API size_t ats_moe_workspace_bytes(int64_t T, int E, int k, int64_t capacity);
+ * Permuted ("expert-major") row space, in one of two layouts:
+ *   ATS_MOE_PACKED: expert e owns rows [seg_start[e], seg_start[e] + kept_e)
+ *     with kept_e = min(count_e, capacity), then zero padding up to a multiple
+ *     of 128 rows; the next expert follows (single-GPU layout).
+ *   ATS_MOE_SLOTS: expert e owns the fixed rows [e*Cp, e*Cp + kept_e) of a
+ *     [E][Cp] buffer, Cp = capacity rounded up to 128, zero padding after the
+ *     kept rows -- the send layout of the expert-parallel exchange, where the
+ *     buffer reads as [rank][local expert][Cp] (equal all-to-all splits).
+ * Tokens inside a segment are in ascending token order (moe.py:109-116).  The
+ * number of permuted rows is ats_moe_max_rows(). */
+#define ATS_MOE_PACKED 0
+#define ATS_MOE_SLOTS 1
+
+ATS_API int64_t ats_moe_max_rows(int64_t T, int E, int k, int64_t capacity, int layout);
+ATS_API size_t ats_moe_workspace_bytes(int64_t T, int E, int k, int64_t capacity, int layout);
 
 /* Device status of the MoE stages that ran with this workspace since the last
  * ats_moe_route_plan: writes 0 to *status and returns ATS_OK when every
  * bounded device-side wait completed, else the wait's code and ATS_ETIMEOUT.
  * Synchronous (copies one int from the device); for diagnostics, not the step. */
 ATS_API int ats_moe_status(const void* workspace, size_t workspace_bytes, int64_t T, int E, int k,
-                   int64_t capacity, int* status);
+                   int64_t capacity, int layout, int* status);
 
-/* Copies the plan's padded segment starts [E+1] and the token of every
- * permuted row [max_rows] (-1 = padding) into caller device buffers (either
- * may be NULL), stream-ordered. */
+/* Copies the plan's segment starts [E+1], the token of every permuted row
+ * [max_rows] (-1 = padding) and the kept rows per expert [E] into caller
+ * device buffers (any may be NULL), stream-ordered. */
 ATS_API int ats_moe_plan_export(const void* workspace, size_t workspace_bytes, int64_t T, int E, int k,
-                        int64_t capacity, int32_t* seg_start, int32_t* row_token, void* stream);
+                        int64_t capacity, int layout, int32_t* seg_start, int32_t* row_token,
+                        int32_t* kept, void* stream);
 
-/* 1 when ats_moe_experts_fwd/bwd run this dtype and shape on tcgen05 tensor
- * cores (bf16, hidden and ffn multiples of 128), 0 when on CUDA cores. */
+/* 1 when the expert GEMMs run this dtype and shape on tcgen05 tensor cores
+ * (bf16, hidden and ffn multiples of 128), 0 when on CUDA cores. */
 ATS_API int ats_moe_uses_tensor_cores(ats_dtype dtype, int64_t H, int64_t F);
 
 /* Stage 1: route + plan + permutation (moe.py:101-116, :136-162).
  * Writes gates/idx like ats_moe_topk, the workspace plan, and
  *   aux_loss[1]   = E * sum_e mean_t(p[t,e]) * count_e/T * lbw   (float32)
  *   utilization[E] = count_e / max(sum count, 1e-8)               (float32)
- *   counts[E]     = pre-capacity dispatch counts                  (int32) */
-ATS_API int ats_moe_route_plan(const float* logits, int64_t T, int E, int k, int64_t capacity,
+ *   counts[E]     = pre-capacity dispatch counts                  (int32)
+ * (aux_loss, utilization and counts may be NULL). */
+ATS_API int ats_moe_route_plan(const float* logits, int64_t T, int E, int k, int64_t capacity, int layout,
                        float lbw, float* gates, int64_t* idx,
                        float* aux_loss, float* utilization, int32_t* counts,
                        void* workspace, size_t workspace_bytes, void* stream);
 
 /* Stage 2: xp[row] = x[token(row)], zero for padding rows.  x [T,H]; xp [max_rows,H]. */
 ATS_API int ats_moe_gather(const void* x, void* xp, ats_dtype dtype, int64_t T, int64_t H,
-                   int E, int k, int64_t capacity,
+                   int E, int k, int64_t capacity, int layout,
                    const void* workspace, size_t workspace_bytes, void* stream);
 
 /* Stage 3: the grouped SwiGLU experts (ats/model/ffn.py:37-45 per expert):
@@ -200,19 +210,19 @@ ATS_API int ats_moe_gather(const void* x, void* xp, ats_dtype dtype, int64_t T, 
  * tensor cores (float32 accumulate); f32 runs on CUDA cores in float32. */
 ATS_API int ats_moe_experts_fwd(const void* xp, const void* w_gate_up, const void* w_down,
                         void* h, void* a, void* y, ats_dtype dtype,
-                        int64_t T, int E, int k, int64_t capacity, int64_t H, int64_t F,
+                        int64_t T, int E, int k, int64_t capacity, int layout, int64_t H, int64_t F,
                         const void* workspace, size_t workspace_bytes, void* stream);
 
 /* Stage 4: out[t] = sum over kept (t,e), ascending e, of round(y[row]*gate)
  * accumulated in the token dtype (moe.py:119-122 index_add_).  out [T,H]. */
 ATS_API int ats_moe_combine(const void* y, void* out, ats_dtype dtype, int64_t T, int64_t H,
-                    int E, int k, int64_t capacity,
+                    int E, int k, int64_t capacity, int layout,
                     const void* workspace, size_t workspace_bytes, void* stream);
 
 /* Backward stage 4: dy[row] = round(dout[token]*gate[row]) (zero on padding),
  * dgate_row[row] = sum_h dout[token,h]*y[row,h] (float32). */
 ATS_API int ats_moe_combine_bwd(const void* dout, const void* y, void* dy, float* dgate_row,
-                        ats_dtype dtype, int64_t T, int64_t H, int E, int k, int64_t capacity,
+                        ats_dtype dtype, int64_t T, int64_t H, int E, int k, int64_t capacity, int layout,
                         const void* workspace, size_t workspace_bytes, void* stream);
 
 /* Backward stage 3: with dh [rows,2F] as caller scratch,
@@ -221,13 +231,13 @@ ATS_API int ats_moe_combine_bwd(const void* dout, const void* y, void* dy, float
 ATS_API int ats_moe_experts_bwd(const void* dy, const void* xp, const void* h, const void* a,
                         const void* w_gate_up, const void* w_down,
                         void* dh, void* dxp, void* dw_gate_up, void* dw_down, ats_dtype dtype,
-                        int64_t T, int E, int k, int64_t capacity, int64_t H, int64_t F,
+                        int64_t T, int E, int k, int64_t capacity, int layout, int64_t H, int64_t F,
                         const void* workspace, size_t workspace_bytes, void* stream);
 
 /* Backward stage 2: dx[t] = round(sum over kept rows of token t of dxp[row]),
  * summed in float32 in ascending expert order; zero for tokens with no kept row. */
 ATS_API int ats_moe_scatter_grad(const void* dxp, void* dx, ats_dtype dtype, int64_t T, int64_t H,
-                         int E, int k, int64_t capacity,
+                         int E, int k, int64_t capacity, int layout,
                          const void* workspace, size_t workspace_bytes, void* stream);
 
 /* Backward stage 1: d(logits) [T,E] float32 from the per-row gate gradients
@@ -236,8 +246,40 @@ ATS_API int ats_moe_scatter_grad(const void* dxp, void* dx, ats_dtype dtype, int
  * pointer to one float32 (the upstream gradient of aux_loss), or NULL for 0. */
 ATS_API int ats_moe_route_bwd(const float* logits, const float* gates, const int64_t* idx,
                       const float* dgate_row, const float* daux, float* dlogits,
-                      int64_t T, int E, int k, int64_t capacity, float lbw,
+                      int64_t T, int E, int k, int64_t capacity, int layout, float lbw,
                       const void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------ MoE expert parallelism
+ * Expert-parallel MoE (the DeepSpeed MoE path the reference delegates to,
+ * ats/model/moe.py:193-214, with ep_size = world size): rank r owns the
+ * E_local = E/W experts [r*E_local, (r+1)*E_local).  Each rank plans its own
+ * tokens in the ATS_MOE_SLOTS layout (capacity from its own token count), the
+ * host exchanges the [W][E_local][Cp] row buffers and the kept-row counts with
+ * NCCL all-to-all, and the experts run on the received buffer
+ * [W (source rank)][E_local][Cp] through the segment table built here: the
+ * GEMMs compute only the kept rows of each (source, expert) segment (rounded
+ * up to 128) and the weight gradients reduce over all W segments of an expert.
+ * recv_kept [W*E_local] (device, int32) are the kept rows received from each
+ * source for each local expert. */
+ATS_API size_t ats_moe_ep_segments_bytes(int W, int E_local);
+ATS_API int ats_moe_ep_segments(const int32_t* recv_kept, int W, int E_local, int64_t capacity,
+                        void* seg_workspace, size_t seg_workspace_bytes, void* stream);
+
+/* The grouped SwiGLU experts on the received buffer (rows W*E_local*Cp): as
+ * ats_moe_experts_fwd/_bwd with w_gate_up [E_local,2F,H], w_down [E_local,H,F]. */
+ATS_API int ats_moe_ep_experts_fwd(const void* xr, const void* w_gate_up, const void* w_down,
+                           void* h, void* a, void* y, ats_dtype dtype, int W, int E_local,
+                           int64_t capacity, int64_t H, int64_t F,
+                           const void* seg_workspace, size_t seg_workspace_bytes, void* stream);
+ATS_API int ats_moe_ep_experts_bwd(const void* dy, const void* xr, const void* h, const void* a,
+                           const void* w_gate_up, const void* w_down,
+                           void* dh, void* dxr, void* dw_gate_up, void* dw_down, ats_dtype dtype,
+                           int W, int E_local, int64_t capacity, int64_t H, int64_t F,
+                           const void* seg_workspace, size_t seg_workspace_bytes, void* stream);
+
+/* Device status of the EP expert GEMMs run with this segment workspace (as ats_moe_status). */
+ATS_API int ats_moe_ep_status(const void* seg_workspace, size_t seg_workspace_bytes, int W, int E_local,
+                      int* status);
 
 #ifdef __cplusplus
 }

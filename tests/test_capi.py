@@ -60,7 +60,7 @@ def test_bad_arguments_rejected_before_any_launch():
     st = lib.ats_moe_topk(None, 4, 2, 3, None, None, None, None)
     assert st == _lib.ATS_EBADARG
     # workspace too small
-    st = lib.ats_moe_route_plan(None, 4, 4, 2, 4, 0.01, None, None, None, None, None, None, 0, None)
+    st = lib.ats_moe_route_plan(None, 4, 4, 2, 4, 0, 0.01, None, None, None, None, None, None, 0, None)
     assert st == _lib.ATS_EBADARG
     assert b"workspace too small" in lib.ats_last_error_message()
 
@@ -68,13 +68,17 @@ def test_bad_arguments_rejected_before_any_launch():
 def test_workspace_queries():
     lib = _lib.load()
     assert lib.ats_rmsnorm_bwd_workspace_bytes(16384, 4096) >= 148 * 4096 * 4
-    assert lib.ats_moe_workspace_bytes(8192, 8, 2, 8192) > 0
-    assert lib.ats_moe_workspace_bytes(8192, 8, 17, 8192) == 0  # k > 16 is invalid
-    mr = lib.ats_moe_max_rows(8192, 8, 2, 8192)
+    P, S = _lib.ATS_MOE_PACKED, _lib.ATS_MOE_SLOTS
+    assert lib.ats_moe_workspace_bytes(8192, 8, 2, 8192, P) > 0
+    assert lib.ats_moe_workspace_bytes(8192, 8, 17, 8192, P) == 0  # k > 16 is invalid
+    assert lib.ats_moe_workspace_bytes(8192, 8, 2, 8192, 7) == 0  # unknown layout
+    mr = lib.ats_moe_max_rows(8192, 8, 2, 8192, P)
     assert mr % 128 == 0 and 16384 <= mr <= 16384 + 8 * 128
-    # capacity bounds the permuted rows
-    assert lib.ats_moe_max_rows(32768, 64, 2, 1280) == 64 * 1280 // 128 * 128 or \
-        lib.ats_moe_max_rows(32768, 64, 2, 1280) <= 65536 + 64 * 128
+    # packed: kept rows plus per-expert padding; slots: E x capacity rounded to 128
+    assert lib.ats_moe_max_rows(32768, 64, 2, 1280, P) <= 65536 + 64 * 128
+    assert lib.ats_moe_max_rows(32768, 64, 2, 1280, S) == 64 * 1280
+    assert lib.ats_moe_max_rows(1000, 4, 2, 300, S) == 4 * 384
+    assert lib.ats_moe_ep_segments_bytes(8, 8) > 0
 
 
 def test_errors_surface_as_python_exceptions():

@@ -1,0 +1,114 @@
+"""Expert-parallel exchange on CPU with two gloo ranks (no GPU).
+
+The row and count exchanges of the expert-parallel MoE only move tensors;
+here they run on CPU tensors: every row of a send buffer carries its
+(source rank, global expert, slot) so the receiver can check where it landed,
+a stand-in expert doubles the rows, and the return exchange must bring each
+row back to its original slot.  A second test makes one rank leave before the
+collective: its peer must fail within the process group's timeout instead of
+waiting for ever."""
+
+from __future__ import annotations
+
+import os
+import socket
+import traceback
+from datetime import timedelta
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from ats_v2_b200.ep import exchange_counts, exchange_rows, slot_rows
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _init(rank, world, port, timeout_s=60):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=timeout_s))
+
+
+def _exchange_worker(rank, world, port, E_local, cap, H, errq):
+    try:
+        _init(rank, world, port)
+        E = world * E_local
+        Cp = slot_rows(cap)
+        g = torch.Generator().manual_seed(rank)
+        kept = torch.randint(0, cap + 1, (E,), generator=g, dtype=torch.int32)
+        send = torch.zeros(E * Cp, H)
+        for e in range(E):
+            for s in range(int(kept[e])):
+                send[e * Cp + s, 0] = rank
+                send[e * Cp + s, 1] = e
+                send[e * Cp + s, 2] = s
+                send[e * Cp + s, 3:] = 1.0
+        recv_kept = exchange_counts(kept)
+        recv = exchange_rows(send)
+        # what every source keeps for my experts, in [source][local expert] order
+        all_kept = [torch.empty_like(kept) for _ in range(world)]
+        dist.all_gather(all_kept, kept)
+        for src in range(world):
+            for el in range(E_local):
+                e = rank * E_local + el
+                assert int(recv_kept[src * E_local + el]) == int(all_kept[src][e])
+                for s in range(int(all_kept[src][e])):
+                    row = recv[(src * E_local + el) * Cp + s]
+                    assert (int(row[0]), int(row[1]), int(row[2])) == (src, e, s)
+        back = exchange_rows(recv * 2.0)  # a stand-in expert, then the return trip
+        assert torch.equal(back, send * 2.0)
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        errq.put((rank, traceback.format_exc()))
+        raise
+
+
+def _leaver_worker(rank, world, port, errq):
+    try:
+        _init(rank, world, port, timeout_s=3)
+        buf = torch.ones(world * 4, 8)
+        if rank == 1:
+            return  # leaves before the collective: no NCCL/GPU involved
+        try:
+            exchange_rows(buf)
+        except Exception as exc:  # the peer's timeout or lost connection
+            errq.put((rank, f"raised: {type(exc).__name__}"))
+            return
+        errq.put((rank, "no error"))
+    except Exception:
+        errq.put((rank, traceback.format_exc()))
+
+
+@pytest.mark.parametrize("E_local,cap,H", [(2, 5, 8), (3, 130, 4)])
+def test_row_and_count_exchange_round_trip(E_local, cap, H):
+    ctx = mp.get_context("spawn")
+    errq = ctx.SimpleQueue()
+    mp.start_processes(_exchange_worker, args=(2, _free_port(), E_local, cap, H, errq), nprocs=2, join=True,
+                       start_method="spawn")
+    assert errq.empty()
+
+
+def test_peer_that_leaves_makes_the_collective_fail_not_hang():
+    ctx = mp.get_context("spawn")
+    errq = ctx.SimpleQueue()
+    port = _free_port()
+    procs = [ctx.Process(target=_leaver_worker, args=(r, 2, port, errq)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=60)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    assert not alive, "a rank hung past the timeout"
+    results = []
+    while not errq.empty():
+        results.append(errq.get())
+    assert any(r == 0 and msg.startswith("raised") for r, msg in results), results

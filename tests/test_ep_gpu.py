@@ -1,0 +1,132 @@
+"""Expert-parallel MoE on the GPU.
+
+Single rank: the expert-parallel layer on the capacity-slot layout must equal
+the single-GPU layer on the packed layout for the same weights (the rows of a
+segment are the same and in the same order; only their place in the buffer
+differs).  Two ranks (runs when two GPUs are visible): every rank's output
+and input gradient equal the oracle run on that rank's own tokens with all
+experts' weights, and every local expert's weight gradient equals the sum
+over both ranks' tokens -- DeepSpeed's local-capacity semantics."""
+
+from __future__ import annotations
+
+import os
+import socket
+import traceback
+from datetime import timedelta
+
+import numpy as np
+import pytest
+import torch
+
+from ats_v2_b200 import moe as bmoe
+from ats_v2_b200.ep import ExpertParallelMoE
+from tests.util import close, np32
+
+pytestmark = pytest.mark.gpu
+
+
+def _init_weights(mod_gate, experts, seed):
+    g = torch.Generator().manual_seed(seed)
+    with torch.no_grad():
+        mod_gate.weight.copy_(0.02 * torch.randn(mod_gate.weight.shape, generator=g))
+        for ex in experts:
+            ex.gate_up_proj.weight.copy_(0.02 * torch.randn(ex.gate_up_proj.weight.shape, generator=g))
+            ex.down_proj.weight.copy_(0.02 * torch.randn(ex.down_proj.weight.shape, generator=g))
+
+
+@pytest.mark.parametrize("T,H,F,E,k,cf", [(1024, 256, 384, 8, 2, 1.25), (700, 128, 128, 4, 2, 0.6)])
+def test_single_rank_slots_layout_equals_packed_layer(T, H, F, E, k, cf):
+    torch.manual_seed(0)
+    ep = ExpertParallelMoE(H, F, E, num_layers=2, top_k=k, capacity_factor=cf)
+    ref = bmoe.MoELayer(H, F, E, num_layers=2, top_k=k, capacity_factor=cf)
+    _init_weights(ep.gate, ep.experts, 1)
+    _init_weights(ref.moe.gate, ref.moe.experts, 1)
+    ep, ref = ep.cuda(), ref.cuda()
+    ep.experts.to(torch.bfloat16)
+    ref.moe.experts.to(torch.bfloat16)
+    x = torch.randn(1, T, H, device="cuda").bfloat16()
+    g = torch.randn(1, T, H, device="cuda").bfloat16()
+    xa, xb = x.clone().requires_grad_(), x.clone().requires_grad_()
+    oa, aa = ep(xa)
+    ob, ab = ref(xb)
+    torch.autograd.backward([oa, aa], [g, torch.ones_like(aa)])
+    torch.autograd.backward([ob, ab], [g, torch.ones_like(ab)])
+    close(oa, np32(ob), "bf16", min_exact=0.999)
+    assert aa.item() == pytest.approx(ab.item(), rel=1e-6)
+    close(xa.grad, np32(xb.grad), "bf16", min_exact=0.999)
+    close(ep.gate.weight.grad, np32(ref.moe.gate.weight.grad), "f32", rtol=1e-5, atol=1e-7)
+    for e in range(E):
+        close(ep.experts[e].gate_up_proj.weight.grad, np32(ref.moe.experts[e].gate_up_proj.weight.grad), "bf16",
+              min_exact=0.999)
+        close(ep.experts[e].down_proj.weight.grad, np32(ref.moe.experts[e].down_proj.weight.grad), "bf16",
+              min_exact=0.999)
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _two_rank_worker(rank, world, port, errq):
+    from oracle import moe as omoe
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        torch.cuda.set_device(rank)
+        torch.distributed.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                                             device_id=torch.device("cuda", rank))
+        T, H, F, E, k, cf = 512, 128, 256, 8, 2, 1.25
+        El = E // world
+        full_gate = torch.nn.Linear(H, E, bias=False)
+        full_experts = torch.nn.ModuleList([bmoe.SwiGLU(H, F) for _ in range(E)])
+        _init_weights(full_gate, full_experts, 5)  # identical on both ranks
+        ep = ExpertParallelMoE(H, F, E, num_layers=2, top_k=k, capacity_factor=cf)
+        with torch.no_grad():
+            ep.gate.weight.copy_(full_gate.weight)
+            for i in range(El):
+                ep.experts[i].gate_up_proj.weight.copy_(full_experts[rank * El + i].gate_up_proj.weight)
+                ep.experts[i].down_proj.weight.copy_(full_experts[rank * El + i].down_proj.weight)
+        ep = ep.cuda()
+        ep.experts.to(torch.bfloat16)
+        gx = torch.Generator(device="cuda").manual_seed(100 + rank)
+        x = torch.randn(1, T, H, device="cuda", generator=gx).bfloat16().requires_grad_()
+        gout = torch.randn(1, T, H, device="cuda", generator=gx).bfloat16()
+        out, aux = ep(x)
+        torch.autograd.backward([out, aux], [gout, torch.ones_like(aux)])
+        torch.cuda.synchronize()
+        # oracle on this rank's tokens with all experts' (bf16) weights
+        xs = np32(x.view(T, H))
+        logits = np32(ep.router_logits(x.detach().view(T, H)))
+        wgu = np.stack([np32(e.gate_up_proj.weight.bfloat16()) for e in full_experts])
+        wd = np.stack([np32(e.down_proj.weight.bfloat16()) for e in full_experts])
+        fwd = omoe.moe_forward(xs, logits, wgu, wd, k, cf, 0.01, "bf16")
+        close(out.view(T, H), fwd["out"], "bf16")
+        b = omoe.moe_layer_backward_full(np32(gout.view(T, H)), fwd, xs, np32(ep.gate.weight), wgu, wd, 0.01,
+                                         "bf16")
+        close(x.grad.view(T, H), b["dx"], "bf16")
+        # expert weight gradients: sum of both ranks' contributions
+        dwgu = torch.from_numpy(b["dwgu"]).cuda()
+        dwd = torch.from_numpy(b["dwd"]).cuda()
+        torch.distributed.all_reduce(dwgu)
+        torch.distributed.all_reduce(dwd)
+        for i in range(El):
+            e = rank * El + i
+            close(ep.experts[i].gate_up_proj.weight.grad, np32(dwgu[e]), "bf16", atol=2e-2)
+            close(ep.experts[i].down_proj.weight.grad, np32(dwd[e]), "bf16", atol=2e-2)
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    except Exception:
+        errq.put((rank, traceback.format_exc()))
+        raise
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_ranks_match_the_oracle_on_local_tokens():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    errq = ctx.SimpleQueue()
+    mp.start_processes(_two_rank_worker, args=(2, _free_port(), errq), nprocs=2, join=True, start_method="spawn")
+    assert errq.empty()

@@ -43,7 +43,7 @@ def _swiglu_grad(g, u, da):
     return dg, du
 
 
-def _run(T, H, F, E, k, cf, seed, starve=None):
+def _run(T, H, F, E, k, cf, seed, starve=None, layout=_lib.ATS_MOE_PACKED):
     assert _lib.query("ats_moe_uses_tensor_cores", _lib.ATS_BF16, H, F) == 1
     g = torch.Generator(device="cuda").manual_seed(seed)
     x = torch.randn(T, H, device="cuda", generator=g).bfloat16()
@@ -53,42 +53,49 @@ def _run(T, H, F, E, k, cf, seed, starve=None):
     wgu = (0.05 * torch.randn(E, 2 * F, H, device="cuda", generator=g)).bfloat16()
     wd = (0.05 * torch.randn(E, H, F, device="cuda", generator=g)).bfloat16()
     C = capacity_for(T, k, E, cf)
-    wsb = _lib.query("ats_moe_workspace_bytes", T, E, k, C)
-    R = _lib.query("ats_moe_max_rows", T, E, k, C)
+    L = layout
+    wsb = _lib.query("ats_moe_workspace_bytes", T, E, k, C, L)
+    R = _lib.query("ats_moe_max_rows", T, E, k, C, L)
     ws = torch.empty(wsb, dtype=torch.uint8, device="cuda")
     st = _lib.stream_of(x)
     gates = torch.empty(T, k, device="cuda")
     idx = torch.empty(T, k, dtype=torch.int64, device="cuda")
     aux = torch.empty((), device="cuda")
-    _lib.call("ats_moe_route_plan", logits.data_ptr(), T, E, k, C, 0.01, gates.data_ptr(), idx.data_ptr(),
+    _lib.call("ats_moe_route_plan", logits.data_ptr(), T, E, k, C, L, 0.01, gates.data_ptr(), idx.data_ptr(),
               aux.data_ptr(), None, None, ws.data_ptr(), wsb, st)
     seg = torch.empty(E + 1, dtype=torch.int32, device="cuda")
-    _lib.call("ats_moe_plan_export", ws.data_ptr(), wsb, T, E, k, C, seg.data_ptr(), None, st)
+    kept = torch.empty(E, dtype=torch.int32, device="cuda")
+    _lib.call("ats_moe_plan_export", ws.data_ptr(), wsb, T, E, k, C, L, seg.data_ptr(), None, kept.data_ptr(), st)
     xp = torch.empty(R, H, dtype=torch.bfloat16, device="cuda")
-    _lib.call("ats_moe_gather", x.data_ptr(), xp.data_ptr(), _lib.ATS_BF16, T, H, E, k, C, ws.data_ptr(), wsb, st)
+    _lib.call("ats_moe_gather", x.data_ptr(), xp.data_ptr(), _lib.ATS_BF16, T, H, E, k, C, L, ws.data_ptr(), wsb, st)
     h = torch.empty(R, 2 * F, dtype=torch.bfloat16, device="cuda")
     a = torch.empty(R, F, dtype=torch.bfloat16, device="cuda")
     y = torch.empty(R, H, dtype=torch.bfloat16, device="cuda")
     _lib.call("ats_moe_experts_fwd", xp.data_ptr(), wgu.data_ptr(), wd.data_ptr(), h.data_ptr(), a.data_ptr(),
-              y.data_ptr(), _lib.ATS_BF16, T, E, k, C, H, F, ws.data_ptr(), wsb, st)
+              y.data_ptr(), _lib.ATS_BF16, T, E, k, C, L, H, F, ws.data_ptr(), wsb, st)
     dout = torch.randn(T, H, device="cuda", generator=g).bfloat16()
     dy = torch.empty(R, H, dtype=torch.bfloat16, device="cuda")
     dgr = torch.empty(R, device="cuda")
     _lib.call("ats_moe_combine_bwd", dout.data_ptr(), y.data_ptr(), dy.data_ptr(), dgr.data_ptr(), _lib.ATS_BF16,
-              T, H, E, k, C, ws.data_ptr(), wsb, st)
+              T, H, E, k, C, L, ws.data_ptr(), wsb, st)
     dh = torch.empty(R, 2 * F, dtype=torch.bfloat16, device="cuda")
     dxp = torch.empty(R, H, dtype=torch.bfloat16, device="cuda")
     dwgu = torch.empty(E, 2 * F, H, dtype=torch.bfloat16, device="cuda")
     dwd = torch.empty(E, H, F, dtype=torch.bfloat16, device="cuda")
     _lib.call("ats_moe_experts_bwd", dy.data_ptr(), xp.data_ptr(), h.data_ptr(), a.data_ptr(), wgu.data_ptr(),
               wd.data_ptr(), dh.data_ptr(), dxp.data_ptr(), dwgu.data_ptr(), dwd.data_ptr(), _lib.ATS_BF16, T, E,
-              k, C, H, F, ws.data_ptr(), wsb, st)
+              k, C, L, H, F, ws.data_ptr(), wsb, st)
     status = ctypes.c_int(-1)
-    _lib.call("ats_moe_status", ws.data_ptr(), wsb, T, E, k, C, ctypes.byref(status))
+    _lib.call("ats_moe_status", ws.data_ptr(), wsb, T, E, k, C, L, ctypes.byref(status))
     assert status.value == 0
-    seg = seg.tolist()
+    seg, kept = seg.tolist(), kept.tolist()
     for e in range(E):
-        r0, r1 = seg[e], seg[e + 1]
+        # the rows the GEMMs compute: kept rows rounded up to 128 (zero padding)
+        r0, r1 = seg[e], seg[e] + (kept[e] + 127) // 128 * 128
+        if layout == _lib.ATS_MOE_PACKED:
+            assert r1 == seg[e + 1]
+        else:
+            assert seg[e] == e * ((C + 127) // 128 * 128)
         if starve == e:
             assert r1 == r0
         xs, hs, as_, dys, dhs = xp[r0:r1], h[r0:r1], a[r0:r1], dy[r0:r1], dh[r0:r1]
@@ -120,3 +127,8 @@ def test_each_grouped_gemm_matches_torch(T, H, F, E, k, cf):
 
 def test_empty_expert_segment_gives_zero_weight_gradient():
     _run(512, 256, 256, 4, 2, 4.0, seed=7, starve=2)
+
+
+@pytest.mark.parametrize("T,H,F,E,k,cf", [(1000, 256, 256, 8, 2, 1.25), (600, 128, 384, 4, 3, 0.7)])
+def test_each_grouped_gemm_on_capacity_slots(T, H, F, E, k, cf):
+    _run(T, H, F, E, k, cf, seed=T + F, layout=_lib.ATS_MOE_SLOTS)
