@@ -208,14 +208,25 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
         decode_tile<BN, KGROUP, EPI>(p, tiles_before, t, ti);
         const int m0 = ti.mt * BM;
         const int n0 = EPI == EPI_SWIGLU_FWD ? ti.nt * (BN / 2) : ti.nt * BN;
-        // K blocks: M-grouped = kb of the fixed K; K-grouped = the expert's segments' rows, in order
-        int u = 0, lkb = 0, seg_s = KGROUP ? p.seg.eseg[ti.g * p.seg.spe] : ti.g;
+        // K blocks: M-grouped = kb of the fixed K; K-grouped = the expert's segments' rows, in order.
+        // The segment's first row and k-block count live in registers; the table is read only
+        // when the walk moves to the next segment.
+        int u = 0, lkb = 0;
+        int seg_kb = 0, seg_r0 = KGROUP ? 0 : p.seg.row0[ti.g];
+        if (KGROUP) {
+          const int s0 = p.seg.eseg[ti.g * p.seg.spe];
+          seg_kb = p.seg.rows[s0] / BK;
+          seg_r0 = p.seg.row0[s0];
+        }
+        const int b_row0 = ti.e * p.b.group_rows;
         for (int kb = 0; kb < ti.kb; ++kb) {
           if (KGROUP) {
-            while (lkb * BK >= p.seg.rows[seg_s]) {  // next non-empty segment of this expert
+            while (lkb >= seg_kb) {  // next non-empty segment of this expert
               ++u;
               lkb = 0;
-              seg_s = p.seg.eseg[ti.g * p.seg.spe + u];
+              const int sn = p.seg.eseg[ti.g * p.seg.spe + u];
+              seg_kb = p.seg.rows[sn] / BK;
+              seg_r0 = p.seg.row0[sn];
             }
           }
           if (!tc::mbar_wait(&empty_bar[stage], phase ^ 1u, &abort_flag, kWaitBudget)) {
@@ -226,19 +237,19 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
           uint8_t* sb = sa + A_BYTES;
           tc::mbar_arrive_expect_tx(&full_bar[stage], STAGE_BYTES);
           if (!A_MN) {  // M-grouped A: rows of the tile's segment, K contiguous
-            tc::tma_load_2d(sa, &tmA, kb * BK, p.seg.row0[ti.g] + m0, &full_bar[stage]);
+            tc::tma_load_2d(sa, &tmA, kb * BK, seg_r0 + m0, &full_bar[stage]);
           } else {      // K-grouped A: M contiguous, K = rows of the current segment
-            const int krow = p.seg.row0[seg_s] + lkb * BK;
+            const int krow = seg_r0 + lkb * BK;
             tc::tma_load_2d(sa, &tmA, m0, krow, &full_bar[stage]);
             tc::tma_load_2d(sa + 8192, &tmA, m0 + 64, krow, &full_bar[stage]);
           }
           if (!B_MN) {  // stacked weights, K contiguous
-            const int brow = ti.e * p.b.group_rows + n0;
+            const int brow = b_row0 + n0;
             tc::tma_load_2d(sb, &tmB, kb * BK, brow, &full_bar[stage]);
             if (p.b.sub_offset)
               tc::tma_load_2d(sb + (BN / 2) * 128, &tmB, kb * BK, brow + p.b.sub_offset, &full_bar[stage]);
           } else {
-            const int krow = KGROUP ? p.seg.row0[seg_s] + lkb * BK : ti.e * p.b.group_rows + kb * BK;
+            const int krow = KGROUP ? seg_r0 + lkb * BK : b_row0 + kb * BK;
 #pragma unroll
             for (int b = 0; b < BN / 64; ++b) tc::tma_load_2d(sb + b * 8192, &tmB, n0 + b * 64, krow, &full_bar[stage]);
           }

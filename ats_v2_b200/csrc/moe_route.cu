@@ -153,53 +153,105 @@ __global__ void __launch_bounds__(32 * kWarps) route_kernel(const float* __restr
   }
 }
 
+// Inclusive warp scan of v (lane order).
+__device__ __forceinline__ int warp_incl_scan(int v, int lane) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int u = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += u;
+  }
+  return v;
+}
+
+// One block of 1024 threads.  Phase 1: warp w scans the per-block counts of
+// experts w, w+32, ...: lane l owns a contiguous run of route blocks, so the
+// exclusive block prefix of every (block, expert) is the warp prefix of the
+// lane sums plus the running sum inside the run.  Probability sums go the
+// same fixed way (run sums, then lane order), so the plan is deterministic.
+// Phase 2: block scan of the padded segment sizes in expert order.
 __global__ void __launch_bounds__(1024) plan_kernel(MoePlan plan, float lbw, float* __restrict__ aux_loss,
                                                     float* __restrict__ util, int* __restrict__ counts_out) {
   __shared__ int padded[kMaxExperts];
   __shared__ float prod[kMaxExperts];
-  const int E = plan.E;
+  __shared__ int wsum[32];
+  __shared__ float wprod[32], wfrac[32];
+  const int E = plan.E, nb = plan.nb;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float Tf = (float)plan.T;
-  for (int e = threadIdx.x; e < E; e += blockDim.x) {
-    int run = 0;
+  const int per = (nb + 31) / 32;
+  const int b0 = lane * per, b1 = min(nb, b0 + per);
+  for (int e = warp; e < E; e += 32) {
+    int c = 0;
     float ps = 0.f;
-    for (int b = 0; b < plan.nb; ++b) {
-      plan.blk_prefix[(size_t)b * E + e] = run;
-      run += plan.cnt_partial[(size_t)b * E + e];
+    for (int b = b0; b < b1; ++b) {
+      c += plan.cnt_partial[(size_t)b * E + e];
       ps += plan.prob_partial[(size_t)b * E + e];
     }
-    const int kept = (int64_t)run < plan.C ? run : (int)plan.C;
-    const int kept_pad = (kept + kSegAlign - 1) / kSegAlign * kSegAlign;
-    plan.counts[e] = run;
-    plan.kept[e] = kept;
-    plan.seg_rows[e] = kept_pad;
-    plan.seg_expert[e] = e;
-    padded[e] = plan.layout == ATS_MOE_SLOTS ? (int)slot_rows(plan.C) : kept_pad;
-    const float fr = plan.T > 0 ? (float)run / Tf : 0.f;
-    const float pm = plan.T > 0 ? ps / Tf : 0.f;
-    plan.frac[e] = fr;
-    plan.prob_mean[e] = pm;
-    prod[e] = pm * fr;
-    if (counts_out) counts_out[e] = run;
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    plan.dev_err[0] = 0;
-    int acc = 0;
-    float a = 0.f, fs = 0.f;
-    for (int e = 0; e < E; ++e) {
-      plan.seg_start[e] = acc;
-      acc += padded[e];
-      a += prod[e];
-      fs += plan.frac[e];
+    const int incl = warp_incl_scan(c, lane);
+    int run = incl - c;  // exclusive prefix of this lane's run
+    for (int b = b0; b < b1; ++b) {
+      plan.blk_prefix[(size_t)b * E + e] = run;
+      run += plan.cnt_partial[(size_t)b * E + e];
     }
-    plan.seg_start[E] = acc;
-    if (aux_loss) aux_loss[0] = (float)E * a * lbw;
-    prod[0] = fs;  // reuse as the frac total
+    // probability total in lane order (fixed)
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ps += __shfl_down_sync(0xffffffffu, ps, o);
+    const int total = __shfl_sync(0xffffffffu, incl, 31);
+    if (lane == 0) {
+      const int kept = (int64_t)total < plan.C ? total : (int)plan.C;
+      const int kept_pad = (kept + kSegAlign - 1) / kSegAlign * kSegAlign;
+      plan.counts[e] = total;
+      plan.kept[e] = kept;
+      plan.seg_rows[e] = kept_pad;
+      plan.seg_expert[e] = e;
+      padded[e] = plan.layout == ATS_MOE_SLOTS ? (int)slot_rows(plan.C) : kept_pad;
+      const float fr = plan.T > 0 ? (float)total / Tf : 0.f;
+      const float pm = plan.T > 0 ? ps / Tf : 0.f;
+      plan.frac[e] = fr;
+      plan.prob_mean[e] = pm;
+      prod[e] = pm * fr;
+      if (counts_out) counts_out[e] = total;
+    }
   }
   __syncthreads();
-  const float fs = fmaxf(prod[0], 1e-8f);
-  if (util)
-    for (int e = threadIdx.x; e < E; e += blockDim.x) util[e] = plan.frac[e] / fs;
+  // block scan of padded[0..E) in expert order; sums of prod and frac in the same fixed tree
+  const int e = threadIdx.x;
+  const int v = e < E ? padded[e] : 0;
+  const float pv = e < E ? prod[e] : 0.f, fv = e < E ? plan.frac[e] : 0.f;
+  const int incl = warp_incl_scan(v, lane);
+  float pr = pv, fr = fv;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    pr += __shfl_down_sync(0xffffffffu, pr, o);
+    fr += __shfl_down_sync(0xffffffffu, fr, o);
+  }
+  if (lane == 31) wsum[warp] = incl;
+  if (lane == 0) {
+    wprod[warp] = pr;
+    wfrac[warp] = fr;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const int ws = wsum[lane];
+    const int wi = warp_incl_scan(ws, lane);
+    wsum[lane] = wi - ws;  // exclusive prefix of the warps
+    float a = wprod[lane], f = wfrac[lane];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      a += __shfl_down_sync(0xffffffffu, a, o);
+      f += __shfl_down_sync(0xffffffffu, f, o);
+    }
+    if (lane == 0) {
+      plan.dev_err[0] = 0;
+      if (aux_loss) aux_loss[0] = (float)E * a * lbw;
+      wfrac[0] = f;  // the frac total
+    }
+  }
+  __syncthreads();
+  if (e < E) plan.seg_start[e] = wsum[warp] + incl - v;
+  if (e == E - 1) plan.seg_start[E] = wsum[warp] + incl;
+  const float fs = fmaxf(wfrac[0], 1e-8f);
+  if (util && e < E) util[e] = plan.frac[e] / fs;
 }
 
 __global__ void __launch_bounds__(kRouteTokensPerBlock) permute_kernel(const int64_t* __restrict__ idx,
@@ -244,12 +296,23 @@ __device__ __forceinline__ int token_rows(const MoePlan& plan, int64_t t, int (&
   return n;
 }
 
+// Rows the grouped GEMMs read: every row of the packed layout; in the slot
+// layout only the first align128(kept) rows of each expert's slot (the rest
+// of the slot is never read, so it is not written either).
+__device__ __forceinline__ bool row_in_segment(const MoePlan& plan, int64_t row) {
+  if (row >= plan.seg_start[plan.E]) return false;
+  if (plan.layout != ATS_MOE_SLOTS) return true;
+  const int64_t cp = slot_rows(plan.C);
+  const int e = (int)(row / cp);
+  return row - (int64_t)e * cp < plan.seg_rows[e];
+}
+
 template <typename T>
 __global__ void __launch_bounds__(256) gather_kernel(const T* __restrict__ x, T* __restrict__ xp, int64_t H,
                                                      MoePlan plan, bool vec) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * 8 + warp;
-  if (row >= plan.seg_start[plan.E]) return;
+  if (!row_in_segment(plan, row)) return;
   const int tok = plan.row_token[row];
   T* dst = xp + row * H;
   if (vec) {
@@ -305,7 +368,7 @@ __global__ void __launch_bounds__(256) combine_bwd_kernel(const T* __restrict__ 
                                                           int64_t H, MoePlan plan, bool vec) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * 8 + warp;
-  if (row >= plan.seg_start[plan.E]) return;
+  if (!row_in_segment(plan, row)) return;
   const int tok = plan.row_token[row];
   const float g = plan.row_gate[row];
   float dot = 0.f;

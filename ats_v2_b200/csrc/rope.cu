@@ -1,10 +1,10 @@
 // Rotate-half rotary embedding for q and k in one launch, forward and adjoint.
 //
-// A thread owns one (token, 16-byte chunk pair): the chunk at column j of
-// the first half of a head row and the matching chunk at j+D/2.  It loads the
-// token's cos/sin chunks once, keeps them in registers, and rotates that
-// chunk pair in all Hq+Hk heads of the token, several heads per step so
-// many loads are in flight.  Consecutive threads take consecutive chunks of
+// A thread owns one (token, group of up to 8 heads, 16-byte chunk pair):
+// the chunk at column j of the first half of a head row and the matching
+// chunk at j+D/2.  It loads the token's cos/sin chunks once, keeps them in
+// registers, and rotates that chunk pair in every head of its group, several
+// heads per step so many loads are in flight.  Consecutive threads take consecutive chunks of
 // a head row, so for the attention layout (BSHD memory viewed as [B,H,S,D])
 // every warp load is whole 128-byte lines.  q/k are read once and written
 // once: one HBM pass in each direction.
@@ -97,52 +97,62 @@ __device__ __forceinline__ void rot_chunk(const uint4& x1, const uint4& x2, cons
   }
 }
 
-// Vectorised: one thread per (token, 16-byte chunk pair).  The thread loads
-// its four cos/sin chunks once and rotates that chunk pair in every q and k
-// head of the token, UH heads per step so 2*UH loads are in flight.
+// Vectorised: one thread per (token, head group, 16-byte chunk pair).  The
+// thread loads its four cos/sin chunks (L2-resident tables) and rotates that
+// chunk pair in the kHG heads of its group, kUH heads per step so 2*kUH loads
+// are in flight.  Groups of 8 heads give about six blocks per resident block
+// slot on 148 SMs at the 7B shapes, so the last wave is short.
 constexpr int kUH = 4;
+constexpr int kHG = 8;
 
 template <typename T, bool adj>
 __global__ void __launch_bounds__(256, 3) rope_vec_kernel(RopeTensor q, RopeTensor k, const T* __restrict__ cosp,
-                                                        const T* __restrict__ sinp, int64_t cs_stride, int64_t S,
-                                                        int64_t D, int64_t n_tokens) {
+                                                        const T* __restrict__ sinp, int64_t cs_stride, int S,
+                                                        int half, int n_tokens, int gq, int gk) {
   constexpr int N = Chunk<T>::N;
-  const int half = (int)(D / 2);
-  const int cph = half / N;  // chunk pairs per head row
-  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int64_t tok = idx / cph;
-  if (tok >= n_tokens) return;
-  const int j = (int)(idx - tok * cph) * N;
-  const int64_t b = tok / S, s = tok - b * S;
-  const uint4* cr = reinterpret_cast<const uint4*>(cosp + s * cs_stride + j);
-  const uint4* sr = reinterpret_cast<const uint4*>(sinp + s * cs_stride + j);
-  const uint4 c1 = cr[0], s1 = sr[0];
-  const uint4 c2 = *reinterpret_cast<const uint4*>(cosp + s * cs_stride + j + half);
-  const uint4 s2 = *reinterpret_cast<const uint4*>(sinp + s * cs_stride + j + half);
+  const unsigned cph = (unsigned)half / N;  // chunk pairs per head row
+  const unsigned G = (unsigned)(gq + gk);
+  // the launcher keeps every thread index below 2^31, so 32-bit index math is exact
+  const unsigned idx = blockIdx.x * blockDim.x + threadIdx.x;
+  const unsigned rest = idx / cph;
+  const unsigned tok = rest / G;
+  if (tok >= (unsigned)n_tokens) return;
+  const int j = (int)(idx - rest * cph) * N;
+  const int g = (int)(rest - tok * G);
+  const unsigned b = tok / (unsigned)S, s = tok - b * (unsigned)S;
+  const T* cs = cosp + (int64_t)s * cs_stride + j;
+  const T* sn = sinp + (int64_t)s * cs_stride + j;
+  const uint4 c1 = *reinterpret_cast<const uint4*>(cs);
+  const uint4 s1 = *reinterpret_cast<const uint4*>(sn);
+  const uint4 c2 = *reinterpret_cast<const uint4*>(cs + half);
+  const uint4 s2 = *reinterpret_cast<const uint4*>(sn + half);
+  // field-wise selects keep the chosen tensor's description in registers
+  const bool isq = g < gq;
+  const int heads = (int)(isq ? q.heads : k.heads);
+  const int64_t is_h = isq ? q.is_h : k.is_h, os_h = isq ? q.os_h : k.os_h;
+  const int hb = (isq ? g : g - gq) * kHG;
+  const int nh = heads - hb < kHG ? heads - hb : kHG;
+  const T* src = static_cast<const T*>(isq ? q.in : k.in) + (int64_t)b * (isq ? q.is_b : k.is_b) +
+                 (int64_t)s * (isq ? q.is_s : k.is_s) + (int64_t)hb * is_h + j;
+  T* dst = static_cast<T*>(isq ? q.out : k.out) + (int64_t)b * (isq ? q.os_b : k.os_b) +
+           (int64_t)s * (isq ? q.os_s : k.os_s) + (int64_t)hb * os_h + j;
 #pragma unroll 1
-  for (int which = 0; which < 2; ++which) {
-    const RopeTensor& t = which == 0 ? q : k;
-    const T* src0 = static_cast<const T*>(t.in) + b * t.is_b + s * t.is_s + j;
-    T* dst0 = static_cast<T*>(t.out) + b * t.os_b + s * t.os_s + j;
-    for (int64_t h0 = 0; h0 < t.heads; h0 += kUH) {
-      uint4 x1[kUH], x2[kUH];
+  for (int h0 = 0; h0 < nh; h0 += kUH, src += kUH * is_h, dst += kUH * os_h) {
+    uint4 x1[kUH], x2[kUH];
 #pragma unroll
-      for (int u = 0; u < kUH; ++u) {
-        if (h0 + u < t.heads) {
-          const T* src = src0 + (h0 + u) * t.is_h;
-          x1[u] = *reinterpret_cast<const uint4*>(src);
-          x2[u] = *reinterpret_cast<const uint4*>(src + half);
-        }
+    for (int u = 0; u < kUH; ++u) {
+      if (h0 + u < nh) {
+        x1[u] = *reinterpret_cast<const uint4*>(src + u * is_h);
+        x2[u] = *reinterpret_cast<const uint4*>(src + u * is_h + half);
       }
+    }
 #pragma unroll
-      for (int u = 0; u < kUH; ++u) {
-        if (h0 + u < t.heads) {
-          uint4 o1, o2;
-          rot_chunk<T, adj>(x1[u], x2[u], c1, c2, s1, s2, o1, o2);
-          T* dst = dst0 + (h0 + u) * t.os_h;
-          *reinterpret_cast<uint4*>(dst) = o1;
-          *reinterpret_cast<uint4*>(dst + half) = o2;
-        }
+    for (int u = 0; u < kUH; ++u) {
+      if (h0 + u < nh) {
+        uint4 o1, o2;
+        rot_chunk<T, adj>(x1[u], x2[u], c1, c2, s1, s2, o1, o2);
+        *reinterpret_cast<uint4*>(dst + u * os_h) = o1;
+        *reinterpret_cast<uint4*>(dst + u * os_h + half) = o2;
       }
     }
   }
@@ -188,23 +198,27 @@ int launch(const RopeTensor& q, const RopeTensor& k, const void* cosp, const voi
            int64_t B, int64_t S, int64_t D, bool adj, cudaStream_t st) {
   constexpr int N = Chunk<T>::N;
   const int64_t heads = q.heads + k.heads;
-  const bool vec = ((D / 2) % N) == 0 && tensor_vec_ok(q, N) && tensor_vec_ok(k, N) && aligned16(cosp) &&
-                   aligned16(sinp) && (cs_stride % N) == 0;
+  bool vec = ((D / 2) % N) == 0 && tensor_vec_ok(q, N) && tensor_vec_ok(k, N) && aligned16(cosp) &&
+             aligned16(sinp) && (cs_stride % N) == 0;
   const int64_t n_tokens = B * S;
   if (n_tokens * heads == 0) return ATS_OK;
   if (vec) {
-    const int64_t threads = n_tokens * ((D / 2) / N);
-    const int64_t blocks = (threads + 255) / 256;
-    if (blocks >= ((int64_t)1 << 31)) return fail(ATS_EUNSUPPORTED, "rope_apply: too many tokens");
-    if (adj)
-      rope_vec_kernel<T, true><<<(unsigned)blocks, 256, 0, st>>>(q, k, static_cast<const T*>(cosp),
-                                                                   static_cast<const T*>(sinp), cs_stride, S, D,
-                                                                   n_tokens);
-    else
-      rope_vec_kernel<T, false><<<(unsigned)blocks, 256, 0, st>>>(q, k, static_cast<const T*>(cosp),
-                                                                    static_cast<const T*>(sinp), cs_stride, S, D,
-                                                                    n_tokens);
-  } else {
+    const int64_t gq = (q.heads + kHG - 1) / kHG, gk = (k.heads + kHG - 1) / kHG;
+    const int64_t threads = n_tokens * (gq + gk) * ((D / 2) / N);
+    vec = threads + 255 < ((int64_t)1 << 31) && S < ((int64_t)1 << 31);
+    if (vec) {
+      const unsigned blocks = (unsigned)((threads + 255) / 256);
+      if (adj)
+        rope_vec_kernel<T, true><<<blocks, 256, 0, st>>>(q, k, static_cast<const T*>(cosp),
+                                                         static_cast<const T*>(sinp), cs_stride, (int)S, (int)(D / 2),
+                                                         (int)n_tokens, (int)gq, (int)gk);
+      else
+        rope_vec_kernel<T, false><<<blocks, 256, 0, st>>>(q, k, static_cast<const T*>(cosp),
+                                                          static_cast<const T*>(sinp), cs_stride, (int)S, (int)(D / 2),
+                                                          (int)n_tokens, (int)gq, (int)gk);
+    }
+  }
+  if (!vec) {  // any strides or head size, or more work items than 32-bit indices cover
     const int64_t n_items = n_tokens * heads * (D / 2);
     const int64_t cap = (int64_t)num_sms() * 16;
     int64_t blocks = (n_items + 255) / 256;

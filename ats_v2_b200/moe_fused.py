@@ -9,8 +9,14 @@ top_k_idx int64)``: float32 softmax over experts, top-k in descending order
 to one -- the math of _pytorch_moe_routing (moe_triton.py:121-127) -- in one
 warp-per-token kernel (``ats_moe_topk``).  Logits of any float dtype are
 routed in float32.  top_k may be up to 16 (the reference Triton kernel
-stopped at 8).  ``_cuda_moe_routing`` is the kernel call without validation,
-the counterpart of the reference's ``_triton_moe_routing``.
+stopped at 8).  ``_cuda_moe_routing`` is the kernel call without validation.
+
+As in the reference module, ``HAS_TRITON`` says whether the fused GPU kernel
+is available (here: whether the CUDA library is built; no Triton is
+involved), ``_triton_moe_routing`` is the fused kernel call and
+``_pytorch_moe_routing`` the plain torch formula the reference's tests compare
+it against (tests/test_triton.py:170-187).  No product path calls
+``_pytorch_moe_routing``.
 """
 
 from __future__ import annotations
@@ -19,6 +25,7 @@ import torch
 
 from ats_v2_b200 import _lib
 
+HAS_TRITON = _lib.LIB_PATH.exists()  # the reference's flag name: fused GPU kernel available
 MAX_TOP_K = 16
 MAX_EXPERTS = 1024
 
@@ -40,6 +47,17 @@ def _topk(logits: torch.Tensor, top_k: int, want_probs: bool = False):
 def _cuda_moe_routing(gate_logits: torch.Tensor, top_k: int):
     _lib.require_cuda("fused_moe_routing", gate_logits)
     return _topk(gate_logits, top_k)
+
+
+# fused-kernel name of the reference module (tests/test_triton.py:170-187)
+_triton_moe_routing = _cuda_moe_routing
+
+
+def _pytorch_moe_routing(gate_logits: torch.Tensor, top_k: int):
+    """The torch formula of moe_triton.py:121-127, the comparison of the reference's kernel test."""
+    probs = torch.softmax(gate_logits, dim=-1)
+    vals, idx = torch.topk(probs, top_k, dim=-1)
+    return vals / vals.sum(dim=-1, keepdim=True), idx
 
 
 def fused_moe_routing(gate_logits: torch.Tensor, top_k: int):

@@ -6,8 +6,15 @@ reference (norm_triton.py:111-120) and computes the reference's PyTorch
 formula (norm_triton.py:88-98), ``residual + (x*rsqrt(mean(x^2)+eps)).to(x.dtype)
 * weight``, with torch's type promotion at each step, in one CUDA pass.
 Unlike the reference's Triton kernel it is differentiable (x, residual and
-weight).  ``_cuda_rmsnorm_residual`` is the kernel call without validation,
-the counterpart of the reference's ``_triton_rmsnorm_residual``.
+weight).  ``_cuda_rmsnorm_residual`` is the kernel call without validation.
+
+The reference's tests import three more names from this module
+(tests/test_triton.py:19-25,142-149), kept here with the same meaning:
+``HAS_TRITON`` says whether the fused GPU kernel is available (here: whether
+the CUDA library is built; no Triton is involved), ``_triton_rmsnorm_residual``
+is the fused kernel call, and ``_pytorch_rmsnorm_residual`` is the plain torch
+formula those tests compare the kernel against.  No product path calls
+``_pytorch_rmsnorm_residual``.
 """
 
 from __future__ import annotations
@@ -15,6 +22,8 @@ from __future__ import annotations
 import torch
 
 from ats_v2_b200 import _lib
+
+HAS_TRITON = _lib.LIB_PATH.exists()  # the reference's flag name: fused GPU kernel available
 
 
 def _out_dtype(x: torch.Tensor, w: torch.Tensor) -> torch.dtype:
@@ -59,6 +68,18 @@ def _cuda_rmsnorm_residual(x: torch.Tensor, residual: torch.Tensor, weight: torc
     if residual.dtype != x.dtype:
         raise TypeError(f"fused_rmsnorm_residual: residual dtype {residual.dtype} must equal x dtype {x.dtype}")
     return _RMSNormResidualFn.apply(x, residual, weight, eps)
+
+
+# fused-kernel name of the reference module (tests/test_triton.py:142-149)
+_triton_rmsnorm_residual = _cuda_rmsnorm_residual
+
+
+def _pytorch_rmsnorm_residual(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor,
+                              eps: float) -> torch.Tensor:
+    """The torch formula of norm_triton.py:88-98, the comparison of the reference's kernel test."""
+    xf = x.to(torch.float32)
+    inv = torch.rsqrt(xf.pow(2).mean(dim=-1, keepdim=True) + eps)
+    return residual + (xf * inv).to(x.dtype) * weight
 
 
 def fused_rmsnorm_residual(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor,
