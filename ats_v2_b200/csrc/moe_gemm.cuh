@@ -56,4 +56,17 @@ int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a,
                    void* dh, void* dxp, void* dwgu, void* dwd, int E, int64_t H, int64_t F, const SegTable& sg,
                    cudaStream_t st);
 
+// Router GEMMs on the tensor cores (bf16 tokens, float32 router weight as three bf16 parts).
+// The expert count is padded to kRouterEp (one 64-wide tile holds every expert).
+constexpr int kRouterEp = 64;
+//   logits[T,E] = x[T,H] . w^T (+ bias), float32;  wparts [3][Ep][H]
+int tc_router_logits(const void* x, const void* wparts, const float* bias, float* logits, int64_t T, int64_t H,
+                     int E, int Ep, const SegTable& one, cudaStream_t st);
+//   dx[T,H] = bf16(dlogits . w) (+ the token's permuted-row gradients);  dlparts [T][3Ep]
+int tc_router_dx(const void* dlparts, const void* wparts, const void* dxp, const int* tok_row, int k, void* dx,
+                 int64_t T, int64_t H, int Ep, const SegTable& one, cudaStream_t st);
+//   partial[g][H][Ep] = x[rows of chunk g]^T . dlogits[rows of chunk g]
+int tc_router_dw(const void* x, const void* dlparts, float* partial, int64_t T, int64_t H, int Ep,
+                 const SegTable& chunks, cudaStream_t st);
+
 }  // namespace ats

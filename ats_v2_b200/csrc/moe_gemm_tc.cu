@@ -42,7 +42,8 @@ constexpr int kEpiWarps = 8;  // two per TMEM lane quadrant, each owning half of
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr long long kWaitBudget = 4000000000LL;  // SM cycles, about 2 s
 
-enum Epi { EPI_STORE = 0, EPI_SWIGLU_FWD = 1, EPI_SWIGLU_BWD = 2 };
+enum Epi { EPI_STORE = 0, EPI_SWIGLU_FWD = 1, EPI_SWIGLU_BWD = 2, EPI_F32 = 3, EPI_SCATTER = 4 };
+constexpr int kMaxParts = 6;
 
 // Where B (the stacked expert weights in M-grouped GEMMs) is read.
 struct OpSpec {
@@ -62,6 +63,16 @@ struct GemmArgs {
   bf16* a_out;        // SWIGLU_FWD: [rows, F]
   int F;
   int* err;
+  // Operand parts (SPLIT > 1): k block kb reads part kb % SPLIT, whose A tile starts a_koff
+  // further along K, and whose B tile starts b_koff further along K and b_noff along N.  All
+  // parts accumulate into one tile, so bf16 parts of a float32 operand give a float32 product.
+  int a_koff[kMaxParts], b_koff[kMaxParts], b_noff[kMaxParts];
+  float* out_f32;        // EPI_F32 output
+  const float* bias;     // EPI_F32: added to every row (per column; may be null)
+  int m_valid, n_valid;  // EPI_F32 / EPI_SCATTER: rows and columns of the output that exist
+  const bf16* dxp;       // EPI_SCATTER: permuted-row gradients summed into each token (may be null)
+  const int* tok_row;    // EPI_SCATTER: [T*topk] permuted row of (token, slot), -1 = dropped
+  int topk;
 };
 
 // tile -> (group, weight index, m tile, n tile, k blocks).  Groups are the
@@ -80,7 +91,7 @@ __device__ __forceinline__ int n_groups(const GemmArgs& p) {
   return KGROUP ? p.seg.E : p.seg.nseg;
 }
 
-template <int BN, bool KGROUP, int EPI>
+template <int BN, bool KGROUP, int EPI, int SPLIT>
 __device__ __forceinline__ bool decode_tile(const GemmArgs& p, const int* tiles_before, int t, TileInfo& ti) {
   const int NT = n_tiles<BN, KGROUP, EPI>(p);
   const int G = n_groups<KGROUP>(p);
@@ -94,10 +105,10 @@ __device__ __forceinline__ bool decode_tile(const GemmArgs& p, const int* tiles_
         ti.e = g;
         int kb = 0;
         for (int u = 0; u < p.seg.spe; ++u) kb += p.seg.rows[p.seg.eseg[g * p.seg.spe + u]] / BK;
-        ti.kb = kb;
+        ti.kb = kb * SPLIT;
       } else {
         ti.e = p.seg.expert[g];
-        ti.kb = p.K / BK;
+        ti.kb = (p.K / BK) * SPLIT;
       }
       return true;
     }
@@ -142,13 +153,14 @@ __device__ __forceinline__ void load32(const bf16* src, float (&v)[32]) {
   }
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI, bool KGROUP>
+template <int BN, bool A_MN, bool B_MN, int EPI, bool KGROUP, int SPLIT, int BPARTS>
 __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                                                               const __grid_constant__ CUtensorMap tmB,
                                                               GemmArgs p) {
   constexpr uint32_t A_BYTES = BM * BK * 2;
   constexpr uint32_t B_BYTES = BN * BK * 2;
-  constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  constexpr uint32_t STAGE_BYTES = A_BYTES + BPARTS * B_BYTES;  // one A tile, BPARTS B tiles
+  static_assert(SPLIT == 1 || BPARTS == 1, "operand parts along K or in the stage, not both");
   constexpr uint32_t IDESC = tc::idesc_bf16(BM, BN, A_MN, B_MN);
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte aligned ring (the 128-byte swizzle atom spans 1024 bytes)
@@ -205,7 +217,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
       for (int s = 0; s < STAGES; ++s) last_parity[s] = -1;
       for (int t = blockIdx.x; t < total && !abort_flag; t += gridDim.x) {
         TileInfo ti;
-        decode_tile<BN, KGROUP, EPI>(p, tiles_before, t, ti);
+        decode_tile<BN, KGROUP, EPI, SPLIT>(p, tiles_before, t, ti);
         const int m0 = ti.mt * BM;
         const int n0 = EPI == EPI_SWIGLU_FWD ? ti.nt * (BN / 2) : ti.nt * BN;
         // K blocks: M-grouped = kb of the fixed K; K-grouped = the expert's segments' rows, in order.
@@ -220,7 +232,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
         }
         const int b_row0 = ti.e * p.b.group_rows;
         for (int kb = 0; kb < ti.kb; ++kb) {
-          if (KGROUP) {
+          const int part = SPLIT == 1 ? 0 : kb % SPLIT;
+          const int kq = SPLIT == 1 ? kb : kb / SPLIT;  // K block of the fixed-K (M-grouped) loop
+          const int a_ko = SPLIT == 1 ? 0 : p.a_koff[part];
+          const int b_ko = SPLIT == 1 ? 0 : p.b_koff[part];
+          const int b_no = SPLIT == 1 ? 0 : p.b_noff[part];
+          if (KGROUP && part == 0) {
             while (lkb >= seg_kb) {  // next non-empty segment of this expert
               ++u;
               lkb = 0;
@@ -237,23 +254,30 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
           uint8_t* sb = sa + A_BYTES;
           tc::mbar_arrive_expect_tx(&full_bar[stage], STAGE_BYTES);
           if (!A_MN) {  // M-grouped A: rows of the tile's segment, K contiguous
-            tc::tma_load_2d(sa, &tmA, kb * BK, seg_r0 + m0, &full_bar[stage]);
+            tc::tma_load_2d(sa, &tmA, a_ko + kq * BK, seg_r0 + m0, &full_bar[stage]);
           } else {      // K-grouped A: M contiguous, K = rows of the current segment
-            const int krow = seg_r0 + lkb * BK;
+            const int krow = seg_r0 + lkb * BK + a_ko;
             tc::tma_load_2d(sa, &tmA, m0, krow, &full_bar[stage]);
             tc::tma_load_2d(sa + 8192, &tmA, m0 + 64, krow, &full_bar[stage]);
           }
           if (!B_MN) {  // stacked weights, K contiguous
-            const int brow = b_row0 + n0;
-            tc::tma_load_2d(sb, &tmB, kb * BK, brow, &full_bar[stage]);
-            if (p.b.sub_offset)
-              tc::tma_load_2d(sb + (BN / 2) * 128, &tmB, kb * BK, brow + p.b.sub_offset, &full_bar[stage]);
-          } else {
-            const int krow = KGROUP ? seg_r0 + lkb * BK : b_row0 + kb * BK;
 #pragma unroll
-            for (int b = 0; b < BN / 64; ++b) tc::tma_load_2d(sb + b * 8192, &tmB, n0 + b * 64, krow, &full_bar[stage]);
+            for (int j = 0; j < BPARTS; ++j) {
+              const int brow = b_row0 + n0 + b_no + (BPARTS > 1 ? p.b_noff[j] : 0);
+              tc::tma_load_2d(sb + j * B_BYTES, &tmB, b_ko + kq * BK, brow, &full_bar[stage]);
+              if (BPARTS == 1 && p.b.sub_offset)
+                tc::tma_load_2d(sb + (BN / 2) * 128, &tmB, b_ko + kq * BK, brow + p.b.sub_offset, &full_bar[stage]);
+            }
+          } else {
+            const int krow = (KGROUP ? seg_r0 + lkb * BK : b_row0 + kq * BK) + b_ko;
+#pragma unroll
+            for (int j = 0; j < BPARTS; ++j)
+#pragma unroll
+              for (int b = 0; b < BN / 64; ++b)
+                tc::tma_load_2d(sb + j * B_BYTES + b * 8192, &tmB, n0 + b_no + (BPARTS > 1 ? p.b_noff[j] : 0) + b * 64,
+                                krow, &full_bar[stage]);
           }
-          ++lkb;
+          if (part == SPLIT - 1) ++lkb;
           last_parity[stage] = (int)phase;
           if (++stage == STAGES) {
             stage = 0;
@@ -277,7 +301,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
       const uint32_t a_step = A_MN ? 2048u : 32u, b_step = B_MN ? 2048u : 32u;
       for (int t = blockIdx.x; t < total && !abort_flag; t += gridDim.x, ++i) {
         TileInfo ti;
-        decode_tile<BN, KGROUP, EPI>(p, tiles_before, t, ti);
+        decode_tile<BN, KGROUP, EPI, SPLIT>(p, tiles_before, t, ti);
         const int acc = i & 1;
         const uint32_t acc_phase = (uint32_t)(i >> 1) & 1u;
         if (!tc::mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, &abort_flag, kWaitBudget)) {
@@ -299,8 +323,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
             const uint64_t ad = tc::smem_desc(sa + k * a_step, a_lbo, 1024u, tc::kLayoutSW128);
-            const uint64_t bd = tc::smem_desc(sb + k * b_step, b_lbo, 1024u, tc::kLayoutSW128);
-            tc::mma_bf16(d_tmem, ad, bd, IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+#pragma unroll
+            for (int j = 0; j < BPARTS; ++j) {  // the B parts of the stage share the A tile
+              const uint64_t bd = tc::smem_desc(sb + j * B_BYTES + k * b_step, b_lbo, 1024u, tc::kLayoutSW128);
+              tc::mma_bf16(d_tmem, ad, bd, IDESC, (kb > 0 || k > 0 || j > 0) ? 1u : 0u);
+            }
           }
           tc::mma_commit(&empty_bar[stage]);
           issued = true;
@@ -329,7 +356,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
     int i = 0;
     for (int t = blockIdx.x; t < total && !abort_flag; t += gridDim.x, ++i) {
       TileInfo ti;
-      decode_tile<BN, KGROUP, EPI>(p, tiles_before, t, ti);
+      decode_tile<BN, KGROUP, EPI, SPLIT>(p, tiles_before, t, ti);
       const int acc = i & 1;
       const uint32_t acc_phase = (uint32_t)(i >> 1) & 1u;
       if constexpr (EPI == EPI_SWIGLU_BWD) {
@@ -409,6 +436,85 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
             store32(p.h_out + row * (2 * (int64_t)p.F) + p.F + n0 + c, uv);
             store32(p.a_out + row * (int64_t)p.F + n0 + c, av);
           }
+        } else if constexpr (EPI == EPI_F32) {
+          // float32 tile, rows below m_valid and columns below n_valid, plus a per-column bias
+          const bool zero = ti.kb == 0;
+          const int c0 = chalf * (BN / 2);
+          const int64_t row = KGROUP ? (int64_t)ti.mt * BM + row_in_tile
+                                     : (int64_t)p.seg.row0[ti.g] + ti.mt * BM + row_in_tile;
+          float* outp = p.out_f32 + (KGROUP ? (int64_t)ti.e * p.out_group : 0) + row * p.ldo;
+          const bool vec4 = (p.ldo & 3) == 0;
+#pragma unroll 1
+          for (int c = 0; c < BN / 2; c += 32) {
+            float v[32];
+            if (!zero) {
+              tc::tmem_ld32(t_row + c0 + c, v);  // warp-wide: every lane loads, stores are guarded
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = 0.f;
+            }
+            const int col0 = ti.nt * BN + c0 + c;
+            if (row < p.m_valid) {
+              if (p.bias != nullptr) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (col0 + j < p.n_valid) v[j] = __fadd_rn(v[j], p.bias[col0 + j]);
+              }
+              if (vec4 && col0 + 32 <= p.n_valid) {
+                float4* d = reinterpret_cast<float4*>(outp + col0);
+#pragma unroll
+                for (int q = 0; q < 8; ++q) d[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+              } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (col0 + j < p.n_valid) outp[col0 + j] = v[j];
+              }
+            }
+          }
+        } else if constexpr (EPI == EPI_SCATTER) {
+          // token gradient: the router's share (this tile, cast to bf16) plus the token's kept
+          // permuted-row gradients summed in ascending row (= expert) order, as two bf16 gradients add
+          const int c0 = chalf * (BN / 2);
+          const int64_t tok = (int64_t)p.seg.row0[ti.g] + ti.mt * BM + row_in_tile;
+          const bool ok = tok < p.m_valid;
+          int rows[kMaxTopK];
+          int n = 0;
+          if (ok && p.dxp != nullptr) {
+            for (int s2 = 0; s2 < p.topk; ++s2) {
+              const int r = p.tok_row[tok * p.topk + s2];
+              if (r < 0) continue;
+              int q = n++;
+              while (q > 0 && rows[q - 1] > r) {
+                rows[q] = rows[q - 1];
+                --q;
+              }
+              rows[q] = r;
+            }
+          }
+          const int64_t col_base = (int64_t)ti.nt * BN + c0;
+          bf16* outp = p.out + tok * p.ldo + col_base;
+#pragma unroll 1
+          for (int c = 0; c < BN / 2; c += 32) {
+            float v[32];
+            tc::tmem_ld32(t_row + c0 + c, v);
+            if (ok) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = round_to<bf16>(v[j]);
+              if (n > 0) {
+                float m[32], u[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) m[j] = 0.f;
+                for (int i2 = 0; i2 < n; ++i2) {
+                  load32(p.dxp + (int64_t)rows[i2] * p.ldo + col_base + c, u);
+#pragma unroll
+                  for (int j = 0; j < 32; ++j) m[j] += u[j];
+                }
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(round_to<bf16>(m[j]), v[j]);
+              }
+              store32(outp + c, v);
+            }
+          }
         } else {
           const bool zero = ti.kb == 0;
           const int c0 = chalf * (BN / 2);
@@ -477,11 +583,11 @@ int make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, u
   return ATS_OK;
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI, bool KGROUP>
+template <int BN, bool A_MN, bool B_MN, int EPI, bool KGROUP, int SPLIT = 1, int BPARTS = 1>
 int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& p, int64_t max_tiles,
               cudaStream_t st) {
-  auto kfn = tc_gemm_kernel<BN, A_MN, B_MN, EPI, KGROUP>;
-  const int smem = STAGES * (BM * BK * 2 + BN * BK * 2) + 1024;
+  auto kfn = tc_gemm_kernel<BN, A_MN, B_MN, EPI, KGROUP, SPLIT, BPARTS>;
+  const int smem = STAGES * (BM * BK * 2 + BPARTS * BN * BK * 2) + 1024;
   cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return fail(ATS_ECUDA, "moe_gemm: smem attribute: %s", cudaGetErrorString(e));
   int grid = num_sms();
@@ -596,6 +702,84 @@ int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a,
     if (bn == 256) return launch_tc<256, true, true, EPI_STORE, true>(ma, mb, p, tiles, st);
     return launch_tc<128, true, true, EPI_STORE, true>(ma, mb, p, tiles, st);
   }
+}
+
+
+
+namespace {
+void set_parts(int (&dst)[kMaxParts], std::initializer_list<int> v) {
+  int i = 0;
+  for (int x : v) dst[i++] = x;
+  for (; i < kMaxParts; ++i) dst[i] = 0;
+}
+}  // namespace
+
+int tc_router_logits(const void* x, const void* wparts, const float* bias, float* logits, int64_t T, int64_t H,
+                     int E, int Ep, const SegTable& one, cudaStream_t st) {
+  if (Ep != kRouterEp) return fail(ATS_EUNSUPPORTED, "moe_router: padded expert count %d", Ep);
+  CUtensorMap ma, mb;
+  GemmArgs p{};
+  p.seg = one;
+  p.N = Ep;
+  p.K = (int)H;
+  p.b = OpSpec{0, 0};
+  set_parts(p.b_noff, {0, Ep, 2 * Ep});  // the three weight parts, one stage each k block
+  p.out_f32 = logits;
+  p.ldo = E;
+  p.bias = bias;
+  p.m_valid = (int)T;
+  p.n_valid = E;
+  ATS_TRY(make_map(&ma, x, H, T, H * 2, 128));
+  ATS_TRY(make_map(&mb, wparts, H, (uint64_t)3 * Ep, H * 2, Ep));
+  return launch_tc<kRouterEp, false, false, EPI_F32, false, 1, 3>(ma, mb, p, (T + BM - 1) / BM, st);
+}
+
+int tc_router_dx(const void* dlparts, const void* wparts, const void* dxp, const int* tok_row, int k, void* dx,
+                 int64_t T, int64_t H, int Ep, const SegTable& one, cudaStream_t st) {
+  CUtensorMap ma, mb;
+  GemmArgs p{};
+  p.seg = one;
+  p.N = (int)H;
+  p.K = Ep;
+  p.b = OpSpec{0, 0};
+  // dl . w over the six part pairs whose product is above 2^-24 of the leading one
+  set_parts(p.a_koff, {0, 0, 0, Ep, Ep, 2 * Ep});
+  set_parts(p.b_koff, {0, Ep, 2 * Ep, 0, Ep, 0});
+  set_parts(p.b_noff, {0, 0, 0, 0, 0, 0});
+  p.out = static_cast<bf16*>(dx);
+  p.ldo = H;
+  p.m_valid = (int)T;
+  p.n_valid = (int)H;
+  p.dxp = static_cast<const bf16*>(dxp);
+  p.tok_row = tok_row;
+  p.topk = k;
+  ATS_TRY(make_map(&ma, dlparts, (uint64_t)3 * Ep, T, (uint64_t)3 * Ep * 2, 128));
+  ATS_TRY(make_map(&mb, wparts, H, (uint64_t)3 * Ep, H * 2, 64));
+  const int64_t mt = (T + BM - 1) / BM;
+  if (Ep != kRouterEp) return fail(ATS_EUNSUPPORTED, "moe_router: padded expert count %d", Ep);
+  if (pick_bn(H) == 256) return launch_tc<256, false, true, EPI_SCATTER, false, 6>(ma, mb, p, mt * (H / 256), st);
+  return launch_tc<128, false, true, EPI_SCATTER, false, 6>(ma, mb, p, mt * (H / 128), st);
+}
+
+int tc_router_dw(const void* x, const void* dlparts, float* partial, int64_t T, int64_t H, int Ep,
+                 const SegTable& chunks, cudaStream_t st) {
+  if (Ep != kRouterEp) return fail(ATS_EUNSUPPORTED, "moe_router: padded expert count %d", Ep);
+  CUtensorMap ma, mb;
+  GemmArgs p{};
+  p.seg = chunks;
+  p.M = (int)H;
+  p.N = Ep;
+  p.K = 0;
+  p.b = OpSpec{0, 0};
+  set_parts(p.b_noff, {0, Ep, 2 * Ep});  // the three gradient parts, one stage each k block
+  p.out_f32 = partial;
+  p.ldo = Ep;
+  p.out_group = H * Ep;
+  p.m_valid = (int)H;
+  p.n_valid = Ep;
+  ATS_TRY(make_map(&ma, x, H, T, H * 2, 64));
+  ATS_TRY(make_map(&mb, dlparts, (uint64_t)3 * Ep, T, (uint64_t)3 * Ep * 2, 64));
+  return launch_tc<kRouterEp, true, true, EPI_F32, true, 1, 3>(ma, mb, p, (int64_t)chunks.E * (H / BM), st);
 }
 
 }  // namespace ats

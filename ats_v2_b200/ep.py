@@ -33,12 +33,12 @@ from __future__ import annotations
 
 import torch
 import torch.distributed as dist
-import torch.nn.functional as F
 from torch import nn
 
 from ats_v2_b200 import _lib
 from ats_v2_b200.ffn import SwiGLU
-from ats_v2_b200.moe import LazyUtilization, capacity_for, init_residual_projection, stacked
+from ats_v2_b200.moe import (LazyUtilization, capacity_for, init_residual_projection, router_backward,
+                             router_forward, stacked)
 
 SLOTS = _lib.ATS_MOE_SLOTS
 
@@ -68,13 +68,14 @@ def exchange_rows(buf: torch.Tensor, group=None) -> torch.Tensor:
 
 class _EPMoEFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x2, logits, meta, wgu_stack, wd_stack, *local_weights):
+    def forward(ctx, x2, gate_w, bias, meta, wgu_stack, wd_stack, *local_weights):
         E, El, k, C, lbw, Fdim, W, group = meta
         T, H = x2.shape
         dev = x2.device
         dt = _lib.dtype_code(x2.dtype)
         st = _lib.stream_of(x2)
         Cp = slot_rows(C)
+        logits, rws, w32 = router_forward(x2, gate_w, bias)
         wsb = _lib.query("ats_moe_workspace_bytes", T, E, k, C, SLOTS)
         R = _lib.query("ats_moe_max_rows", T, E, k, C, SLOTS)  # = E*Cp = W*El*Cp
         ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
@@ -102,15 +103,15 @@ class _EPMoEFn(torch.autograd.Function):
         ys = exchange_rows(yr, group) if W > 1 else yr
         out = torch.empty((T, H), dtype=x2.dtype, device=dev)
         _lib.call("ats_moe_combine", ys.data_ptr(), out.data_ptr(), dt, T, H, E, k, C, SLOTS, ws.data_ptr(), wsb, st)
-        ctx.save_for_backward(logits, gates, idx, ws, xr, h, a, ys, seg, wgu_stack, wd_stack)
-        ctx.meta = (E, El, k, C, lbw, Fdim, W, group, T, H, wsb, R, segb)
+        ctx.save_for_backward(logits, gates, idx, ws, xr, h, a, ys, seg, wgu_stack, wd_stack, x2, w32, rws)
+        ctx.meta = (E, El, k, C, lbw, Fdim, W, group, T, H, wsb, R, segb, gate_w.dtype)
         ctx.mark_non_differentiable(util, counts, idx)
         return out, aux, util, counts, idx
 
     @staticmethod
     def backward(ctx, dout, daux, _dutil, _dcounts, _didx):
-        logits, gates, idx, ws, xr, h, a, ys, seg, wgu_stack, wd_stack = ctx.saved_tensors
-        E, El, k, C, lbw, Fdim, W, group, T, H, wsb, R, segb = ctx.meta
+        logits, gates, idx, ws, xr, h, a, ys, seg, wgu_stack, wd_stack, x2, w32, rws = ctx.saved_tensors
+        E, El, k, C, lbw, Fdim, W, group, T, H, wsb, R, segb, gate_dtype = ctx.meta
         dev = xr.device
         dt = _lib.dtype_code(xr.dtype)
         st = _lib.stream_of(xr)
@@ -130,15 +131,13 @@ class _EPMoEFn(torch.autograd.Function):
                   wgu_stack.data_ptr(), wd_stack.data_ptr(), dh.data_ptr(), dxr.data_ptr(), dwgu.data_ptr(),
                   dwd.data_ptr(), dt, W, El, C, H, Fdim, seg.data_ptr(), segb, st)
         dxs = exchange_rows(dxr, group) if W > 1 else dxr
-        dx = torch.empty((T, H), dtype=xr.dtype, device=dev)
-        _lib.call("ats_moe_scatter_grad", dxs.data_ptr(), dx.data_ptr(), dt, T, H, E, k, C, SLOTS, ws.data_ptr(),
-                  wsb, st)
         dlogits = torch.empty((T, E), dtype=torch.float32, device=dev)
         daux_t = daux.to(torch.float32).contiguous() if daux is not None else None
         _lib.call("ats_moe_route_bwd", logits.data_ptr(), gates.data_ptr(), idx.data_ptr(), dgate_row.data_ptr(),
                   _lib.ptr(daux_t), dlogits.data_ptr(), T, E, k, C, SLOTS, float(lbw), ws.data_ptr(), wsb, st)
+        dx, dgate_w = router_backward(dlogits, x2, w32, rws, dxs, ws, wsb, (T, E, k, C, SLOTS), True)
         grads = [dwgu[e] for e in range(El)] + [dwd[e] for e in range(El)]
-        return (dx, dlogits, None, None, None, *grads)
+        return (dx, dgate_w.to(gate_dtype), None, None, None, None, *grads)
 
 
 class ExpertParallelMoE(nn.Module):
@@ -173,11 +172,13 @@ class ExpertParallelMoE(nn.Module):
         self.last_counts: torch.Tensor | None = None
 
     def router_logits(self, flat_x: torch.Tensor) -> torch.Tensor:
-        return F.linear(flat_x.float(), self.gate.weight.float())
+        """The float32 logits forward() routes on (without a logit bias)."""
+        with torch.no_grad():
+            return router_forward(flat_x.contiguous(), self.gate.weight, None)[0]
 
     def forward(self, x: torch.Tensor, logit_bias: torch.Tensor | None = None):
-        """x [B,S,H] -> (out [B,S,H], aux).  ``logit_bias`` [E] is added to the
-        router logits (used to impose a skewed expert load in benchmarks)."""
+        """x [B,S,H] -> (out [B,S,H], aux).  ``logit_bias`` [E] is a constant added
+        to the router logits (used to impose a skewed expert load in benchmarks)."""
         batch, seq, H = x.shape
         if H != self.hidden_size:
             raise ValueError(f"MoE expected hidden_size={self.hidden_size}, got {H}.")
@@ -185,16 +186,14 @@ class ExpertParallelMoE(nn.Module):
         flat = x.reshape(-1, H).contiguous()
         T = flat.shape[0]
         cap = capacity_for(T, self.top_k, self.num_experts, self.capacity_factor)
-        logits = self.router_logits(flat)
-        if logit_bias is not None:
-            logits = logits + logit_bias.to(logits.dtype)
         wgu = [e.gate_up_proj.weight for e in self.experts]
         wd = [e.down_proj.weight for e in self.experts]
         if wgu[0].dtype != flat.dtype:
             raise TypeError(f"MoE: token dtype {flat.dtype} does not match expert weight dtype {wgu[0].dtype}")
         meta = (self.num_experts, self.num_local_experts, self.top_k, cap, self.load_balancing_weight,
                 wgu[0].shape[0] // 2, self.world, self.group)
-        out, aux, util, counts, _ = _EPMoEFn.apply(flat, logits.contiguous(), meta, stacked(wgu), stacked(wd),
+        bias = logit_bias.detach().float().contiguous() if logit_bias is not None else None
+        out, aux, util, counts, _ = _EPMoEFn.apply(flat, self.gate.weight, bias, meta, stacked(wgu), stacked(wd),
                                                    *wgu, *wd)
         self.last_expert_utilization = LazyUtilization(util)
         self.last_counts = counts

@@ -134,20 +134,47 @@ class LazyUtilization(dict):
         return dict.get(self, key, default)
 
 
+def router_forward(x2: torch.Tensor, gate_w: torch.Tensor, bias: torch.Tensor | None):
+    """float32 router logits [T,E] = x2.float() @ gate_w.float().T (+ bias) and the
+    router workspace (None when the tensor-core path does not cover the shape
+    and a library GEMM computed them)."""
+    T, H = x2.shape
+    E = gate_w.shape[0]
+    w32 = gate_w.detach().float().contiguous()
+    b32 = bias.detach().float().contiguous() if bias is not None else None
+    dt = _lib.dtype_code(x2.dtype)
+    if _lib.query("ats_moe_router_supported", dt, T, H, E) == 1:
+        wsb = _lib.query("ats_moe_router_workspace_bytes", T, H, E)
+        rws = torch.empty(wsb, dtype=torch.uint8, device=x2.device)
+        logits = torch.empty((T, E), dtype=torch.float32, device=x2.device)
+        _lib.call("ats_moe_router_fwd", x2.data_ptr(), w32.data_ptr(), _lib.ptr(b32), logits.data_ptr(), T, H, E,
+                  rws.data_ptr(), wsb, _lib.stream_of(x2))
+        return logits, rws, w32
+    logits = F.linear(x2.float(), w32)
+    if b32 is not None:
+        logits = logits + b32
+    return logits, None, w32
+
+
 class _MoEFn(torch.autograd.Function):
     """Device stages of the MoE layer on flattened tokens x2 [T,H].
 
-    Inputs: x2, logits [T,E] f32, meta=(E,k,C,lbw,F,layout), the two weight
-    stacks, then the per-expert weights (only so autograd routes their
-    gradients)."""
+    Inputs: x2, then either float32 logits [T,E] (gate_w None) or the router
+    weight gate_w [E,H] (logits None; the router runs inside, and its
+    gradient and its share of dx come out of the backward), an optional
+    constant logit bias [E], meta=(E,k,C,lbw,F,layout), the two weight stacks,
+    then the per-expert weights (only so autograd routes their gradients)."""
 
     @staticmethod
-    def forward(ctx, x2, logits, meta, wgu_stack, wd_stack, *expert_weights):
+    def forward(ctx, x2, logits, gate_w, bias, meta, wgu_stack, wd_stack, *expert_weights):
         E, k, C, lbw, Fdim, L = meta
         T, H = x2.shape
         dev = x2.device
         dt = _lib.dtype_code(x2.dtype)
         st = _lib.stream_of(x2)
+        rws = w32 = None
+        if gate_w is not None:
+            logits, rws, w32 = router_forward(x2, gate_w, bias)
         ws_bytes = _lib.query("ats_moe_workspace_bytes", T, E, k, C, L)
         max_rows = _lib.query("ats_moe_max_rows", T, E, k, C, L)
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
@@ -168,15 +195,16 @@ class _MoEFn(torch.autograd.Function):
                   a.data_ptr(), y.data_ptr(), dt, T, E, k, C, L, H, Fdim, ws.data_ptr(), ws_bytes, st)
         out = torch.empty((T, H), dtype=x2.dtype, device=dev)
         _lib.call("ats_moe_combine", y.data_ptr(), out.data_ptr(), dt, T, H, E, k, C, L, ws.data_ptr(), ws_bytes, st)
-        ctx.save_for_backward(logits, gates, idx, ws, xp, h, a, y, wgu_stack, wd_stack)
-        ctx.meta = (E, k, C, lbw, Fdim, L, T, H, ws_bytes, max_rows)
+        ctx.save_for_backward(logits, gates, idx, ws, xp, h, a, y, wgu_stack, wd_stack, x2, w32, rws)
+        ctx.meta = (E, k, C, lbw, Fdim, L, T, H, ws_bytes, max_rows, gate_w is not None,
+                    gate_w.dtype if gate_w is not None else None)
         ctx.mark_non_differentiable(util, counts, idx)
         return out, aux, util, counts, idx
 
     @staticmethod
     def backward(ctx, dout, daux, _dutil, _dcounts, _didx):
-        logits, gates, idx, ws, xp, h, a, y, wgu_stack, wd_stack = ctx.saved_tensors
-        E, k, C, lbw, Fdim, L, T, H, ws_bytes, max_rows = ctx.meta
+        logits, gates, idx, ws, xp, h, a, y, wgu_stack, wd_stack, x2, w32, rws = ctx.saved_tensors
+        E, k, C, lbw, Fdim, L, T, H, ws_bytes, max_rows, has_router, gate_dtype = ctx.meta
         dev = xp.device
         dt = _lib.dtype_code(xp.dtype)
         st = _lib.stream_of(xp)
@@ -194,27 +222,57 @@ class _MoEFn(torch.autograd.Function):
         _lib.call("ats_moe_experts_bwd", dy.data_ptr(), xp.data_ptr(), h.data_ptr(), a.data_ptr(),
                   wgu_stack.data_ptr(), wd_stack.data_ptr(), dh.data_ptr(), dxp.data_ptr(), dwgu.data_ptr(),
                   dwd.data_ptr(), dt, T, E, k, C, L, H, Fdim, ws.data_ptr(), ws_bytes, st)
-        dx = torch.empty((T, H), dtype=xp.dtype, device=dev)
-        _lib.call("ats_moe_scatter_grad", dxp.data_ptr(), dx.data_ptr(), dt, T, H, E, k, C, L, ws.data_ptr(),
-                  ws_bytes, st)
         dlogits = torch.empty((T, E), dtype=torch.float32, device=dev)
         daux_t = daux.to(torch.float32).contiguous() if daux is not None else None
         _lib.call("ats_moe_route_bwd", logits.data_ptr(), gates.data_ptr(), idx.data_ptr(), dgate_row.data_ptr(),
                   _lib.ptr(daux_t), dlogits.data_ptr(), T, E, k, C, L, float(lbw), ws.data_ptr(), ws_bytes, st)
         grads = [dwgu[e] for e in range(E)] + [dwd[e] for e in range(E)]
-        return (dx, dlogits, None, None, None, *grads)
+        dx, dgate_w = router_backward(dlogits, x2, w32, rws, dxp, ws, ws_bytes, (T, E, k, C, L), has_router)
+        if not has_router:
+            return (dx, dlogits, None, None, None, None, None, *grads)
+        return (dx, None, dgate_w.to(gate_dtype), None, None, None, None, *grads)
 
 
-def moe_apply(x2: torch.Tensor, logits: torch.Tensor, wgu: list[torch.Tensor], wd: list[torch.Tensor],
-              top_k: int, capacity: int, lbw: float, layout: int = _lib.ATS_MOE_PACKED):
-    """Run the device MoE stages; returns (out [T,H], aux (0-dim), util [E], counts [E], idx [T,k])."""
+def router_backward(dlogits, x2, w32, rws, dxp, ws, ws_bytes, plan, has_router):
+    """(dx, dgate_w): the token gradient (the permuted-row gradients summed per
+    token, plus the router's share when the router ran inside) and the router
+    weight gradient (float32, None without a router)."""
+    T, E, k, C, L = plan
+    H = x2.shape[1]
+    st = _lib.stream_of(x2)
+    dt = _lib.dtype_code(x2.dtype)
+    dx = torch.empty((T, H), dtype=x2.dtype, device=x2.device)
+    if has_router and rws is not None:
+        dw = torch.empty((E, H), dtype=torch.float32, device=x2.device)
+        _lib.call("ats_moe_router_bwd", dlogits.data_ptr(), x2.data_ptr(), w32.data_ptr(), dxp.data_ptr(),
+                  ws.data_ptr(), ws_bytes, k, C, L, dx.data_ptr(), dw.data_ptr(), T, H, E, rws.data_ptr(),
+                  rws.numel(), st)
+        return dx, dw
+    _lib.call("ats_moe_scatter_grad", dxp.data_ptr(), dx.data_ptr(), dt, T, H, E, k, C, L, ws.data_ptr(), ws_bytes,
+              st)
+    if not has_router:
+        return dx, None
+    # library-GEMM router (shapes the tensor-core router does not cover): the two bf16 token
+    # gradients add as autograd would add them
+    dx = dx + (dlogits @ w32).to(x2.dtype)
+    return dx, dlogits.t() @ x2.float()
+
+
+def moe_apply(x2: torch.Tensor, logits: torch.Tensor | None, wgu: list[torch.Tensor], wd: list[torch.Tensor],
+              top_k: int, capacity: int, lbw: float, layout: int = _lib.ATS_MOE_PACKED,
+              gate_w: torch.Tensor | None = None, bias: torch.Tensor | None = None):
+    """Run the device MoE stages; returns (out [T,H], aux (0-dim), util [E], counts [E], idx [T,k]).
+
+    Either float32 logits or the router weight gate_w (the router then runs
+    inside, on the tensor cores for bf16 tokens)."""
     E = len(wgu)
     Fdim = wgu[0].shape[0] // 2
     wgu_stack = stacked(wgu)
     wd_stack = stacked(wd)
-    logits = logits.float().contiguous()
-    return _MoEFn.apply(x2.contiguous(), logits, (E, top_k, capacity, lbw, Fdim, layout), wgu_stack, wd_stack,
-                        *wgu, *wd)
+    if gate_w is None:
+        logits = logits.float().contiguous()
+    return _MoEFn.apply(x2.contiguous(), logits, gate_w, bias, (E, top_k, capacity, lbw, Fdim, layout), wgu_stack,
+                        wd_stack, *wgu, *wd)
 
 
 def dense_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor) -> torch.Tensor:
@@ -255,15 +313,16 @@ class _CudaMoE(nn.Module):
         self.last_counts: torch.Tensor | None = None
 
     def router_logits(self, flat_x: torch.Tensor) -> torch.Tensor:
-        """float32 router: x @ Wg^T in float32 whatever the token dtype."""
-        return F.linear(flat_x.float(), self.gate.weight.float())
+        """float32 router: x @ Wg^T in float32 whatever the token dtype -- the
+        logits forward() routes on (tensor cores for bf16 tokens)."""
+        with torch.no_grad():
+            return router_forward(flat_x.contiguous(), self.gate.weight, None)[0]
 
     def compute_routing(self, flat_x: torch.Tensor):
         """(top_k_probs [T,k] f32, top_k_idx [T,k] int64, router_probs [T,E] f32)
         as moe.py:76-90, on the router kernel; no gradient is tracked."""
         _lib.require_cuda("compute_routing", flat_x)
-        with torch.no_grad():
-            logits = self.router_logits(flat_x).contiguous()
+        logits = self.router_logits(flat_x)
         from ats_v2_b200.moe_fused import _topk
 
         return _topk(logits, self.top_k, want_probs=True)
@@ -282,9 +341,8 @@ class _CudaMoE(nn.Module):
         wgu, wd = self._weights()
         if wgu[0].dtype != flat_x.dtype:
             raise TypeError(f"MoE: token dtype {flat_x.dtype} does not match expert weight dtype {wgu[0].dtype}")
-        logits = self.router_logits(flat_x)
-        out, aux, util, counts, _ = moe_apply(flat_x, logits, wgu, wd, self.top_k, cap,
-                                              self.load_balancing_weight)
+        out, aux, util, counts, _ = moe_apply(flat_x, None, wgu, wd, self.top_k, cap, self.load_balancing_weight,
+                                              gate_w=self.gate.weight)
         self.last_expert_utilization = LazyUtilization(util)
         self.last_counts = counts
         return out.view(batch, seq_len, hidden_size), aux

@@ -281,6 +281,40 @@ ATS_API int ats_moe_ep_experts_bwd(const void* dy, const void* xr, const void* h
 ATS_API int ats_moe_ep_status(const void* seg_workspace, size_t seg_workspace_bytes, int W, int E_local,
                       int* status);
 
+/* ------------------------------------------------------- router GEMMs
+ * The float32 router of the MoE layer (moe.py:76-90 with the north-star
+ * float32 router: logits = x.float() @ w.T) on the tensor cores, for bf16
+ * tokens and a float32 weight [E, hidden].  The float32 operands are split
+ * into three bf16 parts whose products are exact in the float32 accumulator,
+ * so the results are float32 GEMMs up to summation order.  Shapes: bf16
+ * tokens, T >= 128, hidden % 128 == 0, 1 <= E <= 64; anything else returns
+ * ATS_EUNSUPPORTED (the caller then runs the router with a library GEMM).
+ * The workspace is caller-owned (ats_moe_router_workspace_bytes; 0 when the
+ * shape is unsupported). */
+ATS_API int ats_moe_router_supported(ats_dtype x_dtype, int64_t T, int64_t hidden, int E);
+ATS_API size_t ats_moe_router_workspace_bytes(int64_t T, int64_t hidden, int E);
+
+/* logits[T,E] = x[T,hidden] . w[E,hidden]^T (+ bias[E], may be NULL), float32. */
+ATS_API int ats_moe_router_fwd(const void* x, const float* w, const float* bias, float* logits,
+                       int64_t T, int64_t hidden, int E, void* workspace, size_t workspace_bytes,
+                       void* stream);
+
+/* Backward of the router for upstream dlogits [T,E] float32:
+ *   dx[T,hidden] (bf16) = bf16(dlogits . w) + bf16(sum of the token's kept
+ *     permuted-row gradients dxp, ascending row order) -- the two bf16 token
+ *     gradients autograd adds (router input, expert input); with dxp = NULL
+ *     only the router's share.  dxp uses the MoE plan in moe_workspace, with
+ *     the plan's (T, E, k, capacity, layout); it replaces ats_moe_scatter_grad.
+ *   dw[E,hidden] (float32) = dlogits^T . x, summed in a fixed order. */
+ATS_API int ats_moe_router_bwd(const float* dlogits, const void* x, const float* w, const void* dxp,
+                       const void* moe_workspace, size_t moe_workspace_bytes, int k, int64_t capacity,
+                       int layout, void* dx, float* dw, int64_t T, int64_t hidden, int E,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
+/* Device status of the router GEMMs run with this workspace (as ats_moe_status). */
+ATS_API int ats_moe_router_status(const void* workspace, size_t workspace_bytes, int64_t T, int64_t hidden,
+                          int E, int* status);
+
 #ifdef __cplusplus
 }
 #endif
