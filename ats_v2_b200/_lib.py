@@ -78,7 +78,7 @@ SIGNATURES: dict[str, tuple] = {
     "ats_moe_route_bwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64,
                                   c_int, c_int, c_int64, c_int, c_float, c_void_p, c_size_t, c_void_p]),
     "ats_moe_ep_segments_bytes": (c_size_t, [c_int, c_int]),
-    "ats_moe_ep_segments": (c_int, [c_void_p, c_int, c_int, c_int64, c_void_p, c_size_t, c_void_p]),
+    "ats_moe_ep_segments": (c_int, [c_void_p, c_int, c_int, c_int64, c_int, c_void_p, c_size_t, c_void_p]),
     "ats_moe_ep_experts_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
                                        c_int, c_int64, c_int64, c_int64, c_void_p, c_size_t, c_void_p]),
     "ats_moe_ep_experts_bwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

@@ -248,19 +248,48 @@ int ep_table(const void* ws, size_t bytes, int W, int El, int64_t C, SegTable* s
   return ATS_OK;
 }
 
-// Segment s = source rank * E_local + local expert, at rows s*Cp.
-__global__ void ep_segments_kernel(const int* __restrict__ recv_kept, int W, int El, int Cp, EpSegs q) {
-  const int n = W * El;
-  for (int s = threadIdx.x; s < n; s += blockDim.x) {
-    const int src = s / El, el = s - src * El;
+// Segment s = source rank * E_local + local expert.  ATS_MOE_SLOTS: at rows
+// s*Cp.  ATS_MOE_PACKED: right after segment s-1 (the received rows are the
+// sources' packed segments, each rounded up to 128 rows, in (source, expert) order).
+__global__ void ep_segments_kernel(const int* __restrict__ recv_kept, int W, int El, int Cp, int layout,
+                                   EpSegs q) {
+  __shared__ int wsum[32];
+  const int n = W * El;  // <= kMaxExperts = blockDim.x
+  const int s = threadIdx.x, lane = s & 31, warp = s >> 5;
+  int rows = 0;
+  if (s < n) {
     int kept = recv_kept[s];
     kept = kept < 0 ? 0 : (kept > Cp ? Cp : kept);
-    q.row0[s] = s * Cp;
-    q.rows[s] = (kept + kSegAlign - 1) / kSegAlign * kSegAlign;
+    rows = (kept + kSegAlign - 1) / kSegAlign * kSegAlign;
+  }
+  // exclusive block scan of rows in segment order
+  int incl = rows;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int u = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += u;
+  }
+  if (lane == 31) wsum[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int v = wsum[lane];
+    int wi = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += u;
+    }
+    wsum[lane] = wi - v;
+  }
+  __syncthreads();
+  if (s < n) {
+    const int src = s / El, el = s - src * El;
+    q.row0[s] = layout == ATS_MOE_SLOTS ? s * Cp : wsum[warp] + incl - rows;
+    q.rows[s] = rows;
     q.expert[s] = el;
     q.eseg[el * W + src] = s;
   }
-  if (threadIdx.x == 0) q.err[0] = 0;
+  if (s == 0) q.err[0] = 0;
 }
 
 int check_experts(const void* p0, const void* p1, int64_t H, int64_t F, ats_dtype dt) {
@@ -310,14 +339,16 @@ size_t ats_moe_ep_segments_bytes(int W, int E_local) {
   return ep_carve(nullptr, W, E_local, nullptr);
 }
 
-int ats_moe_ep_segments(const int32_t* recv_kept, int W, int E_local, int64_t capacity, void* seg_workspace,
+int ats_moe_ep_segments(const int32_t* recv_kept, int W, int E_local, int64_t capacity, int layout, void* seg_workspace,
                         size_t seg_workspace_bytes, void* stream) {
   SegTable sg;
   ATS_TRY(ep_table(seg_workspace, seg_workspace_bytes, W, E_local, capacity, &sg));
   if (recv_kept == nullptr) return fail(ATS_EBADARG, "moe_ep_segments: null counts");
   EpSegs q;
   ep_carve(seg_workspace, W, E_local, &q);
-  ep_segments_kernel<<<1, 256, 0, (cudaStream_t)stream>>>(recv_kept, W, E_local, (int)slot_rows(capacity), q);
+  if (layout != ATS_MOE_PACKED && layout != ATS_MOE_SLOTS) return fail(ATS_EBADARG, "moe_ep_segments: layout %d", layout);
+  ep_segments_kernel<<<1, kMaxExperts, 0, (cudaStream_t)stream>>>(recv_kept, W, E_local, (int)slot_rows(capacity),
+                                                                  layout, q);
   return check_launch("moe_ep_segments");
 }
 

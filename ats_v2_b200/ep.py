@@ -8,16 +8,22 @@ replicated.  One forward:
 
   1. every rank routes its own T tokens (float32 router, capacity
      ``max(1, int(cf*T*k/E))`` from its own token count, as the fallback and
-     DeepSpeed compute it) into the capacity-slot layout: a [E][Cp] row buffer
-     (Cp = capacity rounded up to 128) that reads as [W][E_local][Cp];
-  2. the kept-row counts [W][E_local] and the row buffer are exchanged with
-     ``all_to_all_single`` on equal splits -- no host synchronisation, no
-     data-dependent sizes;
-  3. the receiving rank runs its local experts on [W][E_local][Cp] through a
-     segment table that covers only the kept rows of every (source, expert)
-     segment (padding costs link bandwidth, not tensor-core time);
-  4. the outputs go back with a second ``all_to_all_single`` and are combined
-     by each source rank in ascending expert order.
+     DeepSpeed compute it) and gathers its kept rows by expert;
+  2. the kept-row counts [W][E_local] go to the experts' ranks with
+     ``all_to_all_single``, then the rows themselves:
+       exchange="packed" (default): the packed layout, where the experts of a
+         destination rank are one contiguous run of segments (each kept count
+         rounded up to 128 rows), sent with variable splits -- only rows the
+         expert GEMMs read cross NVLink; the split sizes are read from the
+         device once per forward;
+       exchange="slots": the capacity-slot layout [E][Cp] (Cp = capacity
+         rounded up to 128), equal splits, no host synchronisation (what
+         DeepSpeed's capacity-padded exchange does);
+  3. the receiving rank runs its local experts on the received (source,
+     expert) segments through a segment table that covers only their kept
+     rows;
+  4. the outputs go back with the mirror exchange and are combined by each
+     source rank in ascending expert order.
 
 The backward sends the expert-output gradients out, runs the expert
 backward (weight gradients reduce over the W segments of each local expert),
@@ -25,8 +31,9 @@ and sends the input gradients back.  Expert weights are rank-local, so their
 gradients need no all-reduce; the replicated router weight's gradient is the
 usual data-parallel all-reduce of the training loop.
 
-The exchange steps (``exchange_counts``, ``exchange_rows``) only move tensors
-and work on any device and backend; the device stages are the library's.
+The exchange steps (``exchange_counts``, ``exchange_rows``,
+``exchange_rows_varsplit``) only move tensors and work on any device and
+backend; the device stages are the library's.
 """
 
 from __future__ import annotations
@@ -66,52 +73,106 @@ def exchange_rows(buf: torch.Tensor, group=None) -> torch.Tensor:
     return out
 
 
+def exchange_rows_varsplit(buf: torch.Tensor, send_rows: list[int], recv_rows: list[int], out_rows: int,
+                           group=None) -> torch.Tensor:
+    """Variable-split all-to-all of rows: the first sum(send_rows) rows of buf,
+    send_rows[r] of them to rank r; returns [out_rows, H] whose first
+    sum(recv_rows) rows came from the ranks in order."""
+    out = torch.empty((out_rows,) + tuple(buf.shape[1:]), dtype=buf.dtype, device=buf.device)
+    n_in, n_out = sum(send_rows), sum(recv_rows)
+    dist.all_to_all_single(out[:n_out], buf[:n_in].contiguous(), output_split_sizes=recv_rows,
+                           input_split_sizes=send_rows, group=group)
+    return out
+
+
+class _Exchange:
+    """How rows cross between ranks.  "slots": equal splits of the [W][E_local][Cp]
+    capacity-slot buffer (no host synchronisation).  "packed": only the rows
+    the expert GEMMs read (each (source, expert) segment's kept count rounded
+    up to 128), variable splits read once per forward from the device."""
+
+    def __init__(self, mode: str, W: int, El: int, Cp: int, group, seg_start: torch.Tensor | None,
+                 recv_kept: torch.Tensor):
+        self.mode, self.W, self.group = mode, W, group
+        if mode == "packed" and W > 1:
+            host = torch.cat([seg_start.to(torch.int64), recv_kept.to(torch.int64)]).cpu().tolist()
+            E = W * El
+            seg, rk = host[:E + 1], host[E + 1:]
+            self.send = [seg[(r + 1) * El] - seg[r * El] for r in range(W)]
+            self.recv = [sum((min(max(c, 0), Cp) + 127) // 128 * 128 for c in rk[r * El:(r + 1) * El])
+                         for r in range(W)]
+
+    def out(self, buf: torch.Tensor, rows_back: int) -> torch.Tensor:
+        """This rank's rows to their experts' ranks."""
+        if self.W == 1:
+            return buf
+        if self.mode == "slots":
+            return exchange_rows(buf, self.group)
+        return exchange_rows_varsplit(buf, self.send, self.recv, rows_back, self.group)
+
+    def back(self, buf: torch.Tensor, rows_back: int) -> torch.Tensor:
+        """Expert-side rows back to the ranks that own the tokens."""
+        if self.W == 1:
+            return buf
+        if self.mode == "slots":
+            return exchange_rows(buf, self.group)
+        return exchange_rows_varsplit(buf, self.recv, self.send, rows_back, self.group)
+
+
 class _EPMoEFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x2, gate_w, bias, meta, wgu_stack, wd_stack, *local_weights):
-        E, El, k, C, lbw, Fdim, W, group = meta
+        E, El, k, C, lbw, Fdim, W, group, mode = meta
+        L = SLOTS if mode == "slots" else _lib.ATS_MOE_PACKED
         T, H = x2.shape
         dev = x2.device
         dt = _lib.dtype_code(x2.dtype)
         st = _lib.stream_of(x2)
         Cp = slot_rows(C)
         logits, rws, w32 = router_forward(x2, gate_w, bias)
-        wsb = _lib.query("ats_moe_workspace_bytes", T, E, k, C, SLOTS)
-        R = _lib.query("ats_moe_max_rows", T, E, k, C, SLOTS)  # = E*Cp = W*El*Cp
+        wsb = _lib.query("ats_moe_workspace_bytes", T, E, k, C, L)
+        R = _lib.query("ats_moe_max_rows", T, E, k, C, L)  # this rank's permuted rows (upper bound)
+        RX = W * El * Cp  # received rows (upper bound)
         ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
         gates = torch.empty((T, k), dtype=torch.float32, device=dev)
         idx = torch.empty((T, k), dtype=torch.int64, device=dev)
         aux = torch.empty((), dtype=torch.float32, device=dev)
         util = torch.empty(E, dtype=torch.float32, device=dev)
         counts = torch.empty(E, dtype=torch.int32, device=dev)
-        _lib.call("ats_moe_route_plan", logits.data_ptr(), T, E, k, C, SLOTS, float(lbw), gates.data_ptr(),
+        _lib.call("ats_moe_route_plan", logits.data_ptr(), T, E, k, C, L, float(lbw), gates.data_ptr(),
                   idx.data_ptr(), aux.data_ptr(), util.data_ptr(), counts.data_ptr(), ws.data_ptr(), wsb, st)
         kept = torch.empty(E, dtype=torch.int32, device=dev)
-        _lib.call("ats_moe_plan_export", ws.data_ptr(), wsb, T, E, k, C, SLOTS, None, None, kept.data_ptr(), st)
+        seg_start = torch.empty(E + 1, dtype=torch.int32, device=dev)
+        _lib.call("ats_moe_plan_export", ws.data_ptr(), wsb, T, E, k, C, L, seg_start.data_ptr(), None,
+                  kept.data_ptr(), st)
         xs = torch.empty((R, H), dtype=x2.dtype, device=dev)
-        _lib.call("ats_moe_gather", x2.data_ptr(), xs.data_ptr(), dt, T, H, E, k, C, SLOTS, ws.data_ptr(), wsb, st)
+        _lib.call("ats_moe_gather", x2.data_ptr(), xs.data_ptr(), dt, T, H, E, k, C, L, ws.data_ptr(), wsb, st)
         recv_kept = exchange_counts(kept, group) if W > 1 else kept
-        xr = exchange_rows(xs, group) if W > 1 else xs
+        ex = _Exchange(mode, W, El, Cp, group, seg_start, recv_kept)
+        xr = ex.out(xs, RX)
         segb = _lib.query("ats_moe_ep_segments_bytes", W, El)
         seg = torch.empty(segb, dtype=torch.uint8, device=dev)
-        _lib.call("ats_moe_ep_segments", recv_kept.data_ptr(), W, El, C, seg.data_ptr(), segb, st)
-        h = torch.empty((R, 2 * Fdim), dtype=x2.dtype, device=dev)
-        a = torch.empty((R, Fdim), dtype=x2.dtype, device=dev)
-        yr = torch.empty((R, H), dtype=x2.dtype, device=dev)
+        _lib.call("ats_moe_ep_segments", recv_kept.data_ptr(), W, El, C, L, seg.data_ptr(), segb, st)
+        RR = xr.shape[0]
+        h = torch.empty((RR, 2 * Fdim), dtype=x2.dtype, device=dev)
+        a = torch.empty((RR, Fdim), dtype=x2.dtype, device=dev)
+        yr = torch.empty((RR, H), dtype=x2.dtype, device=dev)
         _lib.call("ats_moe_ep_experts_fwd", xr.data_ptr(), wgu_stack.data_ptr(), wd_stack.data_ptr(), h.data_ptr(),
                   a.data_ptr(), yr.data_ptr(), dt, W, El, C, H, Fdim, seg.data_ptr(), segb, st)
-        ys = exchange_rows(yr, group) if W > 1 else yr
+        ys = ex.back(yr, R)
         out = torch.empty((T, H), dtype=x2.dtype, device=dev)
-        _lib.call("ats_moe_combine", ys.data_ptr(), out.data_ptr(), dt, T, H, E, k, C, SLOTS, ws.data_ptr(), wsb, st)
+        _lib.call("ats_moe_combine", ys.data_ptr(), out.data_ptr(), dt, T, H, E, k, C, L, ws.data_ptr(), wsb, st)
         ctx.save_for_backward(logits, gates, idx, ws, xr, h, a, ys, seg, wgu_stack, wd_stack, x2, w32, rws)
-        ctx.meta = (E, El, k, C, lbw, Fdim, W, group, T, H, wsb, R, segb, gate_w.dtype)
+        ctx.meta = (E, El, k, C, lbw, Fdim, W, group, T, H, wsb, R, RX, segb, gate_w.dtype, L)
+        ctx.ex = ex
         ctx.mark_non_differentiable(util, counts, idx)
         return out, aux, util, counts, idx
 
     @staticmethod
     def backward(ctx, dout, daux, _dutil, _dcounts, _didx):
         logits, gates, idx, ws, xr, h, a, ys, seg, wgu_stack, wd_stack, x2, w32, rws = ctx.saved_tensors
-        E, El, k, C, lbw, Fdim, W, group, T, H, wsb, R, segb, gate_dtype = ctx.meta
+        E, El, k, C, lbw, Fdim, W, group, T, H, wsb, R, RX, segb, gate_dtype, L = ctx.meta
+        ex = ctx.ex
         dev = xr.device
         dt = _lib.dtype_code(xr.dtype)
         st = _lib.stream_of(xr)
@@ -121,21 +182,22 @@ class _EPMoEFn(torch.autograd.Function):
         dys = torch.empty((R, H), dtype=xr.dtype, device=dev)
         dgate_row = torch.empty(R, dtype=torch.float32, device=dev)
         _lib.call("ats_moe_combine_bwd", dout.data_ptr(), ys.data_ptr(), dys.data_ptr(), dgate_row.data_ptr(), dt,
-                  T, H, E, k, C, SLOTS, ws.data_ptr(), wsb, st)
-        dyr = exchange_rows(dys, group) if W > 1 else dys
-        dh = torch.empty((R, 2 * Fdim), dtype=xr.dtype, device=dev)
-        dxr = torch.empty((R, H), dtype=xr.dtype, device=dev)
+                  T, H, E, k, C, L, ws.data_ptr(), wsb, st)
+        dyr = ex.out(dys, RX)
+        RR = xr.shape[0]
+        dh = torch.empty((RR, 2 * Fdim), dtype=xr.dtype, device=dev)
+        dxr = torch.empty((RR, H), dtype=xr.dtype, device=dev)
         dwgu = torch.empty_like(wgu_stack)
         dwd = torch.empty_like(wd_stack)
         _lib.call("ats_moe_ep_experts_bwd", dyr.data_ptr(), xr.data_ptr(), h.data_ptr(), a.data_ptr(),
                   wgu_stack.data_ptr(), wd_stack.data_ptr(), dh.data_ptr(), dxr.data_ptr(), dwgu.data_ptr(),
                   dwd.data_ptr(), dt, W, El, C, H, Fdim, seg.data_ptr(), segb, st)
-        dxs = exchange_rows(dxr, group) if W > 1 else dxr
+        dxs = ex.back(dxr, R)
         dlogits = torch.empty((T, E), dtype=torch.float32, device=dev)
         daux_t = daux.to(torch.float32).contiguous() if daux is not None else None
         _lib.call("ats_moe_route_bwd", logits.data_ptr(), gates.data_ptr(), idx.data_ptr(), dgate_row.data_ptr(),
-                  _lib.ptr(daux_t), dlogits.data_ptr(), T, E, k, C, SLOTS, float(lbw), ws.data_ptr(), wsb, st)
-        dx, dgate_w = router_backward(dlogits, x2, w32, rws, dxs, ws, wsb, (T, E, k, C, SLOTS), True)
+                  _lib.ptr(daux_t), dlogits.data_ptr(), T, E, k, C, L, float(lbw), ws.data_ptr(), wsb, st)
+        dx, dgate_w = router_backward(dlogits, x2, w32, rws, dxs, ws, wsb, (T, E, k, C, L), True)
         grads = [dwgu[e] for e in range(El)] + [dwd[e] for e in range(El)]
         return (dx, dgate_w.to(gate_dtype), None, None, None, None, *grads)
 
@@ -149,8 +211,11 @@ class ExpertParallelMoE(nn.Module):
 
     def __init__(self, hidden_size: int, intermediate_size: int, num_experts: int, num_layers: int,
                  top_k: int = 2, capacity_factor: float = 1.25, load_balancing_weight: float = 0.01,
-                 group=None) -> None:
+                 group=None, exchange: str = "packed") -> None:
         super().__init__()
+        if exchange not in ("packed", "slots"):
+            raise ValueError(f"exchange must be 'packed' or 'slots', got {exchange!r}")
+        self.exchange = exchange
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if self.world > 1 else 0
@@ -191,7 +256,7 @@ class ExpertParallelMoE(nn.Module):
         if wgu[0].dtype != flat.dtype:
             raise TypeError(f"MoE: token dtype {flat.dtype} does not match expert weight dtype {wgu[0].dtype}")
         meta = (self.num_experts, self.num_local_experts, self.top_k, cap, self.load_balancing_weight,
-                wgu[0].shape[0] // 2, self.world, self.group)
+                wgu[0].shape[0] // 2, self.world, self.group, self.exchange)
         bias = logit_bias.detach().float().contiguous() if logit_bias is not None else None
         out, aux, util, counts, _ = _EPMoEFn.apply(flat, self.gate.weight, bias, meta, stacked(wgu), stacked(wd),
                                                    *wgu, *wd)

@@ -253,16 +253,20 @@ ATS_API int ats_moe_route_bwd(const float* logits, const float* gates, const int
  * Expert-parallel MoE (the DeepSpeed MoE path the reference delegates to,
  * ats/model/moe.py:193-214, with ep_size = world size): rank r owns the
  * E_local = E/W experts [r*E_local, (r+1)*E_local).  Each rank plans its own
- * tokens in the ATS_MOE_SLOTS layout (capacity from its own token count), the
- * host exchanges the [W][E_local][Cp] row buffers and the kept-row counts with
- * NCCL all-to-all, and the experts run on the received buffer
- * [W (source rank)][E_local][Cp] through the segment table built here: the
- * GEMMs compute only the kept rows of each (source, expert) segment (rounded
- * up to 128) and the weight gradients reduce over all W segments of an expert.
+ * tokens (capacity from its own token count), the host exchanges the row
+ * buffers and the kept-row counts with NCCL all-to-all, and the experts run
+ * on the received buffer through the segment table built here: the GEMMs
+ * compute only the kept rows of each (source, expert) segment (rounded up to
+ * 128) and the weight gradients reduce over all W segments of an expert.
  * recv_kept [W*E_local] (device, int32) are the kept rows received from each
- * source for each local expert. */
+ * source for each local expert.  layout says how the received rows lie:
+ *   ATS_MOE_SLOTS   [W][E_local][Cp] (equal-split exchange of the sources'
+ *                   slot layouts; no host synchronisation);
+ *   ATS_MOE_PACKED  the (source, expert) segments back to back, each kept count
+ *                   rounded up to 128 (variable-split exchange of the sources'
+ *                   packed layouts: only rows the GEMMs read cross the links). */
 ATS_API size_t ats_moe_ep_segments_bytes(int W, int E_local);
-ATS_API int ats_moe_ep_segments(const int32_t* recv_kept, int W, int E_local, int64_t capacity,
+ATS_API int ats_moe_ep_segments(const int32_t* recv_kept, int W, int E_local, int64_t capacity, int layout,
                         void* seg_workspace, size_t seg_workspace_bytes, void* stream);
 
 /* The grouped SwiGLU experts on the received buffer (rows W*E_local*Cp): as

@@ -4,7 +4,9 @@ The row and count exchanges of the expert-parallel MoE only move tensors;
 here they run on CPU tensors: every row of a send buffer carries its
 (source rank, global expert, slot) so the receiver can check where it landed,
 a stand-in expert doubles the rows, and the return exchange must bring each
-row back to its original slot.  A second test makes one rank leave before the
+row back to its original slot.  The packed exchange (variable splits of
+back-to-back expert segments) gets the same check, and also that only the
+kept rows and their padding to 128 travel.  A last test makes one rank leave before the
 collective: its peer must fail within the process group's timeout instead of
 waiting for ever."""
 
@@ -20,7 +22,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from ats_v2_b200.ep import exchange_counts, exchange_rows, slot_rows
+from ats_v2_b200.ep import _Exchange, exchange_counts, exchange_rows, slot_rows
 
 
 def _free_port() -> int:
@@ -70,6 +72,47 @@ def _exchange_worker(rank, world, port, E_local, cap, H, errq):
         raise
 
 
+def _packed_worker(rank, world, port, E_local, cap, H, errq):
+    """Packed exchange: each rank's experts are back-to-back segments of
+    align128(kept) rows; only those rows travel, with variable splits."""
+    try:
+        _init(rank, world, port)
+        E = world * E_local
+        g = torch.Generator().manual_seed(10 + rank)
+        kept = torch.randint(0, cap + 1, (E,), generator=g, dtype=torch.int32)
+        pad = [(int(c) + 127) // 128 * 128 for c in kept]
+        seg_start = torch.tensor([0] + list(torch.tensor(pad).cumsum(0)), dtype=torch.int32)
+        R = int(seg_start[-1])
+        send = torch.zeros(max(R, 1), H)
+        for e in range(E):
+            for s in range(int(kept[e])):
+                send[int(seg_start[e]) + s, :3] = torch.tensor([rank, e, s], dtype=torch.float32)
+                send[int(seg_start[e]) + s, 3:] = 1.0
+        recv_kept = exchange_counts(kept)
+        ex = _Exchange("packed", world, E_local, slot_rows(cap), None, seg_start, recv_kept)
+        RX = world * E_local * slot_rows(cap)
+        recv = ex.out(send, RX)
+        assert sum(ex.recv) <= RX
+        row = 0
+        for src in range(world):
+            for el in range(E_local):
+                e = rank * E_local + el
+                c = int(recv_kept[src * E_local + el])
+                for s in range(c):
+                    got = recv[row + s]
+                    assert (int(got[0]), int(got[1]), int(got[2])) == (src, e, s)
+                assert bool((recv[row + c:row + (c + 127) // 128 * 128] == 0).all())  # padding rows are zero
+                row += (c + 127) // 128 * 128
+        assert row == sum(ex.recv)
+        back = ex.back(recv * 2.0, send.shape[0])
+        assert torch.equal(back[:R], send[:R] * 2.0)
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        errq.put((rank, traceback.format_exc()))
+        raise
+
+
 def _leaver_worker(rank, world, port, errq):
     try:
         _init(rank, world, port, timeout_s=3)
@@ -91,6 +134,15 @@ def test_row_and_count_exchange_round_trip(E_local, cap, H):
     ctx = mp.get_context("spawn")
     errq = ctx.SimpleQueue()
     mp.start_processes(_exchange_worker, args=(2, _free_port(), E_local, cap, H, errq), nprocs=2, join=True,
+                       start_method="spawn")
+    assert errq.empty()
+
+
+@pytest.mark.parametrize("E_local,cap,H", [(2, 5, 8), (3, 300, 4)])
+def test_packed_exchange_sends_only_kept_segments_and_round_trips(E_local, cap, H):
+    ctx = mp.get_context("spawn")
+    errq = ctx.SimpleQueue()
+    mp.start_processes(_packed_worker, args=(2, _free_port(), E_local, cap, H, errq), nprocs=2, join=True,
                        start_method="spawn")
     assert errq.empty()
 

@@ -1,9 +1,9 @@
 """Expert-parallel MoE on the GPU.
 
-Single rank: the expert-parallel layer on the capacity-slot layout must equal
-the single-GPU layer on the packed layout for the same weights (the rows of a
-segment are the same and in the same order; only their place in the buffer
-differs).  Two ranks (runs when two GPUs are visible): every rank's output
+Single rank: the expert-parallel layer, with either exchange (packed rows or
+capacity slots), must equal the single-GPU layer for the same weights (the
+rows of a segment are the same and in the same order; only their place in the
+buffer differs).  Two ranks (runs when two GPUs are visible): every rank's output
 and input gradient equal the oracle run on that rank's own tokens with all
 experts' weights, and every local expert's weight gradient equals the sum
 over both ranks' tokens -- DeepSpeed's local-capacity semantics."""
@@ -35,10 +35,11 @@ def _init_weights(mod_gate, experts, seed):
             ex.down_proj.weight.copy_(0.02 * torch.randn(ex.down_proj.weight.shape, generator=g))
 
 
+@pytest.mark.parametrize("exchange", ["packed", "slots"])
 @pytest.mark.parametrize("T,H,F,E,k,cf", [(1024, 256, 384, 8, 2, 1.25), (700, 128, 128, 4, 2, 0.6)])
-def test_single_rank_slots_layout_equals_packed_layer(T, H, F, E, k, cf):
+def test_single_rank_expert_parallel_layer_equals_the_layer(T, H, F, E, k, cf, exchange):
     torch.manual_seed(0)
-    ep = ExpertParallelMoE(H, F, E, num_layers=2, top_k=k, capacity_factor=cf)
+    ep = ExpertParallelMoE(H, F, E, num_layers=2, top_k=k, capacity_factor=cf, exchange=exchange)
     ref = bmoe.MoELayer(H, F, E, num_layers=2, top_k=k, capacity_factor=cf)
     _init_weights(ep.gate, ep.experts, 1)
     _init_weights(ref.moe.gate, ref.moe.experts, 1)
@@ -69,7 +70,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _two_rank_worker(rank, world, port, errq):
+def _two_rank_worker(rank, world, port, errq, exchange):
     from oracle import moe as omoe
     try:
         os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -83,7 +84,7 @@ def _two_rank_worker(rank, world, port, errq):
         full_gate = torch.nn.Linear(H, E, bias=False)
         full_experts = torch.nn.ModuleList([bmoe.SwiGLU(H, F) for _ in range(E)])
         _init_weights(full_gate, full_experts, 5)  # identical on both ranks
-        ep = ExpertParallelMoE(H, F, E, num_layers=2, top_k=k, capacity_factor=cf)
+        ep = ExpertParallelMoE(H, F, E, num_layers=2, top_k=k, capacity_factor=cf, exchange=exchange)
         with torch.no_grad():
             ep.gate.weight.copy_(full_gate.weight)
             for i in range(El):
@@ -124,9 +125,11 @@ def _two_rank_worker(rank, world, port, errq):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_two_ranks_match_the_oracle_on_local_tokens():
+@pytest.mark.parametrize("exchange", ["packed", "slots"])
+def test_two_ranks_match_the_oracle_on_local_tokens(exchange):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     errq = ctx.SimpleQueue()
-    mp.start_processes(_two_rank_worker, args=(2, _free_port(), errq), nprocs=2, join=True, start_method="spawn")
+    mp.start_processes(_two_rank_worker, args=(2, _free_port(), errq, exchange), nprocs=2, join=True,
+                       start_method="spawn")
     assert errq.empty()
