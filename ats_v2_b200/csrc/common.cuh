@@ -79,11 +79,16 @@ __device__ __forceinline__ void load_chunk(const T* p, float (&v)[Chunk<T>::N]) 
 }
 
 template <typename T>
-__device__ __forceinline__ void store_chunk(T* p, const float (&v)[Chunk<T>::N]) {
-  uint4 raw;
+__device__ __forceinline__ void pack_chunk(const float (&v)[Chunk<T>::N], uint4& raw) {
   T* e = reinterpret_cast<T*>(&raw);
 #pragma unroll
   for (int i = 0; i < Chunk<T>::N; ++i) e[i] = Cvt<T>::from_f(v[i]);
+}
+
+template <typename T>
+__device__ __forceinline__ void store_chunk(T* p, const float (&v)[Chunk<T>::N]) {
+  uint4 raw;
+  pack_chunk<T>(v, raw);
   *reinterpret_cast<uint4*>(p) = raw;
 }
 

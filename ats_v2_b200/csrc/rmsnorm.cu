@@ -416,12 +416,34 @@ __device__ __forceinline__ void weight_chunk(const float* ws, int j, int gt, flo
   }
 }
 
-// The producer: rows blockIdx.x + i*gridDim.x, i < my_rows, into slot i % S.
+// Rows of this CTA: interleaved (blockIdx.x + i*gridDim.x) or, with
+// ATS_RING_CONTIG, one contiguous run per CTA.  Either way fixed per CTA, so
+// the backward's per-CTA dw partial sums are deterministic.
+#ifndef ATS_RING_CONTIG
+#define ATS_RING_CONTIG 1
+#endif
+__device__ __forceinline__ int64_t ring_row(int64_t i, int64_t rows) {
+#if ATS_RING_CONTIG
+  return rows * blockIdx.x / gridDim.x + i;
+#else
+  (void)rows;
+  return blockIdx.x + i * gridDim.x;
+#endif
+}
+__device__ __forceinline__ int64_t ring_my_rows(int64_t rows) {
+#if ATS_RING_CONTIG
+  return rows * (blockIdx.x + 1) / gridDim.x - rows * blockIdx.x / gridDim.x;
+#else
+  return (rows - blockIdx.x + gridDim.x - 1) / gridDim.x;
+#endif
+}
+
+// The producer: row ring_row(i) for i < my_rows, into slot i % S.
 // `nbytes` per tensor; `second` (may be null) goes to the slot's second half.
 template <int S>
 __device__ __forceinline__ void ring_produce(uint8_t* ring, uint32_t slot_bytes, uint32_t half_bytes,
                                              const uint8_t* first, const uint8_t* second, int64_t row_stride_bytes,
-                                             uint32_t nbytes, int64_t my_rows, uint64_t* full_bar,
+                                             uint32_t nbytes, int64_t my_rows, int64_t rows, uint64_t* full_bar,
                                              uint64_t* empty_bar, volatile int* abort_flag, int code) {
   int last_par[S];
 #pragma unroll
@@ -434,7 +456,7 @@ __device__ __forceinline__ void ring_produce(uint8_t* ring, uint32_t slot_bytes,
       ring_fail(abort_flag, code);
       break;
     }
-    const int64_t off = (blockIdx.x + i * gridDim.x) * row_stride_bytes;
+    const int64_t off = ring_row(i, rows) * row_stride_bytes;
     tc::mbar_arrive_expect_tx(&full_bar[slot], tx);
     tc::bulk_load(ring + slot * slot_bytes, first + off, nbytes, &full_bar[slot]);
     if (second) tc::bulk_load(ring + slot * slot_bytes + half_bytes, second + off, nbytes, &full_bar[slot]);
@@ -473,15 +495,16 @@ __global__ void __launch_bounds__(kRingThreads, 1) rmsnorm_fwd_ring_kernel(
   }
   stage_weight<TW, NPL, N>(ws, w, H, threadIdx.x, blockDim.x);
   __syncthreads();
-  const int64_t my_rows = (rows - blockIdx.x + gridDim.x - 1) / gridDim.x;
+  const int64_t my_rows = ring_my_rows(rows);
   if (warp == 0) {
     if (lane == 0)
       ring_produce<S>(ring, slot_bytes, 0, reinterpret_cast<const uint8_t*>(x), nullptr,
-                      xs * (int64_t)sizeof(TX), row_bytes, my_rows, full_bar, empty_bar, &abort_flag, 1);
+                      xs * (int64_t)sizeof(TX), row_bytes, my_rows, rows, full_bar, empty_bar, &abort_flag, 1);
     return;
   }
   const int ct = threadIdx.x - 32;
   const int grp = ct / kGroupThreads, gt = ct % kGroupThreads, gw = gt >> 5;
+  int held = -1;  // slot whose row is still being read by this group's bulk store
   for (int64_t i = grp; i < my_rows; i += kGroups) {
     const int slot = (int)(i % S);
     const bool ok = tc::mbar_wait(&full_bar[slot], (uint32_t)((i / S) & 1), &abort_flag, kRingBudget);
@@ -506,12 +529,11 @@ __global__ void __launch_bounds__(kRingThreads, 1) rmsnorm_fwd_ring_kernel(
       if (gt == 0) ring_fail(&abort_flag, 2);
       break;
     }
-    if (gt == 0) tc::mbar_arrive(&empty_bar[slot]);  // the group holds its chunks: free the slot
     float tot = 0.f;
 #pragma unroll
     for (int q = 0; q < kGroupWarps; ++q) tot += red[grp][rb][q];
     const float r = 1.0f / sqrtf(tot / (float)H + eps);
-    const int64_t row = blockIdx.x + i * gridDim.x;
+    const int64_t row = ring_row(i, rows);
     if (rstd != nullptr && gt == 0) rstd[row] = r;
     TX* yr = y + row * ys;
 #pragma unroll
@@ -523,10 +545,23 @@ __global__ void __launch_bounds__(kRingThreads, 1) rmsnorm_fwd_ring_kernel(
         weight_chunk<N>(ws, j, gt, wv);
 #pragma unroll
         for (int e = 0; e < N; ++e) o[e] = (v[e] * r) * wv[e];
-        store_chunk<TX>(yr + (int64_t)c * N, o);
+        // y goes back into the slot, over x (already in registers); one bulk store sends the row
+        uint4 packed;
+        pack_chunk<TX>(o, packed);
+        reinterpret_cast<uint4*>(ring + slot * slot_bytes)[c] = packed;
       }
     }
+    tc::fence_proxy_async_smem();  // this thread's writes, visible to the bulk copy
+    bar_and(true, 1 + grp, kGroupThreads);
+    if (gt == 0) {
+      tc::bulk_store(yr, ring + slot * slot_bytes, row_bytes);
+      tc::bulk_commit();
+      tc::bulk_wait_read<1>();  // the previous row's store has read its slot: release it
+      if (held >= 0) tc::mbar_arrive(&empty_bar[held]);
+    }
+    held = slot;
   }
+  if (gt == 0) tc::bulk_wait<0>();  // every store of this group complete before the CTA exits
 }
 
 template <typename TX, typename TW, int NPL>
@@ -558,12 +593,12 @@ __global__ void __launch_bounds__(kRingThreads, 1) rmsnorm_bwd_ring_kernel(
   }
   stage_weight<TW, NPL, N>(ws, w, H, threadIdx.x, blockDim.x);
   __syncthreads();
-  const int64_t my_rows = (rows - blockIdx.x + gridDim.x - 1) / gridDim.x;
+  const int64_t my_rows = ring_my_rows(rows);
   if (warp == 0) {
     if (lane == 0)
       ring_produce<S>(ring, slot_bytes, half_bytes, reinterpret_cast<const uint8_t*>(x),
-                      reinterpret_cast<const uint8_t*>(dy), (int64_t)H * sizeof(TX), row_bytes, my_rows, full_bar,
-                      empty_bar, &abort_flag, 3);
+                      reinterpret_cast<const uint8_t*>(dy), (int64_t)H * sizeof(TX), row_bytes, my_rows, rows,
+                      full_bar, empty_bar, &abort_flag, 3);
     return;
   }
   const int ct = threadIdx.x - 32;
@@ -616,7 +651,7 @@ __global__ void __launch_bounds__(kRingThreads, 1) rmsnorm_bwd_ring_kernel(
     }
     const float r = 1.0f / sqrtf(tss * invH + eps);
     const float k2 = r * r * r * tcc * invH;
-    TX* dxr = dx + (blockIdx.x + i * gridDim.x) * (int64_t)H;
+    TX* dxr = dx + ring_row(i, rows) * (int64_t)H;
 #pragma unroll
     for (int j = 0; j < NPL; ++j) {
       const int c = gt + kGroupThreads * j;
