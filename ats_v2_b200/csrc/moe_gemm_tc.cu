@@ -41,6 +41,7 @@ constexpr int BM = 128, BK = 64, STAGES = 4;
 constexpr int kEpiWarps = 8;  // two per TMEM lane quadrant, each owning half of the tile's columns
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr long long kWaitBudget = 4000000000LL;  // SM cycles, about 2 s
+constexpr int kStageBox = 32 * 32 * 2;           // EPI_STORE staging: 32 rows x 32 bf16 columns, 64-byte swizzle
 
 enum Epi { EPI_STORE = 0, EPI_SWIGLU_FWD = 1, EPI_SWIGLU_BWD = 2, EPI_F32 = 3, EPI_SCATTER = 4 };
 constexpr int kMaxParts = 6;
@@ -156,6 +157,7 @@ __device__ __forceinline__ void load32(const bf16* src, float (&v)[32]) {
 template <int BN, bool A_MN, bool B_MN, int EPI, bool KGROUP, int SPLIT, int BPARTS>
 __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                                                               const __grid_constant__ CUtensorMap tmB,
+                                                              const __grid_constant__ CUtensorMap tmO,
                                                               GemmArgs p) {
   constexpr uint32_t A_BYTES = BM * BK * 2;
   constexpr uint32_t B_BYTES = BN * BK * 2;
@@ -163,11 +165,14 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
   static_assert(SPLIT == 1 || BPARTS == 1, "operand parts along K or in the stage, not both");
   constexpr uint32_t IDESC = tc::idesc_bf16(BM, BN, A_MN, B_MN);
   extern __shared__ uint8_t smem_raw[];
-  // 1024-byte aligned ring (the 128-byte swizzle atom spans 1024 bytes)
+  // dynamic shared memory: the 1024-byte aligned ring (the 128-byte swizzle atom spans 1024 bytes),
+  // the epilogue's store staging (EPI_STORE: one 2 KB 32 x 32 bf16 box per epilogue warp), then the
+  // per-group tile prefix
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* staging = ring + STAGES * STAGE_BYTES;
+  int* tiles_before = reinterpret_cast<int*>(staging + (EPI == EPI_STORE ? kEpiWarps * kStageBox : 0));
   __shared__ __align__(8) uint64_t full_bar[STAGES], empty_bar[STAGES], tfull_bar[2], tempty_bar[2], done_bar;
   __shared__ uint32_t tmem_base_s;
-  __shared__ int tiles_before[kMaxExperts + 1];
   __shared__ volatile int abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -516,11 +521,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
             }
           }
         } else {
+          // plain bf16 store: each 32 x 32 chunk (this warp's 32 rows) goes through shared memory in
+          // the 64-byte swizzled layout and out with one TMA store, so global writes are whole lines
           const bool zero = ti.kb == 0;
           const int c0 = chalf * (BN / 2);
-          const int64_t row = KGROUP ? (int64_t)ti.mt * BM + row_in_tile
-                                     : (int64_t)p.seg.row0[ti.g] + ti.mt * BM + row_in_tile;
-          bf16* outp = p.out + (KGROUP ? (int64_t)ti.e * p.out_group : 0) + row * p.ldo + (int64_t)ti.nt * BN + c0;
+          // first of this warp's rows in the output map: [E][M] stacked weight rows, or the permuted rows
+          const int row_base = (KGROUP ? ti.e * p.M : p.seg.row0[ti.g]) + ti.mt * BM + quad * 32;
+          uint8_t* box = staging + (warp - 2) * kStageBox;
 #pragma unroll 1
           for (int c = 0; c < BN / 2; c += 32) {
             float v[32];
@@ -530,7 +537,22 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] = 0.f;
             }
-            store32(outp + c, v);
+            uint32_t pk[16];
+#pragma unroll
+            for (int q = 0; q < 16; ++q) pk[q] = pack_bf16(v[2 * q], v[2 * q + 1]);
+            if (lane == 0) tc::bulk_wait_read<0>();  // the previous chunk's store has read the box
+            __syncwarp();
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {  // row `lane`, 16-byte chunk q at its swizzled place
+              uint4* d = reinterpret_cast<uint4*>(box + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4));
+              *d = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+            }
+            tc::fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tc::tma_store_2d(&tmO, box, ti.nt * BN + c0 + c, row_base);
+              tc::bulk_commit();
+            }
           }
         }
       }
@@ -538,6 +560,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&tempty_bar[acc]);
     }
+    if (EPI == EPI_STORE && lane == 0) tc::bulk_wait<0>();  // every TMA store done before the CTA exits
   }
   tc::tc_fence_before();
   __syncthreads();
@@ -564,35 +587,49 @@ int encode_fn(PFN_cuTensorMapEncodeTiled_v12000* out) {
   return ATS_OK;
 }
 
-// 2-D bf16 tensor map, inner dim contiguous, 128-byte swizzle, box {64, box_outer}.
-int make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
-             uint32_t box_outer) {
+// 2-D bf16 tensor map, inner dim contiguous, box {box_inner, box_outer}.
+int encode_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+               uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz) {
   PFN_cuTensorMapEncodeTiled_v12000 enc;
   ATS_TRY(encode_fn(&enc));
-  if ((reinterpret_cast<uintptr_t>(base) & 15) || (row_bytes & 15) || inner < 64 || outer < box_outer)
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (row_bytes & 15) || inner < box_inner || outer < box_outer)
     return fail(ATS_EBADARG, "moe_gemm: operand not TMA-compatible (base %p, row %llu B, %llu x %llu)", base,
                 (unsigned long long)row_bytes, (unsigned long long)inner, (unsigned long long)outer);
   cuuint64_t dims[2] = {inner, outer};
   cuuint64_t strides[1] = {row_bytes};
-  cuuint32_t box[2] = {64, box_outer};
+  cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t es[2] = {1, 1};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(ATS_ECUDA, "moe_gemm: cuTensorMapEncodeTiled failed (%d)", (int)r);
   return ATS_OK;
 }
 
+// Operand map: 128-byte swizzle, box {64, box_outer}.
+int make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+             uint32_t box_outer) {
+  return encode_map(m, base, inner, outer, row_bytes, 64, box_outer, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+// Output map of the staged epilogue: 64-byte swizzle, box {32, 32} (one warp's chunk).
+int make_out_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes) {
+  return encode_map(m, base, inner, outer, row_bytes, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+}
+
 template <int BN, bool A_MN, bool B_MN, int EPI, bool KGROUP, int SPLIT = 1, int BPARTS = 1>
 int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& p, int64_t max_tiles,
-              cudaStream_t st) {
+              cudaStream_t st, const CUtensorMap* to = nullptr) {
   auto kfn = tc_gemm_kernel<BN, A_MN, B_MN, EPI, KGROUP, SPLIT, BPARTS>;
-  const int smem = STAGES * (BM * BK * 2 + BPARTS * BN * BK * 2) + 1024;
+  if (EPI == EPI_STORE && to == nullptr) return fail(ATS_EBADARG, "moe_gemm: store epilogue needs an output map");
+  const int groups = KGROUP ? p.seg.E : p.seg.nseg;
+  const int smem = 1024 + STAGES * (BM * BK * 2 + BPARTS * BN * BK * 2) +
+                   (EPI == EPI_STORE ? kEpiWarps * kStageBox : 0) + (groups + 1) * (int)sizeof(int);
   cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return fail(ATS_ECUDA, "moe_gemm: smem attribute: %s", cudaGetErrorString(e));
   int grid = num_sms();
   if (max_tiles < grid) grid = (int)(max_tiles > 0 ? max_tiles : 1);
-  kfn<<<grid, kThreads, smem, st>>>(ta, tb, p);
+  kfn<<<grid, kThreads, smem, st>>>(ta, tb, to != nullptr ? *to : ta, p);
   return check_launch("moe_tc_gemm");
 }
 
@@ -627,8 +664,10 @@ int tc_experts_fwd(const void* xp, const void* wgu, const void* wd, void* h, voi
   p.b = OpSpec{(int)H, 0};
   p.out = static_cast<bf16*>(y);
   p.ldo = H;
-  if (bn == 256) return launch_tc<256, false, false, EPI_STORE, false>(ma, mb, p, (R / BM) * (H / 256), st);
-  return launch_tc<128, false, false, EPI_STORE, false>(ma, mb, p, (R / BM) * (H / 128), st);
+  CUtensorMap mo;
+  ATS_TRY(make_out_map(&mo, y, H, R, H * 2));
+  if (bn == 256) return launch_tc<256, false, false, EPI_STORE, false>(ma, mb, p, (R / BM) * (H / 256), st, &mo);
+  return launch_tc<128, false, false, EPI_STORE, false>(ma, mb, p, (R / BM) * (H / 128), st, &mo);
 }
 
 int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a, const void* wgu, const void* wd,
@@ -665,10 +704,12 @@ int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a,
     p.b = OpSpec{(int)(2 * F), 0};
     p.out = static_cast<bf16*>(dxp);
     p.ldo = H;
+    CUtensorMap mo;
+    ATS_TRY(make_out_map(&mo, dxp, H, R, H * 2));
     if (bn == 256)
-      ATS_TRY((launch_tc<256, false, true, EPI_STORE, false>(ma, mb, p, (R / BM) * (H / 256), st)));
+      ATS_TRY((launch_tc<256, false, true, EPI_STORE, false>(ma, mb, p, (R / BM) * (H / 256), st, &mo)));
     else
-      ATS_TRY((launch_tc<128, false, true, EPI_STORE, false>(ma, mb, p, (R / BM) * (H / 128), st)));
+      ATS_TRY((launch_tc<128, false, true, EPI_STORE, false>(ma, mb, p, (R / BM) * (H / 128), st, &mo)));
   }
   // dWd_e[h][f] = sum over the expert's rows r of dy[r][h] a[r][f]   (A M-major, B N-major)
   {
@@ -682,11 +723,13 @@ int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a,
     p.out = static_cast<bf16*>(dwd);
     p.ldo = F;
     p.out_group = H * F;
+    CUtensorMap mo;
+    ATS_TRY(make_out_map(&mo, dwd, F, (uint64_t)sg.E * H, F * 2));
     const int64_t tiles = (int64_t)sg.E * (H / BM) * (F / bn);
     if (bn == 256)
-      ATS_TRY((launch_tc<256, true, true, EPI_STORE, true>(ma, mb, p, tiles, st)));
+      ATS_TRY((launch_tc<256, true, true, EPI_STORE, true>(ma, mb, p, tiles, st, &mo)));
     else
-      ATS_TRY((launch_tc<128, true, true, EPI_STORE, true>(ma, mb, p, tiles, st)));
+      ATS_TRY((launch_tc<128, true, true, EPI_STORE, true>(ma, mb, p, tiles, st, &mo)));
   }
   // dWgu_e[j][h] = sum over the expert's rows r of dh[r][j] xp[r][h]
   {
@@ -698,9 +741,11 @@ int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a,
     p.out = static_cast<bf16*>(dwgu);
     p.ldo = H;
     p.out_group = 2 * F * H;
+    CUtensorMap mo;
+    ATS_TRY(make_out_map(&mo, dwgu, H, (uint64_t)sg.E * 2 * F, H * 2));
     const int64_t tiles = (int64_t)sg.E * (2 * F / BM) * (H / bn);
-    if (bn == 256) return launch_tc<256, true, true, EPI_STORE, true>(ma, mb, p, tiles, st);
-    return launch_tc<128, true, true, EPI_STORE, true>(ma, mb, p, tiles, st);
+    if (bn == 256) return launch_tc<256, true, true, EPI_STORE, true>(ma, mb, p, tiles, st, &mo);
+    return launch_tc<128, true, true, EPI_STORE, true>(ma, mb, p, tiles, st, &mo);
   }
 }
 
