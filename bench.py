@@ -188,7 +188,11 @@ class RMSNormWorkload(Workload):
     def dominant(self):
         # rmsnorm_bwd_kernel (+ the tiny dw reduce): reads x, dy, writes dx
         return {"kernel": "rmsnorm_bwd_kernel<bf16,float>", "bytes": 3 * self.ROWS * self.H * 2 + 2 * self.H * 4,
-                "bound": "hbm"}
+                "bound": "hbm",
+                # DRAM read+write of one backward launch (ring kernel + dw reduce), ncu, cold caches
+                "traffic": (268.5 + 100.8 + 2.4) * 1e6,
+                "traffic_source": "profiles/rmsnorm_ring_16384x4096_bf16_fp32w.md (writes still in L2 at kernel "
+                                  "end are not counted)"}
 
     # e2e through the public module with pinned host buffers
     def e2e_setup(self):
@@ -289,7 +293,9 @@ class RopeWorkload(Workload):
 
     def dominant(self):
         return {"kernel": "rope_vec_kernel<bf16> (forward launch)", "bytes": self.bytes_per_step() // 2,
-                "bound": "hbm"}
+                "bound": "hbm", "traffic": (174.2 + 117.4) * 1e6,
+                "traffic_source": "profiles/rope_vec_q4x4096x32x128_k4x4096x8x128_bf16.md (ncu, cold caches; "
+                                  "writes still in L2 at kernel end are not counted)"}
 
     def e2e_setup(self):
         t = self.torch
@@ -403,7 +409,9 @@ class MoEWorkload(Workload):
 
     def dominant(self):
         return {"kernel": "expert grouped GEMMs (whole layer fwd+bwd timed)", "flops": self.flops_per_step(),
-                "bound": "tensor"}
+                "bound": "tensor", "traffic": (3718.7 + 1487.8) * 1e6,
+                "traffic_source": "profiles/moe_gemms_8192tok_h2048_e8_top2_f5632_bf16.md: DRAM read+write of "
+                                  "the six expert GEMM launches of one step (ncu, cold caches)"}
 
     def e2e_setup(self):
         t = self.torch
@@ -669,15 +677,17 @@ def measure(torch, dist, wl: Workload, steps: int, warmup: int, world: int, with
             peak = wl.peaks["hbm_gbs"]
             res["roofline"] = {"bound": "hbm", "kernel": dom["kernel"], "achieved": ach, "peak": peak,
                                "unit": "GB/s", "frac": ach / peak, "peak_source": wl.peaks_kind,
-                               "traffic": None, "algorithmic_bytes": dom["bytes"], "kernel_ms": kms}
+                               "traffic": dom.get("traffic"), "algorithmic_bytes": dom["bytes"], "kernel_ms": kms}
         else:
             ach = dom["flops"] / (kms * 1e-3) / 1e12
             peak = wl.peaks.get("bf16_tflops_sustained", wl.peaks["bf16_tflops"])
             res["roofline"] = {"bound": "tensor", "kernel": dom["kernel"], "achieved": ach, "peak": peak,
                                "unit": "TFLOP/s", "frac": ach / peak, "peak_source": wl.peaks_kind + " sustained",
-                               "traffic": None, "algorithmic_flops": dom["flops"], "kernel_ms": kms}
+                               "traffic": dom.get("traffic"), "algorithmic_flops": dom["flops"], "kernel_ms": kms}
             if "kept_rows" in dom:
                 res["roofline"]["kept_rows"] = dom["kept_rows"]
+        if "traffic_source" in dom:
+            res["roofline"]["traffic_source"] = dom["traffic_source"]
     # end to end through the public module with host buffers
     wl.e2e_setup()
     e2e_steps = max(3, min(steps, 10))
