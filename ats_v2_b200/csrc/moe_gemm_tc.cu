@@ -41,7 +41,8 @@ constexpr int BM = 128, BK = 64, STAGES = 4;
 constexpr int kEpiWarps = 8;  // two per TMEM lane quadrant, each owning half of the tile's columns
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr long long kWaitBudget = 4000000000LL;  // SM cycles, about 2 s
-constexpr int kStageBox = 32 * 32 * 2;           // EPI_STORE staging: 32 rows x 32 bf16 columns, 64-byte swizzle
+constexpr int kStageBox = 32 * 32 * 2;           // staging box: 32 rows x 32 bf16 columns, 64-byte swizzle
+constexpr int kBoxesPerWarp = 2;
 
 enum Epi { EPI_STORE = 0, EPI_SWIGLU_FWD = 1, EPI_SWIGLU_BWD = 2, EPI_F32 = 3, EPI_SCATTER = 4 };
 constexpr int kMaxParts = 6;
@@ -92,30 +93,74 @@ __device__ __forceinline__ int n_groups(const GemmArgs& p) {
   return KGROUP ? p.seg.E : p.seg.nseg;
 }
 
-template <int BN, bool KGROUP, int EPI, int SPLIT>
-__device__ __forceinline__ bool decode_tile(const GemmArgs& p, const int* tiles_before, int t, TileInfo& ti) {
-  const int NT = n_tiles<BN, KGROUP, EPI>(p);
-  const int G = n_groups<KGROUP>(p);
-  for (int g = 0; g < G; ++g) {
-    if (t < tiles_before[g + 1]) {
-      const int q = t - tiles_before[g];
-      ti.g = g;
-      ti.mt = q / NT;
-      ti.nt = q - ti.mt * NT;
-      if (KGROUP) {
-        ti.e = g;
-        int kb = 0;
-        for (int u = 0; u < p.seg.spe; ++u) kb += p.seg.rows[p.seg.eseg[g * p.seg.spe + u]] / BK;
-        ti.kb = kb * SPLIT;
-      } else {
-        ti.e = p.seg.expert[g];
-        ti.kb = (p.K / BK) * SPLIT;
-      }
-      return true;
-    }
-  }
-  return false;
+// Tiles of group g: its M tiles times the N tiles.
+template <int BN, bool KGROUP, int EPI>
+__device__ __forceinline__ int group_tiles(const GemmArgs& p, int g) {
+  return (KGROUP ? p.M / BM : p.seg.rows[g] / BM) * n_tiles<BN, KGROUP, EPI>(p);
 }
+
+// Walks the groups in order: a role visits its tiles t = blockIdx.x + i*gridDim.x in increasing order,
+// so a cursor (group, first tile of the group) that only moves forward decodes every tile.
+struct TileCursor {
+  int g = 0, first = 0;
+};
+
+template <int BN, bool KGROUP, int EPI, int SPLIT>
+__device__ __forceinline__ void decode_tile(const GemmArgs& p, TileCursor& cur, int t, TileInfo& ti) {
+  const int NT = n_tiles<BN, KGROUP, EPI>(p);
+  int n = group_tiles<BN, KGROUP, EPI>(p, cur.g);
+  while (t >= cur.first + n) {  // t < total, so a later group holds it
+    cur.first += n;
+    ++cur.g;
+    n = group_tiles<BN, KGROUP, EPI>(p, cur.g);
+  }
+  const int g = cur.g;
+  const int q = t - cur.first;
+  ti.g = g;
+  ti.mt = q / NT;
+  ti.nt = q - ti.mt * NT;
+  if (KGROUP) {
+    ti.e = g;
+    int kb = 0;
+    for (int u = 0; u < p.seg.spe; ++u) kb += p.seg.rows[p.seg.eseg[g * p.seg.spe + u]] / BK;
+    ti.kb = kb * SPLIT;
+  } else {
+    ti.e = p.seg.expert[g];
+    ti.kb = (p.K / BK) * SPLIT;
+  }
+}
+
+// Shared memory of the epilogue's staging boxes: the bf16-output epilogues write through them.
+__host__ __device__ constexpr int staging_bytes(int epi) {
+  return (epi == EPI_STORE || epi == EPI_SWIGLU_FWD || epi == EPI_SWIGLU_BWD) ? kEpiWarps * kBoxesPerWarp * kStageBox
+                                                                             : 0;
+}
+
+// One epilogue warp's bf16 output path: a 32 x 32 chunk (row = lane, 32 packed bf16 pairs per lane
+// in pk[16]) goes into the next of the warp's staging boxes in the 64-byte swizzled layout, then out
+// with one TMA store, so global writes are whole lines and asynchronous.  A box is reused once the
+// store that last read it is done reading.
+struct BoxWriter {
+  uint8_t* base;  // this warp's kBoxesPerWarp boxes
+  int n;          // stores issued
+  __device__ __forceinline__ void put(const uint32_t (&pk)[16], const CUtensorMap* map, int x, int y, int lane) {
+    uint8_t* box = base + (n % kBoxesPerWarp) * kStageBox;
+    if (lane == 0) tc::bulk_wait_read<kBoxesPerWarp - 1>();
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {  // row `lane`, 16-byte chunk q at its swizzled place (conflict-free)
+      uint4* d = reinterpret_cast<uint4*>(box + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4));
+      *d = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+    }
+    tc::fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tc::tma_store_2d(map, box, x, y);
+      tc::bulk_commit();
+    }
+    ++n;
+  }
+};
 
 __device__ __forceinline__ void fail_abort(int* err, volatile int* abort, int code) {
   if (*abort == 0) {
@@ -127,6 +172,11 @@ __device__ __forceinline__ void fail_abort(int* err, volatile int* abort, int co
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ void pack32(const float (&v)[32], uint32_t (&pk)[16]) {
+#pragma unroll
+  for (int q = 0; q < 16; ++q) pk[q] = pack_bf16(v[2 * q], v[2 * q + 1]);
 }
 
 // Store 32 floats as bf16 (64 contiguous bytes, 16-byte aligned).
@@ -158,6 +208,7 @@ template <int BN, bool A_MN, bool B_MN, int EPI, bool KGROUP, int SPLIT, int BPA
 __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                                                               const __grid_constant__ CUtensorMap tmB,
                                                               const __grid_constant__ CUtensorMap tmO,
+                                                              const __grid_constant__ CUtensorMap tmO2,
                                                               GemmArgs p) {
   constexpr uint32_t A_BYTES = BM * BK * 2;
   constexpr uint32_t B_BYTES = BN * BK * 2;
@@ -170,9 +221,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
   // per-group tile prefix
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* staging = ring + STAGES * STAGE_BYTES;
-  int* tiles_before = reinterpret_cast<int*>(staging + (EPI == EPI_STORE ? kEpiWarps * kStageBox : 0));
   __shared__ __align__(8) uint64_t full_bar[STAGES], empty_bar[STAGES], tfull_bar[2], tempty_bar[2], done_bar;
   __shared__ uint32_t tmem_base_s;
+  __shared__ int total_s;
   __shared__ volatile int abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -189,16 +240,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
     tc::fence_barrier_init();
     tc::fence_proxy_async_smem();
     abort_flag = 0;
-    // tiles per group, prefix-summed
-    const int NT = n_tiles<BN, KGROUP, EPI>(p);
-    const int G = n_groups<KGROUP>(p);
-    int acc = 0;
-    tiles_before[0] = 0;
-    for (int g = 0; g < G; ++g) {
-      const int mt = KGROUP ? p.M / BM : p.seg.rows[g] / BM;
-      acc += mt * NT;
-      tiles_before[g + 1] = acc;
-    }
+    int total = 0;
+    for (int g = 0; g < n_groups<KGROUP>(p); ++g) total += group_tiles<BN, KGROUP, EPI>(p, g);
+    total_s = total;
   }
   if (warp == 1) {
     tc::tmem_alloc(&tmem_base_s, 2 * BN);
@@ -208,7 +252,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem_base = tmem_base_s;
-  const int total = tiles_before[n_groups<KGROUP>(p)];
+  const int total = total_s;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -220,9 +264,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
       int last_parity[STAGES];
 #pragma unroll
       for (int s = 0; s < STAGES; ++s) last_parity[s] = -1;
+      TileCursor cur;
       for (int t = blockIdx.x; t < total && !abort_flag; t += gridDim.x) {
         TileInfo ti;
-        decode_tile<BN, KGROUP, EPI, SPLIT>(p, tiles_before, t, ti);
+        decode_tile<BN, KGROUP, EPI, SPLIT>(p, cur, t, ti);
         const int m0 = ti.mt * BM;
         const int n0 = EPI == EPI_SWIGLU_FWD ? ti.nt * (BN / 2) : ti.nt * BN;
         // K blocks: M-grouped = kb of the fixed K; K-grouped = the expert's segments' rows, in order.
@@ -304,9 +349,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
       bool issued = false;
       const uint32_t a_lbo = A_MN ? 8192u : 16u, b_lbo = B_MN ? 8192u : 16u;
       const uint32_t a_step = A_MN ? 2048u : 32u, b_step = B_MN ? 2048u : 32u;
+      TileCursor cur;
       for (int t = blockIdx.x; t < total && !abort_flag; t += gridDim.x, ++i) {
         TileInfo ti;
-        decode_tile<BN, KGROUP, EPI, SPLIT>(p, tiles_before, t, ti);
+        decode_tile<BN, KGROUP, EPI, SPLIT>(p, cur, t, ti);
         const int acc = i & 1;
         const uint32_t acc_phase = (uint32_t)(i >> 1) & 1u;
         if (!tc::mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, &abort_flag, kWaitBudget)) {
@@ -358,10 +404,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
     const int quad = warp & 3;         // TMEM lanes [32*quad, 32*quad + 32)
     const int chalf = (warp - 2) >> 2;  // which half of the tile's columns
     const int row_in_tile = quad * 32 + lane;
+    BoxWriter bw{staging + (warp - 2) * kBoxesPerWarp * kStageBox, 0};
     int i = 0;
+    TileCursor cur;
     for (int t = blockIdx.x; t < total && !abort_flag; t += gridDim.x, ++i) {
       TileInfo ti;
-      decode_tile<BN, KGROUP, EPI, SPLIT>(p, tiles_before, t, ti);
+      decode_tile<BN, KGROUP, EPI, SPLIT>(p, cur, t, ti);
       const int acc = i & 1;
       const uint32_t acc_phase = (uint32_t)(i >> 1) & 1u;
       if constexpr (EPI == EPI_SWIGLU_BWD) {
@@ -383,7 +431,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
         }
         tc::tc_fence_after();
         const uint32_t t_row = tmem_base + (uint32_t)(acc * BN + c0) + ((uint32_t)(quad * 32) << 16);
-        bf16* dg_out = p.out + row * F2 + ti.nt * BN + c0;
+        const int row_base = p.seg.row0[ti.g] + ti.mt * BM + quad * 32;
+        const int x0 = ti.nt * BN + c0;
 #pragma unroll 1
         for (int c = 0; c < BN / 2; c += 32) {
           float dv[32], gv[32], uv[32];
@@ -412,8 +461,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
             gv[j] = dg;
             uv[j] = du;
           }
-          store32(dg_out + c, gv);
-          store32(dg_out + p.F + c, uv);
+          uint32_t pk[16];
+          pack32(gv, pk);
+          bw.put(pk, &tmO, x0 + c, row_base, lane);        // dg into dh[:, :F]
+          pack32(uv, pk);
+          bw.put(pk, &tmO, p.F + x0 + c, row_base, lane);  // du into dh[:, F:]
         }
       } else {
         if (!tc::mbar_wait(&tfull_bar[acc], acc_phase, &abort_flag, kWaitBudget)) {
@@ -423,9 +475,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
         tc::tc_fence_after();
         const uint32_t t_row = tmem_base + (uint32_t)(acc * BN) + ((uint32_t)(quad * 32) << 16);
         if constexpr (EPI == EPI_SWIGLU_FWD) {
-          const int64_t row = (int64_t)p.seg.row0[ti.g] + ti.mt * BM + row_in_tile;
           const int c0 = chalf * (BN / 4);
           const int n0 = ti.nt * (BN / 2) + c0;
+          const int row_base = p.seg.row0[ti.g] + ti.mt * BM + quad * 32;
 #pragma unroll 1
           for (int c = 0; c < BN / 4; c += 32) {
             float gv[32], uv[32], av[32];
@@ -437,9 +489,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
               uv[j] = round_to<bf16>(uv[j]);
               av[j] = silu_mul_fast_bf16(gv[j], uv[j]);
             }
-            store32(p.h_out + row * (2 * (int64_t)p.F) + n0 + c, gv);
-            store32(p.h_out + row * (2 * (int64_t)p.F) + p.F + n0 + c, uv);
-            store32(p.a_out + row * (int64_t)p.F + n0 + c, av);
+            uint32_t pk[16];
+            pack32(gv, pk);
+            bw.put(pk, &tmO, n0 + c, row_base, lane);        // gate half of h
+            pack32(uv, pk);
+            bw.put(pk, &tmO, p.F + n0 + c, row_base, lane);  // up half of h
+            pack32(av, pk);
+            bw.put(pk, &tmO2, n0 + c, row_base, lane);       // a
           }
         } else if constexpr (EPI == EPI_F32) {
           // float32 tile, rows below m_valid and columns below n_valid, plus a per-column bias
@@ -527,7 +583,6 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
           const int c0 = chalf * (BN / 2);
           // first of this warp's rows in the output map: [E][M] stacked weight rows, or the permuted rows
           const int row_base = (KGROUP ? ti.e * p.M : p.seg.row0[ti.g]) + ti.mt * BM + quad * 32;
-          uint8_t* box = staging + (warp - 2) * kStageBox;
 #pragma unroll 1
           for (int c = 0; c < BN / 2; c += 32) {
             float v[32];
@@ -538,21 +593,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
               for (int j = 0; j < 32; ++j) v[j] = 0.f;
             }
             uint32_t pk[16];
-#pragma unroll
-            for (int q = 0; q < 16; ++q) pk[q] = pack_bf16(v[2 * q], v[2 * q + 1]);
-            if (lane == 0) tc::bulk_wait_read<0>();  // the previous chunk's store has read the box
-            __syncwarp();
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {  // row `lane`, 16-byte chunk q at its swizzled place
-              uint4* d = reinterpret_cast<uint4*>(box + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4));
-              *d = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-            }
-            tc::fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-              tc::tma_store_2d(&tmO, box, ti.nt * BN + c0 + c, row_base);
-              tc::bulk_commit();
-            }
+            pack32(v, pk);
+            bw.put(pk, &tmO, ti.nt * BN + c0 + c, row_base, lane);
           }
         }
       }
@@ -560,7 +602,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&tempty_bar[acc]);
     }
-    if (EPI == EPI_STORE && lane == 0) tc::bulk_wait<0>();  // every TMA store done before the CTA exits
+    if (staging_bytes(EPI) > 0 && lane == 0) tc::bulk_wait<0>();  // every TMA store done before the CTA exits
   }
   tc::tc_fence_before();
   __syncthreads();
@@ -619,17 +661,16 @@ int make_out_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t oute
 
 template <int BN, bool A_MN, bool B_MN, int EPI, bool KGROUP, int SPLIT = 1, int BPARTS = 1>
 int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& p, int64_t max_tiles,
-              cudaStream_t st, const CUtensorMap* to = nullptr) {
+              cudaStream_t st, const CUtensorMap* to = nullptr, const CUtensorMap* to2 = nullptr) {
   auto kfn = tc_gemm_kernel<BN, A_MN, B_MN, EPI, KGROUP, SPLIT, BPARTS>;
-  if (EPI == EPI_STORE && to == nullptr) return fail(ATS_EBADARG, "moe_gemm: store epilogue needs an output map");
-  const int groups = KGROUP ? p.seg.E : p.seg.nseg;
-  const int smem = 1024 + STAGES * (BM * BK * 2 + BPARTS * BN * BK * 2) +
-                   (EPI == EPI_STORE ? kEpiWarps * kStageBox : 0) + (groups + 1) * (int)sizeof(int);
+  if (staging_bytes(EPI) > 0 && to == nullptr) return fail(ATS_EBADARG, "moe_gemm: bf16 epilogue needs an output map");
+  if (EPI == EPI_SWIGLU_FWD && to2 == nullptr) return fail(ATS_EBADARG, "moe_gemm: SwiGLU epilogue needs the a map");
+  const int smem = 1024 + STAGES * (BM * BK * 2 + BPARTS * BN * BK * 2) + staging_bytes(EPI);
   cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return fail(ATS_ECUDA, "moe_gemm: smem attribute: %s", cudaGetErrorString(e));
   int grid = num_sms();
   if (max_tiles < grid) grid = (int)(max_tiles > 0 ? max_tiles : 1);
-  kfn<<<grid, kThreads, smem, st>>>(ta, tb, to != nullptr ? *to : ta, p);
+  kfn<<<grid, kThreads, smem, st>>>(ta, tb, to != nullptr ? *to : ta, to2 != nullptr ? *to2 : ta, p);
   return check_launch("moe_tc_gemm");
 }
 
@@ -654,7 +695,10 @@ int tc_experts_fwd(const void* xp, const void* wgu, const void* wd, void* h, voi
   p.b = OpSpec{(int)(2 * F), (int)F};
   p.h_out = static_cast<bf16*>(h);
   p.a_out = static_cast<bf16*>(a);
-  ATS_TRY((launch_tc<256, false, false, EPI_SWIGLU_FWD, false>(ma, mb, p, (R / BM) * (F / 128), st)));
+  CUtensorMap mh, mact;
+  ATS_TRY(make_out_map(&mh, h, 2 * F, R, 2 * F * 2));
+  ATS_TRY(make_out_map(&mact, a, F, R, F * 2));
+  ATS_TRY((launch_tc<256, false, false, EPI_SWIGLU_FWD, false>(ma, mb, p, (R / BM) * (F / 128), st, &mh, &mact)));
   // y = a Wd_e^T
   const int bn = pick_bn(H);
   ATS_TRY(make_map(&ma, a, F, R, F * 2, 128));
@@ -689,10 +733,12 @@ int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a,
     p.b = OpSpec{(int)H, 0};
     p.h = static_cast<const bf16*>(h);
     p.out = static_cast<bf16*>(dh);
+    CUtensorMap mdh;
+    ATS_TRY(make_out_map(&mdh, dh, 2 * F, R, 2 * F * 2));
     if (bn == 256)
-      ATS_TRY((launch_tc<256, false, true, EPI_SWIGLU_BWD, false>(ma, mb, p, (R / BM) * (F / 256), st)));
+      ATS_TRY((launch_tc<256, false, true, EPI_SWIGLU_BWD, false>(ma, mb, p, (R / BM) * (F / 256), st, &mdh)));
     else
-      ATS_TRY((launch_tc<128, false, true, EPI_SWIGLU_BWD, false>(ma, mb, p, (R / BM) * (F / 128), st)));
+      ATS_TRY((launch_tc<128, false, true, EPI_SWIGLU_BWD, false>(ma, mb, p, (R / BM) * (F / 128), st, &mdh)));
   }
   // dxp = dh Wgu_e (B N-major: Wgu_e[j][h])
   {
