@@ -85,6 +85,14 @@ SIGNATURES: dict[str, tuple] = {
                                        c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int64, c_int64,
                                        c_int64, c_void_p, c_size_t, c_void_p]),
     "ats_moe_ep_status": (c_int, [c_void_p, c_size_t, c_int, c_int, POINTER(c_int)]),
+    "ats_swiglu_supported": (c_int, [c_int, c_int64, c_int64, c_int64]),
+    "ats_swiglu_workspace_bytes": (c_size_t, []),
+    "ats_swiglu_rows": (c_int64, [c_int64]),
+    "ats_swiglu_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int64, c_int64,
+                               c_int64, c_void_p, c_size_t, c_void_p]),
+    "ats_swiglu_bwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                               c_void_p, c_void_p, c_int, c_int64, c_int64, c_int64, c_void_p, c_size_t, c_void_p]),
+    "ats_swiglu_status": (c_int, [c_void_p, c_size_t, POINTER(c_int)]),
     "ats_moe_router_supported": (c_int, [c_int, c_int64, c_int64, c_int]),
     "ats_moe_router_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int]),
     "ats_moe_router_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int, c_void_p,

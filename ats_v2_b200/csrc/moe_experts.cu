@@ -292,6 +292,39 @@ __global__ void ep_segments_kernel(const int* __restrict__ recv_kept, int W, int
   if (s == 0) q.err[0] = 0;
 }
 
+// ---- dense SwiGLU FFN: one expert over the T token rows, table [row0, rows, expert, eseg, status]
+constexpr size_t kDenseWsBytes = 256;
+
+int64_t dense_rows(int64_t T) { return (T + kSegAlign - 1) / kSegAlign * kSegAlign; }
+
+bool dense_supported(ats_dtype dt, int64_t T, int64_t H, int64_t F) {
+  return dt == ATS_BF16 && tc_shape_supported(H, F) && T >= kSegAlign && dense_rows(T) < ((int64_t)1 << 31);
+}
+
+__global__ void dense_table_kernel(int* tab, int rows) {
+  tab[0] = 0;
+  tab[1] = rows;
+  tab[2] = 0;
+  tab[3] = 0;
+  tab[4] = 0;
+}
+
+int dense_table(void* ws, size_t bytes, int64_t T, SegTable* sg) {
+  if (ws == nullptr || bytes < kDenseWsBytes) return fail(ATS_EBADARG, "swiglu: workspace too small");
+  int* tab = static_cast<int*>(ws);
+  sg->row0 = tab;
+  sg->rows = tab + 1;
+  sg->expert = tab + 2;
+  sg->eseg = tab + 3;
+  sg->nseg = 1;
+  sg->spe = 1;
+  sg->E = 1;
+  sg->max_rows = dense_rows(T);
+  sg->max_seg_rows = sg->max_rows;
+  sg->err = tab + 4;
+  return ATS_OK;
+}
+
 int check_experts(const void* p0, const void* p1, int64_t H, int64_t F, ats_dtype dt) {
   if (H <= 0 || F <= 0 || p0 == nullptr || p1 == nullptr) return fail(ATS_EBADARG, "moe_experts: bad arguments");
   if (dt != ATS_BF16 && dt != ATS_F32) return fail(ATS_EBADARG, "moe_experts: dtype");
@@ -308,6 +341,56 @@ extern "C" {
 
 int ats_moe_uses_tensor_cores(ats_dtype dtype, int64_t H, int64_t F) {
   return dtype == ATS_BF16 && tc_shape_supported(H, F) ? 1 : 0;
+}
+
+int ats_swiglu_supported(ats_dtype dtype, int64_t T, int64_t H, int64_t F) {
+  return dense_supported(dtype, T, H, F) ? 1 : 0;
+}
+
+size_t ats_swiglu_workspace_bytes(void) { return kDenseWsBytes; }
+
+int64_t ats_swiglu_rows(int64_t T) { return T > 0 ? dense_rows(T) : 0; }
+
+int ats_swiglu_fwd(const void* x, const void* w_gate_up, const void* w_down, void* h, void* a, void* y,
+                   ats_dtype dtype, int64_t T, int64_t H, int64_t F, void* workspace, size_t workspace_bytes,
+                   void* stream) {
+  if (!dense_supported(dtype, T, H, F))
+    return fail(ATS_EUNSUPPORTED, "swiglu_fwd: needs bf16, T >= 128 and hidden, ffn multiples of 128 "
+                "(T=%lld hidden=%lld ffn=%lld)", (long long)T, (long long)H, (long long)F);
+  ATS_TRY(check_experts(w_gate_up, w_down, H, F, dtype));
+  if (x == nullptr || h == nullptr || a == nullptr || y == nullptr) return fail(ATS_EBADARG, "swiglu_fwd: null");
+  SegTable sg;
+  ATS_TRY(dense_table(workspace, workspace_bytes, T, &sg));
+  cudaStream_t st = (cudaStream_t)stream;
+  dense_table_kernel<<<1, 1, 0, st>>>(static_cast<int*>(workspace), (int)dense_rows(T));
+  ATS_TRY(check_launch("swiglu_table"));
+  return tc_experts_fwd(x, w_gate_up, w_down, h, a, y, 1, H, F, sg, st, T);
+}
+
+int ats_swiglu_bwd(const void* dy, const void* x, const void* h, const void* a, const void* w_gate_up,
+                   const void* w_down, void* dh, void* dx, void* dw_gate_up, void* dw_down, ats_dtype dtype,
+                   int64_t T, int64_t H, int64_t F, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!dense_supported(dtype, T, H, F))
+    return fail(ATS_EUNSUPPORTED, "swiglu_bwd: unsupported shape (T=%lld hidden=%lld ffn=%lld)", (long long)T,
+                (long long)H, (long long)F);
+  ATS_TRY(check_experts(w_gate_up, w_down, H, F, dtype));
+  if (dy == nullptr || x == nullptr || h == nullptr || a == nullptr || dh == nullptr || dx == nullptr ||
+      dw_gate_up == nullptr || dw_down == nullptr)
+    return fail(ATS_EBADARG, "swiglu_bwd: null");
+  SegTable sg;
+  ATS_TRY(dense_table(workspace, workspace_bytes, T, &sg));
+  cudaStream_t st = (cudaStream_t)stream;
+  dense_table_kernel<<<1, 1, 0, st>>>(static_cast<int*>(workspace), (int)dense_rows(T));
+  ATS_TRY(check_launch("swiglu_table"));
+  return tc_experts_bwd(dy, x, h, a, w_gate_up, w_down, dh, dx, dw_gate_up, dw_down, 1, H, F, sg, st, T);
+}
+
+int ats_swiglu_status(const void* workspace, size_t workspace_bytes, int* status) {
+  if (workspace == nullptr || workspace_bytes < kDenseWsBytes || status == nullptr)
+    return fail(ATS_EBADARG, "swiglu_status: bad arguments");
+  cudaError_t e = cudaMemcpy(status, static_cast<const int*>(workspace) + 4, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return fail(ATS_ECUDA, "swiglu_status: %s", cudaGetErrorString(e));
+  return *status == 0 ? ATS_OK : fail(ATS_ETIMEOUT, "swiglu: a bounded device wait gave up (code %d)", *status);
 }
 
 int ats_moe_experts_fwd(const void* xp, const void* w_gate_up, const void* w_down, void* h, void* a, void* y,

@@ -50,11 +50,13 @@ inline bool tc_shape_supported(int64_t H, int64_t F) {
 
 // tcgen05 tensor-core expert GEMMs (bf16).  Return ATS_EUNSUPPORTED for shapes
 // the tensor-core tiling does not cover; the caller then uses the CUDA-core path.
+// io_rows > 0: the token-side tensors (xp, y, dy, dxp) have only io_rows rows (TMA reads past them
+// are zero and stores are clipped); h, a and dh always have sg.max_rows rows.
 int tc_experts_fwd(const void* xp, const void* wgu, const void* wd, void* h, void* a, void* y, int E, int64_t H,
-                   int64_t F, const SegTable& sg, cudaStream_t st);
+                   int64_t F, const SegTable& sg, cudaStream_t st, int64_t io_rows = 0);
 int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a, const void* wgu, const void* wd,
                    void* dh, void* dxp, void* dwgu, void* dwd, int E, int64_t H, int64_t F, const SegTable& sg,
-                   cudaStream_t st);
+                   cudaStream_t st, int64_t io_rows = 0);
 
 // Router GEMMs on the tensor cores (bf16 tokens, float32 router weight as three bf16 parts).
 // The expert count is padded to kRouterEp (one 64-wide tile holds every expert).

@@ -132,8 +132,9 @@ __device__ __forceinline__ void decode_tile(const GemmArgs& p, TileCursor& cur, 
 
 // Shared memory of the epilogue's staging boxes: the bf16-output epilogues write through them.
 __host__ __device__ constexpr int staging_bytes(int epi) {
-  return (epi == EPI_STORE || epi == EPI_SWIGLU_FWD || epi == EPI_SWIGLU_BWD) ? kEpiWarps * kBoxesPerWarp * kStageBox
-                                                                             : 0;
+  return (epi == EPI_STORE || epi == EPI_SWIGLU_FWD || epi == EPI_SWIGLU_BWD || epi == EPI_SCATTER)
+             ? kEpiWarps * kBoxesPerWarp * kStageBox
+             : 0;
 }
 
 // One epilogue warp's bf16 output path: a 32 x 32 chunk (row = lane, 32 packed bf16 pairs per lane
@@ -177,20 +178,6 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 __device__ __forceinline__ void pack32(const float (&v)[32], uint32_t (&pk)[16]) {
 #pragma unroll
   for (int q = 0; q < 16; ++q) pk[q] = pack_bf16(v[2 * q], v[2 * q + 1]);
-}
-
-// Store 32 floats as bf16 (64 contiguous bytes, 16-byte aligned).
-__device__ __forceinline__ void store32(bf16* dst, const float (&v)[32]) {
-  uint4* d = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    uint4 w;
-    w.x = pack_bf16(v[q * 8 + 0], v[q * 8 + 1]);
-    w.y = pack_bf16(v[q * 8 + 2], v[q * 8 + 3]);
-    w.z = pack_bf16(v[q * 8 + 4], v[q * 8 + 5]);
-    w.w = pack_bf16(v[q * 8 + 6], v[q * 8 + 7]);
-    d[q] = w;
-  }
 }
 
 __device__ __forceinline__ void load32(const bf16* src, float (&v)[32]) {
@@ -553,7 +540,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
             }
           }
           const int64_t col_base = (int64_t)ti.nt * BN + c0;
-          bf16* outp = p.out + tok * p.ldo + col_base;
+          const int row_base = p.seg.row0[ti.g] + ti.mt * BM + quad * 32;  // rows at or past T are clipped
 #pragma unroll 1
           for (int c = 0; c < BN / 2; c += 32) {
             float v[32];
@@ -573,8 +560,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
 #pragma unroll
                 for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(round_to<bf16>(m[j]), v[j]);
               }
-              store32(outp + c, v);
             }
+            uint32_t pk[16];
+            pack32(v, pk);
+            bw.put(pk, &tmO, (int)(col_base + c), row_base, lane);
           }
         } else {
           // plain bf16 store: each 32 x 32 chunk (this warp's 32 rows) goes through shared memory in
@@ -680,15 +669,16 @@ int pick_bn(int64_t n) { return n % 256 == 0 ? 256 : 128; }
 }  // namespace
 
 int tc_experts_fwd(const void* xp, const void* wgu, const void* wd, void* h, void* a, void* y, int E, int64_t H,
-                   int64_t F, const SegTable& sg, cudaStream_t st) {
+                   int64_t F, const SegTable& sg, cudaStream_t st, int64_t io_rows) {
   if (!tc_shape_supported(H, F)) return ATS_EUNSUPPORTED;
   const int64_t R = sg.max_rows;
+  const int64_t IO = io_rows > 0 ? io_rows : R;  // rows of xp and y (reads past them are zero, stores clipped)
   CUtensorMap ma, mb;
   GemmArgs p{};
   p.seg = sg;
   p.F = (int)F;
   // h = xp Wgu_e^T with the SwiGLU epilogue: tile N = 128 gate + 128 up columns
-  ATS_TRY(make_map(&ma, xp, H, R, H * 2, 128));
+  ATS_TRY(make_map(&ma, xp, H, IO, H * 2, 128));
   ATS_TRY(make_map(&mb, wgu, H, (uint64_t)E * 2 * F, H * 2, 128));
   p.N = (int)F;
   p.K = (int)H;
@@ -709,16 +699,17 @@ int tc_experts_fwd(const void* xp, const void* wgu, const void* wd, void* h, voi
   p.out = static_cast<bf16*>(y);
   p.ldo = H;
   CUtensorMap mo;
-  ATS_TRY(make_out_map(&mo, y, H, R, H * 2));
+  ATS_TRY(make_out_map(&mo, y, H, IO, H * 2));
   if (bn == 256) return launch_tc<256, false, false, EPI_STORE, false>(ma, mb, p, (R / BM) * (H / 256), st, &mo);
   return launch_tc<128, false, false, EPI_STORE, false>(ma, mb, p, (R / BM) * (H / 128), st, &mo);
 }
 
 int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a, const void* wgu, const void* wd,
                    void* dh, void* dxp, void* dwgu, void* dwd, int E, int64_t H, int64_t F, const SegTable& sg,
-                   cudaStream_t st) {
+                   cudaStream_t st, int64_t io_rows) {
   if (!tc_shape_supported(H, F)) return ATS_EUNSUPPORTED;
   const int64_t R = sg.max_rows;
+  const int64_t IO = io_rows > 0 ? io_rows : R;  // rows of dy, xp and dxp
   CUtensorMap ma, mb;
   GemmArgs p{};
   p.seg = sg;
@@ -726,7 +717,7 @@ int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a,
   // da = dy Wd_e (B N-major: Wd_e[h][f]) with the SwiGLU backward epilogue -> dh
   {
     const int bn = pick_bn(F);
-    ATS_TRY(make_map(&ma, dy, H, R, H * 2, 128));
+    ATS_TRY(make_map(&ma, dy, H, IO, H * 2, 128));
     ATS_TRY(make_map(&mb, wd, F, (uint64_t)E * H, F * 2, 64));
     p.N = (int)F;
     p.K = (int)H;
@@ -751,7 +742,7 @@ int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a,
     p.out = static_cast<bf16*>(dxp);
     p.ldo = H;
     CUtensorMap mo;
-    ATS_TRY(make_out_map(&mo, dxp, H, R, H * 2));
+    ATS_TRY(make_out_map(&mo, dxp, H, IO, H * 2));
     if (bn == 256)
       ATS_TRY((launch_tc<256, false, true, EPI_STORE, false>(ma, mb, p, (R / BM) * (H / 256), st, &mo)));
     else
@@ -760,7 +751,7 @@ int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a,
   // dWd_e[h][f] = sum over the expert's rows r of dy[r][h] a[r][f]   (A M-major, B N-major)
   {
     const int bn = pick_bn(F);
-    ATS_TRY(make_map(&ma, dy, H, R, H * 2, 64));
+    ATS_TRY(make_map(&ma, dy, H, IO, H * 2, 64));
     ATS_TRY(make_map(&mb, a, F, R, F * 2, 64));
     p.M = (int)H;
     p.N = (int)F;
@@ -781,7 +772,7 @@ int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a,
   {
     const int bn = pick_bn(H);
     ATS_TRY(make_map(&ma, dh, 2 * F, R, 2 * F * 2, 64));
-    ATS_TRY(make_map(&mb, xp, H, R, H * 2, 64));
+    ATS_TRY(make_map(&mb, xp, H, IO, H * 2, 64));
     p.M = (int)(2 * F);
     p.N = (int)H;
     p.out = static_cast<bf16*>(dwgu);
@@ -846,10 +837,13 @@ int tc_router_dx(const void* dlparts, const void* wparts, const void* dxp, const
   p.topk = k;
   ATS_TRY(make_map(&ma, dlparts, (uint64_t)3 * Ep, T, (uint64_t)3 * Ep * 2, 128));
   ATS_TRY(make_map(&mb, wparts, H, (uint64_t)3 * Ep, H * 2, 64));
+  CUtensorMap mo;
+  ATS_TRY(make_out_map(&mo, dx, H, T, H * 2));
   const int64_t mt = (T + BM - 1) / BM;
   if (Ep != kRouterEp) return fail(ATS_EUNSUPPORTED, "moe_router: padded expert count %d", Ep);
-  if (pick_bn(H) == 256) return launch_tc<256, false, true, EPI_SCATTER, false, 6>(ma, mb, p, mt * (H / 256), st);
-  return launch_tc<128, false, true, EPI_SCATTER, false, 6>(ma, mb, p, mt * (H / 128), st);
+  if (pick_bn(H) == 256)
+    return launch_tc<256, false, true, EPI_SCATTER, false, 6>(ma, mb, p, mt * (H / 256), st, &mo);
+  return launch_tc<128, false, true, EPI_SCATTER, false, 6>(ma, mb, p, mt * (H / 128), st, &mo);
 }
 
 int tc_router_dw(const void* x, const void* dlparts, float* partial, int64_t T, int64_t H, int Ep,

@@ -275,18 +275,68 @@ def moe_apply(x2: torch.Tensor, logits: torch.Tensor | None, wgu: list[torch.Ten
                         wd_stack, *wgu, *wd)
 
 
+class _DenseSwiGLUFn(torch.autograd.Function):
+    """SwiGLU FFN on the tensor-core GEMMs as one expert over the token rows
+    (no routing, no gather or combine pass)."""
+
+    @staticmethod
+    def forward(ctx, x2, w_gate_up, w_down):
+        T, H = x2.shape
+        Fdim = w_down.shape[1]
+        dev = x2.device
+        dt = _lib.dtype_code(x2.dtype)
+        st = _lib.stream_of(x2)
+        R = _lib.query("ats_swiglu_rows", T)
+        wsb = _lib.query("ats_swiglu_workspace_bytes")
+        ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+        wgu, wd = w_gate_up.contiguous(), w_down.contiguous()
+        h = torch.empty((R, 2 * Fdim), dtype=x2.dtype, device=dev)
+        a = torch.empty((R, Fdim), dtype=x2.dtype, device=dev)
+        y = torch.empty((T, H), dtype=x2.dtype, device=dev)
+        _lib.call("ats_swiglu_fwd", x2.data_ptr(), wgu.data_ptr(), wd.data_ptr(), h.data_ptr(), a.data_ptr(),
+                  y.data_ptr(), dt, T, H, Fdim, ws.data_ptr(), wsb, st)
+        ctx.save_for_backward(x2, h, a, wgu, wd, ws)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, h, a, wgu, wd, ws = ctx.saved_tensors
+        T, H = x2.shape
+        Fdim = wd.shape[1]
+        dt = _lib.dtype_code(x2.dtype)
+        st = _lib.stream_of(x2)
+        dy = dy.to(x2.dtype).contiguous()
+        dh = torch.empty_like(h)
+        dx = torch.empty_like(x2)
+        dwgu = torch.empty_like(wgu)
+        dwd = torch.empty_like(wd)
+        _lib.call("ats_swiglu_bwd", dy.data_ptr(), x2.data_ptr(), h.data_ptr(), a.data_ptr(), wgu.data_ptr(),
+                  wd.data_ptr(), dh.data_ptr(), dx.data_ptr(), dwgu.data_ptr(), dwd.data_ptr(), dt, T, H, Fdim,
+                  ws.data_ptr(), ws.numel(), st)
+        return dx, dwgu, dwd
+
+
 def dense_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor) -> torch.Tensor:
-    """One SwiGLU FFN (ffn.py:42-44) on the grouped kernels: a single expert
-    that every token selects with gate 1.0."""
+    """One SwiGLU FFN (ffn.py:42-44).  bf16 shapes the tensor-core tiling covers
+    run as one expert directly over the token rows; others as a single expert
+    that every token selects with gate 1.0 through the MoE stages."""
     _lib.require_cuda("SwiGLU", x, w_gate_up, w_down)
     H = x.shape[-1]
-    x2 = x.reshape(-1, H)
+    x2 = x.reshape(-1, H).contiguous()
     if x2.dtype != w_gate_up.dtype:
         raise TypeError(f"SwiGLU: input dtype {x2.dtype} does not match weight dtype {w_gate_up.dtype}")
     T = x2.shape[0]
-    logits = torch.zeros((T, 1), dtype=torch.float32, device=x.device)
-    out = moe_apply(x2, logits, [w_gate_up], [w_down], 1, max(1, T), 0.0)[0]
-    return out.view(x.shape)
+    Fdim = w_down.shape[1]
+    if _lib.query("ats_swiglu_supported", _lib.dtype_code(x2.dtype), T, H, Fdim) == 1:
+        return _DenseSwiGLUFn.apply(x2, w_gate_up, w_down).view(x.shape)
+    return routed_swiglu(x2, w_gate_up, w_down).view(x.shape)
+
+
+def routed_swiglu(x2: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor) -> torch.Tensor:
+    """The SwiGLU FFN through the MoE stages as one expert with gate 1.0."""
+    T = x2.shape[0]
+    logits = torch.zeros((T, 1), dtype=torch.float32, device=x2.device)
+    return moe_apply(x2, logits, [w_gate_up], [w_down], 1, max(1, T), 0.0)[0]
 
 
 class _CudaMoE(nn.Module):

@@ -9,6 +9,8 @@ Workloads (synthetic, seeded; the reference publishes no dataset for this path):
             bf16, theta 5e5 (metric: HBM GB/s)
   moe       MoE layer forward+backward, 8192 tokens, hidden 2048, 8 experts
             top-2, ffn 5632, bf16, fp32 router, no capacity drop (metric: tokens/s)
+  ffn       dense SwiGLU FFN forward+backward, 16384 tokens, hidden 4096, ffn
+            11008, bf16 (metric: tokens/s)
   moe_ep    expert-parallel MoE layer forward+backward, 32768 tokens per GPU,
             hidden 4096, 64 experts top-2 sharded over the GPUs, ffn 1408,
             capacity factor 1.25, Zipf(1.1) expert skew (metric: tokens/s)
@@ -468,6 +470,98 @@ class MoEWorkload(Workload):
                           f"(numpy oracle, BLAS on {threads} threads)"}
 
 
+class FFNWorkload(Workload):
+    """Dense SwiGLU FFN (ffn.py:37-45) of a 7B-shaped block on the expert GEMMs (one expert, no routing)."""
+    name = "ffn"
+    metric = "swiglu_ffn_fwd_bwd_tokens_per_s"
+    unit = "tokens/s"
+    T, H, F = 16384, 4096, 11008
+
+    def flops_per_step(self) -> int:
+        return 18 * self.T * self.H * self.F  # 3 GEMMs forward (4HF + 2HF per token), twice that backward
+
+    def config(self):
+        return {"workload": "dense SwiGLU FFN fwd+bwd, 16384 tokens, hidden 4096, ffn 11008, bf16",
+                "per_rank": "full workload per GPU (replicas)", "l2": "inputs larger than L2"}
+
+    def setup(self):
+        t = self.torch
+        from ats_v2_b200.ffn import SwiGLU
+        t.manual_seed(3000 + self.rank)
+        with t.device("cuda"):
+            self.m = SwiGLU(self.H, self.F)
+        with t.no_grad():
+            self.m.gate_up_proj.weight.normal_(0, 0.02)
+            self.m.down_proj.weight.normal_(0, 0.02)
+        self.m.bfloat16()
+        g = t.Generator(device="cuda").manual_seed(self.rank)
+        self.x = t.randn(4, self.T // 4, self.H, device="cuda", generator=g).bfloat16().requires_grad_()
+        self.dy = t.randn(4, self.T // 4, self.H, device="cuda", generator=g).bfloat16()
+
+    def step(self, evs):
+        for p in self.m.parameters():
+            p.grad = None
+        self.x.grad = None
+        if evs:
+            evs[0].record()
+        self.m(self.x).backward(self.dy)
+        if evs:
+            evs[1].record()
+
+    def dominant(self):
+        return {"kernel": "dense SwiGLU GEMMs (whole FFN fwd+bwd timed)", "flops": self.flops_per_step(),
+                "bound": "tensor"}
+
+    def e2e_setup(self):
+        t = self.torch
+        self.hx = self.x.detach().cpu().pin_memory()
+        self.hdy = self.dy.cpu().pin_memory()
+        self.hdx = t.empty_like(self.hx).pin_memory()
+        self.hout = t.empty_like(self.hx).pin_memory()
+        self.dx_in = t.empty_like(self.x.detach())
+        self.ddy = t.empty_like(self.dy)
+        self.h2d = 2 * self.hx.numel() * 2
+        self.d2h = 2 * self.hx.numel() * 2
+
+    def e2e_step(self):
+        self.dx_in.copy_(self.hx, non_blocking=True)
+        self.ddy.copy_(self.hdy, non_blocking=True)
+        x = self.dx_in.requires_grad_()
+        for p in self.m.parameters():
+            p.grad = None
+        out = self.m(x)
+        out.backward(self.ddy)
+        self.hout.copy_(out.detach(), non_blocking=True)
+        self.hdx.copy_(x.grad, non_blocking=True)
+        x.grad = None
+        x.requires_grad_(False)
+
+    def units_to_value(self, steps, ms):
+        return self.T * steps / (ms * 1e-3)
+
+    def cpu_baseline(self, seconds: float):
+        from oracle import moe as omoe
+        from oracle.bf16 import round_bf16
+        threads = cpu_threads()
+        T = 256
+        rng = np.random.default_rng(0)
+        x = round_bf16(rng.standard_normal((T, self.H)).astype(np.float32))
+        wgu = round_bf16((0.02 * rng.standard_normal((2 * self.F, self.H))).astype(np.float32))
+        wd = round_bf16((0.02 * rng.standard_normal((self.H, self.F))).astype(np.float32))
+        t0 = time.perf_counter()
+        n = 0
+        while True:
+            omoe.expert_fwd(x, wgu, wd, "bf16")
+            n += 1
+            if time.perf_counter() - t0 >= seconds:
+                break
+        dt = time.perf_counter() - t0
+        # the backward costs twice the forward's GEMMs; count a pass as forward + backward
+        return {"value": T * n / dt / 3.0, "unit": self.unit, "cores": threads, "kind": "port",
+                "sample": f"{T} tokens, forward only ({n} passes in {dt:.1f} s), scaled by 1/3 for the backward's "
+                          f"two GEMMs per forward GEMM (numpy oracle, BLAS on {threads} threads)"}
+
+
 def zipf_bias(E: int, s_exp: float = 1.1, seed: int = 1):
     """Per-expert router-logit bias log(p_pi(e)), p_r ~ r^-s over ranks r=1..E,
     pi a fixed permutation (generator seed 1), mean-centred."""
@@ -599,7 +693,8 @@ class MoEEPWorkload(Workload):
                           f"experts' FFNs), {n} passes in {dt:.1f} s (numpy oracle, BLAS on {threads} threads)"}
 
 
-WORKLOADS = {"rmsnorm": RMSNormWorkload, "rope": RopeWorkload, "moe": MoEWorkload, "moe_ep": MoEEPWorkload}
+WORKLOADS = {"rmsnorm": RMSNormWorkload, "rope": RopeWorkload, "moe": MoEWorkload, "moe_ep": MoEEPWorkload,
+             "ffn": FFNWorkload}
 
 
 # ---------------------------------------------------------------- timing

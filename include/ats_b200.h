@@ -285,6 +285,26 @@ ATS_API int ats_moe_ep_experts_bwd(const void* dy, const void* xr, const void* h
 ATS_API int ats_moe_ep_status(const void* seg_workspace, size_t seg_workspace_bytes, int W, int E_local,
                       int* status);
 
+/* ------------------------------------------------------- dense SwiGLU FFN
+ * SwiGLU.forward (ats/model/ffn.py:37-45): y = down(silu(g) * u), [g, u] =
+ * chunk(x . w_gate_up^T, 2), for bf16 x [T, hidden], w_gate_up [2F, hidden],
+ * w_down [hidden, F], on the same tensor-core GEMMs as the experts (one
+ * expert, no routing).  h [R, 2F] and a [R, F] (R = ats_swiglu_rows(T), T
+ * rounded up to 128) are saved for the backward; rows past T are zero.
+ * Needs T >= 128 and hidden, F multiples of 128 (ats_swiglu_supported). */
+ATS_API int ats_swiglu_supported(ats_dtype dtype, int64_t T, int64_t hidden, int64_t F);
+ATS_API size_t ats_swiglu_workspace_bytes(void);
+ATS_API int64_t ats_swiglu_rows(int64_t T);
+ATS_API int ats_swiglu_fwd(const void* x, const void* w_gate_up, const void* w_down, void* h, void* a, void* y,
+                   ats_dtype dtype, int64_t T, int64_t hidden, int64_t F, void* workspace,
+                   size_t workspace_bytes, void* stream);
+/* dy [T, hidden] -> dh [R, 2F] (scratch), dx [T, hidden], dw_gate_up, dw_down (bf16, the weights' layout). */
+ATS_API int ats_swiglu_bwd(const void* dy, const void* x, const void* h, const void* a, const void* w_gate_up,
+                   const void* w_down, void* dh, void* dx, void* dw_gate_up, void* dw_down,
+                   ats_dtype dtype, int64_t T, int64_t hidden, int64_t F, void* workspace,
+                   size_t workspace_bytes, void* stream);
+ATS_API int ats_swiglu_status(const void* workspace, size_t workspace_bytes, int* status);
+
 /* ------------------------------------------------------- router GEMMs
  * The float32 router of the MoE layer (moe.py:76-90 with the north-star
  * float32 router: logits = x.float() @ w.T) on the tensor cores, for bf16
