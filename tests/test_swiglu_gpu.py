@@ -61,8 +61,8 @@ def test_swiglu_module_forward_and_backward_against_the_oracle():
     dy = torch.randn_like(out)
     out.backward(dy)
     # gradients against a float32 chain on the same bf16 values with the kernels' rounding points
-    xs, wgu, wd, d = x.detach().view(T, H).float(), m.gate_up_proj.weight.detach().float(), m.down_proj.weight.detach().float(), \
-        dy.view(T, H).float()
+    xs, d = x.detach().view(T, H).float(), dy.view(T, H).float()
+    wgu, wd = m.gate_up_proj.weight.detach().float(), m.down_proj.weight.detach().float()
     hh = (xs @ wgu.T).bfloat16().float()
     gg, uu = hh[:, :F], hh[:, F:]
     s = torch.nn.functional.silu(gg).bfloat16().float()
