@@ -202,12 +202,33 @@ class _EPMoEFn(torch.autograd.Function):
         return (dx, dgate_w.to(gate_dtype), None, None, None, None, *grads)
 
 
+def balanced_placement(load: list[float], world: int) -> list[int]:
+    """A permutation perm of the experts such that rank r hosts the experts
+    perm[r*E_local:(r+1)*E_local] and the ranks' summed loads are close:
+    experts in decreasing load (ties by label) go to the rank with the least
+    load so far that still has a free slot (every rank hosts E_local
+    experts).  Within a rank the experts keep ascending label order."""
+    E = len(load)
+    if world < 1 or E % world != 0:
+        raise ValueError(f"{E} experts do not split over {world} ranks")
+    el = E // world
+    order = sorted(range(E), key=lambda e: (-float(load[e]), e))
+    bins: list[list[int]] = [[] for _ in range(world)]
+    tot = [0.0] * world
+    for e in order:
+        r = min((r for r in range(world) if len(bins[r]) < el), key=lambda r: (tot[r], r))
+        bins[r].append(e)
+        tot[r] += float(load[e])
+    return [e for b in bins for e in sorted(b)]
+
+
 class ExpertParallelMoE(nn.Module):
     """MoE layer with its experts sharded over a process group.
 
-    ``experts[i]`` is global expert ``rank*E_local + i``; ``gate`` is the
-    replicated router (Linear(hidden, num_experts)).  With a world size of 1
-    it is the single-GPU layer on the capacity-slot layout."""
+    ``experts[i]`` is expert ``rank*E_local + i``; ``gate`` is the replicated
+    router (Linear(hidden, num_experts)).  With a world size of 1 it is the
+    single-GPU layer on the expert-parallel path.  ``rebalance`` relabels the
+    experts so that the ranks carry about equal expected rows."""
 
     def __init__(self, hidden_size: int, intermediate_size: int, num_experts: int, num_layers: int,
                  top_k: int = 2, capacity_factor: float = 1.25, load_balancing_weight: float = 0.01,
@@ -235,6 +256,51 @@ class ExpertParallelMoE(nn.Module):
             init_residual_projection(ex.down_proj, num_layers)
         self.last_expert_utilization: dict[int, float] | None = None
         self.last_counts: torch.Tensor | None = None
+
+    @torch.no_grad()
+    def rebalance(self, load=None, perm=None) -> torch.Tensor:
+        """Relabel the experts so that every rank's experts carry about the same
+        expected rows, and return the permutation perm (int64 [E]): the expert
+        now labelled j is the one that was labelled perm[j].
+
+        ``load`` [E] is the expected rows per expert label, the same on every
+        rank (for example the kept counts of a calibration batch, summed over
+        the ranks).  An expert's gate row and weights move with it, so the layer
+        computes the same function; the experts only change rank (the gate
+        weight is replicated; the expert weights are all-gathered once and each
+        rank keeps its new experts).  Which rank runs an expert changes no
+        result.  What does change is the label order: ties in the top-k go to
+        the lower new label, a token's expert outputs are summed in new label
+        order (with top_k = 2 the sum of two rows rounds the same in either
+        order), and the router's share of the input gradient sums over the
+        experts in new label order (float32, so its last bits can differ).
+        Per-expert inputs indexed by label, such as a logit
+        bias, must be re-indexed with perm by the caller.  Call it before an
+        optimizer holds per-parameter state: that state does not move.  An
+        explicit ``perm`` (same on every rank) may be given instead of ``load``."""
+        if perm is None:
+            load = [float(v) for v in torch.as_tensor(load).flatten().tolist()]
+            if len(load) != self.num_experts:
+                raise ValueError(f"rebalance: load has {len(load)} entries, expected {self.num_experts}")
+            perm = balanced_placement(load, self.world)
+        else:
+            perm = [int(v) for v in torch.as_tensor(perm).flatten().tolist()]
+            if sorted(perm) != list(range(self.num_experts)):
+                raise ValueError("rebalance: perm must be a permutation of the expert labels")
+        W, El = self.world, self.num_local_experts
+        gw = self.gate.weight
+        gw.copy_(gw[torch.as_tensor(perm, device=gw.device)].clone())
+        for name in ("gate_up_proj", "down_proj"):
+            local = torch.stack([getattr(ex, name).weight.detach() for ex in self.experts])
+            if W > 1:
+                parts = [torch.empty_like(local) for _ in range(W)]
+                dist.all_gather(parts, local.contiguous(), group=self.group)
+                full = torch.cat(parts)
+            else:
+                full = local.clone()
+            for i, ex in enumerate(self.experts):
+                getattr(ex, name).weight.copy_(full[perm[self.rank * El + i]])
+        return torch.as_tensor(perm, dtype=torch.int64)
 
     def router_logits(self, flat_x: torch.Tensor) -> torch.Tensor:
         """The float32 logits forward() routes on (without a logit bias)."""

@@ -582,8 +582,11 @@ class MoEEPWorkload(Workload):
     def config(self):
         return {"workload": "expert-parallel MoE layer fwd+bwd, 32768 tokens per GPU, hidden 4096, 64 experts "
                             "top-2, ffn 1408, capacity factor 1.25, Zipf(1.1) router-logit bias, bf16, fp32 router",
-                "experts_per_gpu": self.E // self.world, "exchange": "NCCL all_to_all_single, equal splits "
-                "on capacity slots" if self.world > 1 else "none (all experts local)",
+                "experts_per_gpu": self.E // self.world,
+                "exchange": "NCCL all_to_all_single of the kept rows (variable splits)" if self.world > 1
+                            else "none (all experts local)",
+                "expert_placement": "balanced by the rows each expert received on a calibration forward "
+                                    "(ExpertParallelMoE.rebalance)",
                 "per_rank": "32768 tokens per GPU (weak scaling)", "l2": "inputs larger than L2"}
 
     def setup(self):
@@ -605,6 +608,23 @@ class MoEEPWorkload(Workload):
         self.x = t.randn(1, self.T, self.H, device="cuda", generator=g).bfloat16().requires_grad_()
         self.dy = t.randn(1, self.T, self.H, device="cuda", generator=g).bfloat16()
         self.one = t.ones((), device="cuda")
+        # expert placement: rows each expert receives on a calibration forward (kept counts rounded up to
+        # 128, summed over the ranks), experts spread so every rank gets about the same; one rank: no change
+        from ats_v2_b200.moe import capacity_for
+        with t.no_grad():
+            self.layer(self.x.detach(), logit_bias=self.bias)
+        cap = capacity_for(self.T, self.K, self.E, self.CF)
+        load = ((self.layer.last_counts.clamp(max=cap) + 127) // 128 * 128).to(t.float64)
+        if self.world > 1:
+            import torch.distributed as tdist
+            tdist.all_reduce(load)
+        self.perm = self.layer.rebalance(load.cpu())
+        self.bias = self.bias[self.perm.cuda()]
+        self.load_max_over_mean = float(self._rank_loads(load.cpu()).max() / self._rank_loads(load.cpu()).mean())
+
+    def _rank_loads(self, load):
+        el = self.E // self.world
+        return load[self.perm].view(self.world, el).sum(1)
 
     def _zero(self):
         for p in self.layer.parameters():
@@ -635,7 +655,8 @@ class MoEEPWorkload(Workload):
     def dominant(self):
         rows = self.kept_rows()
         return {"kernel": "whole expert-parallel layer fwd+bwd (expert GEMMs 18*rows*H*F flops)",
-                "flops": 18 * rows * self.H * self.F, "bound": "tensor", "kept_rows": rows}
+                "flops": 18 * rows * self.H * self.F, "bound": "tensor", "kept_rows": rows,
+                "rank_rows_max_over_mean": round(self.load_max_over_mean, 4)}
 
     def e2e_setup(self):
         t = self.torch
@@ -779,8 +800,9 @@ def measure(torch, dist, wl: Workload, steps: int, warmup: int, world: int, with
             res["roofline"] = {"bound": "tensor", "kernel": dom["kernel"], "achieved": ach, "peak": peak,
                                "unit": "TFLOP/s", "frac": ach / peak, "peak_source": wl.peaks_kind + " sustained",
                                "traffic": dom.get("traffic"), "algorithmic_flops": dom["flops"], "kernel_ms": kms}
-            if "kept_rows" in dom:
-                res["roofline"]["kept_rows"] = dom["kept_rows"]
+            for key in ("kept_rows", "rank_rows_max_over_mean"):
+                if key in dom:
+                    res["roofline"][key] = dom[key]
         if "traffic_source" in dom:
             res["roofline"]["traffic_source"] = dom["traffic_source"]
     # end to end through the public module with host buffers

@@ -22,7 +22,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from ats_v2_b200.ep import _Exchange, exchange_counts, exchange_rows, slot_rows
+from ats_v2_b200.ep import ExpertParallelMoE, _Exchange, balanced_placement, exchange_counts, exchange_rows, slot_rows
 
 
 def _free_port() -> int:
@@ -113,6 +113,40 @@ def _packed_worker(rank, world, port, E_local, cap, H, errq):
         raise
 
 
+def _rebalance_worker(rank, world, port, errq):
+    """Every expert's weights carry its label; after rebalance each rank must
+    hold exactly the experts the permutation gives it, with their weights and
+    gate rows."""
+    try:
+        _init(rank, world, port)
+        E, H, F = 8, 16, 8
+        El = E // world
+        m = ExpertParallelMoE(H, F, E, num_layers=2, top_k=2)
+        with torch.no_grad():
+            for e in range(E):
+                m.gate.weight[e].fill_(float(e))
+            for i, ex in enumerate(m.experts):
+                ex.gate_up_proj.weight.fill_(float(rank * El + i))
+                ex.down_proj.weight.fill_(100.0 + rank * El + i)
+        load = torch.tensor([1.0, 1.0, 9.0, 8.0, 1.0, 1.0, 1.0, 1.0])  # experts 2 and 3 are hot
+        perm = m.rebalance(load).tolist()
+        assert sorted(perm) == list(range(E))
+        assert perm == balanced_placement(load.tolist(), world)
+        for j in range(E):
+            assert bool((m.gate.weight[j] == float(perm[j])).all())
+        for i, ex in enumerate(m.experts):
+            old = perm[rank * El + i]
+            assert bool((ex.gate_up_proj.weight == float(old)).all())
+            assert bool((ex.down_proj.weight == 100.0 + old).all())
+        hot = {2, 3}
+        assert len(hot & set(perm[:El])) == 1 and len(hot & set(perm[El:])) == 1  # one hot expert per rank
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        errq.put((rank, traceback.format_exc()))
+        raise
+
+
 def _leaver_worker(rank, world, port, errq):
     try:
         _init(rank, world, port, timeout_s=3)
@@ -144,6 +178,29 @@ def test_packed_exchange_sends_only_kept_segments_and_round_trips(E_local, cap, 
     errq = ctx.SimpleQueue()
     mp.start_processes(_packed_worker, args=(2, _free_port(), E_local, cap, H, errq), nprocs=2, join=True,
                        start_method="spawn")
+    assert errq.empty()
+
+
+def test_balanced_placement_spreads_the_load():
+    load = [float(2 ** (-i)) for i in range(16)]  # one expert far hotter than the rest
+    for world in (1, 2, 4, 8):
+        perm = balanced_placement(load, world)
+        el = 16 // world
+        assert sorted(perm) == list(range(16))
+        ranks = [perm[r * el:(r + 1) * el] for r in range(world)]
+        assert all(b == sorted(b) for b in ranks)
+        per = [sum(load[e] for e in b) for b in ranks]
+        contiguous = [sum(load[r * el:(r + 1) * el]) for r in range(world)]
+        assert max(per) <= max(contiguous) + 1e-12
+    assert balanced_placement(load, 1) == list(range(16))  # one rank: nothing moves
+    with pytest.raises(ValueError):
+        balanced_placement(load, 3)
+
+
+def test_rebalance_moves_gate_rows_and_expert_weights_between_ranks():
+    ctx = mp.get_context("spawn")
+    errq = ctx.SimpleQueue()
+    mp.start_processes(_rebalance_worker, args=(2, _free_port(), errq), nprocs=2, join=True, start_method="spawn")
     assert errq.empty()
 
 

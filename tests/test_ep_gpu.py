@@ -64,6 +64,49 @@ def test_single_rank_expert_parallel_layer_equals_the_layer(T, H, F, E, k, cf, e
               min_exact=0.999)
 
 
+def test_rebalanced_layer_computes_the_same_function():
+    """Relabelling the experts (rebalance) moves gate rows and weights with
+    them.  With top-2 routing the output is bit-equal and every expert's
+    weight gradient is the old one under the permutation.  The router reduces
+    over the experts in label order (the softmax sums, its backward, and the
+    K dimension of the router's share of the input gradient), so the input
+    gradient matches at bf16 tolerance with almost every element bit-equal
+    and the gate gradient at float32 tolerance."""
+    T, H, F, E, k = 1024, 256, 384, 8, 2
+    torch.manual_seed(0)
+    ep = ExpertParallelMoE(H, F, E, num_layers=2, top_k=k, capacity_factor=1.25)
+    _init_weights(ep.gate, ep.experts, 3)
+    ep = ep.cuda()
+    ep.experts.to(torch.bfloat16)
+    bias = torch.linspace(-1.0, 1.0, E, device="cuda")
+    x = torch.randn(1, T, H, device="cuda").bfloat16()
+    g = torch.randn(1, T, H, device="cuda").bfloat16()
+
+    def run(b):
+        xa = x.clone().requires_grad_()
+        for p in ep.parameters():
+            p.grad = None
+        out, aux = ep(xa, logit_bias=b)
+        torch.autograd.backward([out, aux], [g, torch.ones_like(aux)])
+        return (out.detach(), xa.grad, aux.detach(), ep.gate.weight.grad.clone(),
+                [e.gate_up_proj.weight.grad.clone() for e in ep.experts],
+                [e.down_proj.weight.grad.clone() for e in ep.experts])
+
+    before = run(bias)
+    perm = ep.rebalance(perm=torch.randperm(E, generator=torch.Generator().manual_seed(4)))
+    assert sorted(perm.tolist()) == list(range(E)) and perm.tolist() != list(range(E))
+    after = run(bias[perm.cuda()])
+    assert torch.equal(before[0], after[0])
+    close(after[1], np32(before[1]), "bf16", min_exact=0.99)
+    assert after[2].item() == pytest.approx(before[2].item(), rel=1e-6)
+    # the router's softmax and its backward reduce over the experts in label order (float32)
+    ref = before[3][perm.cuda()]
+    torch.testing.assert_close(after[3], ref, rtol=1e-5, atol=1e-5 * float(ref.abs().max()))
+    for j in range(E):
+        assert torch.equal(after[4][j], before[4][perm[j]])
+        assert torch.equal(after[5][j], before[5][perm[j]])
+
+
 def _free_port() -> int:
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
