@@ -43,6 +43,7 @@ constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr long long kWaitBudget = 4000000000LL;  // SM cycles, about 2 s
 constexpr int kStageBox = 32 * 32 * 2;           // staging box: 32 rows x 32 bf16 columns, 64-byte swizzle
 constexpr int kBoxesPerWarp = 2;
+constexpr int kBandM = 16;  // M tiles per band of the tile order
 
 enum Epi { EPI_STORE = 0, EPI_SWIGLU_FWD = 1, EPI_SWIGLU_BWD = 2, EPI_F32 = 3, EPI_SCATTER = 4 };
 constexpr int kMaxParts = 6;
@@ -117,8 +118,15 @@ __device__ __forceinline__ void decode_tile(const GemmArgs& p, TileCursor& cur, 
   const int g = cur.g;
   const int q = t - cur.first;
   ti.g = g;
-  ti.mt = q / NT;
-  ti.nt = q - ti.mt * NT;
+  // bands of kBandM M tiles, M fastest inside a band: the CTAs that run together share their B tiles
+  // and the band's A rows, so both stay in L2 even when a weight is larger than L2
+  const int MT = n / NT;
+  const int band = q / (kBandM * NT);
+  const int m0 = band * kBandM;
+  const int gm = MT - m0 < kBandM ? MT - m0 : kBandM;
+  const int r = q - band * kBandM * NT;
+  ti.nt = r / gm;
+  ti.mt = m0 + (r - ti.nt * gm);
   if (KGROUP) {
     ti.e = g;
     int kb = 0;
