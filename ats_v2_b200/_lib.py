@@ -7,6 +7,7 @@ there is no fallback implementation behind these entry points.
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import os
 import threading
@@ -37,6 +38,8 @@ SIGNATURES: dict[str, tuple] = {
     "ats_strerror": (c_char_p, [c_int]),
     "ats_last_error_message": (c_char_p, []),
     "ats_kernel_launches": (ctypes.c_uint64, []),
+    "ats_set_gemm_sm_limit": (c_int, [c_int]),
+    "ats_gemm_sm_limit": (c_int, []),
     "ats_rmsnorm_fwd": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_int, c_void_p, c_int64, c_void_p,
                                 c_int64, c_int64, c_float, c_void_p]),
     "ats_rmsnorm_bwd_workspace_bytes": (c_size_t, [c_int64, c_int64]),
@@ -146,6 +149,19 @@ def call(name: str, *args) -> None:
 
 def query(name: str, *args):
     return getattr(load(), name)(*args)
+
+
+@contextlib.contextmanager
+def gemm_sm_limit(sms: int):
+    """Launch the persistent tensor-core GEMMs of this thread on at most ``sms``
+    SMs inside the block (0: all), leaving the rest to a collective that runs
+    beside them on another stream."""
+    prev = query("ats_gemm_sm_limit")
+    call("ats_set_gemm_sm_limit", int(sms))
+    try:
+        yield
+    finally:
+        call("ats_set_gemm_sm_limit", prev)
 
 
 def dtype_code(t: torch.dtype) -> int:

@@ -32,6 +32,16 @@ int num_sms() {
   return cache[dev];
 }
 
+// CTAs a persistent GEMM may launch with on this host thread: 0 = one per SM.
+// A caller that runs a collective on another stream beside the GEMMs lowers it
+// so that the collective's blocks find free SMs (a GEMM CTA fills its SM).
+static thread_local int g_gemm_sm_limit = 0;
+
+int gemm_ctas() {
+  const int n = num_sms();
+  return (g_gemm_sm_limit > 0 && g_gemm_sm_limit < n) ? g_gemm_sm_limit : n;
+}
+
 }  // namespace ats
 
 extern "C" {
@@ -52,5 +62,13 @@ const char* ats_strerror(int status) {
 const char* ats_last_error_message(void) { return ats::g_last_error; }
 
 uint64_t ats_kernel_launches(void) { return ats::g_launches.load(std::memory_order_relaxed); }
+
+int ats_set_gemm_sm_limit(int sms) {
+  if (sms < 0) return ats::fail(ATS_EBADARG, "set_gemm_sm_limit: %d SMs", sms);
+  ats::g_gemm_sm_limit = sms;
+  return ATS_OK;
+}
+
+int ats_gemm_sm_limit(void) { return ats::g_gemm_sm_limit; }
 
 }  // extern "C"

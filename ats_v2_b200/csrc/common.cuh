@@ -45,6 +45,7 @@ inline int check_launch(const char* what) {
   } while (0)
 
 int num_sms();  // SM count of the current device (cached per device)
+int gemm_ctas();  // CTAs of a persistent GEMM: num_sms() or this thread's lower limit
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 

@@ -665,7 +665,7 @@ int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& p, i
   const int smem = 1024 + STAGES * (BM * BK * 2 + BPARTS * BN * BK * 2) + staging_bytes(EPI);
   cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return fail(ATS_ECUDA, "moe_gemm: smem attribute: %s", cudaGetErrorString(e));
-  int grid = num_sms();
+  int grid = gemm_ctas();
   if (max_tiles < grid) grid = (int)(max_tiles > 0 ? max_tiles : 1);
   kfn<<<grid, kThreads, smem, st>>>(ta, tb, to != nullptr ? *to : ta, to2 != nullptr ? *to2 : ta, p);
   return check_launch("moe_tc_gemm");

@@ -31,9 +31,11 @@ and sends the input gradients back.  Expert weights are rank-local, so their
 gradients need no all-reduce; the replicated router weight's gradient is the
 usual data-parallel all-reduce of the training loop.
 
-The exchange steps (``exchange_counts``, ``exchange_rows``,
-``exchange_rows_varsplit``) only move tensors and work on any device and
-backend; the device stages are the library's.
+The exchange steps (``exchange_counts``, ``exchange_rows``, ``_Exchange``)
+only move tensors and work on any device and backend; the device stages are
+the library's.  With ``overlap_parts`` P > 1 the local experts run in P parts
+and each part's row transfers overlap the other parts' expert GEMMs, which
+then leave ``comm_sms`` SMs to the transfers.
 """
 
 from __future__ import annotations
@@ -73,56 +75,134 @@ def exchange_rows(buf: torch.Tensor, group=None) -> torch.Tensor:
     return out
 
 
-def exchange_rows_varsplit(buf: torch.Tensor, send_rows: list[int], recv_rows: list[int], out_rows: int,
-                           group=None) -> torch.Tensor:
-    """Variable-split all-to-all of rows: the first sum(send_rows) rows of buf,
-    send_rows[r] of them to rank r; returns [out_rows, H] whose first
-    sum(recv_rows) rows came from the ranks in order."""
-    out = torch.empty((out_rows,) + tuple(buf.shape[1:]), dtype=buf.dtype, device=buf.device)
-    n_in, n_out = sum(send_rows), sum(recv_rows)
-    dist.all_to_all_single(out[:n_out], buf[:n_in].contiguous(), output_split_sizes=recv_rows,
-                           input_split_sizes=send_rows, group=group)
-    return out
+class _Pending:
+    """Exchange steps in flight; wait() orders the current stream after them."""
+
+    def __init__(self, works):
+        self.works = [w for w in works if w is not None]
+
+    def wait(self) -> None:
+        for w in self.works:
+            w.wait()
+
+
+def _rounded(count: int, Cp: int) -> int:
+    """Rows a received segment takes in the packed layout: its kept count,
+    clamped to [0, Cp], rounded up to 128."""
+    return (min(max(count, 0), Cp) + 127) // 128 * 128
 
 
 class _Exchange:
-    """How rows cross between ranks.  "slots": equal splits of the [W][E_local][Cp]
-    capacity-slot buffer (no host synchronisation).  "packed": only the rows
-    the expert GEMMs read (each (source, expert) segment's kept count rounded
-    up to 128), variable splits read once per forward from the device."""
+    """How rows cross between ranks.
+
+    Layouts: "slots" sends the [W][E_local][Cp] capacity-slot buffer; "packed"
+    only the rows the expert GEMMs read (each (source, expert) segment's kept
+    count rounded up to 128), with split sizes read once per forward from the
+    device.
+
+    ``parts`` P splits each rank's local experts into P runs of E_local/P.  Part
+    p's rows leave as soon as they are gathered; the expert GEMMs of part p
+    start when its rows have arrived, and its results go back while part p+1
+    computes, so all but one part's transfer each way hides behind the GEMMs.
+    With P = 1 a part is the whole exchange, one all_to_all_single; with P > 1
+    each part is a batch of per-peer sends and receives of contiguous row runs
+    (this rank's own run is a local copy).  The expert-side buffer of part p
+    holds its (source, expert) segments in that order, W*(E_local/P)*Cp rows."""
 
     def __init__(self, mode: str, W: int, El: int, Cp: int, group, seg_start: torch.Tensor | None,
-                 recv_kept: torch.Tensor):
-        self.mode, self.W, self.group = mode, W, group
-        if mode == "packed" and W > 1:
+                 recv_kept: torch.Tensor, parts: int = 1):
+        if W == 1:
+            parts = 1
+        if El % parts != 0:
+            raise ValueError(f"{El} local experts do not split into {parts} parts")
+        self.mode, self.W, self.El, self.Cp, self.group, self.parts = mode, W, El, Cp, group, parts
+        self.Ep = El // parts
+        if W == 1 or (mode == "slots" and parts == 1):
+            return
+        self.me = dist.get_rank(group)
+        self.peers = [dist.get_global_rank(group, r) if group is not None else r for r in range(W)]
+        E = W * El
+        if mode == "packed":
             host = torch.cat([seg_start.to(torch.int64), recv_kept.to(torch.int64)]).cpu().tolist()
-            E = W * El
             seg, rk = host[:E + 1], host[E + 1:]
-            self.send = [seg[(r + 1) * El] - seg[r * El] for r in range(W)]
-            self.recv = [sum((min(max(c, 0), Cp) + 127) // 128 * 128 for c in rk[r * El:(r + 1) * El])
-                         for r in range(W)]
+            rr = [_rounded(c, Cp) for c in rk]
+        else:
+            seg = [e * Cp for e in range(E + 1)]
+            rr = [Cp] * E
+        Ep = self.Ep
+        # send[p][r]: (first row, rows) of part p for rank r in the token-side buffer;
+        # recv[p][src]: (first row, rows) of source src in part p's expert-side buffer.
+        self.send, self.recv = [], []
+        for p in range(parts):
+            self.send.append([(seg[r * El + p * Ep], seg[r * El + (p + 1) * Ep] - seg[r * El + p * Ep])
+                              for r in range(W)])
+            runs, off = [], 0
+            for src in range(W):
+                n = sum(rr[src * El + p * Ep:src * El + (p + 1) * Ep])
+                runs.append((off, n))
+                off += n
+            self.recv.append(runs)
 
-    def out(self, buf: torch.Tensor, rows_back: int) -> torch.Tensor:
-        """This rank's rows to their experts' ranks."""
-        if self.W == 1:
-            return buf
-        if self.mode == "slots":
-            return exchange_rows(buf, self.group)
-        return exchange_rows_varsplit(buf, self.send, self.recv, rows_back, self.group)
+    def part_rows(self) -> int:
+        """Rows of one part's expert-side buffer (an upper bound in the packed layout)."""
+        return self.W * self.Ep * self.Cp
 
-    def back(self, buf: torch.Tensor, rows_back: int) -> torch.Tensor:
-        """Expert-side rows back to the ranks that own the tokens."""
+    def out(self, buf: torch.Tensor, p: int):
+        """Start sending part p of this rank's rows to their experts' ranks.
+        Returns (expert-side buffer of part p, pending)."""
         if self.W == 1:
-            return buf
-        if self.mode == "slots":
-            return exchange_rows(buf, self.group)
-        return exchange_rows_varsplit(buf, self.recv, self.send, rows_back, self.group)
+            return buf, _Pending([])
+        dst = torch.empty((self.part_rows(),) + tuple(buf.shape[1:]), dtype=buf.dtype, device=buf.device)
+        if self.parts == 1:
+            if self.mode == "slots":
+                w = dist.all_to_all_single(dst, buf.contiguous(), group=self.group, async_op=True)
+            else:
+                sizes_in = [n for _, n in self.send[0]]
+                sizes_out = [n for _, n in self.recv[0]]
+                w = dist.all_to_all_single(dst[:sum(sizes_out)], buf[:sum(sizes_in)], output_split_sizes=sizes_out,
+                                           input_split_sizes=sizes_in, group=self.group, async_op=True)
+            return dst, _Pending([w])
+        sends = [buf[s:s + n] for s, n in self.send[p]]
+        recvs = [dst[s:s + n] for s, n in self.recv[p]]
+        return dst, self._p2p(sends, recvs)
+
+    def back(self, buf: torch.Tensor, dst: torch.Tensor | None, p: int):
+        """Start sending part p's expert-side rows back into the token-side
+        buffer dst (at the rows they left from).  Returns (dst, pending); with
+        one rank dst is buf itself."""
+        if self.W == 1:
+            return buf, _Pending([])
+        if self.parts == 1:
+            if self.mode == "slots":
+                w = dist.all_to_all_single(dst, buf, group=self.group, async_op=True)
+            else:
+                sizes_in = [n for _, n in self.recv[0]]
+                sizes_out = [n for _, n in self.send[0]]
+                w = dist.all_to_all_single(dst[:sum(sizes_out)], buf[:sum(sizes_in)], output_split_sizes=sizes_out,
+                                           input_split_sizes=sizes_in, group=self.group, async_op=True)
+            return dst, _Pending([w])
+        sends = [buf[s:s + n] for s, n in self.recv[p]]
+        recvs = [dst[s:s + n] for s, n in self.send[p]]
+        return dst, self._p2p(sends, recvs)
+
+    def _p2p(self, sends: list, recvs: list) -> _Pending:
+        ops = []
+        for r in range(self.W):
+            if r == self.me:
+                if recvs[r].shape[0]:
+                    recvs[r].copy_(sends[r])
+                continue
+            if sends[r].shape[0]:
+                ops.append(dist.P2POp(dist.isend, sends[r], self.peers[r], self.group))
+            if recvs[r].shape[0]:
+                ops.append(dist.P2POp(dist.irecv, recvs[r], self.peers[r], self.group))
+        return _Pending(dist.batch_isend_irecv(ops) if ops else [])
 
 
 class _EPMoEFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x2, gate_w, bias, meta, wgu_stack, wd_stack, *local_weights):
-        E, El, k, C, lbw, Fdim, W, group, mode = meta
+        E, El, k, C, lbw, Fdim, W, group, mode, parts, gemm_sms = meta
         L = SLOTS if mode == "slots" else _lib.ATS_MOE_PACKED
         T, H = x2.shape
         dev = x2.device
@@ -132,7 +212,6 @@ class _EPMoEFn(torch.autograd.Function):
         logits, rws, w32 = router_forward(x2, gate_w, bias)
         wsb = _lib.query("ats_moe_workspace_bytes", T, E, k, C, L)
         R = _lib.query("ats_moe_max_rows", T, E, k, C, L)  # this rank's permuted rows (upper bound)
-        RX = W * El * Cp  # received rows (upper bound)
         ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
         gates = torch.empty((T, k), dtype=torch.float32, device=dev)
         idx = torch.empty((T, k), dtype=torch.int64, device=dev)
@@ -148,55 +227,82 @@ class _EPMoEFn(torch.autograd.Function):
         xs = torch.empty((R, H), dtype=x2.dtype, device=dev)
         _lib.call("ats_moe_gather", x2.data_ptr(), xs.data_ptr(), dt, T, H, E, k, C, L, ws.data_ptr(), wsb, st)
         recv_kept = exchange_counts(kept, group) if W > 1 else kept
-        ex = _Exchange(mode, W, El, Cp, group, seg_start, recv_kept)
-        xr = ex.out(xs, RX)
-        segb = _lib.query("ats_moe_ep_segments_bytes", W, El)
-        seg = torch.empty(segb, dtype=torch.uint8, device=dev)
-        _lib.call("ats_moe_ep_segments", recv_kept.data_ptr(), W, El, C, L, seg.data_ptr(), segb, st)
-        RR = xr.shape[0]
-        h = torch.empty((RR, 2 * Fdim), dtype=x2.dtype, device=dev)
-        a = torch.empty((RR, Fdim), dtype=x2.dtype, device=dev)
-        yr = torch.empty((RR, H), dtype=x2.dtype, device=dev)
-        _lib.call("ats_moe_ep_experts_fwd", xr.data_ptr(), wgu_stack.data_ptr(), wd_stack.data_ptr(), h.data_ptr(),
-                  a.data_ptr(), yr.data_ptr(), dt, W, El, C, H, Fdim, seg.data_ptr(), segb, st)
-        ys = ex.back(yr, R)
+        ex = _Exchange(mode, W, El, Cp, group, seg_start, recv_kept, parts)
+        P, Ep = ex.parts, ex.Ep
+        pend = [ex.out(xs, p) for p in range(P)]
+        segb = _lib.query("ats_moe_ep_segments_bytes", W, Ep)
+        rk = recv_kept.view(W, El)
+        ys = torch.empty((R, H), dtype=x2.dtype, device=dev) if W > 1 else None
+        keep, backs = [], []
+        with _lib.gemm_sm_limit(gemm_sms if P > 1 else 0):
+            for p in range(P):
+                seg = torch.empty(segb, dtype=torch.uint8, device=dev)
+                _lib.call("ats_moe_ep_segments", rk[:, p * Ep:(p + 1) * Ep].contiguous().data_ptr(), W, Ep, C, L,
+                          seg.data_ptr(), segb, st)
+                xr, arrived = pend[p]
+                arrived.wait()
+                RR = xr.shape[0]
+                h = torch.empty((RR, 2 * Fdim), dtype=x2.dtype, device=dev)
+                a = torch.empty((RR, Fdim), dtype=x2.dtype, device=dev)
+                yr = torch.empty((RR, H), dtype=x2.dtype, device=dev)
+                _lib.call("ats_moe_ep_experts_fwd", xr.data_ptr(), wgu_stack[p * Ep].data_ptr(),
+                          wd_stack[p * Ep].data_ptr(), h.data_ptr(), a.data_ptr(), yr.data_ptr(), dt, W, Ep, C, H,
+                          Fdim, seg.data_ptr(), segb, st)
+                ys, sent = ex.back(yr, ys, p)
+                backs.append(sent)
+                keep += [xr, h, a, seg]
+        for b in backs:
+            b.wait()
         out = torch.empty((T, H), dtype=x2.dtype, device=dev)
         _lib.call("ats_moe_combine", ys.data_ptr(), out.data_ptr(), dt, T, H, E, k, C, L, ws.data_ptr(), wsb, st)
-        ctx.save_for_backward(logits, gates, idx, ws, xr, h, a, ys, seg, wgu_stack, wd_stack, x2, w32, rws)
-        ctx.meta = (E, El, k, C, lbw, Fdim, W, group, T, H, wsb, R, RX, segb, gate_w.dtype, L)
+        ctx.save_for_backward(logits, gates, idx, ws, ys, wgu_stack, wd_stack, x2, w32, rws, *keep)
+        ctx.meta = (E, El, k, C, lbw, Fdim, W, group, T, H, wsb, R, segb, gate_w.dtype, L, gemm_sms)
         ctx.ex = ex
         ctx.mark_non_differentiable(util, counts, idx)
         return out, aux, util, counts, idx
 
     @staticmethod
     def backward(ctx, dout, daux, _dutil, _dcounts, _didx):
-        logits, gates, idx, ws, xr, h, a, ys, seg, wgu_stack, wd_stack, x2, w32, rws = ctx.saved_tensors
-        E, El, k, C, lbw, Fdim, W, group, T, H, wsb, R, RX, segb, gate_dtype, L = ctx.meta
+        logits, gates, idx, ws, ys, wgu_stack, wd_stack, x2, w32, rws, *keep = ctx.saved_tensors
+        E, El, k, C, lbw, Fdim, W, group, T, H, wsb, R, segb, gate_dtype, L, gemm_sms = ctx.meta
         ex = ctx.ex
-        dev = xr.device
-        dt = _lib.dtype_code(xr.dtype)
-        st = _lib.stream_of(xr)
+        P, Ep = ex.parts, ex.Ep
+        dev = x2.device
+        dt = _lib.dtype_code(x2.dtype)
+        st = _lib.stream_of(x2)
         if dout is None:
-            dout = torch.zeros((T, H), dtype=xr.dtype, device=dev)
-        dout = dout.to(xr.dtype).contiguous()
-        dys = torch.empty((R, H), dtype=xr.dtype, device=dev)
+            dout = torch.zeros((T, H), dtype=x2.dtype, device=dev)
+        dout = dout.to(x2.dtype).contiguous()
+        dys = torch.empty((R, H), dtype=x2.dtype, device=dev)
         dgate_row = torch.empty(R, dtype=torch.float32, device=dev)
         _lib.call("ats_moe_combine_bwd", dout.data_ptr(), ys.data_ptr(), dys.data_ptr(), dgate_row.data_ptr(), dt,
                   T, H, E, k, C, L, ws.data_ptr(), wsb, st)
-        dyr = ex.out(dys, RX)
-        RR = xr.shape[0]
-        dh = torch.empty((RR, 2 * Fdim), dtype=xr.dtype, device=dev)
-        dxr = torch.empty((RR, H), dtype=xr.dtype, device=dev)
+        pend = [ex.out(dys, p) for p in range(P)]
+        dxs = torch.empty((R, H), dtype=x2.dtype, device=dev) if W > 1 else None
         dwgu = torch.empty_like(wgu_stack)
         dwd = torch.empty_like(wd_stack)
-        _lib.call("ats_moe_ep_experts_bwd", dyr.data_ptr(), xr.data_ptr(), h.data_ptr(), a.data_ptr(),
-                  wgu_stack.data_ptr(), wd_stack.data_ptr(), dh.data_ptr(), dxr.data_ptr(), dwgu.data_ptr(),
-                  dwd.data_ptr(), dt, W, El, C, H, Fdim, seg.data_ptr(), segb, st)
-        dxs = ex.back(dxr, R)
+        backs = []
+        with _lib.gemm_sm_limit(gemm_sms if P > 1 else 0):
+            for p in range(P):
+                xr, h, a, seg = keep[4 * p:4 * p + 4]
+                dyr, arrived = pend[p]
+                arrived.wait()
+                RR = xr.shape[0]
+                dh = torch.empty((RR, 2 * Fdim), dtype=x2.dtype, device=dev)
+                dxr = torch.empty((RR, H), dtype=x2.dtype, device=dev)
+                _lib.call("ats_moe_ep_experts_bwd", dyr.data_ptr(), xr.data_ptr(), h.data_ptr(), a.data_ptr(),
+                          wgu_stack[p * Ep].data_ptr(), wd_stack[p * Ep].data_ptr(), dh.data_ptr(), dxr.data_ptr(),
+                          dwgu[p * Ep].data_ptr(), dwd[p * Ep].data_ptr(), dt, W, Ep, C, H, Fdim, seg.data_ptr(),
+                          segb, st)
+                dxs, sent = ex.back(dxr, dxs, p)
+                backs.append(sent)
+        # the routing gradient needs only the gate-row gradients: it runs while the last part returns
         dlogits = torch.empty((T, E), dtype=torch.float32, device=dev)
         daux_t = daux.to(torch.float32).contiguous() if daux is not None else None
         _lib.call("ats_moe_route_bwd", logits.data_ptr(), gates.data_ptr(), idx.data_ptr(), dgate_row.data_ptr(),
                   _lib.ptr(daux_t), dlogits.data_ptr(), T, E, k, C, L, float(lbw), ws.data_ptr(), wsb, st)
+        for b in backs:
+            b.wait()
         dx, dgate_w = router_backward(dlogits, x2, w32, rws, dxs, ws, wsb, (T, E, k, C, L), True)
         grads = [dwgu[e] for e in range(El)] + [dwd[e] for e in range(El)]
         return (dx, dgate_w.to(gate_dtype), None, None, None, None, *grads)
@@ -228,11 +334,16 @@ class ExpertParallelMoE(nn.Module):
     ``experts[i]`` is expert ``rank*E_local + i``; ``gate`` is the replicated
     router (Linear(hidden, num_experts)).  With a world size of 1 it is the
     single-GPU layer on the expert-parallel path.  ``rebalance`` relabels the
-    experts so that the ranks carry about equal expected rows."""
+    experts so that the ranks carry about equal expected rows.
+
+    ``overlap_parts`` P runs the local experts in P parts so that each part's
+    row transfers overlap the expert GEMMs of the others (P must divide the
+    local expert count; 1 exchanges everything at once); meanwhile the GEMMs
+    leave ``comm_sms`` SMs to the transfers."""
 
     def __init__(self, hidden_size: int, intermediate_size: int, num_experts: int, num_layers: int,
                  top_k: int = 2, capacity_factor: float = 1.25, load_balancing_weight: float = 0.01,
-                 group=None, exchange: str = "packed") -> None:
+                 group=None, exchange: str = "packed", overlap_parts: int = 1, comm_sms: int = 16) -> None:
         super().__init__()
         if exchange not in ("packed", "slots"):
             raise ValueError(f"exchange must be 'packed' or 'slots', got {exchange!r}")
@@ -247,6 +358,12 @@ class ExpertParallelMoE(nn.Module):
         self.hidden_size = hidden_size
         self.num_experts = num_experts
         self.num_local_experts = num_experts // self.world
+        if overlap_parts < 1 or self.num_local_experts % overlap_parts != 0:
+            raise ValueError(f"overlap_parts={overlap_parts} must divide the {self.num_local_experts} local experts")
+        if comm_sms < 0:
+            raise ValueError(f"comm_sms must be >= 0, got {comm_sms}")
+        self.overlap_parts = overlap_parts
+        self.comm_sms = comm_sms
         self.top_k = top_k
         self.capacity_factor = capacity_factor
         self.load_balancing_weight = load_balancing_weight
@@ -302,6 +419,12 @@ class ExpertParallelMoE(nn.Module):
                 getattr(ex, name).weight.copy_(full[perm[self.rank * El + i]])
         return torch.as_tensor(perm, dtype=torch.int64)
 
+    def _gemm_sms(self, device: torch.device) -> int:
+        """SMs the expert GEMMs may use while transfers are in flight."""
+        if self.overlap_parts == 1 or self.world == 1 or self.comm_sms == 0:
+            return 0
+        return max(1, torch.cuda.get_device_properties(device).multi_processor_count - self.comm_sms)
+
     def router_logits(self, flat_x: torch.Tensor) -> torch.Tensor:
         """The float32 logits forward() routes on (without a logit bias)."""
         with torch.no_grad():
@@ -322,7 +445,8 @@ class ExpertParallelMoE(nn.Module):
         if wgu[0].dtype != flat.dtype:
             raise TypeError(f"MoE: token dtype {flat.dtype} does not match expert weight dtype {wgu[0].dtype}")
         meta = (self.num_experts, self.num_local_experts, self.top_k, cap, self.load_balancing_weight,
-                wgu[0].shape[0] // 2, self.world, self.group, self.exchange)
+                wgu[0].shape[0] // 2, self.world, self.group, self.exchange, self.overlap_parts,
+                self._gemm_sms(flat.device))
         bias = logit_bias.detach().float().contiguous() if logit_bias is not None else None
         out, aux, util, counts, _ = _EPMoEFn.apply(flat, self.gate.weight, bias, meta, stacked(wgu), stacked(wd),
                                                    *wgu, *wd)

@@ -578,12 +578,18 @@ class MoEEPWorkload(Workload):
     metric = "moe_ep_layer_fwd_bwd_tokens_per_s"
     unit = "tokens/s"
     T, H, F, E, K, CF = 32768, 4096, 1408, 64, 2, 1.25
+    PARTS, COMM_SMS = 1, 16  # exchange overlap: expert parts, SMs left to the transfers
+
+    def parts(self):
+        return self.PARTS if self.world > 1 else 1
 
     def config(self):
         return {"workload": "expert-parallel MoE layer fwd+bwd, 32768 tokens per GPU, hidden 4096, 64 experts "
                             "top-2, ffn 1408, capacity factor 1.25, Zipf(1.1) router-logit bias, bf16, fp32 router",
                 "experts_per_gpu": self.E // self.world,
-                "exchange": "NCCL all_to_all_single of the kept rows (variable splits)" if self.world > 1
+                "exchange": ("NCCL all_to_all_single of the kept rows (variable splits)" if self.parts() == 1 else
+                             f"kept rows in {self.parts()} expert parts, NCCL per-peer sends overlapped with the "
+                             f"expert GEMMs on {self.COMM_SMS} fewer SMs") if self.world > 1
                             else "none (all experts local)",
                 "expert_placement": "balanced by the rows each expert received on a calibration forward "
                                     "(ExpertParallelMoE.rebalance)",
@@ -594,7 +600,8 @@ class MoEEPWorkload(Workload):
         from ats_v2_b200.ep import ExpertParallelMoE
         t.manual_seed(2000 + self.rank)
         with t.device("cuda"):
-            layer = ExpertParallelMoE(self.H, self.F, self.E, num_layers=2, top_k=self.K, capacity_factor=self.CF)
+            layer = ExpertParallelMoE(self.H, self.F, self.E, num_layers=2, top_k=self.K, capacity_factor=self.CF,
+                                      overlap_parts=self.parts(), comm_sms=self.COMM_SMS)
         with t.no_grad():
             # the router weight is replicated: every rank draws the same one
             layer.gate.weight.copy_(0.02 * t.randn(layer.gate.weight.shape, generator=t.Generator().manual_seed(7)))

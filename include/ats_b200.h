@@ -52,6 +52,15 @@ ATS_API const char* ats_last_error_message(void);
  * all threads); a benchmark reads it before and after a timed region. */
 ATS_API uint64_t ats_kernel_launches(void);
 
+/* Cap on the CTAs (one per SM) that the persistent tensor-core GEMMs launch
+ * with, for launches made later by the calling host thread; 0 (the default)
+ * means every SM.  A caller that overlaps a collective on another stream with
+ * the expert GEMMs leaves SMs free for it: a GEMM CTA occupies a whole SM, so
+ * a collective launched beside a full-width GEMM would wait for its end.
+ * No reference counterpart (DeepSpeed's all-to-all does not overlap). */
+ATS_API int ats_set_gemm_sm_limit(int sms);
+ATS_API int ats_gemm_sm_limit(void);
+
 /* ------------------------------------------------------------------ RMSNorm
  * y = round(x * rsqrt(mean(x^2) + eps) * w), float32 arithmetic, one rounding
  * to x's dtype.  Replaces RMSNorm.forward, ats/model/norm.py:23-31 (F.rms_norm).

@@ -65,6 +65,22 @@ def test_bad_arguments_rejected_before_any_launch():
     assert b"workspace too small" in lib.ats_last_error_message()
 
 
+def test_gemm_sm_limit_is_per_thread_host_state():
+    import threading
+    lib = _lib.load()
+    assert lib.ats_gemm_sm_limit() == 0
+    with _lib.gemm_sm_limit(100):
+        assert lib.ats_gemm_sm_limit() == 100
+        seen = []
+        t = threading.Thread(target=lambda: seen.append(lib.ats_gemm_sm_limit()))
+        t.start()
+        t.join()
+        assert seen == [0]  # another thread's launches are not limited
+    assert lib.ats_gemm_sm_limit() == 0
+    assert lib.ats_set_gemm_sm_limit(-1) == _lib.ATS_EBADARG
+    assert lib.ats_gemm_sm_limit() == 0
+
+
 def test_workspace_queries():
     lib = _lib.load()
     assert lib.ats_rmsnorm_bwd_workspace_bytes(16384, 4096) >= 148 * 4096 * 4

@@ -6,7 +6,8 @@ here they run on CPU tensors: every row of a send buffer carries its
 a stand-in expert doubles the rows, and the return exchange must bring each
 row back to its original slot.  The packed exchange (variable splits of
 back-to-back expert segments) gets the same check, and also that only the
-kept rows and their padding to 128 travel.  A last test makes one rank leave before the
+kept rows and their padding to 128 travel; so does the exchange in parts
+(per-peer sends of each part's row runs, all parts in flight at once).  A last test makes one rank leave before the
 collective: its peer must fail within the process group's timeout instead of
 waiting for ever."""
 
@@ -72,15 +73,24 @@ def _exchange_worker(rank, world, port, E_local, cap, H, errq):
         raise
 
 
-def _packed_worker(rank, world, port, E_local, cap, H, errq):
-    """Packed exchange: each rank's experts are back-to-back segments of
-    align128(kept) rows; only those rows travel, with variable splits."""
+def _parts_worker(rank, world, port, mode, parts, E_local, cap, H, errq):
+    """Exchange in parts: part p carries the rows of local experts
+    [p*E_local/P, (p+1)*E_local/P) of every rank.  Packed: each rank's experts
+    are back-to-back segments of align128(kept) rows and only those rows
+    travel; slots: the [E][Cp] buffer.  Each part's expert-side buffer must
+    hold its (source, expert) segments in that order, and the return trip must
+    put every row back where it left from."""
     try:
         _init(rank, world, port)
         E = world * E_local
+        Cp = slot_rows(cap)
+        Ep = E_local // parts
         g = torch.Generator().manual_seed(10 + rank)
         kept = torch.randint(0, cap + 1, (E,), generator=g, dtype=torch.int32)
-        pad = [(int(c) + 127) // 128 * 128 for c in kept]
+        if mode == "packed":
+            pad = [(int(c) + 127) // 128 * 128 for c in kept]
+        else:
+            pad = [Cp] * E
         seg_start = torch.tensor([0] + list(torch.tensor(pad).cumsum(0)), dtype=torch.int32)
         R = int(seg_start[-1])
         send = torch.zeros(max(R, 1), H)
@@ -89,22 +99,29 @@ def _packed_worker(rank, world, port, E_local, cap, H, errq):
                 send[int(seg_start[e]) + s, :3] = torch.tensor([rank, e, s], dtype=torch.float32)
                 send[int(seg_start[e]) + s, 3:] = 1.0
         recv_kept = exchange_counts(kept)
-        ex = _Exchange("packed", world, E_local, slot_rows(cap), None, seg_start, recv_kept)
-        RX = world * E_local * slot_rows(cap)
-        recv = ex.out(send, RX)
-        assert sum(ex.recv) <= RX
-        row = 0
-        for src in range(world):
-            for el in range(E_local):
-                e = rank * E_local + el
-                c = int(recv_kept[src * E_local + el])
-                for s in range(c):
-                    got = recv[row + s]
-                    assert (int(got[0]), int(got[1]), int(got[2])) == (src, e, s)
-                assert bool((recv[row + c:row + (c + 127) // 128 * 128] == 0).all())  # padding rows are zero
-                row += (c + 127) // 128 * 128
-        assert row == sum(ex.recv)
-        back = ex.back(recv * 2.0, send.shape[0])
+        ex = _Exchange(mode, world, E_local, Cp, None, seg_start, recv_kept, parts)
+        assert (ex.parts, ex.Ep) == (parts, Ep)
+        pending = [ex.out(send, p) for p in range(parts)]  # every part in flight at once
+        back = torch.zeros_like(send)
+        for p in range(parts):
+            recv, arrived = pending[p]
+            arrived.wait()
+            assert recv.shape[0] == world * Ep * Cp
+            row = 0
+            for src in range(world):
+                for el in range(p * Ep, (p + 1) * Ep):
+                    e = rank * E_local + el
+                    c = int(recv_kept[src * E_local + el])
+                    for s in range(c):
+                        got = recv[row + s]
+                        assert (int(got[0]), int(got[1]), int(got[2])) == (src, e, s)
+                    span = (c + 127) // 128 * 128 if mode == "packed" else Cp
+                    assert bool((recv[row + c:row + span] == 0).all())  # padding rows are zero
+                    row += span
+            if mode == "packed" or parts > 1:
+                assert row == sum(n for _, n in ex.recv[p])
+            back, returned = ex.back(recv * 2.0, back, p)  # a stand-in expert, then the return trip
+            returned.wait()
         assert torch.equal(back[:R], send[:R] * 2.0)
         dist.barrier()
         dist.destroy_process_group()
@@ -172,12 +189,14 @@ def test_row_and_count_exchange_round_trip(E_local, cap, H):
     assert errq.empty()
 
 
-@pytest.mark.parametrize("E_local,cap,H", [(2, 5, 8), (3, 300, 4)])
-def test_packed_exchange_sends_only_kept_segments_and_round_trips(E_local, cap, H):
+@pytest.mark.parametrize("mode,parts,world,E_local,cap,H", [("packed", 1, 2, 2, 5, 8), ("packed", 1, 2, 3, 300, 4),
+                                                           ("packed", 2, 2, 4, 300, 4), ("slots", 2, 2, 2, 5, 8),
+                                                           ("packed", 3, 3, 3, 130, 4)])
+def test_exchange_in_parts_sends_only_kept_segments_and_round_trips(mode, parts, world, E_local, cap, H):
     ctx = mp.get_context("spawn")
     errq = ctx.SimpleQueue()
-    mp.start_processes(_packed_worker, args=(2, _free_port(), E_local, cap, H, errq), nprocs=2, join=True,
-                       start_method="spawn")
+    mp.start_processes(_parts_worker, args=(world, _free_port(), mode, parts, E_local, cap, H, errq), nprocs=world,
+                       join=True, start_method="spawn")
     assert errq.empty()
 
 

@@ -6,7 +6,9 @@ rows of a segment are the same and in the same order; only their place in the
 buffer differs).  Two ranks (runs when two GPUs are visible): every rank's output
 and input gradient equal the oracle run on that rank's own tokens with all
 experts' weights, and every local expert's weight gradient equals the sum
-over both ranks' tokens -- DeepSpeed's local-capacity semantics."""
+over both ranks' tokens -- DeepSpeed's local-capacity semantics.  The
+exchange in overlapped parts (with the GEMMs held to fewer SMs) must give
+bit-equal results to the exchange in one piece."""
 
 from __future__ import annotations
 
@@ -113,7 +115,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _two_rank_worker(rank, world, port, errq, exchange):
+def _two_rank_worker(rank, world, port, errq, exchange, parts):
     from oracle import moe as omoe
     try:
         os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -127,20 +129,37 @@ def _two_rank_worker(rank, world, port, errq, exchange):
         full_gate = torch.nn.Linear(H, E, bias=False)
         full_experts = torch.nn.ModuleList([bmoe.SwiGLU(H, F) for _ in range(E)])
         _init_weights(full_gate, full_experts, 5)  # identical on both ranks
-        ep = ExpertParallelMoE(H, F, E, num_layers=2, top_k=k, capacity_factor=cf, exchange=exchange)
-        with torch.no_grad():
-            ep.gate.weight.copy_(full_gate.weight)
-            for i in range(El):
-                ep.experts[i].gate_up_proj.weight.copy_(full_experts[rank * El + i].gate_up_proj.weight)
-                ep.experts[i].down_proj.weight.copy_(full_experts[rank * El + i].down_proj.weight)
-        ep = ep.cuda()
-        ep.experts.to(torch.bfloat16)
+        def layer(p):
+            m = ExpertParallelMoE(H, F, E, num_layers=2, top_k=k, capacity_factor=cf, exchange=exchange,
+                                  overlap_parts=p, comm_sms=20)
+            with torch.no_grad():
+                m.gate.weight.copy_(full_gate.weight)
+                for i in range(El):
+                    m.experts[i].gate_up_proj.weight.copy_(full_experts[rank * El + i].gate_up_proj.weight)
+                    m.experts[i].down_proj.weight.copy_(full_experts[rank * El + i].down_proj.weight)
+            m = m.cuda()
+            m.experts.to(torch.bfloat16)
+            return m
+
+        ep = layer(parts)
         gx = torch.Generator(device="cuda").manual_seed(100 + rank)
         x = torch.randn(1, T, H, device="cuda", generator=gx).bfloat16().requires_grad_()
         gout = torch.randn(1, T, H, device="cuda", generator=gx).bfloat16()
         out, aux = ep(x)
         torch.autograd.backward([out, aux], [gout, torch.ones_like(aux)])
         torch.cuda.synchronize()
+        if parts > 1:
+            # the overlapped exchange moves the same rows to the same GEMMs: bit-equal to one part
+            one = layer(1)
+            x1 = x.detach().clone().requires_grad_()
+            out1, aux1 = one(x1)
+            torch.autograd.backward([out1, aux1], [gout, torch.ones_like(aux1)])
+            torch.cuda.synchronize()
+            assert torch.equal(out, out1) and torch.equal(aux, aux1) and torch.equal(x.grad, x1.grad)
+            for i in range(El):
+                assert torch.equal(ep.experts[i].gate_up_proj.weight.grad, one.experts[i].gate_up_proj.weight.grad)
+                assert torch.equal(ep.experts[i].down_proj.weight.grad, one.experts[i].down_proj.weight.grad)
+            assert torch.equal(ep.gate.weight.grad, one.gate.weight.grad)
         # oracle on this rank's tokens with all experts' (bf16) weights
         xs = np32(x.view(T, H))
         logits = np32(ep.router_logits(x.detach().view(T, H)))
@@ -168,11 +187,11 @@ def _two_rank_worker(rank, world, port, errq, exchange):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("exchange", ["packed", "slots"])
-def test_two_ranks_match_the_oracle_on_local_tokens(exchange):
+@pytest.mark.parametrize("exchange,parts", [("packed", 1), ("slots", 1), ("packed", 2), ("slots", 4)])
+def test_two_ranks_match_the_oracle_on_local_tokens(exchange, parts):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     errq = ctx.SimpleQueue()
-    mp.start_processes(_two_rank_worker, args=(2, _free_port(), errq, exchange), nprocs=2, join=True,
+    mp.start_processes(_two_rank_worker, args=(2, _free_port(), errq, exchange, parts), nprocs=2, join=True,
                        start_method="spawn")
     assert errq.empty()

@@ -50,6 +50,45 @@ def test_dense_path_is_bit_identical_to_the_routed_single_expert(T, H, F):
     close(res[0][0], y_ref, "bf16")
 
 
+def _swiglu_c_abi(x, wgu, wd, dy):
+    """Forward and backward through the C ABI on this thread (autograd would run
+    the backward on its own device thread, outside a thread's SM limit)."""
+    T, H = x.shape
+    F = wd.shape[1]
+    st = _lib.stream_of(x)
+    R = _lib.query("ats_swiglu_rows", T)
+    wsb = _lib.query("ats_swiglu_workspace_bytes")
+    ws = torch.empty(wsb, dtype=torch.uint8, device="cuda")
+    h = torch.empty(R, 2 * F, dtype=x.dtype, device="cuda")
+    a = torch.empty(R, F, dtype=x.dtype, device="cuda")
+    y = torch.empty(T, H, dtype=x.dtype, device="cuda")
+    _lib.call("ats_swiglu_fwd", x.data_ptr(), wgu.data_ptr(), wd.data_ptr(), h.data_ptr(), a.data_ptr(),
+              y.data_ptr(), _lib.ATS_BF16, T, H, F, ws.data_ptr(), wsb, st)
+    dh, dx = torch.empty_like(h), torch.empty_like(x)
+    dwgu, dwd = torch.empty_like(wgu), torch.empty_like(wd)
+    _lib.call("ats_swiglu_bwd", dy.data_ptr(), x.data_ptr(), h.data_ptr(), a.data_ptr(), wgu.data_ptr(),
+              wd.data_ptr(), dh.data_ptr(), dx.data_ptr(), dwgu.data_ptr(), dwd.data_ptr(), _lib.ATS_BF16, T, H, F,
+              ws.data_ptr(), wsb, st)
+    return y, dx, dwgu, dwd
+
+
+@pytest.mark.parametrize("sms", [1, 37, 147])
+def test_fewer_gemm_ctas_give_the_same_bits(sms):
+    """A GEMM held to fewer SMs computes the same tiles in another order
+    across its CTAs: every output is bit-equal."""
+    T, H, F = 1100, 256, 384
+    wgu, wd = _weights(H, F, 7)
+    g = torch.Generator(device="cuda").manual_seed(8)
+    x = torch.randn(T, H, device="cuda", generator=g).bfloat16()
+    dy = torch.randn(T, H, device="cuda", generator=g).bfloat16()
+    full = _swiglu_c_abi(x, wgu, wd, dy)
+    with _lib.gemm_sm_limit(sms):
+        assert _lib.query("ats_gemm_sm_limit") == sms
+        held = _swiglu_c_abi(x, wgu, wd, dy)
+    for name, a, b in zip(("out", "dx", "dw_gate_up", "dw_down"), full, held):
+        assert torch.equal(a, b), f"{name}: differs with the GEMMs on {sms} SMs"
+
+
 def test_swiglu_module_forward_and_backward_against_the_oracle():
     T, H, F = 512, 256, 512
     torch.manual_seed(0)
