@@ -40,6 +40,8 @@ then leave ``comm_sms`` SMs to the transfers.
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 import torch.distributed as dist
 from torch import nn
@@ -199,6 +201,229 @@ class _Exchange:
         return _Pending(dist.batch_isend_irecv(ops) if ops else [])
 
 
+def peer_plan(kept: list[list[int]], Cp: int, El: int, parts: int, me: int):
+    """Copy plan of the peer-memory exchange for rank ``me``.
+
+    kept[s][e] is the rows source rank s keeps for global expert e.  Clamped to
+    [0, Cp] and rounded up to 128 they are the segment sizes of the packed
+    layout: the token side of rank s holds its segments in global expert order,
+    and part p of rank d's expert side holds, for each source in rank order,
+    the segments of d's local experts [p*Ep, (p+1)*Ep), Ep = El/parts (the
+    layout ``ats_moe_ep_segments`` reads).  Returns (seg, out, back):
+      seg[s]   the token-side segment starts of rank s ([E+1]);
+      out[p]   (d, src_row, dst_row, rows): my token-side rows [src_row, +rows)
+               go to rows [dst_row, +rows) of part p on rank d;
+      back[p]  (s, src_row, dst_row, rows): rows [src_row, +rows) of my part p
+               go back to rows [dst_row, +rows) of rank s's token side.
+    Runs of zero rows are left out."""
+    W = len(kept)
+    E = W * El
+    if El % parts != 0:
+        raise ValueError(f"{El} local experts do not split into {parts} parts")
+    Ep = El // parts
+    rnd = [[_rounded(int(c), Cp) for c in row] for row in kept]
+    seg = []
+    for s in range(W):
+        acc = [0]
+        for e in range(E):
+            acc.append(acc[-1] + rnd[s][e])
+        seg.append(acc)
+
+    def run(s, d, p):  # rows source s holds for part p of rank d
+        return sum(rnd[s][d * El + p * Ep:d * El + (p + 1) * Ep])
+
+    out, back = [], []
+    for p in range(parts):
+        o = []
+        for d in range(W):
+            n = run(me, d, p)
+            if n:
+                o.append((d, seg[me][d * El + p * Ep], sum(run(s, d, p) for s in range(me)), n))
+        out.append(o)
+        b, off = [], 0
+        for src in range(W):
+            n = run(src, me, p)
+            if n:
+                b.append((src, off, seg[src][me * El + p * Ep], n))
+            off += n
+        back.append(b)
+    return seg, out, back
+
+
+_OPENED: dict[bytes, list] = {}  # IPC handle -> [mapped base, opens]; one open per handle and process
+
+
+def _ipc_open(handle: bytes) -> int:
+    ent = _OPENED.get(handle)
+    if ent is None:
+        base = ctypes.c_void_p()
+        _lib.call("ats_ipc_open", handle, ctypes.byref(base))
+        ent = _OPENED[handle] = [base.value, 0]
+    ent[1] += 1
+    return ent[0]
+
+
+def _ipc_close(handle: bytes) -> None:
+    ent = _OPENED[handle]
+    ent[1] -= 1
+    if ent[1] == 0:
+        del _OPENED[handle]
+        _lib.call("ats_ipc_close", ctypes.c_void_p(ent[0]))
+
+
+def _copies(copies: list, stream) -> None:
+    """copies: (dst address, src address, bytes); one copy-engine copy each."""
+    n = len(copies)
+    if n == 0:
+        return
+    dst = (ctypes.c_void_p * n)(*[c[0] for c in copies])
+    src = (ctypes.c_void_p * n)(*[c[1] for c in copies])
+    nb = (ctypes.c_uint64 * n)(*[c[2] for c in copies])
+    _lib.call("ats_peer_copies", n, dst, src, nb, stream.cuda_stream)
+
+
+class _PeerSet:
+    """The buffers other ranks copy into for one forward and backward of the
+    layer, allocated on every rank and mapped by every peer:
+      xr  [rows_x, H]  expert-side input rows (part p from row p*W*Ep*Cp)
+      ys  [rows_t, H]  token-side expert outputs
+      dyr [rows_x, H]  expert-side output gradients
+      dxs [rows_t, H]  token-side input gradients
+    ``addr[r][name]`` is rank r's buffer as an address in this process."""
+
+    NAMES = ("xr", "ys", "dyr", "dxs")
+
+    def __init__(self, rows_x: int, rows_t: int, H: int, dtype, device, group, W: int, me: int):
+        self.rows_x, self.rows_t, self.H, self.dtype = rows_x, rows_t, H, dtype
+        self.local = {n: torch.empty((rows_x if n in ("xr", "dyr") else rows_t, H), dtype=dtype, device=device)
+                      for n in self.NAMES}
+        hb = _lib.query("ats_ipc_handle_bytes")
+        mine = {}
+        for n, t in self.local.items():
+            h = ctypes.create_string_buffer(hb)
+            off, size = ctypes.c_uint64(), ctypes.c_uint64()
+            _lib.call("ats_ipc_export", t.data_ptr(), h, ctypes.byref(off), ctypes.byref(size))
+            mine[n] = (h.raw, off.value)
+        every = [None] * W
+        dist.all_gather_object(every, mine, group=group)
+        self.handles: list[bytes] = []
+        self.addr: list[dict] = []
+        for r in range(W):
+            if r == me:
+                self.addr.append({n: t.data_ptr() for n, t in self.local.items()})
+                continue
+            a = {}
+            for n, (h, off) in every[r].items():
+                a[n] = _ipc_open(h) + off
+                self.handles.append(h)
+            self.addr.append(a)
+        self.busy = False
+
+    def fits(self, rows_x: int, rows_t: int, H: int, dtype) -> bool:
+        return rows_x <= self.rows_x and rows_t <= self.rows_t and H == self.H and dtype == self.dtype
+
+    def close(self) -> None:
+        for h in self.handles:
+            _ipc_close(h)
+        self.handles = []
+
+
+class _PeerState:
+    """Per-layer state of the peer-memory exchange: a pool of buffer sets (one
+    per forward whose backward has not run yet), the streams the copies run on,
+    the one-element tensor of the collectives that order them and a pinned
+    buffer for the counts."""
+
+    MAX_SETS = 4
+
+    def __init__(self):
+        self.sets: list[_PeerSet] = []
+        self.streams: dict = {}
+        self.flags: dict = {}
+        self.host: torch.Tensor | None = None
+
+    def acquire(self, rows_x, rows_t, H, dtype, device, group, W, me) -> _PeerSet:
+        # every rank makes the same choice: the sizes are maxima over the ranks and
+        # the ranks run the same sequence of forwards and backwards
+        for ps in self.sets:
+            if not ps.busy and ps.fits(rows_x, rows_t, H, dtype):
+                ps.busy = True
+                return ps
+        for ps in [q for q in self.sets if not q.busy]:
+            ps.close()
+            self.sets.remove(ps)
+        if len(self.sets) >= self.MAX_SETS:
+            raise RuntimeError(f"ExpertParallelMoE: {len(self.sets)} forwards are waiting for their backward; the "
+                               f"peer exchange keeps one buffer set per forward")
+        ps = _PeerSet(rows_x, rows_t, H, dtype, device, group, W, me)
+        ps.busy = True
+        self.sets.append(ps)
+        return ps
+
+    @staticmethod
+    def release(ps: _PeerSet) -> None:
+        ps.busy = False
+
+    def copy_streams(self, device, W: int) -> list:
+        """One stream per destination rank, so that the copies to different
+        ranks (and this rank's own rows) run on different copy engines at once;
+        the first also carries the collectives that order them."""
+        key = (device, W)
+        if key not in self.streams:
+            self.streams[key] = [torch.cuda.Stream(device=device) for _ in range(W)]
+        return self.streams[key]
+
+    def host_buffer(self, n: int) -> torch.Tensor:
+        """Pinned int32 host buffer for the counts every forward reads."""
+        if self.host is None or self.host.numel() < n:
+            self.host = torch.empty(n, dtype=torch.int32, pin_memory=True)
+        return self.host[:n]
+
+    def flag(self, device) -> torch.Tensor:
+        if device not in self.flags:
+            self.flags[device] = torch.zeros(1, dtype=torch.int32, device=device)
+        return self.flags[device]
+
+    def close(self) -> None:
+        for ps in self.sets:
+            ps.close()
+        self.sets = []
+
+
+def _route(x2, gate_w, bias, E, k, C, L, lbw):
+    """Route this rank's tokens over all E experts into layout L.  R is this
+    rank's permuted rows (an upper bound); kept [E] and seg_start [E+1] (int32,
+    device) describe the segments the gather writes."""
+    T, H = x2.shape
+    dev = x2.device
+    st = _lib.stream_of(x2)
+    logits, rws, w32 = router_forward(x2, gate_w, bias)
+    wsb = _lib.query("ats_moe_workspace_bytes", T, E, k, C, L)
+    R = _lib.query("ats_moe_max_rows", T, E, k, C, L)
+    ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+    gates = torch.empty((T, k), dtype=torch.float32, device=dev)
+    idx = torch.empty((T, k), dtype=torch.int64, device=dev)
+    aux = torch.empty((), dtype=torch.float32, device=dev)
+    util = torch.empty(E, dtype=torch.float32, device=dev)
+    counts = torch.empty(E, dtype=torch.int32, device=dev)
+    _lib.call("ats_moe_route_plan", logits.data_ptr(), T, E, k, C, L, float(lbw), gates.data_ptr(),
+              idx.data_ptr(), aux.data_ptr(), util.data_ptr(), counts.data_ptr(), ws.data_ptr(), wsb, st)
+    kept = torch.empty(E, dtype=torch.int32, device=dev)
+    seg_start = torch.empty(E + 1, dtype=torch.int32, device=dev)
+    _lib.call("ats_moe_plan_export", ws.data_ptr(), wsb, T, E, k, C, L, seg_start.data_ptr(), None,
+              kept.data_ptr(), st)
+    return logits, rws, w32, ws, wsb, R, gates, idx, aux, util, counts, kept, seg_start
+
+
+def _gather(x2, ws, wsb, R, E, k, C, L):
+    """This rank's kept rows, gathered by segment: [R, H]."""
+    T, H = x2.shape
+    xs = torch.empty((R, H), dtype=x2.dtype, device=x2.device)
+    _lib.call("ats_moe_gather", x2.data_ptr(), xs.data_ptr(), _lib.dtype_code(x2.dtype), T, H, E, k, C, L,
+              ws.data_ptr(), wsb, _lib.stream_of(x2))
+    return xs
+
+
 class _EPMoEFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x2, gate_w, bias, meta, wgu_stack, wd_stack, *local_weights):
@@ -209,23 +434,9 @@ class _EPMoEFn(torch.autograd.Function):
         dt = _lib.dtype_code(x2.dtype)
         st = _lib.stream_of(x2)
         Cp = slot_rows(C)
-        logits, rws, w32 = router_forward(x2, gate_w, bias)
-        wsb = _lib.query("ats_moe_workspace_bytes", T, E, k, C, L)
-        R = _lib.query("ats_moe_max_rows", T, E, k, C, L)  # this rank's permuted rows (upper bound)
-        ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
-        gates = torch.empty((T, k), dtype=torch.float32, device=dev)
-        idx = torch.empty((T, k), dtype=torch.int64, device=dev)
-        aux = torch.empty((), dtype=torch.float32, device=dev)
-        util = torch.empty(E, dtype=torch.float32, device=dev)
-        counts = torch.empty(E, dtype=torch.int32, device=dev)
-        _lib.call("ats_moe_route_plan", logits.data_ptr(), T, E, k, C, L, float(lbw), gates.data_ptr(),
-                  idx.data_ptr(), aux.data_ptr(), util.data_ptr(), counts.data_ptr(), ws.data_ptr(), wsb, st)
-        kept = torch.empty(E, dtype=torch.int32, device=dev)
-        seg_start = torch.empty(E + 1, dtype=torch.int32, device=dev)
-        _lib.call("ats_moe_plan_export", ws.data_ptr(), wsb, T, E, k, C, L, seg_start.data_ptr(), None,
-                  kept.data_ptr(), st)
-        xs = torch.empty((R, H), dtype=x2.dtype, device=dev)
-        _lib.call("ats_moe_gather", x2.data_ptr(), xs.data_ptr(), dt, T, H, E, k, C, L, ws.data_ptr(), wsb, st)
+        (logits, rws, w32, ws, wsb, R, gates, idx, aux, util, counts, kept,
+         seg_start) = _route(x2, gate_w, bias, E, k, C, L, lbw)
+        xs = _gather(x2, ws, wsb, R, E, k, C, L)
         recv_kept = exchange_counts(kept, group) if W > 1 else kept
         ex = _Exchange(mode, W, El, Cp, group, seg_start, recv_kept, parts)
         P, Ep = ex.parts, ex.Ep
@@ -308,6 +519,190 @@ class _EPMoEFn(torch.autograd.Function):
         return (dx, dgate_w.to(gate_dtype), None, None, None, None, *grads)
 
 
+def _issue_copies(plan_p: list, streams: list, dst_addr, src_base: int, rowb: int) -> None:
+    """Copies of one part, grouped by the rank on the other side: entry
+    (r, src_row, dst_row, rows) goes on streams[r] to dst_addr(r) + dst_row."""
+    by_rank: dict[int, list] = {}
+    for r, src_row, dst_row, n in plan_p:
+        by_rank.setdefault(r, []).append((dst_addr(r) + dst_row * rowb, src_base + src_row * rowb, n * rowb))
+    for r, cps in by_rank.items():
+        with torch.cuda.stream(streams[r]):
+            _copies(cps, streams[r])
+
+
+def _barrier_after(streams: list, flag: torch.Tensor, group):
+    """A collective on streams[0] after the copies queued so far on every stream:
+    when it completes, every rank's copies have landed."""
+    for st in streams[1:]:
+        streams[0].wait_stream(st)
+    with torch.cuda.stream(streams[0]):
+        return dist.all_reduce(flag, group=group, async_op=True)
+
+
+def _follow(streams: list, cur, *tensors) -> None:
+    """Make every copy stream wait for the current stream's work so far, and
+    keep the tensors' memory until the copies that read them have run."""
+    for st in streams:
+        st.wait_stream(cur)
+        for t in tensors:
+            t.record_stream(st)
+
+
+class _EPPeerFn(torch.autograd.Function):
+    """The expert-parallel layer with the rows copied by the copy engines
+    straight into the peers' buffers (packed layout, in overlapped parts), one
+    stream per destination rank.
+
+    Ordering between ranks comes from collectives on the layer's group, each
+    issued on the stream whose work it must follow:
+      - the all-gather of the kept counts, issued right after routing: every
+        rank's earlier work on its buffers (the last backward) is done when it
+        completes, and the copies wait for it.  Its result reaches the host
+        through a pinned buffer while the gather kernel runs, so the host plans
+        the copies in the gather's shadow;
+      - a one-element all-reduce after each part's copies: when it completes,
+        every rank's rows of that part have landed, and the expert GEMMs of the
+        part wait for it;
+      - one more after the return copies, before the combine (forward) or the
+        router backward (backward)."""
+
+    @staticmethod
+    def forward(ctx, x2, gate_w, bias, meta, wgu_stack, wd_stack, *local_weights):
+        E, El, k, C, lbw, Fdim, W, group, parts, gemm_sms, state, me, will_backward = meta
+        L = _lib.ATS_MOE_PACKED
+        T, H = x2.shape
+        dev = x2.device
+        dt = _lib.dtype_code(x2.dtype)
+        st = _lib.stream_of(x2)
+        Cp = slot_rows(C)
+        cur = torch.cuda.current_stream(dev)
+        cs = state.copy_streams(dev, W)
+        flag = state.flag(dev)
+        (logits, rws, w32, ws, wsb, R, gates, idx, aux, util, counts, kept,
+         seg_start) = _route(x2, gate_w, bias, E, k, C, L, lbw)
+        mine = torch.cat([kept, torch.tensor([Cp, R], dtype=torch.int32, device=dev), seg_start])
+        allv = torch.empty((W, 2 * E + 3), dtype=torch.int32, device=dev)
+        gathered = dist.all_gather_into_tensor(allv, mine, group=group, async_op=True)
+        xs = _gather(x2, ws, wsb, R, E, k, C, L)
+        host_buf = state.host_buffer(allv.numel())
+        with torch.cuda.stream(cs[0]):
+            gathered.wait()
+            allv.record_stream(cs[0])
+            host_buf.copy_(allv.view(-1), non_blocking=True)
+            ready = torch.cuda.Event()
+            ready.record(cs[0])
+        gathered.wait()  # the copies below follow the current stream
+        ready.synchronize()
+        host = host_buf.tolist()
+        rows = [host[s_ * (2 * E + 3):(s_ + 1) * (2 * E + 3)] for s_ in range(W)]
+        if len({r[E] for r in rows}) != 1:
+            raise ValueError("ExpertParallelMoE: every rank must route the same number of tokens")
+        seg, out_plan, back_plan = peer_plan([r[:E] for r in rows], Cp, El, parts, me)
+        if any(seg[s_] != rows[s_][E + 2:] for s_ in range(W)):
+            raise RuntimeError("ExpertParallelMoE: the packed layout differs from the copy plan")
+        rows_t = max(r[E + 1] for r in rows)
+        ps = state.acquire(W * El * Cp, rows_t, H, x2.dtype, dev, group, W, me)
+        Ep = El // parts
+        part_rows = W * Ep * Cp
+        rowb = H * x2.element_size()
+        for p in range(parts):
+            for d, src_row, dst_row, n in out_plan[p]:
+                assert src_row + n <= R and dst_row + n <= part_rows
+            for s_, src_row, dst_row, n in back_plan[p]:
+                assert src_row + n <= part_rows and dst_row + n <= rows_t
+        _follow(cs, cur, xs)
+        arrived = []
+        for p in range(parts):
+            _issue_copies(out_plan[p], cs, lambda d, p=p: ps.addr[d]["xr"] + p * part_rows * rowb, xs.data_ptr(),
+                          rowb)
+            arrived.append(_barrier_after(cs, flag, group))
+        segb = _lib.query("ats_moe_ep_segments_bytes", W, Ep)
+        keep = []
+        with _lib.gemm_sm_limit(gemm_sms):
+            for p in range(parts):
+                seg_ws = torch.empty(segb, dtype=torch.uint8, device=dev)
+                rk = allv[:, me * El + p * Ep:me * El + (p + 1) * Ep].contiguous()
+                _lib.call("ats_moe_ep_segments", rk.data_ptr(), W, Ep, C, L, seg_ws.data_ptr(), segb, st)
+                arrived[p].wait()
+                xr = ps.local["xr"][p * part_rows:(p + 1) * part_rows]
+                h = torch.empty((part_rows, 2 * Fdim), dtype=x2.dtype, device=dev)
+                a = torch.empty((part_rows, Fdim), dtype=x2.dtype, device=dev)
+                yr = torch.empty((part_rows, H), dtype=x2.dtype, device=dev)
+                _lib.call("ats_moe_ep_experts_fwd", xr.data_ptr(), wgu_stack[p * Ep].data_ptr(),
+                          wd_stack[p * Ep].data_ptr(), h.data_ptr(), a.data_ptr(), yr.data_ptr(), dt, W, Ep, C, H,
+                          Fdim, seg_ws.data_ptr(), segb, st)
+                _follow(cs, cur, yr)
+                _issue_copies(back_plan[p], cs, lambda s_: ps.addr[s_]["ys"], yr.data_ptr(), rowb)
+                keep += [h, a, seg_ws]
+        _barrier_after(cs, flag, group).wait()
+        out = torch.empty((T, H), dtype=x2.dtype, device=dev)
+        _lib.call("ats_moe_combine", ps.local["ys"].data_ptr(), out.data_ptr(), dt, T, H, E, k, C, L, ws.data_ptr(),
+                  wsb, st)
+        ctx.save_for_backward(logits, gates, idx, ws, wgu_stack, wd_stack, x2, w32, rws, *keep)
+        ctx.meta = (E, El, k, C, lbw, Fdim, W, group, T, H, wsb, R, segb, gate_w.dtype, gemm_sms, parts, part_rows)
+        ctx.plans = (out_plan, back_plan)
+        ctx.ps, ctx.state = ps, state
+        if not will_backward:
+            state.release(ps)
+        ctx.mark_non_differentiable(util, counts, idx)
+        return out, aux, util, counts, idx
+
+    @staticmethod
+    def backward(ctx, dout, daux, _dutil, _dcounts, _didx):
+        logits, gates, idx, ws, wgu_stack, wd_stack, x2, w32, rws, *keep = ctx.saved_tensors
+        E, El, k, C, lbw, Fdim, W, group, T, H, wsb, R, segb, gate_dtype, gemm_sms, parts, part_rows = ctx.meta
+        out_plan, back_plan = ctx.plans
+        ps, state = ctx.ps, ctx.state
+        L = _lib.ATS_MOE_PACKED
+        Ep = El // parts
+        dev = x2.device
+        dt = _lib.dtype_code(x2.dtype)
+        st = _lib.stream_of(x2)
+        rowb = H * x2.element_size()
+        cur = torch.cuda.current_stream(dev)
+        cs = state.copy_streams(dev, W)
+        flag = state.flag(dev)
+        if dout is None:
+            dout = torch.zeros((T, H), dtype=x2.dtype, device=dev)
+        dout = dout.to(x2.dtype).contiguous()
+        dys = torch.empty((R, H), dtype=x2.dtype, device=dev)
+        dgate_row = torch.empty(R, dtype=torch.float32, device=dev)
+        _lib.call("ats_moe_combine_bwd", dout.data_ptr(), ps.local["ys"].data_ptr(), dys.data_ptr(),
+                  dgate_row.data_ptr(), dt, T, H, E, k, C, L, ws.data_ptr(), wsb, st)
+        _follow(cs, cur, dys)
+        arrived = []
+        for p in range(parts):
+            _issue_copies(out_plan[p], cs, lambda d, p=p: ps.addr[d]["dyr"] + p * part_rows * rowb, dys.data_ptr(),
+                          rowb)
+            arrived.append(_barrier_after(cs, flag, group))
+        dwgu = torch.empty_like(wgu_stack)
+        dwd = torch.empty_like(wd_stack)
+        with _lib.gemm_sm_limit(gemm_sms):
+            for p in range(parts):
+                h, a, seg_ws = keep[3 * p:3 * p + 3]
+                arrived[p].wait()
+                xr = ps.local["xr"][p * part_rows:(p + 1) * part_rows]
+                dyr = ps.local["dyr"][p * part_rows:(p + 1) * part_rows]
+                dh = torch.empty((part_rows, 2 * Fdim), dtype=x2.dtype, device=dev)
+                dxr = torch.empty((part_rows, H), dtype=x2.dtype, device=dev)
+                _lib.call("ats_moe_ep_experts_bwd", dyr.data_ptr(), xr.data_ptr(), h.data_ptr(), a.data_ptr(),
+                          wgu_stack[p * Ep].data_ptr(), wd_stack[p * Ep].data_ptr(), dh.data_ptr(), dxr.data_ptr(),
+                          dwgu[p * Ep].data_ptr(), dwd[p * Ep].data_ptr(), dt, W, Ep, C, H, Fdim, seg_ws.data_ptr(),
+                          segb, st)
+                _follow(cs, cur, dxr)
+                _issue_copies(back_plan[p], cs, lambda s_: ps.addr[s_]["dxs"], dxr.data_ptr(), rowb)
+        # the routing gradient needs only the gate-row gradients: it runs while the last part returns
+        dlogits = torch.empty((T, E), dtype=torch.float32, device=dev)
+        daux_t = daux.to(torch.float32).contiguous() if daux is not None else None
+        _lib.call("ats_moe_route_bwd", logits.data_ptr(), gates.data_ptr(), idx.data_ptr(), dgate_row.data_ptr(),
+                  _lib.ptr(daux_t), dlogits.data_ptr(), T, E, k, C, L, float(lbw), ws.data_ptr(), wsb, st)
+        _barrier_after(cs, flag, group).wait()
+        dx, dgate_w = router_backward(dlogits, x2, w32, rws, ps.local["dxs"], ws, wsb, (T, E, k, C, L), True)
+        state.release(ps)
+        grads = [dwgu[e] for e in range(El)] + [dwd[e] for e in range(El)]
+        return (dx, dgate_w.to(gate_dtype), None, None, None, None, *grads)
+
+
 def balanced_placement(load: list[float], world: int) -> list[int]:
     """A permutation perm of the experts such that rank r hosts the experts
     perm[r*E_local:(r+1)*E_local] and the ranks' summed loads are close:
@@ -336,17 +731,24 @@ class ExpertParallelMoE(nn.Module):
     single-GPU layer on the expert-parallel path.  ``rebalance`` relabels the
     experts so that the ranks carry about equal expected rows.
 
+    ``exchange`` says how rows cross between ranks: "packed" and "slots" are
+    NCCL all-to-alls (see ``_Exchange``); "peer" copies the packed rows with
+    the copy engines straight into buffers the peers mapped once (CUDA IPC),
+    so the transfers take no SMs and run beside the expert GEMMs.
     ``overlap_parts`` P runs the local experts in P parts so that each part's
     row transfers overlap the expert GEMMs of the others (P must divide the
     local expert count; 1 exchanges everything at once); meanwhile the GEMMs
-    leave ``comm_sms`` SMs to the transfers."""
+    leave ``comm_sms`` SMs to the collectives (default: 16 for the NCCL
+    exchanges, whose transfers run on SMs, none for "peer")."""
 
     def __init__(self, hidden_size: int, intermediate_size: int, num_experts: int, num_layers: int,
                  top_k: int = 2, capacity_factor: float = 1.25, load_balancing_weight: float = 0.01,
-                 group=None, exchange: str = "packed", overlap_parts: int = 1, comm_sms: int = 16) -> None:
+                 group=None, exchange: str = "packed", overlap_parts: int = 1, comm_sms: int | None = None) -> None:
         super().__init__()
-        if exchange not in ("packed", "slots"):
-            raise ValueError(f"exchange must be 'packed' or 'slots', got {exchange!r}")
+        if exchange not in ("packed", "slots", "peer"):
+            raise ValueError(f"exchange must be 'packed', 'slots' or 'peer', got {exchange!r}")
+        if comm_sms is None:
+            comm_sms = 0 if exchange == "peer" else 16
         self.exchange = exchange
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
@@ -364,6 +766,7 @@ class ExpertParallelMoE(nn.Module):
             raise ValueError(f"comm_sms must be >= 0, got {comm_sms}")
         self.overlap_parts = overlap_parts
         self.comm_sms = comm_sms
+        self._peer = _PeerState()
         self.top_k = top_k
         self.capacity_factor = capacity_factor
         self.load_balancing_weight = load_balancing_weight
@@ -421,9 +824,17 @@ class ExpertParallelMoE(nn.Module):
 
     def _gemm_sms(self, device: torch.device) -> int:
         """SMs the expert GEMMs may use while transfers are in flight."""
-        if self.overlap_parts == 1 or self.world == 1 or self.comm_sms == 0:
+        if self.world == 1 or self.comm_sms == 0 or (self.overlap_parts == 1 and self.exchange != "peer"):
             return 0
         return max(1, torch.cuda.get_device_properties(device).multi_processor_count - self.comm_sms)
+
+    def release_peer_buffers(self) -> None:
+        """Unmap the peers' exchange buffers (exchange="peer"; every rank, together,
+        with no forward waiting for its backward).  The next forward maps new ones."""
+        if self.world > 1 and self._peer.sets:
+            torch.cuda.synchronize()
+            dist.barrier(group=self.group)
+        self._peer.close()
 
     def router_logits(self, flat_x: torch.Tensor) -> torch.Tensor:
         """The float32 logits forward() routes on (without a logit bias)."""
@@ -444,12 +855,19 @@ class ExpertParallelMoE(nn.Module):
         wd = [e.down_proj.weight for e in self.experts]
         if wgu[0].dtype != flat.dtype:
             raise TypeError(f"MoE: token dtype {flat.dtype} does not match expert weight dtype {wgu[0].dtype}")
-        meta = (self.num_experts, self.num_local_experts, self.top_k, cap, self.load_balancing_weight,
-                wgu[0].shape[0] // 2, self.world, self.group, self.exchange, self.overlap_parts,
-                self._gemm_sms(flat.device))
         bias = logit_bias.detach().float().contiguous() if logit_bias is not None else None
-        out, aux, util, counts, _ = _EPMoEFn.apply(flat, self.gate.weight, bias, meta, stacked(wgu), stacked(wd),
-                                                   *wgu, *wd)
+        head = (self.num_experts, self.num_local_experts, self.top_k, cap, self.load_balancing_weight,
+                wgu[0].shape[0] // 2, self.world, self.group)
+        if self.exchange == "peer" and self.world > 1:
+            will_backward = torch.is_grad_enabled() and (flat.requires_grad or any(
+                p.requires_grad for p in self.parameters()))
+            meta = head + (self.overlap_parts, self._gemm_sms(flat.device), self._peer, self.rank, will_backward)
+            fn = _EPPeerFn
+        else:
+            mode = "packed" if self.exchange == "peer" else self.exchange
+            meta = head + (mode, self.overlap_parts, self._gemm_sms(flat.device))
+            fn = _EPMoEFn
+        out, aux, util, counts, _ = fn.apply(flat, self.gate.weight, bias, meta, stacked(wgu), stacked(wd), *wgu, *wd)
         self.last_expert_utilization = LazyUtilization(util)
         self.last_counts = counts
         return out.view(batch, seq, H), aux

@@ -578,19 +578,31 @@ class MoEEPWorkload(Workload):
     metric = "moe_ep_layer_fwd_bwd_tokens_per_s"
     unit = "tokens/s"
     T, H, F, E, K, CF = 32768, 4096, 1408, 64, 2, 1.25
-    PARTS, COMM_SMS = 1, 16  # exchange overlap: expert parts, SMs left to the transfers
+    # row exchange: the kept rows copied by the copy engines into the peers' mapped buffers,
+    # in 2 expert parts so that one part's transfers overlap the other's expert GEMMs
+    EXCHANGE, PARTS, COMM_SMS = "peer", 2, 0
 
     def parts(self):
         return self.PARTS if self.world > 1 else 1
+
+    def exchange_text(self):
+        if self.EXCHANGE == "peer":
+            how = "copy-engine copies of the kept rows into the peers' IPC-mapped buffers over NVLink"
+        elif self.EXCHANGE == "packed":
+            how = "NCCL all-to-all of the kept rows (variable splits)"
+        else:
+            how = "NCCL all-to-all of the capacity slots"
+        if self.parts() > 1:
+            how += f", in {self.parts()} expert parts overlapped with the expert GEMMs"
+        if self.COMM_SMS:
+            how += f" (GEMMs leave {self.COMM_SMS} SMs free)"
+        return how
 
     def config(self):
         return {"workload": "expert-parallel MoE layer fwd+bwd, 32768 tokens per GPU, hidden 4096, 64 experts "
                             "top-2, ffn 1408, capacity factor 1.25, Zipf(1.1) router-logit bias, bf16, fp32 router",
                 "experts_per_gpu": self.E // self.world,
-                "exchange": ("NCCL all_to_all_single of the kept rows (variable splits)" if self.parts() == 1 else
-                             f"kept rows in {self.parts()} expert parts, NCCL per-peer sends overlapped with the "
-                             f"expert GEMMs on {self.COMM_SMS} fewer SMs") if self.world > 1
-                            else "none (all experts local)",
+                "exchange": self.exchange_text() if self.world > 1 else "none (all experts local)",
                 "expert_placement": "balanced by the rows each expert received on a calibration forward "
                                     "(ExpertParallelMoE.rebalance)",
                 "per_rank": "32768 tokens per GPU (weak scaling)", "l2": "inputs larger than L2"}
@@ -601,7 +613,7 @@ class MoEEPWorkload(Workload):
         t.manual_seed(2000 + self.rank)
         with t.device("cuda"):
             layer = ExpertParallelMoE(self.H, self.F, self.E, num_layers=2, top_k=self.K, capacity_factor=self.CF,
-                                      overlap_parts=self.parts(), comm_sms=self.COMM_SMS)
+                                      exchange=self.EXCHANGE, overlap_parts=self.parts(), comm_sms=self.COMM_SMS)
         with t.no_grad():
             # the router weight is replicated: every rank draws the same one
             layer.gate.weight.copy_(0.02 * t.randn(layer.gate.weight.shape, generator=t.Generator().manual_seed(7)))

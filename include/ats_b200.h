@@ -294,6 +294,24 @@ ATS_API int ats_moe_ep_experts_bwd(const void* dy, const void* xr, const void* h
 ATS_API int ats_moe_ep_status(const void* seg_workspace, size_t seg_workspace_bytes, int W, int E_local,
                       int* status);
 
+/* Peer-memory row exchange.  Instead of NCCL all-to-alls, a rank can copy
+ * its rows straight into the receive buffers of the experts' ranks with the
+ * copy engines (no SMs taken, so the copies run beside the expert GEMMs).
+ * ats_ipc_export gives the CUDA IPC handle (ats_ipc_handle_bytes() bytes) of
+ * the allocation holding ptr, ptr's offset in it and the allocation's size;
+ * a peer process maps it with ats_ipc_open (and ats_ipc_close when done; one
+ * open per handle and process).  ats_peer_copies issues n copies
+ * dst[i] <- src[i] of bytes[i] bytes on the stream (one cudaMemcpyAsync each;
+ * any of them may be a mapped peer address).  The caller orders them against
+ * the peers' use of the buffers (a collective before and after).  No
+ * reference counterpart: DeepSpeed exchanges with NCCL all-to-alls. */
+ATS_API size_t ats_ipc_handle_bytes(void);
+ATS_API int ats_ipc_export(const void* ptr, void* handle, uint64_t* offset, uint64_t* alloc_bytes);
+ATS_API int ats_ipc_open(const void* handle, void** base);
+ATS_API int ats_ipc_close(void* base);
+ATS_API int ats_peer_copies(int n, void* const* dst, const void* const* src, const uint64_t* bytes,
+                            void* stream);
+
 /* ------------------------------------------------------- dense SwiGLU FFN
  * SwiGLU.forward (ats/model/ffn.py:37-45): y = down(silu(g) * u), [g, u] =
  * chunk(x . w_gate_up^T, 2), for bf16 x [T, hidden], w_gate_up [2F, hidden],

@@ -81,6 +81,23 @@ def test_gemm_sm_limit_is_per_thread_host_state():
     assert lib.ats_gemm_sm_limit() == 0
 
 
+def test_peer_exchange_entry_points_check_arguments_on_the_host():
+    import ctypes
+    lib = _lib.load()
+    assert lib.ats_ipc_handle_bytes() == 64  # sizeof(cudaIpcMemHandle_t)
+    h = ctypes.create_string_buffer(64)
+    off, size = ctypes.c_uint64(), ctypes.c_uint64()
+    assert lib.ats_ipc_export(None, h, ctypes.byref(off), ctypes.byref(size)) == _lib.ATS_EBADARG
+    assert lib.ats_ipc_open(None, None) == _lib.ATS_EBADARG
+    assert lib.ats_ipc_close(None) == _lib.ATS_EBADARG
+    assert lib.ats_peer_copies(-1, None, None, None, None) == _lib.ATS_EBADARG
+    assert lib.ats_peer_copies(2, None, None, None, None) == _lib.ATS_EBADARG
+    zero = (ctypes.c_uint64 * 1)(0)
+    nul = (ctypes.c_void_p * 1)(None)
+    assert lib.ats_peer_copies(1, nul, nul, zero, None) == _lib.ATS_OK  # empty copies issue nothing
+    assert lib.ats_peer_copies(0, None, None, None, None) == _lib.ATS_OK
+
+
 def test_workspace_queries():
     lib = _lib.load()
     assert lib.ats_rmsnorm_bwd_workspace_bytes(16384, 4096) >= 148 * 4096 * 4

@@ -23,7 +23,10 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from ats_v2_b200.ep import ExpertParallelMoE, _Exchange, balanced_placement, exchange_counts, exchange_rows, slot_rows
+import numpy as np
+
+from ats_v2_b200.ep import (ExpertParallelMoE, _Exchange, balanced_placement, exchange_counts, exchange_rows, peer_plan,
+                            slot_rows)
 
 
 def _free_port() -> int:
@@ -198,6 +201,60 @@ def test_exchange_in_parts_sends_only_kept_segments_and_round_trips(mode, parts,
     mp.start_processes(_parts_worker, args=(world, _free_port(), mode, parts, E_local, cap, H, errq), nprocs=world,
                        join=True, start_method="spawn")
     assert errq.empty()
+
+
+@pytest.mark.parametrize("W,El,parts,cap", [(2, 4, 2, 300), (3, 2, 1, 5), (4, 2, 2, 130), (8, 8, 4, 257),
+                                            (2, 1, 1, 1)])
+def test_peer_copy_plan_builds_the_packed_expert_side_layout(W, El, parts, cap):
+    """Every rank's copy plan, applied to simulated buffers of all ranks, must
+    give each part of each rank's expert side the (source, expert) segments
+    in order -- the layout the NCCL packed exchange delivers and the segment
+    table reads -- and the return copies must bring every row home."""
+    E = W * El
+    Cp = slot_rows(cap)
+    Ep = El // parts
+    part_rows = W * Ep * Cp
+    rng = np.random.default_rng(W * 100 + El * 10 + parts)
+    kept = rng.integers(0, cap + 1, size=(W, E))
+    kept[0, :El] = 0  # a source that keeps nothing for rank 0's experts
+    rnd = (np.minimum(kept, Cp) + 127) // 128 * 128
+    xs = []
+    for s_ in range(W):
+        seg0 = np.concatenate([[0], np.cumsum(rnd[s_])])
+        buf = np.zeros((max(int(seg0[-1]), 1), 3), dtype=np.int64)
+        for e in range(E):
+            for r in range(int(kept[s_, e])):
+                buf[seg0[e] + r] = (s_ + 1, e + 1, r + 1)
+        xs.append(buf)
+    plans = [peer_plan(kept.tolist(), Cp, El, parts, me) for me in range(W)]
+    xr = [np.full((W * El * Cp, 3), -1, dtype=np.int64) for _ in range(W)]
+    for me in range(W):
+        seg, out, _ = plans[me]
+        assert seg[me] == [0] + np.cumsum(rnd[me]).tolist()
+        for p in range(parts):
+            for d, src, dst, n in out[p]:
+                assert n > 0 and src + n <= xs[me].shape[0] and dst + n <= part_rows
+                xr[d][p * part_rows + dst:p * part_rows + dst + n] = xs[me][src:src + n]
+    for d in range(W):
+        for p in range(parts):
+            row = p * part_rows
+            for src in range(W):
+                for i in range(p * Ep, (p + 1) * Ep):
+                    e = d * El + i
+                    c = int(kept[src, e])
+                    for r in range(c):
+                        assert tuple(xr[d][row + r]) == (src + 1, e + 1, r + 1)
+                    assert (xr[d][row + c:row + int(rnd[src, e])] == 0).all()  # padding rows arrive as zeros
+                    row += int(rnd[src, e])
+    ys = [np.full_like(b, -1) for b in xs]
+    for me in range(W):
+        _, _, back = plans[me]
+        for p in range(parts):
+            for s_, src, dst, n in back[p]:
+                ys[s_][dst:dst + n] = 2 * xr[me][p * part_rows + src:p * part_rows + src + n]
+    for s_ in range(W):
+        n = int(rnd[s_].sum())
+        assert (ys[s_][:n] == 2 * xs[s_][:n]).all()
 
 
 def test_balanced_placement_spreads_the_load():

@@ -7,8 +7,9 @@ buffer differs).  Two ranks (runs when two GPUs are visible): every rank's outpu
 and input gradient equal the oracle run on that rank's own tokens with all
 experts' weights, and every local expert's weight gradient equals the sum
 over both ranks' tokens -- DeepSpeed's local-capacity semantics.  The
-exchange in overlapped parts (with the GEMMs held to fewer SMs) must give
-bit-equal results to the exchange in one piece."""
+exchange in overlapped parts (with the GEMMs held to fewer SMs), and the
+peer-memory exchange (copy-engine copies into IPC-mapped peer buffers), must
+give bit-equal results to the NCCL exchange in one piece."""
 
 from __future__ import annotations
 
@@ -129,8 +130,8 @@ def _two_rank_worker(rank, world, port, errq, exchange, parts):
         full_gate = torch.nn.Linear(H, E, bias=False)
         full_experts = torch.nn.ModuleList([bmoe.SwiGLU(H, F) for _ in range(E)])
         _init_weights(full_gate, full_experts, 5)  # identical on both ranks
-        def layer(p):
-            m = ExpertParallelMoE(H, F, E, num_layers=2, top_k=k, capacity_factor=cf, exchange=exchange,
+        def layer(p, mode=exchange):
+            m = ExpertParallelMoE(H, F, E, num_layers=2, top_k=k, capacity_factor=cf, exchange=mode,
                                   overlap_parts=p, comm_sms=20)
             with torch.no_grad():
                 m.gate.weight.copy_(full_gate.weight)
@@ -148,9 +149,10 @@ def _two_rank_worker(rank, world, port, errq, exchange, parts):
         out, aux = ep(x)
         torch.autograd.backward([out, aux], [gout, torch.ones_like(aux)])
         torch.cuda.synchronize()
-        if parts > 1:
-            # the overlapped exchange moves the same rows to the same GEMMs: bit-equal to one part
-            one = layer(1)
+        if parts > 1 or exchange == "peer":
+            # the overlapped and the peer-memory exchanges move the same rows to the same GEMMs:
+            # bit-equal to the NCCL exchange in one piece
+            one = layer(1, "packed" if exchange == "peer" else exchange)
             x1 = x.detach().clone().requires_grad_()
             out1, aux1 = one(x1)
             torch.autograd.backward([out1, aux1], [gout, torch.ones_like(aux1)])
@@ -160,6 +162,23 @@ def _two_rank_worker(rank, world, port, errq, exchange, parts):
                 assert torch.equal(ep.experts[i].gate_up_proj.weight.grad, one.experts[i].gate_up_proj.weight.grad)
                 assert torch.equal(ep.experts[i].down_proj.weight.grad, one.experts[i].down_proj.weight.grad)
             assert torch.equal(ep.gate.weight.grad, one.gate.weight.grad)
+        if exchange == "peer":
+            # buffer sets are reused: a forward without backward, then a second step, give the same bits
+            with torch.no_grad():
+                out_ng, _ = ep(x.detach())
+            assert torch.equal(out_ng, out.detach())
+            first = (out.detach().clone(), x.grad.clone(), ep.experts[0].down_proj.weight.grad.clone())
+            for prm in ep.parameters():
+                prm.grad = None
+            x2 = x.detach().clone().requires_grad_()
+            out2, aux2 = ep(x2)
+            torch.autograd.backward([out2, aux2], [gout, torch.ones_like(aux2)])
+            torch.cuda.synchronize()
+            assert torch.equal(out2, first[0]) and torch.equal(x2.grad, first[1])
+            assert torch.equal(ep.experts[0].down_proj.weight.grad, first[2])
+            assert len(ep._peer.sets) == 1 and not ep._peer.sets[0].busy
+            ep.release_peer_buffers()
+            assert not ep._peer.sets
         # oracle on this rank's tokens with all experts' (bf16) weights
         xs = np32(x.view(T, H))
         logits = np32(ep.router_logits(x.detach().view(T, H)))
@@ -187,7 +206,8 @@ def _two_rank_worker(rank, world, port, errq, exchange, parts):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("exchange,parts", [("packed", 1), ("slots", 1), ("packed", 2), ("slots", 4)])
+@pytest.mark.parametrize("exchange,parts", [("packed", 1), ("slots", 1), ("packed", 2), ("slots", 4), ("peer", 1),
+                                            ("peer", 2)])
 def test_two_ranks_match_the_oracle_on_local_tokens(exchange, parts):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
