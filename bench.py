@@ -411,7 +411,7 @@ class MoEWorkload(Workload):
 
     def dominant(self):
         return {"kernel": "expert grouped GEMMs (whole layer fwd+bwd timed)", "flops": self.flops_per_step(),
-                "bound": "tensor", "traffic": (3718.7 + 1487.8) * 1e6,
+                "bound": "tensor", "traffic": (3523.6 + 1488.0) * 1e6,
                 "traffic_source": "profiles/moe_gemms_8192tok_h2048_e8_top2_f5632_bf16.md: DRAM read+write of "
                                   "the six expert GEMM launches of one step (ncu, cold caches)"}
 
@@ -510,7 +510,9 @@ class FFNWorkload(Workload):
 
     def dominant(self):
         return {"kernel": "dense SwiGLU GEMMs (whole FFN fwd+bwd timed)", "flops": self.flops_per_step(),
-                "bound": "tensor"}
+                "bound": "tensor", "traffic": (14244.6 + 2283.7) * 1e6,
+                "traffic_source": "profiles/ffn_gemms_16384tok_h4096_f11008_bf16.md: DRAM read+write of the six "
+                                  "GEMM launches of one step (ncu, cold caches)"}
 
     def e2e_setup(self):
         t = self.torch
