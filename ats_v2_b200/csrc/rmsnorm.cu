@@ -321,27 +321,28 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_stream_kernel(
   }
 }
 
-// dw[i] = round_W(sum_b partial[b][i]).  A block of 256 threads takes 32
-// columns; thread (c, q) sums the partial rows b = q, q+8, ... of column c
-// (independent loads, so the latency overlaps), and the eight sums are added
-// in q order: a fixed summation order, so dw is deterministic.
+// dw[i] = round_W(sum_b partial[b][i]).  A block of 1024 threads takes 32
+// columns; thread (c, q) sums the partial rows b = q, q+32, ... of column c
+// (a handful of independent loads, so the latency overlaps), and the 32 sums
+// are added in q order: a fixed summation order, so dw is deterministic.
+constexpr int kReduceLanes = 32;
 template <typename TW>
-__global__ void __launch_bounds__(256) dw_reduce_kernel(const float* __restrict__ partial, int nblk, int H,
-                                                        TW* __restrict__ dw) {
-  __shared__ float part[8][33];
+__global__ void __launch_bounds__(32 * kReduceLanes) dw_reduce_kernel(const float* __restrict__ partial, int nblk,
+                                                                      int H, TW* __restrict__ dw) {
+  __shared__ float part[kReduceLanes][33];
   const int cx = threadIdx.x & 31, q = threadIdx.x >> 5;
   const int col = blockIdx.x * 32 + cx;
   float s = 0.f;
   if (col < H) {
 #pragma unroll 4
-    for (int b = q; b < nblk; b += 8) s += partial[(size_t)b * H + col];
+    for (int b = q; b < nblk; b += kReduceLanes) s += partial[(size_t)b * H + col];
   }
   part[q][cx] = s;
   __syncthreads();
   if (q == 0 && col < H) {
     float t = 0.f;
 #pragma unroll
-    for (int r = 0; r < 8; ++r) t += part[r][cx];
+    for (int r = 0; r < kReduceLanes; ++r) t += part[r][cx];
     dw[col] = Cvt<TW>::from_f(t);
   }
 }
@@ -804,7 +805,7 @@ int launch_bwd(const void* dy, const void* x, const void* w, void* dx, void* dre
     cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     kfn<<<grid, kRingThreads, smem, st>>>(dyp, xp, wp, dxo, partial, rows, (int)H, eps);
     ATS_TRY(check_launch("rmsnorm_bwd_ring"));
-    dw_reduce_kernel<TW><<<(unsigned)((H + 31) / 32), 256, 0, st>>>(partial, grid, (int)H, static_cast<TW*>(dw));
+    dw_reduce_kernel<TW><<<(unsigned)((H + 31) / 32), 32 * kReduceLanes, 0, st>>>(partial, grid, (int)H, static_cast<TW*>(dw));
     return check_launch("rmsnorm_dw_reduce");
   }
   if (rows > 0) {
@@ -831,7 +832,7 @@ int launch_bwd(const void* dy, const void* x, const void* w, void* dx, void* dre
     ATS_TRY(check_launch("rmsnorm_bwd"));
   }
   const int nblk = rows > 0 ? blocks : 0;
-  dw_reduce_kernel<TW><<<(unsigned)((H + 31) / 32), 256, 0, st>>>(partial, nblk, (int)H, static_cast<TW*>(dw));
+  dw_reduce_kernel<TW><<<(unsigned)((H + 31) / 32), 32 * kReduceLanes, 0, st>>>(partial, nblk, (int)H, static_cast<TW*>(dw));
   return check_launch("rmsnorm_dw_reduce");
 }
 

@@ -60,7 +60,8 @@ def test_cpu_parity_workload_shape_f32():
     close(dw, edw, "f32", rtol=1e-5, atol=1e-4)
 
 
-@pytest.mark.parametrize("rows,H", [(1, 6), (3, 16), (7, 100), (33, 1000), (130, 4096), (5, 8192), (2, 12288)])
+@pytest.mark.parametrize("rows,H", [(1, 6), (3, 16), (7, 100), (33, 1000), (130, 4096), (5, 8192), (2, 12288),
+                                    (301, 2048), (777, 4096), (3, 4096)])
 @pytest.mark.parametrize("xd,wd", [("f32", "f32"), ("bf16", "f32"), ("bf16", "bf16"), ("f32", "bf16")])
 def test_shapes_and_dtypes(rows, H, xd, wd):
     seed = rows * 7919 + H
@@ -93,11 +94,12 @@ def test_zero_rows_and_strided_input():
     close(ys, ref, "f32")
 
 
-def test_dw_is_deterministic():
+@pytest.mark.parametrize("H", [1024, 2048, 4096])
+def test_dw_is_deterministic(H):
     torch.manual_seed(0)
-    x = torch.randn(4096, 1024, device="cuda", dtype=torch.bfloat16, requires_grad=True)
-    w = torch.nn.Parameter(torch.ones(1024, device="cuda"))
-    dy = torch.randn(4096, 1024, device="cuda", dtype=torch.bfloat16)
+    x = torch.randn(4096, H, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    w = torch.nn.Parameter(torch.ones(H, device="cuda"))
+    dy = torch.randn(4096, H, device="cuda", dtype=torch.bfloat16)
     grads = []
     for _ in range(2):
         w.grad = None
