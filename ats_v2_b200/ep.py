@@ -19,6 +19,10 @@ replicated.  One forward:
        exchange="slots": the capacity-slot layout [E][Cp] (Cp = capacity
          rounded up to 128), equal splits, no host synchronisation (what
          DeepSpeed's capacity-padded exchange does);
+       exchange="peer" (one node): the packed rows, copied by the copy
+         engines straight into receive buffers every peer mapped once through
+         CUDA IPC, with collectives as the ordering points (no SMs spent on
+         the transfers, so they overlap the expert GEMMs);
   3. the receiving rank runs its local experts on the received (source,
      expert) segments through a segment table that covers only their kept
      rows;
@@ -41,6 +45,7 @@ then leave ``comm_sms`` SMs to the transfers.
 from __future__ import annotations
 
 import ctypes
+import socket
 
 import torch
 import torch.distributed as dist
@@ -305,7 +310,11 @@ class _PeerSet:
             _lib.call("ats_ipc_export", t.data_ptr(), h, ctypes.byref(off), ctypes.byref(size))
             mine[n] = (h.raw, off.value)
         every = [None] * W
-        dist.all_gather_object(every, mine, group=group)
+        dist.all_gather_object(every, (socket.gethostname(), mine), group=group)
+        if len({host for host, _ in every}) != 1:
+            raise ValueError("ExpertParallelMoE(exchange='peer') maps the peers' memory with CUDA IPC, which needs "
+                             "every rank of the group on one node; use exchange='packed' across nodes")
+        every = [m for _, m in every]
         self.handles: list[bytes] = []
         self.addr: list[dict] = []
         for r in range(W):

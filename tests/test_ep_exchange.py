@@ -257,6 +257,47 @@ def test_peer_copy_plan_builds_the_packed_expert_side_layout(W, El, parts, cap):
         assert (ys[s_][:n] == 2 * xs[s_][:n]).all()
 
 
+def test_peer_buffer_pool_reuses_free_sets_and_bounds_waiting_forwards(monkeypatch):
+    """The pool behind exchange="peer": a forward takes a free set that fits,
+    else maps a new one (dropping free sets that no longer fit); a backward
+    gives its set back; forwards waiting for their backward are bounded."""
+    from ats_v2_b200 import ep as epm
+
+    made, closed = [], []
+
+    class FakeSet:
+        def __init__(self, rows_x, rows_t, H, dtype, device, group, W, me):
+            self.rows_x, self.rows_t, self.H, self.dtype = rows_x, rows_t, H, dtype
+            self.busy = False
+            made.append(self)
+
+        def fits(self, rows_x, rows_t, H, dtype):
+            return rows_x <= self.rows_x and rows_t <= self.rows_t and H == self.H and dtype == self.dtype
+
+        def close(self):
+            closed.append(self)
+
+    monkeypatch.setattr(epm, "_PeerSet", FakeSet)
+    st = epm._PeerState()
+    args = (None, None, 2, 0)
+    a = st.acquire(1024, 512, 64, torch.bfloat16, *args)
+    assert a.busy and made == [a]
+    st.release(a)
+    assert st.acquire(1000, 500, 64, torch.bfloat16, *args) is a  # smaller sizes fit the free set
+    b = st.acquire(1024, 512, 64, torch.bfloat16, *args)  # a is busy: a second set
+    assert b is not a and len(made) == 2
+    st.release(a)
+    st.release(b)
+    c = st.acquire(4096, 512, 64, torch.bfloat16, *args)  # grown: free sets that no longer fit are unmapped
+    assert closed == [a, b] and st.sets == [c]
+    for _ in range(epm._PeerState.MAX_SETS - 1):
+        st.acquire(4096, 512, 64, torch.bfloat16, *args)
+    with pytest.raises(RuntimeError, match="waiting for their backward"):
+        st.acquire(4096, 512, 64, torch.bfloat16, *args)
+    st.close()
+    assert st.sets == [] and len(closed) == 2 + epm._PeerState.MAX_SETS
+
+
 def test_balanced_placement_spreads_the_load():
     load = [float(2 ** (-i)) for i in range(16)]  # one expert far hotter than the rest
     for world in (1, 2, 4, 8):
