@@ -1,8 +1,8 @@
 """ats_v2_b200 -- B200 (sm_100a) kernels for the ats-v2 hot path.
 
-RMSNorm, rotary embedding and the MoE layer, forward and backward, as
-hand-written CUDA behind a C ABI (``include/ats_b200.h``,
-``libats_b200.so``), with PyTorch as the host.  The Python modules mirror
+RMSNorm, rotary embedding, the MoE layer and the MLA KV decompression GEMM,
+forward and backward, as hand-written CUDA behind a C ABI
+(``include/ats_b200.h``, ``libats_b200.so``), with PyTorch as the host.  The Python modules mirror
 the reference's ``ats/model`` interfaces:
 
     ats/model/norm.py         -> ats_v2_b200.norm        (RMSNorm)
@@ -12,6 +12,7 @@ the reference's ``ats/model`` interfaces:
     ats/model/moe.py          -> ats_v2_b200.moe         (MoELayer)
     ats/model/moe_triton.py   -> ats_v2_b200.moe_fused   (fused_moe_routing, fused_moe_dispatch)
     ats/model/ffn.py          -> ats_v2_b200.ffn         (SwiGLU)
+    ats/model/mla_triton.py   -> ats_v2_b200.mla_fused   (fused_mla_kv_decompress)
 
 All compute runs on CUDA tensors; CPU tensors raise.
 """

@@ -39,6 +39,12 @@ SIGNATURES: dict[str, tuple] = {
     "ats_last_error_message": (c_char_p, []),
     "ats_kernel_launches": (ctypes.c_uint64, []),
     "ats_set_gemm_sm_limit": (c_int, [c_int]),
+    "ats_gemm_supported": (c_int, [c_int, c_int64, c_int64, c_int64]),
+    "ats_gemm_workspace_bytes": (c_size_t, []),
+    "ats_gemm_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int64, c_int64, c_int64, c_void_p, c_size_t,
+                             c_void_p]),
+    "ats_gemm_bwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int64, c_int64, c_int64,
+                             c_void_p, c_size_t, c_void_p]),
     "ats_ipc_handle_bytes": (c_size_t, []),
     "ats_ipc_export": (c_int, [c_void_p, c_void_p, POINTER(ctypes.c_uint64), POINTER(ctypes.c_uint64)]),
     "ats_ipc_open": (c_int, [c_void_p, POINTER(c_void_p)]),

@@ -385,6 +385,41 @@ int ats_swiglu_bwd(const void* dy, const void* x, const void* h, const void* a, 
   return tc_experts_bwd(dy, x, h, a, w_gate_up, w_down, dh, dx, dw_gate_up, dw_down, 1, H, F, sg, st, T);
 }
 
+int ats_gemm_supported(ats_dtype dtype, int64_t M, int64_t N, int64_t K) {
+  return dense_supported(dtype, M, N, K) ? 1 : 0;
+}
+
+size_t ats_gemm_workspace_bytes(void) { return kDenseWsBytes; }
+
+int ats_gemm_fwd(const void* a, const void* b, void* c, ats_dtype dtype, int64_t M, int64_t N, int64_t K,
+                 void* workspace, size_t workspace_bytes, void* stream) {
+  if (!ats_gemm_supported(dtype, M, N, K))
+    return fail(ATS_EUNSUPPORTED, "gemm_fwd: needs bf16, M >= 128 and N, K multiples of 128 (M=%lld N=%lld K=%lld)",
+                (long long)M, (long long)N, (long long)K);
+  if (a == nullptr || b == nullptr || c == nullptr) return fail(ATS_EBADARG, "gemm_fwd: null");
+  SegTable sg;
+  ATS_TRY(dense_table(workspace, workspace_bytes, M, &sg));
+  cudaStream_t st = (cudaStream_t)stream;
+  dense_table_kernel<<<1, 1, 0, st>>>(static_cast<int*>(workspace), (int)dense_rows(M));
+  ATS_TRY(check_launch("gemm_table"));
+  return tc_gemm_nt_fwd(a, b, c, N, K, sg, st, M);
+}
+
+int ats_gemm_bwd(const void* dc, const void* a, const void* b, void* da, void* db, ats_dtype dtype, int64_t M,
+                 int64_t N, int64_t K, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!ats_gemm_supported(dtype, M, N, K))
+    return fail(ATS_EUNSUPPORTED, "gemm_bwd: unsupported shape (M=%lld N=%lld K=%lld)", (long long)M, (long long)N,
+                (long long)K);
+  if (dc == nullptr || (da != nullptr && b == nullptr) || (db != nullptr && a == nullptr))
+    return fail(ATS_EBADARG, "gemm_bwd: null");
+  SegTable sg;
+  ATS_TRY(dense_table(workspace, workspace_bytes, M, &sg));
+  cudaStream_t st = (cudaStream_t)stream;
+  dense_table_kernel<<<1, 1, 0, st>>>(static_cast<int*>(workspace), (int)dense_rows(M));
+  ATS_TRY(check_launch("gemm_table"));
+  return tc_gemm_nt_bwd(dc, a, b, da, db, N, K, sg, st, M);
+}
+
 int ats_swiglu_status(const void* workspace, size_t workspace_bytes, int* status) {
   if (workspace == nullptr || workspace_bytes < kDenseWsBytes || status == nullptr)
     return fail(ATS_EBADARG, "swiglu_status: bad arguments");

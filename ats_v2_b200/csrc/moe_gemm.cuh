@@ -52,6 +52,12 @@ inline bool tc_shape_supported(int64_t H, int64_t F) {
 // the tensor-core tiling does not cover; the caller then uses the CUDA-core path.
 // io_rows > 0: the token-side tensors (xp, y, dy, dxp) have only io_rows rows (TMA reads past them
 // are zero and stores are clipped); h, a and dh always have sg.max_rows rows.
+// C[M,N] = A[M,K] B[N,K]^T and its gradients on the same kernel (bf16; N, K multiples of 128; sg one
+// segment of M rounded up to 128 rows; A, C, dC, dA have io_rows = M rows).
+int tc_gemm_nt_fwd(const void* a, const void* b, void* c, int64_t N, int64_t K, const SegTable& sg, cudaStream_t st,
+                   int64_t io_rows);
+int tc_gemm_nt_bwd(const void* dc, const void* a, const void* b, void* da, void* db, int64_t N, int64_t K,
+                   const SegTable& sg, cudaStream_t st, int64_t io_rows);
 int tc_experts_fwd(const void* xp, const void* wgu, const void* wd, void* h, void* a, void* y, int E, int64_t H,
                    int64_t F, const SegTable& sg, cudaStream_t st, int64_t io_rows = 0);
 int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a, const void* wgu, const void* wd,

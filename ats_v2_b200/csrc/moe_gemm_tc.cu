@@ -796,6 +796,75 @@ int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a,
 
 
 
+// Plain GEMM on the same kernel, one segment over the rows (the dense table):
+// C[M,N] = A[M,K] B[N,K]^T.  A and C have io_rows rows (reads past them are zero,
+// stores clipped); the tiles cover sg.max_rows = M rounded up to 128.
+int tc_gemm_nt_fwd(const void* a, const void* b, void* c, int64_t N, int64_t K, const SegTable& sg, cudaStream_t st,
+                   int64_t io_rows) {
+  if (!tc_shape_supported(N, K)) return ATS_EUNSUPPORTED;
+  const int64_t R = sg.max_rows;
+  const int bn = pick_bn(N);
+  CUtensorMap ma, mb, mo;
+  GemmArgs p{};
+  p.seg = sg;
+  ATS_TRY(make_map(&ma, a, K, io_rows, K * 2, 128));
+  ATS_TRY(make_map(&mb, b, K, N, K * 2, bn));
+  p.N = (int)N;
+  p.K = (int)K;
+  p.b = OpSpec{(int)N, 0};
+  p.out = static_cast<bf16*>(c);
+  p.ldo = N;
+  ATS_TRY(make_out_map(&mo, c, N, io_rows, N * 2));
+  if (bn == 256) return launch_tc<256, false, false, EPI_STORE, false>(ma, mb, p, (R / BM) * (N / 256), st, &mo);
+  return launch_tc<128, false, false, EPI_STORE, false>(ma, mb, p, (R / BM) * (N / 128), st, &mo);
+}
+
+// Its gradients: dA[M,K] = dC[M,N] B[N,K] (B N-major), dB[N,K] = dC^T A summed over the
+// rows (K-grouped, both operands MN-major).  A null da or db skips that GEMM.
+int tc_gemm_nt_bwd(const void* dc, const void* a, const void* b, void* da, void* db, int64_t N, int64_t K,
+                   const SegTable& sg, cudaStream_t st, int64_t io_rows) {
+  if (!tc_shape_supported(N, K)) return ATS_EUNSUPPORTED;
+  const int64_t R = sg.max_rows;
+  if (da != nullptr) {
+    const int bn = pick_bn(K);
+    CUtensorMap ma, mb, mo;
+    GemmArgs p{};
+    p.seg = sg;
+    ATS_TRY(make_map(&ma, dc, N, io_rows, N * 2, 128));
+    ATS_TRY(make_map(&mb, b, K, N, K * 2, 64));
+    p.N = (int)K;
+    p.K = (int)N;
+    p.b = OpSpec{(int)N, 0};
+    p.out = static_cast<bf16*>(da);
+    p.ldo = K;
+    ATS_TRY(make_out_map(&mo, da, K, io_rows, K * 2));
+    if (bn == 256)
+      ATS_TRY((launch_tc<256, false, true, EPI_STORE, false>(ma, mb, p, (R / BM) * (K / 256), st, &mo)));
+    else
+      ATS_TRY((launch_tc<128, false, true, EPI_STORE, false>(ma, mb, p, (R / BM) * (K / 128), st, &mo)));
+  }
+  if (db != nullptr) {
+    const int bn = pick_bn(K);
+    CUtensorMap ma, mb, mo;
+    GemmArgs p{};
+    p.seg = sg;
+    ATS_TRY(make_map(&ma, dc, N, io_rows, N * 2, 64));
+    ATS_TRY(make_map(&mb, a, K, io_rows, K * 2, 64));
+    p.M = (int)N;
+    p.N = (int)K;
+    p.K = 0;
+    p.b = OpSpec{0, 0};
+    p.out = static_cast<bf16*>(db);
+    p.ldo = K;
+    p.out_group = N * K;
+    ATS_TRY(make_out_map(&mo, db, K, N, K * 2));
+    const int64_t tiles = (N / BM) * (K / bn);
+    if (bn == 256) return launch_tc<256, true, true, EPI_STORE, true>(ma, mb, p, tiles, st, &mo);
+    return launch_tc<128, true, true, EPI_STORE, true>(ma, mb, p, tiles, st, &mo);
+  }
+  return ATS_OK;
+}
+
 namespace {
 void set_parts(int (&dst)[kMaxParts], std::initializer_list<int> v) {
   int i = 0;

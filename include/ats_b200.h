@@ -294,6 +294,22 @@ ATS_API int ats_moe_ep_experts_bwd(const void* dy, const void* xr, const void* h
 ATS_API int ats_moe_ep_status(const void* seg_workspace, size_t seg_workspace_bytes, int W, int E_local,
                       int* status);
 
+/* ------------------------------------------------------------ plain GEMM
+ * C[M,N] = A[M,K] . B[N,K]^T in bf16 (float32 accumulation, one rounding) on
+ * the expert GEMM kernel as one segment over the rows: the fused MLA KV
+ * decompression of ats/model/mla_triton.py:122-151 ((k, v) = (c W_uk^T,
+ * c W_uv^T) as one matmul against [W_uk; W_uv]; `_triton_matmul` at :78-104).
+ * Needs bf16, M >= 128, N and K multiples of 128 (ats_gemm_supported);
+ * A, C, dC, dA are [M, *] row-major, B and dB [N, K].  ats_gemm_bwd writes
+ * dA = dC . B and dB = dC^T . A; pass NULL for one to skip it.  The workspace
+ * (ats_gemm_workspace_bytes) holds the segment table and the wait status. */
+ATS_API int ats_gemm_supported(ats_dtype dtype, int64_t M, int64_t N, int64_t K);
+ATS_API size_t ats_gemm_workspace_bytes(void);
+ATS_API int ats_gemm_fwd(const void* a, const void* b, void* c, ats_dtype dtype, int64_t M, int64_t N, int64_t K,
+                         void* workspace, size_t workspace_bytes, void* stream);
+ATS_API int ats_gemm_bwd(const void* dc, const void* a, const void* b, void* da, void* db, ats_dtype dtype, int64_t M,
+                         int64_t N, int64_t K, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Peer-memory row exchange.  Instead of NCCL all-to-alls, a rank can copy
  * its rows straight into the receive buffers of the experts' ranks with the
  * copy engines (no SMs taken, so the copies run beside the expert GEMMs).

@@ -16,7 +16,7 @@ import numpy as np
 import pytest
 import torch
 
-from ats_v2_b200 import moe_fused, norm_fused, rope_fused
+from ats_v2_b200 import mla_fused, moe_fused, norm_fused, rope_fused
 from ats_v2_b200.rope import RotaryEmbedding
 from oracle import moe as omoe
 from oracle import norm as onorm
@@ -28,7 +28,8 @@ def test_reference_test_names_exist():
                                      "_pytorch_rmsnorm_residual")),
                        (rope_fused, ("HAS_TRITON", "fused_apply_rope", "_triton_apply_rope", "_pytorch_apply_rope")),
                        (moe_fused, ("HAS_TRITON", "fused_moe_routing", "fused_moe_dispatch", "_triton_moe_routing",
-                                    "_pytorch_moe_routing"))):
+                                    "_pytorch_moe_routing")),
+                       (mla_fused, ("HAS_TRITON", "fused_mla_kv_decompress", "_triton_matmul"))):
         for n in names:
             assert hasattr(mod, n), f"{mod.__name__}.{n}"
         assert isinstance(mod.HAS_TRITON, bool)
@@ -64,6 +65,19 @@ def test_fused_functions_refuse_cpu_tensors():
         rope_fused.fused_apply_rope(torch.randn(1, 2, 6, 8), torch.ones(6, 8), torch.zeros(6, 8))
     with pytest.raises((RuntimeError, ValueError, TypeError)):
         moe_fused.fused_moe_routing(torch.randn(4, 8), 2)
+    with pytest.raises((RuntimeError, ValueError, TypeError)):
+        mla_fused.fused_mla_kv_decompress(torch.randn(2, 5, 8), torch.randn(16, 8), torch.randn(16, 8))
+
+
+def test_mla_dim_mismatch_raises_before_any_device_work():
+    """tests/test_triton.py:121-126 of the reference."""
+    c = torch.randn(2, 5, 8)
+    with pytest.raises(ValueError):
+        mla_fused.fused_mla_kv_decompress(c, torch.randn(16, 8), torch.randn(16, 4))
+    with pytest.raises(ValueError):
+        mla_fused.fused_mla_kv_decompress(c, torch.randn(16, 8), torch.randn(12, 8))
+    with pytest.raises(ValueError):
+        mla_fused._triton_matmul(torch.randn(4, 8), torch.randn(6, 3))
 
 
 @pytest.mark.gpu
