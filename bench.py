@@ -564,6 +564,101 @@ class FFNWorkload(Workload):
                           f"two GEMMs per forward GEMM (numpy oracle, BLAS on {threads} threads)"}
 
 
+class MLAWorkload(Workload):
+    """MLA KV decompression (mla_triton.py:122-151) of a 7B-shaped block with MLA on: latent
+    hidden/4 = 1024 (mla_compression_ratio 0.25), k and v each 32 heads x 128."""
+    name = "mla"
+    metric = "mla_kv_decompress_fwd_bwd_tokens_per_s"
+    unit = "tokens/s"
+    T, L, O = 16384, 1024, 4096
+
+    def flops_per_step(self) -> int:
+        return 12 * self.T * self.O * self.L  # forward 2*T*(2*O)*L, backward twice that
+
+    def config(self):
+        return {"workload": "MLA KV decompression fwd+bwd, 16384 tokens, latent 1024, k and v 4096 each, bf16",
+                "per_rank": "full workload per GPU (replicas)", "l2": "outputs larger than L2"}
+
+    def setup(self):
+        t = self.torch
+        g = t.Generator(device="cuda").manual_seed(4000 + self.rank)
+        self.c = t.randn(4, self.T // 4, self.L, device="cuda", generator=g).bfloat16().requires_grad_()
+        self.w_uk = (0.02 * t.randn(self.O, self.L, device="cuda", generator=g)).bfloat16().requires_grad_()
+        self.w_uv = (0.02 * t.randn(self.O, self.L, device="cuda", generator=g)).bfloat16().requires_grad_()
+        self.dk = t.randn(4, self.T // 4, self.O, device="cuda", generator=g).bfloat16()
+        self.dv = t.randn(4, self.T // 4, self.O, device="cuda", generator=g).bfloat16()
+
+    def _run(self, c, dk, dv):
+        from ats_v2_b200.mla_fused import fused_mla_kv_decompress
+        self.w_uk.grad = None
+        self.w_uv.grad = None
+        k, v = fused_mla_kv_decompress(c, self.w_uk, self.w_uv)
+        self.torch.autograd.backward([k, v], [dk, dv])
+        return k, v
+
+    def step(self, evs):
+        self.c.grad = None
+        if evs:
+            evs[0].record()
+        self._run(self.c, self.dk, self.dv)
+        if evs:
+            evs[1].record()
+
+    def dominant(self):
+        return {"kernel": "MLA KV decompression GEMMs (forward, dgrad, weight gradient; whole fwd+bwd timed)",
+                "flops": self.flops_per_step(), "bound": "tensor"}
+
+    def e2e_setup(self):
+        t = self.torch
+        self.hc = self.c.detach().cpu().pin_memory()
+        self.hdk = self.dk.cpu().pin_memory()
+        self.hdv = self.dv.cpu().pin_memory()
+        self.hk = t.empty_like(self.hdk).pin_memory()
+        self.hv = t.empty_like(self.hdv).pin_memory()
+        self.hdc = t.empty_like(self.hc).pin_memory()
+        self.c_in = t.empty_like(self.c.detach())
+        self.dk_in = t.empty_like(self.dk)
+        self.dv_in = t.empty_like(self.dv)
+        self.h2d = 2 * (self.hc.numel() + self.hdk.numel() + self.hdv.numel())
+        self.d2h = 2 * (self.hk.numel() + self.hv.numel() + self.hc.numel())
+
+    def e2e_step(self):
+        self.c_in.copy_(self.hc, non_blocking=True)
+        self.dk_in.copy_(self.hdk, non_blocking=True)
+        self.dv_in.copy_(self.hdv, non_blocking=True)
+        c = self.c_in.requires_grad_()
+        k, v = self._run(c, self.dk_in, self.dv_in)
+        self.hk.copy_(k.detach(), non_blocking=True)
+        self.hv.copy_(v.detach(), non_blocking=True)
+        self.hdc.copy_(c.grad, non_blocking=True)
+        c.grad = None
+        c.requires_grad_(False)
+
+    def units_to_value(self, steps, ms):
+        return self.T * steps / (ms * 1e-3)
+
+    def cpu_baseline(self, seconds: float):
+        from oracle import mla as omla
+        from oracle.bf16 import round_bf16
+        threads = cpu_threads()
+        T = 512
+        rng = np.random.default_rng(0)
+        c = round_bf16(rng.standard_normal((T, self.L)).astype(np.float32))
+        w_uk = round_bf16((0.02 * rng.standard_normal((self.O, self.L))).astype(np.float32))
+        w_uv = round_bf16((0.02 * rng.standard_normal((self.O, self.L))).astype(np.float32))
+        t0 = time.perf_counter()
+        n = 0
+        while True:
+            omla.kv_decompress(c, w_uk, w_uv, "bf16")
+            n += 1
+            if time.perf_counter() - t0 >= seconds:
+                break
+        dt = time.perf_counter() - t0
+        return {"value": T * n / dt / 3.0, "unit": self.unit, "cores": threads, "kind": "port",
+                "sample": f"{T} tokens, forward only ({n} passes in {dt:.1f} s), scaled by 1/3 for the backward's "
+                          f"two GEMMs per forward GEMM (numpy oracle, float64 BLAS on {threads} threads)"}
+
+
 def zipf_bias(E: int, s_exp: float = 1.1, seed: int = 1):
     """Per-expert router-logit bias log(p_pi(e)), p_r ~ r^-s over ranks r=1..E,
     pi a fixed permutation (generator seed 1), mean-centred."""
@@ -736,7 +831,7 @@ class MoEEPWorkload(Workload):
 
 
 WORKLOADS = {"rmsnorm": RMSNormWorkload, "rope": RopeWorkload, "moe": MoEWorkload, "moe_ep": MoEEPWorkload,
-             "ffn": FFNWorkload}
+             "ffn": FFNWorkload, "mla": MLAWorkload}
 
 
 # ---------------------------------------------------------------- timing

@@ -6,7 +6,8 @@ Run in a container that holds the reference source tree (default
     python tests/golden/make_golden.py
 
 It imports the reference's own modules (``ats.model.norm``, ``rope``,
-``norm_triton``, ``rope_triton``, ``moe_triton``, ``moe``, ``ffn``) with their
+``norm_triton``, ``rope_triton``, ``moe_triton``, ``moe``, ``ffn``,
+``mla_triton``) with their
 Triton paths disabled, runs them forward and backward (torch autograd) on
 seeded CPU inputs, and writes ``tests/golden/*.npz``.  bfloat16 tensors are
 stored as uint16 bit patterns (key suffix ``_bf16``).
@@ -41,6 +42,7 @@ def _import_reference():
     if not Path(REF, "ats", "model").is_dir():
         raise SystemExit(f"reference tree not found at {REF}")
     sys.path.insert(0, REF)
+    import ats.model.mla_triton as mla_triton
     import ats.model.moe as moe
     import ats.model.moe_triton as moe_triton
     import ats.model.norm as norm
@@ -48,9 +50,9 @@ def _import_reference():
     import ats.model.rope as rope
     import ats.model.rope_triton as rope_triton
     # never take the unverified Triton kernels: the PyTorch path is the reference
-    for m in (norm_triton, rope_triton, moe_triton):
+    for m in (norm_triton, rope_triton, moe_triton, mla_triton):
         m.HAS_TRITON = False
-    return norm, norm_triton, rope, rope_triton, moe, moe_triton
+    return norm, norm_triton, rope, rope_triton, moe, moe_triton, mla_triton
 
 
 def _np(t: torch.Tensor, key: str, store: dict) -> None:
@@ -302,10 +304,30 @@ def _moe_case_bf16(moe, T, H, F, E, k, cf, lbw, seed) -> dict:
     return s
 
 
+def gen_mla(mla_triton) -> dict:
+    """fused_mla_kv_decompress (mla_triton.py:122-151) forward and autograd
+    backward, float32 and bfloat16, on seeded [2, 24, latent] latents."""
+    s = {}
+    for tag, dt, (B, S, L, O), seed in (("f32", torch.float32, (2, 24, 64, 96), 21),
+                                          ("bf16", torch.bfloat16, (2, 24, 128, 64), 22)):
+        g = torch.Generator().manual_seed(seed)
+        c = torch.randn(B, S, L, generator=g).to(dt).requires_grad_()
+        w_uk = (0.1 * torch.randn(O, L, generator=g)).to(dt).requires_grad_()
+        w_uv = (0.1 * torch.randn(O, L, generator=g)).to(dt).requires_grad_()
+        dk = torch.randn(B, S, O, generator=g).to(dt)
+        dv = torch.randn(B, S, O, generator=g).to(dt)
+        k, v = mla_triton.fused_mla_kv_decompress(c, w_uk, w_uv)
+        torch.autograd.backward([k, v], [dk, dv])
+        for name, t in (("c", c), ("w_uk", w_uk), ("w_uv", w_uv), ("dk", dk), ("dv", dv), ("k", k), ("v", v),
+                        ("dc", c.grad), ("dw_uk", w_uk.grad), ("dw_uv", w_uv.grad)):
+            _np(t, f"{tag}_{name}", s)
+    return s
+
+
 def main() -> None:
     torch.set_num_threads(min(8, os.cpu_count() or 1))
     torch.backends.cuda.matmul.allow_tf32 = False
-    norm, norm_triton, rope, rope_triton, moe, moe_triton = _import_reference()
+    norm, norm_triton, rope, rope_triton, moe, moe_triton, mla_triton = _import_reference()
     files = {
         "rmsnorm.npz": gen_rmsnorm(norm, norm_triton),
         "rope.npz": gen_rope(rope, rope_triton),
@@ -316,6 +338,7 @@ def main() -> None:
         "moe_f32_nodrop.npz": _moe_case_fp32(moe, 1, 48, 32, 96, 8, 2, 4.0, 0.01, 12),
         "moe_bf16.npz": _moe_case_bf16(moe, 96, 64, 128, 8, 2, 4.0, 0.01, 13),
         "moe_bf16_drop.npz": _moe_case_bf16(moe, 80, 64, 64, 4, 2, 1.0, 0.01, 14),
+        "mla.npz": gen_mla(mla_triton),
     }
     manifest = {}
     for name, d in files.items():

@@ -12,6 +12,7 @@ from __future__ import annotations
 import numpy as np
 import pytest
 
+from oracle import mla as omla
 from oracle import moe as omoe
 from oracle import norm as onorm
 from oracle import rope as orope
@@ -159,3 +160,18 @@ def test_capacity_formula():
     assert omoe.capacity(32768, 2, 64, 1.25) == 1280
     assert omoe.capacity(8192, 2, 8, 4.0) == 8192
     assert omoe.capacity(1, 1, 64, 0.01) == 1
+
+
+@pytest.mark.parametrize("tag", ["f32", "bf16"])
+def test_mla_kv_decompress_matches_reference(tag):
+    g = load_golden("mla")
+    c, w_uk, w_uv = g[f"{tag}_c"], g[f"{tag}_w_uk"], g[f"{tag}_w_uv"]
+    k, v = omla.kv_decompress(c, w_uk, w_uv, tag)
+    dc, dwk, dwv = omla.kv_decompress_bwd(g[f"{tag}_dk"], g[f"{tag}_dv"], c, w_uk, w_uv, tag)
+    pairs = ((k, "k"), (v, "v"), (dc, "dc"), (dwk, "dw_uk"), (dwv, "dw_uv"))
+    for got, name in pairs:
+        if tag == "f32":
+            np.testing.assert_allclose(got, g[f"f32_{name}"], rtol=1e-5, atol=1e-5, err_msg=name)
+        else:
+            _bf16_close(got, g[f"bf16_{name}"], min_exact=0.97)
+
