@@ -10,7 +10,8 @@ replicated.  One forward:
      ``max(1, int(cf*T*k/E))`` from its own token count, as the fallback and
      DeepSpeed compute it) and gathers its kept rows by expert;
   2. the kept-row counts [W][E_local] go to the experts' ranks with
-     ``all_to_all_single``, then the rows themselves:
+     ``all_to_all_single`` (the peer exchange all-gathers every rank's counts
+     instead, to place its copies), then the rows themselves:
        exchange="packed" (default): the packed layout, where the experts of a
          destination rank are one contiguous run of segments (each kept count
          rounded up to 128 rows), sent with variable splits -- only rows the
@@ -35,11 +36,12 @@ and sends the input gradients back.  Expert weights are rank-local, so their
 gradients need no all-reduce; the replicated router weight's gradient is the
 usual data-parallel all-reduce of the training loop.
 
-The exchange steps (``exchange_counts``, ``exchange_rows``, ``_Exchange``)
-only move tensors and work on any device and backend; the device stages are
-the library's.  With ``overlap_parts`` P > 1 the local experts run in P parts
-and each part's row transfers overlap the other parts' expert GEMMs, which
-then leave ``comm_sms`` SMs to the transfers.
+The NCCL exchange steps (``exchange_counts``, ``exchange_rows``,
+``_Exchange``) only move tensors and work on any device and backend; the copy
+plan of the peer exchange (``peer_plan``) is plain host arithmetic; the device
+stages are the library's.  With ``overlap_parts`` P > 1 the local experts run
+in P parts and each part's row transfers overlap the other parts' expert
+GEMMs, which then leave ``comm_sms`` SMs to the collectives.
 """
 
 from __future__ import annotations
