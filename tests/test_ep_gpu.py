@@ -38,7 +38,7 @@ def _init_weights(mod_gate, experts, seed):
             ex.down_proj.weight.copy_(0.02 * torch.randn(ex.down_proj.weight.shape, generator=g))
 
 
-@pytest.mark.parametrize("exchange", ["packed", "slots"])
+@pytest.mark.parametrize("exchange", ["packed", "slots", "peer"])
 @pytest.mark.parametrize("T,H,F,E,k,cf", [(1024, 256, 384, 8, 2, 1.25), (700, 128, 128, 4, 2, 0.6)])
 def test_single_rank_expert_parallel_layer_equals_the_layer(T, H, F, E, k, cf, exchange):
     torch.manual_seed(0)
