@@ -48,6 +48,7 @@ from __future__ import annotations
 
 import ctypes
 import socket
+import weakref
 
 import torch
 import torch.distributed as dist
@@ -329,6 +330,7 @@ class _PeerSet:
                 self.handles.append(h)
             self.addr.append(a)
         self.busy = False
+        self.owner = None  # weak reference to the autograd context of the forward holding the set
 
     def fits(self, rows_x: int, rows_t: int, H: int, dtype) -> bool:
         return rows_x <= self.rows_x and rows_t <= self.rows_t and H == self.H and dtype == self.dtype
@@ -343,7 +345,9 @@ class _PeerState:
     """Per-layer state of the peer-memory exchange: a pool of buffer sets (one
     per forward whose backward has not run yet), the streams the copies run on,
     the one-element tensor of the collectives that order them and a pinned
-    buffer for the counts."""
+    buffer for the counts.  A set goes back to the pool when its backward has
+    run, at the end of a forward no backward will follow, or -- when no free
+    set fits -- once its forward's graph is gone on every rank."""
 
     MAX_SETS = 4
 
@@ -356,10 +360,19 @@ class _PeerState:
     def acquire(self, rows_x, rows_t, H, dtype, device, group, W, me) -> _PeerSet:
         # every rank makes the same choice: the sizes are maxima over the ranks and
         # the ranks run the same sequence of forwards and backwards
-        for ps in self.sets:
-            if not ps.busy and ps.fits(rows_x, rows_t, H, dtype):
-                ps.busy = True
-                return ps
+        ps = self._free(rows_x, rows_t, H, dtype)
+        if ps is None and any(q.busy for q in self.sets):
+            # a forward whose graph is gone without a backward (activation checkpointing
+            # recomputes the forward inside the backward and drops that graph) leaves its set
+            # busy; take such sets back, but only those orphaned on every rank
+            mask = [int(q.busy and q.owner is not None and q.owner() is None) for q in self.sets]
+            for q, m in zip(self.sets, self._agree(mask, group, device)):
+                if m:
+                    q.busy = False
+            ps = self._free(rows_x, rows_t, H, dtype)
+        if ps is not None:
+            ps.busy = True
+            return ps
         for ps in [q for q in self.sets if not q.busy]:
             ps.close()
             self.sets.remove(ps)
@@ -371,9 +384,23 @@ class _PeerState:
         self.sets.append(ps)
         return ps
 
+    def _free(self, rows_x, rows_t, H, dtype):
+        for ps in self.sets:
+            if not ps.busy and ps.fits(rows_x, rows_t, H, dtype):
+                return ps
+        return None
+
+    @staticmethod
+    def _agree(mask: list, group, device) -> list:
+        """Element-wise minimum of the mask over the ranks."""
+        t = torch.tensor(mask, dtype=torch.int32, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MIN, group=group)
+        return t.tolist()
+
     @staticmethod
     def release(ps: _PeerSet) -> None:
         ps.busy = False
+        ps.owner = None
 
     def copy_streams(self, device, W: int) -> list:
         """One stream per destination rank, so that the copies to different
@@ -613,6 +640,7 @@ class _EPPeerFn(torch.autograd.Function):
             raise RuntimeError("ExpertParallelMoE: the packed layout differs from the copy plan")
         rows_t = max(r[E + 1] for r in rows)
         ps = state.acquire(W * El * Cp, rows_t, H, x2.dtype, dev, group, W, me)
+        ps.owner = weakref.ref(ctx)
         Ep = El // parts
         part_rows = W * Ep * Cp
         rowb = H * x2.element_size()

@@ -167,6 +167,26 @@ def _rebalance_worker(rank, world, port, errq):
         raise
 
 
+def _agree_worker(rank, world, port, errq):
+    try:
+        _init(rank, world, port)
+        from ats_v2_b200.ep import _PeerState
+        mine = [[1, 0, 1, 1], [1, 1, 0, 1]][rank]
+        assert _PeerState._agree(mine, None, "cpu") == [1, 0, 0, 1]
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        errq.put((rank, traceback.format_exc()))
+        raise
+
+
+def test_orphan_masks_agree_over_ranks():
+    ctx = mp.get_context("spawn")
+    errq = ctx.SimpleQueue()
+    mp.start_processes(_agree_worker, args=(2, _free_port(), errq), nprocs=2, join=True, start_method="spawn")
+    assert errq.empty()
+
+
 def _leaver_worker(rank, world, port, errq):
     try:
         _init(rank, world, port, timeout_s=3)
@@ -269,6 +289,7 @@ def test_peer_buffer_pool_reuses_free_sets_and_bounds_waiting_forwards(monkeypat
         def __init__(self, rows_x, rows_t, H, dtype, device, group, W, me):
             self.rows_x, self.rows_t, self.H, self.dtype = rows_x, rows_t, H, dtype
             self.busy = False
+            self.owner = None
             made.append(self)
 
         def fits(self, rows_x, rows_t, H, dtype):
@@ -279,6 +300,7 @@ def test_peer_buffer_pool_reuses_free_sets_and_bounds_waiting_forwards(monkeypat
 
     monkeypatch.setattr(epm, "_PeerSet", FakeSet)
     st = epm._PeerState()
+    monkeypatch.setattr(st, "_agree", lambda mask, group, device: mask)  # one rank: its own mask
     args = (None, None, 2, 0)
     a = st.acquire(1024, 512, 64, torch.bfloat16, *args)
     assert a.busy and made == [a]
@@ -296,6 +318,62 @@ def test_peer_buffer_pool_reuses_free_sets_and_bounds_waiting_forwards(monkeypat
         st.acquire(4096, 512, 64, torch.bfloat16, *args)
     st.close()
     assert st.sets == [] and len(closed) == 2 + epm._PeerState.MAX_SETS
+
+
+def test_peer_buffer_sets_of_dropped_graphs_come_back_only_when_every_rank_agrees(monkeypatch):
+    """Activation checkpointing recomputes a forward inside the backward and
+    drops that graph, so its set is never released by a backward.  When no
+    free set fits, sets whose forward's context is gone are taken back --
+    only those orphaned on every rank (a minimum over the ranks' masks)."""
+    import gc
+    import weakref
+
+    from ats_v2_b200 import ep as epm
+
+    class FakeSet:
+        def __init__(self, rows_x, rows_t, H, dtype, device, group, W, me):
+            self.rows_x, self.rows_t, self.H, self.dtype = rows_x, rows_t, H, dtype
+            self.busy = False
+            self.owner = None
+
+        def fits(self, rows_x, rows_t, H, dtype):
+            return rows_x <= self.rows_x and rows_t <= self.rows_t and H == self.H and dtype == self.dtype
+
+        def close(self):
+            pass
+
+    class Ctx:  # stands in for an autograd context
+        pass
+
+    monkeypatch.setattr(epm, "_PeerSet", FakeSet)
+    st = epm._PeerState()
+    other_rank = {"mask": None}
+    seen = []
+
+    def agree(mask, group, device):
+        seen.append(list(mask))
+        peer = other_rank["mask"] if other_rank["mask"] is not None else mask
+        return [min(a, b) for a, b in zip(mask, peer)]
+
+    monkeypatch.setattr(st, "_agree", agree)
+    shape = (1024, 512, 64, torch.bfloat16, None, None, 2, 0)
+    kept, dropped = Ctx(), Ctx()
+    a = st.acquire(*shape)
+    a.owner = weakref.ref(kept)       # the original forward: its backward will run
+    b = st.acquire(*shape)
+    b.owner = weakref.ref(dropped)    # the recomputed forward: its graph is dropped
+    assert seen == [[0]]              # b's acquire asked, but a's context is alive
+    del dropped
+    gc.collect()
+    other_rank["mask"] = [0, 0]       # another rank still holds b's graph: nothing comes back
+    c = st.acquire(*shape)
+    assert c is not b and len(st.sets) == 3 and b.busy
+    other_rank["mask"] = None         # every rank has dropped it
+    d = st.acquire(*shape)
+    assert d is b and seen[-1] == [0, 1, 0]
+    st.release(a)
+    assert st.acquire(*shape) is a    # a free set is taken without asking the other ranks
+    assert len(seen) == 3
 
 
 def test_balanced_placement_spreads_the_load():
