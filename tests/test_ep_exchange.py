@@ -416,3 +416,54 @@ def test_peer_that_leaves_makes_the_collective_fail_not_hang():
     while not errq.empty():
         results.append(errq.get())
     assert any(r == 0 and msg.startswith("raised") for r, msg in results), results
+
+
+def test_peer_copy_plan_invariants_over_random_layouts():
+    """Property check of ``peer_plan`` (it decides where the copy engines write
+    into other GPUs' memory): over random world sizes, parts and kept counts,
+    every rank's token rows leave exactly once, every part buffer of every
+    rank is tiled by the incoming runs without gaps or overlaps and stays
+    within W*Ep*Cp rows, and the return runs mirror the outgoing ones."""
+    from hypothesis import given, settings
+    from hypothesis import strategies as st
+
+    @settings(max_examples=200, deadline=None)
+    @given(st.data())
+    def check(data):
+        W = data.draw(st.sampled_from([1, 2, 3, 4, 8]))
+        El = data.draw(st.sampled_from([1, 2, 4, 6, 8]))
+        parts = data.draw(st.sampled_from([p for p in (1, 2, 3, 4) if El % p == 0]))
+        cap = data.draw(st.integers(1, 700))
+        Cp = slot_rows(cap)
+        E = W * El
+        kept = [[data.draw(st.integers(0, cap)) for _ in range(E)] for _ in range(W)]
+        Ep = El // parts
+        part_rows = W * Ep * Cp
+        plans = [peer_plan(kept, Cp, El, parts, me) for me in range(W)]
+        incoming = {(d, p): [] for d in range(W) for p in range(parts)}
+        for me, (seg, out, back) in enumerate(plans):
+            sent = []
+            for p in range(parts):
+                for d, src, dst, n in out[p]:
+                    assert n > 0 and 0 <= dst and dst + n <= part_rows
+                    sent.append((src, src + n))
+                    incoming[(d, p)].append((dst, dst + n, me, src))
+            sent.sort()
+            covered = 0
+            for a, b in sent:  # the runs cover [0, seg[me][E]) exactly once
+                assert a == covered
+                covered = b
+            assert covered == seg[me][E]
+        for (d, p), runs in incoming.items():
+            runs.sort()
+            pos = 0
+            for a, b, src_rank, _ in runs:  # sources in rank order, back to back from row 0
+                assert a == pos
+                pos = b
+            assert pos <= part_rows
+            back = sorted(plans[d][2][p])
+            mirror = sorted((s_, a, src, b - a) for a, b, s_, src in runs)
+            assert [(s_, srow, drow, n) for s_, srow, drow, n in back] == \
+                   [(s_, a, src, n) for s_, a, src, n in mirror]
+
+    check()
