@@ -51,6 +51,8 @@ SIGNATURES: dict[str, tuple] = {
     "ats_ipc_close": (c_int, [c_void_p]),
     "ats_peer_copies": (c_int, [c_int, POINTER(c_void_p), POINTER(c_void_p), POINTER(ctypes.c_uint64), c_void_p]),
     "ats_gemm_sm_limit": (c_int, []),
+    "ats_device_status": (c_int, [POINTER(c_int)]),
+    "ats_set_wait_budget": (c_int, [c_int64]),
     "ats_rmsnorm_fwd": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_int, c_void_p, c_int64, c_void_p,
                                 c_int64, c_int64, c_float, c_void_p]),
     "ats_rmsnorm_bwd_workspace_bytes": (c_size_t, [c_int64, c_int64]),
@@ -149,6 +151,11 @@ def load() -> ctypes.CDLL:
     return _lib
 
 
+# ATS_CHECK_STATUS=1: after every call, wait for the device and raise if a
+# bounded device wait gave up in it (a debugging mode: it synchronises).
+_CHECK_EACH_CALL = os.environ.get("ATS_CHECK_STATUS", "0") not in ("", "0")
+
+
 def call(name: str, *args) -> None:
     """Call a status-returning entry point; raise AtsError on failure."""
     lib = load()
@@ -156,6 +163,21 @@ def call(name: str, *args) -> None:
     if st != ATS_OK:
         detail = lib.ats_last_error_message().decode(errors="replace") or lib.ats_strerror(st).decode()
         raise AtsError(name, st, detail)
+    if _CHECK_EACH_CALL and not name.endswith("_status"):
+        check_device_status(name)
+
+
+def check_device_status(after: str = "an earlier call") -> None:
+    """Raise AtsError if a bounded wait of a tensor-core GEMM or an RMSNorm ring
+    kernel on the current device gave up since the last check (the status word
+    is cleared by reading it).  Synchronous: the modules call it only where the
+    host waits for the device anyway."""
+    lib = load()
+    code = c_int(0)
+    st = lib.ats_device_status(ctypes.byref(code))
+    if st != ATS_OK:
+        detail = lib.ats_last_error_message().decode(errors="replace") or lib.ats_strerror(st).decode()
+        raise AtsError(after, st, detail)
 
 
 def query(name: str, *args):
@@ -193,6 +215,24 @@ def stream_of(t: torch.Tensor) -> int:
 
 def strides3(*s: int):
     return _I64x3(*s)
+
+
+def on_cpu(name: str, *tensors: torch.Tensor | None) -> bool:
+    """True when every given tensor is a CPU tensor, False when every one is a
+    CUDA tensor on one device; mixed devices raise.
+
+    The mirror modules use it as the reference's own modules do (for example
+    ``fused_mla_kv_decompress``, mla_triton.py:144-151, runs its kernel only
+    for CUDA tensors): CPU tensors take the reference's torch formulas, which
+    its CPU tests pin, and CUDA tensors always take this library's kernels --
+    a CUDA tensor never runs the torch formula, and a missing library raises."""
+    devs = {t.device.type for t in tensors if t is not None}
+    if devs == {"cpu"}:
+        return True
+    if "cpu" in devs:
+        raise RuntimeError(f"{name}: tensors on different devices ({sorted(devs)})")
+    require_cuda(name, *tensors)
+    return False
 
 
 def require_cuda(name: str, *tensors: torch.Tensor) -> None:

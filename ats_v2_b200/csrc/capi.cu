@@ -1,5 +1,6 @@
 // Library-wide C ABI pieces: version, status strings, last-error text, SM count.
 #include "common.cuh"
+#include "moe_gemm.cuh"
 
 #include <atomic>
 #include <string.h>
@@ -70,5 +71,21 @@ int ats_set_gemm_sm_limit(int sms) {
 }
 
 int ats_gemm_sm_limit(void) { return ats::g_gemm_sm_limit; }
+
+int ats_set_wait_budget(int64_t cycles) {
+  ATS_TRY(ats::gemm_set_wait_budget((long long)cycles));
+  return ats::ring_set_wait_budget((long long)cycles);
+}
+
+int ats_device_status(int* status) {
+  if (status == nullptr) return ats::fail(ATS_EBADARG, "device_status: null output");
+  int g = 0, r = 0;
+  ATS_TRY(ats::gemm_take_status(&g));
+  ATS_TRY(ats::ring_take_status(&r));
+  *status = g != 0 ? g : r;
+  if (*status == 0) return ATS_OK;
+  return ats::fail(ATS_ETIMEOUT, "a bounded device wait gave up (%s code %d); the results of that call are undefined",
+                   g != 0 ? "tensor-core GEMM" : "RMSNorm ring", *status);
+}
 
 }  // extern "C"

@@ -45,6 +45,11 @@ inline int check_launch(const char* what) {
   } while (0)
 
 int num_sms();  // SM count of the current device (cached per device)
+// Main-loop wait budget of the RMSNorm ring kernels on the current device (SM
+// cycles; <= 0 restores the default), and the first code of a ring wait that
+// gave up there since the last call (0: none), which this call clears.
+int ring_set_wait_budget(long long cycles);
+int ring_take_status(int* code);
 int gemm_ctas();  // CTAs of a persistent GEMM: num_sms() or this thread's lower limit
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }

@@ -77,4 +77,10 @@ int tc_router_dx(const void* dlparts, const void* wparts, const void* dxp, const
 int tc_router_dw(const void* x, const void* dlparts, float* partial, int64_t T, int64_t H, int Ep,
                  const SegTable& chunks, cudaStream_t st);
 
+// Main-loop wait budget of the GEMM kernels on the current device (SM cycles;
+// <= 0 restores the default of about 2 s), and the first code of a GEMM wait
+// that gave up there since the last call (0: none), which this call clears.
+int gemm_set_wait_budget(long long cycles);
+int gemm_take_status(int* code);
+
 }  // namespace ats

@@ -41,6 +41,15 @@ constexpr int BM = 128, BK = 64, STAGES = 4;
 constexpr int kEpiWarps = 8;  // two per TMEM lane quadrant, each owning half of the tile's columns
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr long long kWaitBudget = 4000000000LL;  // SM cycles, about 2 s
+
+// Budget of the main-loop waits of this device's GEMM launches, read once per
+// CTA.  ats_set_wait_budget shortens it so a test can make a wait run out; the
+// drain waits, which make every issued TMA load and MMA finish before the CTA
+// frees TMEM and exits, always keep the full kWaitBudget.
+__device__ long long g_gemm_wait_budget = kWaitBudget;
+// First GEMM wait on this device that gave up since the status was last taken
+// (0: none).  The same code also goes to the call's own status word.
+__device__ int g_gemm_status;
 constexpr int kStageBox = 32 * 32 * 2;           // staging box: 32 rows x 32 bf16 columns, 64-byte swizzle
 constexpr int kBoxesPerWarp = 2;
 constexpr int kBandM = 16;  // M tiles per band of the tile order
@@ -175,7 +184,13 @@ __device__ __forceinline__ void fail_abort(int* err, volatile int* abort, int co
   if (*abort == 0) {
     *abort = 1;
     atomicCAS(err, 0, code);
+    atomicCAS(&g_gemm_status, 0, code);
   }
+}
+
+__device__ __forceinline__ void fail_drain(int* err, int code) {
+  atomicCAS(err, 0, code);
+  atomicCAS(&g_gemm_status, 0, code);
 }
 
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
@@ -222,6 +237,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
   __shared__ volatile int abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long budget = g_gemm_wait_budget;
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       tc::mbar_init(&full_bar[s], 1);
@@ -291,7 +307,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
               seg_r0 = p.seg.row0[sn];
             }
           }
-          if (!tc::mbar_wait(&empty_bar[stage], phase ^ 1u, &abort_flag, kWaitBudget)) {
+          if (!tc::mbar_wait(&empty_bar[stage], phase ^ 1u, &abort_flag, budget)) {
             fail_abort(p.seg.err, &abort_flag, 1);
             break;
           }
@@ -333,7 +349,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
       // drain: every issued load lands before the CTA may exit
       for (int s = 0; s < STAGES; ++s)
         if (last_parity[s] >= 0 && !tc::mbar_wait(&full_bar[s], (uint32_t)last_parity[s], nullptr, kWaitBudget))
-          atomicCAS(p.seg.err, 0, 11);
+          fail_drain(p.seg.err, 11);
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA
@@ -350,7 +366,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
         decode_tile<BN, KGROUP, EPI, SPLIT>(p, cur, t, ti);
         const int acc = i & 1;
         const uint32_t acc_phase = (uint32_t)(i >> 1) & 1u;
-        if (!tc::mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, &abort_flag, kWaitBudget)) {
+        if (!tc::mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, &abort_flag, budget)) {
           fail_abort(p.seg.err, &abort_flag, 2);
           break;
         }
@@ -358,7 +374,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
         bool ok = true;
         for (int kb = 0; kb < ti.kb; ++kb) {
-          if (!tc::mbar_wait(&full_bar[stage], phase, &abort_flag, kWaitBudget)) {
+          if (!tc::mbar_wait(&full_bar[stage], phase, &abort_flag, budget)) {
             fail_abort(p.seg.err, &abort_flag, 3);
             ok = false;
             break;
@@ -391,7 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
       // drain: all issued MMAs complete before TMEM may be freed
       if (issued) {
         tc::mma_commit(&done_bar);
-        if (!tc::mbar_wait(&done_bar, 0u, nullptr, kWaitBudget)) atomicCAS(p.seg.err, 0, 12);
+        if (!tc::mbar_wait(&done_bar, 0u, nullptr, kWaitBudget)) fail_drain(p.seg.err, 12);
       }
     }
   } else {
@@ -420,7 +436,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
           gq[q] = reinterpret_cast<const uint4*>(hg)[q];
           uq[q] = reinterpret_cast<const uint4*>(hu)[q];
         }
-        if (!tc::mbar_wait(&tfull_bar[acc], acc_phase, &abort_flag, kWaitBudget)) {
+        if (!tc::mbar_wait(&tfull_bar[acc], acc_phase, &abort_flag, budget)) {
           fail_abort(p.seg.err, &abort_flag, 4);
           break;
         }
@@ -463,7 +479,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
           bw.put(pk, &tmO, p.F + x0 + c, row_base, lane);  // du into dh[:, F:]
         }
       } else {
-        if (!tc::mbar_wait(&tfull_bar[acc], acc_phase, &abort_flag, kWaitBudget)) {
+        if (!tc::mbar_wait(&tfull_bar[acc], acc_phase, &abort_flag, budget)) {
           fail_abort(p.seg.err, &abort_flag, 4);
           break;
         }
@@ -942,6 +958,21 @@ int tc_router_dw(const void* x, const void* dlparts, float* partial, int64_t T, 
   ATS_TRY(make_map(&ma, x, H, T, H * 2, 64));
   ATS_TRY(make_map(&mb, dlparts, (uint64_t)3 * Ep, T, (uint64_t)3 * Ep * 2, 64));
   return launch_tc<kRouterEp, true, true, EPI_F32, true, 1, 3>(ma, mb, p, (int64_t)chunks.E * (H / BM), st);
+}
+
+int gemm_set_wait_budget(long long cycles) {
+  const long long v = cycles > 0 ? cycles : kWaitBudget;
+  cudaError_t e = cudaMemcpyToSymbol(g_gemm_wait_budget, &v, sizeof(v));
+  if (e != cudaSuccess) return fail(ATS_ECUDA, "set_wait_budget (gemm): %s", cudaGetErrorString(e));
+  return ATS_OK;
+}
+
+int gemm_take_status(int* code) {
+  const int zero = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(code, g_gemm_status, sizeof(int));
+  if (e == cudaSuccess && *code != 0) e = cudaMemcpyToSymbol(g_gemm_status, &zero, sizeof(int));
+  if (e != cudaSuccess) return fail(ATS_ECUDA, "device_status (gemm): %s", cudaGetErrorString(e));
+  return ATS_OK;
 }
 
 }  // namespace ats

@@ -365,6 +365,11 @@ constexpr int kConsumerThreads = kGroups * kGroupThreads;
 constexpr int kRingThreads = 32 + kConsumerThreads;
 constexpr int kSlotsFwd = 16, kSlotsBwd = 8;
 constexpr long long kRingBudget = 4000000000LL;  // SM cycles, about 2 s
+
+// Budget of the ring kernels' main-loop waits on this device, read once per
+// CTA.  ats_set_wait_budget shortens it so a test can make a wait run out; the
+// producer's final wait for its own copies in flight always keeps kRingBudget.
+__device__ long long g_ring_wait_budget = kRingBudget;
 constexpr int kRingMaxRowBytes = 8192;
 
 // First bounded wait of a ring kernel that gave up (diagnostics; 0 = none).
@@ -445,7 +450,8 @@ template <int S>
 __device__ __forceinline__ void ring_produce(uint8_t* ring, uint32_t slot_bytes, uint32_t half_bytes,
                                              const uint8_t* first, const uint8_t* second, int64_t row_stride_bytes,
                                              uint32_t nbytes, int64_t my_rows, int64_t rows, uint64_t* full_bar,
-                                             uint64_t* empty_bar, volatile int* abort_flag, int code) {
+                                             uint64_t* empty_bar, volatile int* abort_flag, int code,
+                                             long long budget) {
   int last_par[S];
 #pragma unroll
   for (int q = 0; q < S; ++q) last_par[q] = -1;
@@ -453,7 +459,7 @@ __device__ __forceinline__ void ring_produce(uint8_t* ring, uint32_t slot_bytes,
   for (int64_t i = 0; i < my_rows && !*abort_flag; ++i) {
     const int slot = (int)(i % S);
     const uint32_t par = (uint32_t)((i / S) & 1);
-    if (!tc::mbar_wait(&empty_bar[slot], par ^ 1u, abort_flag, kRingBudget)) {
+    if (!tc::mbar_wait(&empty_bar[slot], par ^ 1u, abort_flag, budget)) {
       ring_fail(abort_flag, code);
       break;
     }
@@ -479,6 +485,7 @@ __global__ void __launch_bounds__(kRingThreads, 1) rmsnorm_fwd_ring_kernel(
   __shared__ __align__(8) uint64_t full_bar[S], empty_bar[S];
   __shared__ float red[kGroups][2][kGroupWarps];
   __shared__ volatile int abort_flag;
+  const long long budget = g_ring_wait_budget;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nch = H / N;
   const uint32_t row_bytes = (uint32_t)H * sizeof(TX);
@@ -500,7 +507,7 @@ __global__ void __launch_bounds__(kRingThreads, 1) rmsnorm_fwd_ring_kernel(
   if (warp == 0) {
     if (lane == 0)
       ring_produce<S>(ring, slot_bytes, 0, reinterpret_cast<const uint8_t*>(x), nullptr,
-                      xs * (int64_t)sizeof(TX), row_bytes, my_rows, rows, full_bar, empty_bar, &abort_flag, 1);
+                      xs * (int64_t)sizeof(TX), row_bytes, my_rows, rows, full_bar, empty_bar, &abort_flag, 1, budget);
     return;
   }
   const int ct = threadIdx.x - 32;
@@ -508,7 +515,7 @@ __global__ void __launch_bounds__(kRingThreads, 1) rmsnorm_fwd_ring_kernel(
   int held = -1;  // slot whose row is still being read by this group's bulk store
   for (int64_t i = grp; i < my_rows; i += kGroups) {
     const int slot = (int)(i % S);
-    const bool ok = tc::mbar_wait(&full_bar[slot], (uint32_t)((i / S) & 1), &abort_flag, kRingBudget);
+    const bool ok = tc::mbar_wait(&full_bar[slot], (uint32_t)((i / S) & 1), &abort_flag, budget);
     const uint4* src = reinterpret_cast<const uint4*>(ring + slot * slot_bytes);
     uint4 raw[NPL];
     float ss = 0.f;
@@ -576,6 +583,7 @@ __global__ void __launch_bounds__(kRingThreads, 1) rmsnorm_bwd_ring_kernel(
   __shared__ __align__(8) uint64_t full_bar[S], empty_bar[S];
   __shared__ float2 red[kGroups][2][kGroupWarps];
   __shared__ volatile int abort_flag;
+  const long long budget = g_ring_wait_budget;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nch = H / N;
   const uint32_t row_bytes = (uint32_t)H * sizeof(TX);
@@ -599,7 +607,7 @@ __global__ void __launch_bounds__(kRingThreads, 1) rmsnorm_bwd_ring_kernel(
     if (lane == 0)
       ring_produce<S>(ring, slot_bytes, half_bytes, reinterpret_cast<const uint8_t*>(x),
                       reinterpret_cast<const uint8_t*>(dy), (int64_t)H * sizeof(TX), row_bytes, my_rows, rows,
-                      full_bar, empty_bar, &abort_flag, 3);
+                      full_bar, empty_bar, &abort_flag, 3, budget);
     return;
   }
   const int ct = threadIdx.x - 32;
@@ -612,7 +620,7 @@ __global__ void __launch_bounds__(kRingThreads, 1) rmsnorm_bwd_ring_kernel(
     for (int e = 0; e < N; ++e) acc[j][e] = 0.f;
   for (int64_t i = grp; i < my_rows; i += kGroups) {
     const int slot = (int)(i % S);
-    const bool ok = tc::mbar_wait(&full_bar[slot], (uint32_t)((i / S) & 1), &abort_flag, kRingBudget);
+    const bool ok = tc::mbar_wait(&full_bar[slot], (uint32_t)((i / S) & 1), &abort_flag, budget);
     const uint4* sx = reinterpret_cast<const uint4*>(ring + slot * slot_bytes);
     const uint4* sd = reinterpret_cast<const uint4*>(ring + slot * slot_bytes + half_bytes);
     uint4 xr[NPL], dr[NPL];
@@ -862,12 +870,30 @@ using namespace ats;
   ((xd) == ATS_BF16 ? ((wd) == ATS_BF16 ? FN<bf16, bf16, R> : FN<bf16, float, R>)        \
                     : ((wd) == ATS_BF16 ? FN<float, bf16, R> : FN<float, float, R>))
 
+namespace ats {
+
+int ring_set_wait_budget(long long cycles) {
+  const long long v = cycles > 0 ? cycles : kRingBudget;
+  cudaError_t e = cudaMemcpyToSymbol(g_ring_wait_budget, &v, sizeof(v));
+  if (e != cudaSuccess) return fail(ATS_ECUDA, "set_wait_budget (rmsnorm): %s", cudaGetErrorString(e));
+  return ATS_OK;
+}
+
+int ring_take_status(int* code) {
+  const int zero = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(code, g_ring_status, sizeof(int));
+  if (e == cudaSuccess && *code != 0) e = cudaMemcpyToSymbol(g_ring_status, &zero, sizeof(int));
+  if (e != cudaSuccess) return fail(ATS_ECUDA, "rmsnorm_status: %s", cudaGetErrorString(e));
+  return ATS_OK;
+}
+
+}  // namespace ats
+
 extern "C" {
 
 int ats_rmsnorm_status(int* status) {
   if (status == nullptr) return fail(ATS_EBADARG, "rmsnorm_status: null output");
-  cudaError_t e = cudaMemcpyFromSymbol(status, g_ring_status, sizeof(int));
-  if (e != cudaSuccess) return fail(ATS_ECUDA, "rmsnorm_status: %s", cudaGetErrorString(e));
+  ATS_TRY(ring_take_status(status));
   return *status == 0 ? ATS_OK : fail(ATS_ETIMEOUT, "rmsnorm: a bounded device wait gave up (code %d)", *status);
 }
 
@@ -983,7 +1009,10 @@ extern "C" int ats_rmsnorm_bwd_noalloc(const void* dy, const void* x, ats_dtype 
   ATS_TRY(scratch_for_current_device(&scratch));
   // kBwdMaxBlocks partial rows of `hidden` floats fit: hidden <= kNoAllocMaxHidden.
   // Every block that runs writes its whole partial row before the reduce reads
-  // it, and the reduce reads only those rows, so nothing needs clearing.
+  // it (a block whose bounded wait gave up writes one too), and the reduce
+  // reads only those rows, so nothing needs clearing.  A call whose wait gave
+  // up (ats_rmsnorm_status) leaves undefined dx and dw; the next call's rows
+  // overwrite what it left.
   auto fn = ATS_DISPATCH2(x_dtype, w_dtype, launch_bwd, false);
   return fn(dy, x, w, dx, nullptr, dw, scratch, rows, hidden, eps, (cudaStream_t)stream);
 }

@@ -782,7 +782,8 @@ class ExpertParallelMoE(nn.Module):
 
     def __init__(self, hidden_size: int, intermediate_size: int, num_experts: int, num_layers: int,
                  top_k: int = 2, capacity_factor: float = 1.25, load_balancing_weight: float = 0.01,
-                 group=None, exchange: str = "packed", overlap_parts: int = 1, comm_sms: int | None = None) -> None:
+                 group=None, exchange: str = "packed", overlap_parts: int = 1, comm_sms: int | None = None,
+                 ep_size: int | None = None) -> None:
         super().__init__()
         if exchange not in ("packed", "slots", "peer"):
             raise ValueError(f"exchange must be 'packed', 'slots' or 'peer', got {exchange!r}")
@@ -790,8 +791,14 @@ class ExpertParallelMoE(nn.Module):
             comm_sms = 0 if exchange == "peer" else 16
         self.exchange = exchange
         self.group = group
-        self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
-        self.rank = dist.get_rank(group) if self.world > 1 else 0
+        if ep_size is None:  # the given group (or the default one), bound now
+            self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+            self.rank = dist.get_rank(group) if self.world > 1 else 0
+            self._bound = True
+        else:  # ep_size ranks, bound at the first forward (the process group may not exist yet)
+            if ep_size < 1:
+                raise ValueError(f"ep_size must be >= 1, got {ep_size}")
+            self.world, self.rank, self._bound = ep_size, 0, ep_size == 1
         if num_experts % self.world != 0:
             raise ValueError(f"num_experts={num_experts} must be divisible by the expert-parallel size {self.world}")
         if not 1 <= top_k <= min(num_experts, 16):
@@ -816,6 +823,27 @@ class ExpertParallelMoE(nn.Module):
         self.last_expert_utilization: dict[int, float] | None = None
         self.last_counts: torch.Tensor | None = None
 
+    def _bind(self) -> None:
+        """Resolve the expert-parallel group of an ``ep_size`` layer: the default
+        group when its size is ep_size, else groups of ep_size consecutive ranks
+        (every rank creates all of them, in the same order, at its first forward)."""
+        if self._bound:
+            return
+        if not (dist.is_available() and dist.is_initialized()):
+            raise RuntimeError(f"MoELayer(ep_size={self.world}) needs torch.distributed initialised before its "
+                               f"first forward. Fix: launch with torchrun and init the process group, or use "
+                               f"ep_size=1.")
+        ws, me = dist.get_world_size(), dist.get_rank()
+        if ws % self.world != 0:
+            raise ValueError(f"ep_size={self.world} must divide the world size {ws}")
+        if ws != self.world:
+            for i in range(ws // self.world):
+                g = dist.new_group(list(range(i * self.world, (i + 1) * self.world)))
+                if i == me // self.world:
+                    self.group = g
+        self.rank = dist.get_rank(self.group)
+        self._bound = True
+
     @torch.no_grad()
     def rebalance(self, load=None, perm=None) -> torch.Tensor:
         """Relabel the experts so that every rank's experts carry about the same
@@ -837,6 +865,7 @@ class ExpertParallelMoE(nn.Module):
         bias, must be re-indexed with perm by the caller.  Call it before an
         optimizer holds per-parameter state: that state does not move.  An
         explicit ``perm`` (same on every rank) may be given instead of ``load``."""
+        self._bind()
         if perm is None:
             load = [float(v) for v in torch.as_tensor(load).flatten().tolist()]
             if len(load) != self.num_experts:
@@ -887,6 +916,7 @@ class ExpertParallelMoE(nn.Module):
         if H != self.hidden_size:
             raise ValueError(f"MoE expected hidden_size={self.hidden_size}, got {H}.")
         _lib.require_cuda("ExpertParallelMoE", x)
+        self._bind()
         flat = x.reshape(-1, H).contiguous()
         T = flat.shape[0]
         cap = capacity_for(T, self.top_k, self.num_experts, self.capacity_factor)

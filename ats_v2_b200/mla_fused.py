@@ -14,7 +14,8 @@ As in the reference module, ``HAS_TRITON`` says whether the fused GPU kernel
 is available (here: whether the CUDA library is built; no Triton is
 involved) and ``_triton_matmul(a, b)`` is the kernel call for a [M, K] and
 b [K, N] (mla_triton.py:78-104), the name the reference's kernel test imports
-(tests/test_triton.py:194-207).  CPU tensors raise.
+(tests/test_triton.py:194-207).  As in the reference (mla_triton.py:144-148),
+CPU tensors take two plain torch matmuls.
 """
 
 from __future__ import annotations
@@ -102,6 +103,9 @@ def fused_mla_kv_decompress(
     latent_dim = orig_shape[-1]
     out_dim = w_uk.shape[0]
     c_flat = c.reshape(-1, latent_dim)
+    if _lib.on_cpu("fused_mla_kv_decompress", c, w_uk, w_uv):
+        k_flat, v_flat = c_flat @ w_uk.t(), c_flat @ w_uv.t()
+        return k_flat.reshape(*orig_shape[:-1], out_dim), v_flat.reshape(*orig_shape[:-1], out_dim)
     combined = _matmul_nt(c_flat, torch.cat([w_uk, w_uv], dim=0))  # [rows, 2*out_dim]
     k_flat, v_flat = combined.split(out_dim, dim=-1)
     return k_flat.reshape(*orig_shape[:-1], out_dim), v_flat.reshape(*orig_shape[:-1], out_dim)

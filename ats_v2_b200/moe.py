@@ -29,7 +29,7 @@ import torch.nn.functional as F
 from torch import nn
 
 from ats_v2_b200 import _lib
-from ats_v2_b200.ffn import SwiGLU
+from ats_v2_b200.ffn import SwiGLU, require_plain_weights
 
 BASE_LINEAR_STD = 0.02
 
@@ -87,9 +87,12 @@ class LazyUtilization(dict):
 
     def _fill(self) -> None:
         if self._t is not None:
-            vals = self._t.tolist()
-            self._t = None
+            t, self._t = self._t, None
+            vals = t.tolist()
             dict.update(self, {i: float(v) for i, v in enumerate(vals)})
+            if t.is_cuda:  # the host has waited for the device here anyway: report a wait that gave up
+                with torch.cuda.device(t.device):
+                    _lib.check_device_status("MoE layer")
 
     def __getitem__(self, key):
         self._fill()
@@ -340,7 +343,10 @@ def routed_swiglu(x2: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tenso
 
 
 class _CudaMoE(nn.Module):
-    """Counterpart of _PyTorchMoEFallback (moe.py:36-164) on the device stages."""
+    """Counterpart of _PyTorchMoEFallback (moe.py:36-164): the device stages for
+    CUDA tensors; for CPU tensors the reference's own loop over the experts
+    (``_forward_cpu``), so the reference's CPU tests and CPU-built models run
+    unchanged.  A CUDA tensor never takes the CPU loop."""
 
     def __init__(self, hidden_size: int, intermediate_size: int, num_experts: int, top_k: int,
                  capacity_factor: float, load_balancing_weight: float, num_layers: int,
@@ -354,6 +360,7 @@ class _CudaMoE(nn.Module):
         self.top_k = top_k
         self.capacity_factor = capacity_factor
         self.load_balancing_weight = load_balancing_weight
+        self.quantization = quantization
         self.gate = nn.Linear(hidden_size, num_experts, bias=False)
         self.experts = nn.ModuleList(
             [SwiGLU(hidden_size, intermediate_size, quantization=quantization) for _ in range(num_experts)])
@@ -370,8 +377,12 @@ class _CudaMoE(nn.Module):
 
     def compute_routing(self, flat_x: torch.Tensor):
         """(top_k_probs [T,k] f32, top_k_idx [T,k] int64, router_probs [T,E] f32)
-        as moe.py:76-90, on the router kernel; no gradient is tracked."""
-        _lib.require_cuda("compute_routing", flat_x)
+        as moe.py:76-90, on the router kernel; no gradient is tracked.  CPU
+        tensors: the reference's torch formula, with gradients."""
+        if _lib.on_cpu("compute_routing", flat_x, self.gate.weight):
+            router_probs = F.softmax(self.gate(flat_x), dim=-1)
+            top_k_probs, top_k_idx = torch.topk(router_probs, self.top_k, dim=-1)
+            return top_k_probs / top_k_probs.sum(dim=-1, keepdim=True), top_k_idx, router_probs
         logits = self.router_logits(flat_x)
         from ats_v2_b200.moe_fused import _topk
 
@@ -380,11 +391,33 @@ class _CudaMoE(nn.Module):
     def _weights(self):
         return ([e.gate_up_proj.weight for e in self.experts], [e.down_proj.weight for e in self.experts])
 
+    def _forward_cpu(self, x: torch.Tensor):
+        """The reference's single-process loop (moe.py:92-164) on CPU tensors."""
+        batch, seq_len, hidden_size = x.shape
+        flat_x = x.reshape(-1, hidden_size)
+        T = flat_x.shape[0]
+        top_k_probs, top_k_idx, router_probs = self.compute_routing(flat_x)
+        cap = capacity_for(T, self.top_k, self.num_experts, self.capacity_factor)
+        output = torch.zeros_like(flat_x)
+        for e, expert in enumerate(self.experts):
+            tokens = (top_k_idx == e).any(dim=-1).nonzero(as_tuple=True)[0][:cap]
+            if tokens.numel() == 0:
+                continue
+            gate = (top_k_probs[tokens] * (top_k_idx[tokens] == e)).sum(dim=-1, keepdim=True)
+            output.index_add_(0, tokens, expert(flat_x[tokens]) * gate)
+        frac = F.one_hot(top_k_idx, self.num_experts).float().sum(dim=1).mean(dim=0)
+        aux = self.num_experts * torch.sum(router_probs.mean(dim=0) * frac) * self.load_balancing_weight
+        util = frac / frac.sum().clamp(min=1e-8)
+        self.last_expert_utilization = {i: float(v) for i, v in enumerate(util.tolist())}
+        return output.reshape(batch, seq_len, hidden_size), aux
+
     def forward(self, x: torch.Tensor):
         batch, seq_len, hidden_size = x.shape
         if hidden_size != self.hidden_size:
             raise ValueError(f"MoE expected hidden_size={self.hidden_size}, got {hidden_size}.")
-        _lib.require_cuda("MoELayer", x)
+        if _lib.on_cpu("MoELayer", x, self.gate.weight):
+            return self._forward_cpu(x)
+        require_plain_weights(self.quantization, "MoELayer")
         flat_x = x.reshape(-1, hidden_size)
         T = flat_x.shape[0]
         cap = capacity_for(T, self.top_k, self.num_experts, self.capacity_factor)
@@ -398,8 +431,35 @@ class _CudaMoE(nn.Module):
         return out.view(batch, seq_len, hidden_size), aux
 
 
+def expert_parallel_world(ep_size: int) -> bool:
+    """True when ``ep_size`` > 1 ranks can hold the experts: torch.distributed is
+    initialised, or a launcher (torchrun, DeepSpeed) has set WORLD_SIZE for a
+    group it will initialise before the first forward, and the world size is a
+    multiple of ep_size."""
+    if ep_size <= 1:
+        return False
+    import os
+
+    import torch.distributed as dist
+
+    if dist.is_available() and dist.is_initialized():
+        world = dist.get_world_size()
+    else:
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+    return world > 1 and world % ep_size == 0
+
+
 class MoELayer(nn.Module):
-    """Drop-in for ats.model.moe.MoELayer; always the CUDA path (uses_deepspeed=False)."""
+    """Drop-in for ats.model.moe.MoELayer (moe.py:167-274); uses_deepspeed=False.
+
+    ``ep_size`` > 1 in a multi-process run (see ``expert_parallel_world``) makes
+    the layer expert-parallel, as the reference's DeepSpeed MoE does with the
+    same argument (moe.py:193-214, set from gpus*nodes by ats/cli/train.py:
+    400-402): ``self.moe`` is an ``ExpertParallelMoE`` holding num_experts /
+    ep_size local experts, with the router replicated; the ranks of an
+    expert-parallel group are consecutive, bound at the first forward.
+    Otherwise all experts are local, which is what the reference's
+    single-process fallback computes whatever ep_size says."""
 
     def __init__(self, hidden_size: int, intermediate_size: int, num_experts: int, num_layers: int,
                  top_k: int = 2, capacity_factor: float = 1.25, load_balancing_weight: float = 0.01,
@@ -410,8 +470,17 @@ class MoELayer(nn.Module):
         self.ep_size = ep_size
         self.last_expert_utilization: dict[int, float] | None = None
         self.load_balancing_weight = load_balancing_weight
-        self.moe = _CudaMoE(hidden_size, intermediate_size, num_experts, top_k, capacity_factor,
-                            load_balancing_weight, num_layers=num_layers, quantization=quantization)
+        if expert_parallel_world(ep_size):
+            require_plain_weights(quantization, "MoELayer(ep_size > 1)")
+            from ats_v2_b200.ep import ExpertParallelMoE
+
+            self.moe = ExpertParallelMoE(hidden_size, intermediate_size, num_experts, num_layers, top_k=top_k,
+                                         capacity_factor=capacity_factor,
+                                         load_balancing_weight=load_balancing_weight, ep_size=ep_size,
+                                         exchange="peer")
+        else:
+            self.moe = _CudaMoE(hidden_size, intermediate_size, num_experts, top_k, capacity_factor,
+                                load_balancing_weight, num_layers=num_layers, quantization=quantization)
 
     def forward(self, x: torch.Tensor):
         output, aux_loss = self.moe(x)

@@ -15,8 +15,9 @@ As in the reference module, ``HAS_TRITON`` says whether the fused GPU kernel
 is available (here: whether the CUDA library is built; no Triton is
 involved), ``_triton_moe_routing`` is the fused kernel call and
 ``_pytorch_moe_routing`` the plain torch formula the reference's tests compare
-it against (tests/test_triton.py:170-187).  No product path calls
-``_pytorch_moe_routing``.
+it against (tests/test_triton.py:170-187).  ``fused_moe_routing`` runs that
+formula for CPU tensors, as the reference does (moe_triton.py:144-146); CUDA
+tensors always take the kernel.
 """
 
 from __future__ import annotations
@@ -61,7 +62,7 @@ def _pytorch_moe_routing(gate_logits: torch.Tensor, top_k: int):
 
 
 def fused_moe_routing(gate_logits: torch.Tensor, top_k: int):
-    """(top_k_probs, top_k_idx) for gate_logits [num_tokens, num_experts] (CUDA only)."""
+    """(top_k_probs, top_k_idx) for gate_logits [num_tokens, num_experts]."""
     if gate_logits.dim() != 2:
         raise ValueError(
             f"fused_moe_routing expected gate_logits of shape [num_tokens, num_experts], "
@@ -69,6 +70,8 @@ def fused_moe_routing(gate_logits: torch.Tensor, top_k: int):
         )
     if top_k < 1:
         raise ValueError(f"fused_moe_routing requires top_k >= 1, got {top_k}.")
+    if _lib.on_cpu("fused_moe_routing", gate_logits):
+        return _pytorch_moe_routing(gate_logits, top_k)
     return _cuda_moe_routing(gate_logits, top_k)
 
 

@@ -4,12 +4,16 @@
 ``weight`` parameter (ones, [hidden]) and ValueError messages
 (norm.py:11-29).  Its forward computes what F.rms_norm computes
 (norm.py:30-31): float32 arithmetic, one rounding to x's dtype.  Forward and
-backward are single-pass CUDA kernels (``ats_rmsnorm_fwd`` / ``ats_rmsnorm_bwd``).
+backward are single-pass CUDA kernels (``ats_rmsnorm_fwd`` / ``ats_rmsnorm_bwd``)
+for CUDA tensors.  CPU tensors take the reference's own computation,
+``F.rms_norm`` (norm.py:30-31), so the reference's CPU tests and CPU-built
+models run unchanged; a CUDA tensor never does.
 """
 
 from __future__ import annotations
 
 import torch
+import torch.nn.functional as F
 from torch import nn
 
 from ats_v2_b200 import _lib
@@ -56,10 +60,12 @@ class _RMSNormFn(torch.autograd.Function):
 
 
 def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
-    """Functional RMSNorm over the last dim on CUDA (no CPU path)."""
-    _lib.require_cuda("rms_norm", x, weight)
+    """Functional RMSNorm over the last dim: the CUDA kernels for CUDA tensors,
+    the reference's F.rms_norm for CPU tensors."""
     if weight.shape != (x.shape[-1],):
         raise ValueError(f"rms_norm: weight shape {tuple(weight.shape)} must be ({x.shape[-1]},).")
+    if _lib.on_cpu("rms_norm", x, weight):
+        return F.rms_norm(x, (x.shape[-1],), weight, eps)
     return _RMSNormFn.apply(x, weight, eps)
 
 

@@ -13,8 +13,9 @@ The reference's tests import three more names from this module
 ``HAS_TRITON`` says whether the fused GPU kernel is available (here: whether
 the CUDA library is built; no Triton is involved), ``_triton_rmsnorm_residual``
 is the fused kernel call, and ``_pytorch_rmsnorm_residual`` is the plain torch
-formula those tests compare the kernel against.  No product path calls
-``_pytorch_rmsnorm_residual``.
+formula those tests compare the kernel against.  ``fused_rmsnorm_residual``
+runs that formula for CPU tensors, as the reference does
+(norm_triton.py:121-123); CUDA tensors always take the kernel.
 """
 
 from __future__ import annotations
@@ -84,7 +85,7 @@ def _pytorch_rmsnorm_residual(x: torch.Tensor, residual: torch.Tensor, weight: t
 
 def fused_rmsnorm_residual(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor,
                            eps: float = 1e-6) -> torch.Tensor:
-    """``residual + rms_norm(x) * weight`` in one memory pass (CUDA tensors only)."""
+    """``residual + rms_norm(x) * weight``: one memory pass on CUDA; the torch formula on CPU."""
     if x.shape != residual.shape:
         raise ValueError(
             f"fused_rmsnorm_residual: x shape {tuple(x.shape)} must match "
@@ -95,4 +96,6 @@ def fused_rmsnorm_residual(x: torch.Tensor, residual: torch.Tensor, weight: torc
             f"fused_rmsnorm_residual: weight last dim {weight.shape[-1]} must match "
             f"x last dim {x.shape[-1]}."
         )
+    if _lib.on_cpu("fused_rmsnorm_residual", x, residual, weight):
+        return _pytorch_rmsnorm_residual(x, residual, weight, eps)
     return _cuda_rmsnorm_residual(x, residual, weight, eps)

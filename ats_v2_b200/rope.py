@@ -156,12 +156,17 @@ def _prepare(q: torch.Tensor, k: torch.Tensor | None, cos: torch.Tensor, sin: to
 
 def apply_rotary_pos_emb(q: torch.Tensor, k: torch.Tensor, cos: torch.Tensor,
                          sin: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-    """q, k: [batch, heads, seq_len, head_dim] (any b/h/s strides); cos, sin: [seq_len, head_dim]."""
+    """q, k: [batch, heads, seq_len, head_dim] (any b/h/s strides); cos, sin: [seq_len, head_dim].
+    One CUDA launch rotates q and k; CPU tensors take the reference's torch formula."""
     if q.shape[-1] != cos.shape[-1]:
         raise ValueError(
             f"apply_rotary_pos_emb: q head_dim ({q.shape[-1]}) does not match "
             f"cos/sin dim ({cos.shape[-1]})."
         )
+    if _lib.on_cpu("apply_rotary_pos_emb", q, k, cos, sin):
+        # CPU tensors: the reference's torch formula (rope.py:83-86)
+        c, s = cos[None, None], sin[None, None]
+        return q * c + rotate_half(q) * s, (k * c + rotate_half(k) * s if k is not None else None)
     if q.dim() != 4:
         raise ValueError(f"apply_rotary_pos_emb: q must be [batch, heads, seq_len, head_dim], got {tuple(q.shape)}")
     q, k, cos, sin, cs = _prepare(q, k, cos, sin, "apply_rotary_pos_emb")

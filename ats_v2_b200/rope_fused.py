@@ -10,8 +10,9 @@ As in the reference module, ``HAS_TRITON`` says whether the fused GPU kernel
 is available (here: whether the CUDA library is built; no Triton is
 involved), ``_triton_apply_rope`` is the fused kernel call and
 ``_pytorch_apply_rope`` the plain torch formula the reference's tests compare
-it against (tests/test_triton.py:152-167).  No product path calls
-``_pytorch_apply_rope``.
+it against (tests/test_triton.py:152-167).  ``fused_apply_rope`` runs that
+formula for CPU tensors, as the reference does (rope_triton.py:126-128); CUDA
+tensors always take the kernel.
 """
 
 from __future__ import annotations
@@ -40,7 +41,7 @@ def _pytorch_apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -
 
 
 def fused_apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
-    """RoPE on x [batch, heads, seq_len, head_dim] with cos/sin [seq_len, head_dim] (CUDA only)."""
+    """RoPE on x [batch, heads, seq_len, head_dim] with cos/sin [seq_len, head_dim]."""
     if x.dim() != 4:
         raise ValueError(
             f"fused_apply_rope expected x of shape [batch, heads, seq_len, head_dim], "
@@ -51,4 +52,6 @@ def fused_apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> t
             f"fused_apply_rope: x head_dim ({x.shape[-1]}) must match cos/sin dim "
             f"({cos.shape[-1]})."
         )
+    if _lib.on_cpu("fused_apply_rope", x, cos, sin):
+        return _pytorch_apply_rope(x, cos, sin)
     return _cuda_apply_rope(x, cos, sin)

@@ -61,6 +61,24 @@ ATS_API uint64_t ats_kernel_launches(void);
 ATS_API int ats_set_gemm_sm_limit(int sms);
 ATS_API int ats_gemm_sm_limit(void);
 
+/* Status of the bounded device waits on the current device: ATS_OK when no
+ * wait of a tensor-core GEMM or an RMSNorm ring kernel has given up since the
+ * last call, else ATS_ETIMEOUT with the first wait's code in *status.  Reading
+ * clears it.  The outputs of a call whose wait gave up are undefined.
+ * Synchronous (copies two ints from the device): call it where the host waits
+ * for the device anyway.  No reference counterpart (the reference's kernels
+ * have no device-side waits). */
+ATS_API int ats_device_status(int* status);
+
+/* Budget, in SM clock cycles, of the main-loop waits of the tensor-core GEMMs
+ * and the RMSNorm ring kernels launched later on the current device; <= 0
+ * restores the default (about 2 s).  Only a test shortens it, to make a wait
+ * run out and check the ATS_ETIMEOUT path; the waits that drain a CTA's copies
+ * and MMAs in flight before it exits always keep the default budget.
+ * Process-wide per device; not for use while other work runs on the device.
+ * No reference counterpart. */
+ATS_API int ats_set_wait_budget(int64_t cycles);
+
 /* ------------------------------------------------------------------ RMSNorm
  * y = round(x * rsqrt(mean(x^2) + eps) * w), float32 arithmetic, one rounding
  * to x's dtype.  Replaces RMSNorm.forward, ats/model/norm.py:23-31 (F.rms_norm).
@@ -86,7 +104,8 @@ ATS_API int ats_rmsnorm_bwd(const void* dy, const void* x, ats_dtype x_dtype,
 
 /* Device status of the RMSNorm ring kernels since the library loaded: 0 and
  * ATS_OK when every bounded device-side wait completed, else the wait's code
- * and ATS_ETIMEOUT.  Synchronous; for diagnostics. */
+ * and ATS_ETIMEOUT.  Reading clears the word; the outputs of the call whose
+ * wait gave up are undefined.  Synchronous; for diagnostics. */
 ATS_API int ats_rmsnorm_status(int* status);
 
 /* Allocation-free variant of ats_rmsnorm_bwd (no counterpart in the

@@ -40,3 +40,18 @@ def close(actual, expected, dtype: str, min_exact: float | None = None, **tol) -
 def seeded_normal(shape, seed: int, scale: float = 1.0, shift: float = 0.0) -> np.ndarray:
     rng = np.random.default_rng(seed)
     return (shift + scale * rng.standard_normal(shape)).astype(np.float32)
+
+
+def close_f32_sum(actual, expected, abs_sum, rtol: float = 1e-5, k: float = 2e-6) -> None:
+    """A float32 reduction against its float64 value: per element
+    |a - e| <= rtol*|e| + k*sum|terms|.  The first term is the north-star
+    1e-5 relative bound; the second is the rounding a float32 sum of those
+    terms can carry (a sum that cancels to near zero has no relative accuracy
+    to offer), the criterion torch's own float32 reductions meet."""
+    a = np32(actual) if isinstance(actual, torch.Tensor) else np.asarray(actual, np.float32)
+    e = np.asarray(expected, np.float64)
+    bound = rtol * np.abs(e) + k * np.asarray(abs_sum, np.float64)
+    err = np.abs(a.astype(np.float64) - e)
+    bad = err > bound
+    assert not bad.any(), (f"{int(bad.sum())} of {bad.size} elements outside rtol={rtol} + {k}*sum|terms|; "
+                           f"worst excess {float((err - bound).max()):.3e}")
