@@ -101,6 +101,13 @@ SIGNATURES: dict[str, tuple] = {
                                        c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int64, c_int64,
                                        c_int64, c_void_p, c_size_t, c_void_p]),
     "ats_moe_ep_status": (c_int, [c_void_p, c_size_t, c_int, c_int, POINTER(c_int)]),
+    "ats_moe_ep_counts_ints": (c_size_t, [c_int]),
+    "ats_moe_ep_push": (c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int,
+                                c_void_p, c_int64, c_int64, c_int, c_void_p]),
+    "ats_moe_ep_pull": (c_int, [c_void_p, c_int64, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p,
+                                c_int64, c_int64, c_int, c_void_p]),
+    "ats_moe_ep_zero_padding": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int64,
+                                        c_int64, c_int, c_void_p]),
     "ats_swiglu_supported": (c_int, [c_int, c_int64, c_int64, c_int64]),
     "ats_swiglu_workspace_bytes": (c_size_t, []),
     "ats_swiglu_rows": (c_int64, [c_int64]),

@@ -79,13 +79,18 @@ int ats_set_wait_budget(int64_t cycles) {
 
 int ats_device_status(int* status) {
   if (status == nullptr) return ats::fail(ATS_EBADARG, "device_status: null output");
-  int g = 0, r = 0;
+  int g = 0, r = 0, x = 0;
   ATS_TRY(ats::gemm_take_status(&g));
   ATS_TRY(ats::ring_take_status(&r));
+  ATS_TRY(ats::ep_take_status(&x));
   *status = g != 0 ? g : r;
-  if (*status == 0) return ATS_OK;
-  return ats::fail(ATS_ETIMEOUT, "a bounded device wait gave up (%s code %d); the results of that call are undefined",
-                   g != 0 ? "tensor-core GEMM" : "RMSNorm ring", *status);
+  if (*status != 0)
+    return ats::fail(ATS_ETIMEOUT, "a bounded device wait gave up (%s code %d); the results of that call are undefined",
+                     g != 0 ? "tensor-core GEMM" : "RMSNorm ring", *status);
+  *status = x;
+  if (x == 0) return ATS_OK;
+  return ats::fail(ATS_EBADARG, "expert-parallel exchange: a row fell outside its buffer or the ranks' capacities "
+                   "differ (code %d); the rows of that step are undefined", x);
 }
 
 }  // extern "C"

@@ -50,6 +50,9 @@ int num_sms();  // SM count of the current device (cached per device)
 // gave up there since the last call (0: none), which this call clears.
 int ring_set_wait_budget(long long cycles);
 int ring_take_status(int* code);
+// The first failed check of a device-driven exchange kernel on the current
+// device since the last call (0: none), which this call clears.
+int ep_take_status(int* code);
 int gemm_ctas();  // CTAs of a persistent GEMM: num_sms() or this thread's lower limit
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }

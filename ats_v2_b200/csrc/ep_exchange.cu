@@ -1,0 +1,291 @@
+// Device-driven row exchange of the expert-parallel MoE layer.
+//
+// Every rank holds its kept rows in the packed layout: the segment of global
+// expert e starts at seg[e] and is its kept count rounded up to 128 rows.  The
+// expert side of rank d holds, for each part p of its local experts (experts
+// [d*El + p*Ep, +Ep), Ep = El/parts), the segments every source rank keeps for
+// them, source by source in rank order -- the layout ats_moe_ep_segments reads.
+// So row r of rank s, in the segment of expert e = d*El + p*Ep + j, lives on
+// rank d at part p, row
+//   base(s, d, p) + (r - seg_s[d*El + p*Ep]),
+//   base(s, d, p) = sum over sources q < s of the rounded kept rows q keeps for
+//                   the experts of (d, p).
+// The counts every rank all-gathered ([W][2E+3] int32: kept[E], Cp, R,
+// seg[E+1]) are all the kernels need, so the split sizes never visit the host.
+//
+//   push: a warp per kept row stores it (16-byte stores) straight into the
+//         expert rank's buffer through its mapped address (CUDA IPC); the rows
+//         come from the tokens through the plan's row_token (no gathered copy)
+//         or from a row buffer in the packed layout.
+//   pull: the reverse: a warp per kept row loads it from the expert rank's
+//         buffer into the local packed layout.
+//   zero: the receiving rank zeroes the padding rows of its own buffer (the
+//         K-grouped weight-gradient GEMMs sum over them); peers send only
+//         kept rows.
+//
+// No kernel waits on another rank: the caller orders them with collectives
+// (the counts all-gather before a push; a one-element all-reduce after it,
+// before the expert GEMMs read the rows; another after the GEMMs, before a
+// pull).  Each kernel ends with a system-scope fence.  Every index is checked
+// against its buffer before the access; a row that would fall outside is
+// skipped and recorded in the exchange status word (ats_device_status).
+#include "moe_plan.cuh"
+
+namespace ats {
+namespace {
+
+constexpr int kMaxRanks = 64;
+constexpr int kXThreads = 256;
+constexpr int kXWarps = kXThreads / 32;
+constexpr int kUnroll = 8;
+
+}  // namespace
+
+// First failed check of an exchange kernel on this device since the status
+// was last taken (0: none).
+__device__ int g_ep_status;
+
+namespace {
+
+struct XArgs {
+  const int* counts;  // [W][2E+3]
+  int W, me, E, El, Ep, part_lo, part_hi;
+  const uint64_t* peer;  // [W] part-0 addresses of each rank's expert-side buffer
+  int64_t part_rows;     // rows of one part of an expert-side buffer
+  int vec;               // 16-byte chunks per row
+};
+
+__device__ __forceinline__ int cnt_kept(const XArgs& a, int s, int e) { return a.counts[s * (2 * a.E + 3) + e]; }
+__device__ __forceinline__ int cnt_cp(const XArgs& a, int s) { return a.counts[s * (2 * a.E + 3) + a.E]; }
+__device__ __forceinline__ int cnt_seg(const XArgs& a, int s, int e) { return a.counts[s * (2 * a.E + 3) + a.E + 2 + e]; }
+
+__device__ __forceinline__ int rounded(int kept, int cp) {
+  kept = kept < 0 ? 0 : (kept > cp ? cp : kept);
+  return (kept + 127) / 128 * 128;
+}
+
+__device__ __forceinline__ void flag(int code) { atomicCAS(&g_ep_status, 0, code); }
+
+// Shared state of a push/pull block: this rank's segment starts and kept
+// counts, and base(me, d, p) for every destination rank and part.
+struct XShared {
+  int seg[kMaxExperts + 1];
+  int kept[kMaxExperts];
+  int base[kMaxExperts];  // [d * parts + p]
+  int ok;
+};
+
+__device__ void load_shared(const XArgs& a, XShared& sh) {
+  const int parts = a.El / a.Ep;
+  const int cp = cnt_cp(a, a.me);
+  for (int e = threadIdx.x; e <= a.E; e += blockDim.x) {
+    sh.seg[e] = cnt_seg(a, a.me, e);
+    if (e < a.E) sh.kept[e] = cnt_kept(a, a.me, e);
+  }
+  for (int dp = threadIdx.x; dp < a.W * parts; dp += blockDim.x) {
+    const int d = dp / parts, p = dp - d * parts;
+    int b = 0;
+    for (int q = 0; q < a.me; ++q) {
+      const int cq = cnt_cp(a, q);
+      for (int j = 0; j < a.Ep; ++j) b += rounded(cnt_kept(a, q, d * a.El + p * a.Ep + j), cq);
+    }
+    sh.base[dp] = b;
+  }
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    for (int q = 0; q < a.W; ++q) ok &= cnt_cp(a, q) == cp;  // one capacity: one slot size everywhere
+    sh.ok = ok;
+    if (!ok) flag(1);
+  }
+  __syncthreads();
+}
+
+// The expert segment of row r (seg[e] <= r < seg[e+1]).
+__device__ __forceinline__ int seg_of(const XShared& sh, int E, int r) {
+  int lo = 0, hi = E;  // seg[lo] <= r < seg[hi]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (sh.seg[mid] <= r) lo = mid; else hi = mid;
+  }
+  return lo;
+}
+
+// Copies one row of `vec` 16-byte chunks with one warp, kUnroll chunks in flight per lane.
+__device__ __forceinline__ void copy_row(uint4* __restrict__ dst, const uint4* __restrict__ src, int vec, int lane) {
+  for (int c0 = 0; c0 < vec; c0 += 32 * kUnroll) {
+    uint4 v[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int c = c0 + u * 32 + lane;
+      if (c < vec) v[u] = src[c];
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int c = c0 + u * 32 + lane;
+      if (c < vec) dst[c] = v[u];
+    }
+  }
+}
+
+// push (to_peer) or pull (!to_peer) of this rank's kept rows.
+//   push: local source row = src[row_token[r]] (tokens) or src[r] (rows); remote destination.
+//   pull: remote source; local destination dst[r].
+__global__ void __launch_bounds__(kXThreads) ep_move_kernel(XArgs a, const uint4* __restrict__ src,
+                                                            const int* __restrict__ row_token, int64_t src_rows,
+                                                            uint4* __restrict__ dst, int64_t dst_rows, int to_peer) {
+  __shared__ XShared sh;
+  load_shared(a, sh);
+  if (!sh.ok) return;
+  const int parts = a.El / a.Ep;
+  const int lane = threadIdx.x & 31;
+  const int nrows = sh.seg[a.E];
+  for (int r = blockIdx.x * kXWarps + (threadIdx.x >> 5); r < nrows; r += gridDim.x * kXWarps) {
+    const int e = seg_of(sh, a.E, r);
+    if (r - sh.seg[e] >= sh.kept[e]) continue;  // padding row: the receiver zeroes its own
+    const int d = e / a.El, p = (e - d * a.El) / a.Ep;
+    if (p < a.part_lo || p >= a.part_hi) continue;
+    const int64_t prow = (int64_t)sh.base[d * parts + p] + (r - sh.seg[d * a.El + p * a.Ep]);
+    if (prow < 0 || prow >= a.part_rows) {
+      if (lane == 0) flag(2);
+      continue;
+    }
+    uint4* remote = reinterpret_cast<uint4*>(a.peer[d]) + ((int64_t)p * a.part_rows + prow) * a.vec;
+    if (to_peer) {
+      int64_t s = r;
+      if (row_token != nullptr) s = row_token[r];
+      if (s < 0 || s >= src_rows) {
+        if (lane == 0) flag(3);
+        continue;
+      }
+      copy_row(remote, src + s * a.vec, a.vec, lane);
+    } else {
+      if (r >= dst_rows) {
+        if (lane == 0) flag(4);
+        continue;
+      }
+      copy_row(dst + (int64_t)r * a.vec, remote, a.vec, lane);
+    }
+  }
+  __threadfence_system();
+}
+
+// The receiving rank zeroes the padding rows of parts [part_lo, part_hi) of
+// its expert-side buffer: one block per (part, source, local expert) segment.
+__global__ void __launch_bounds__(kXThreads) ep_zero_kernel(XArgs a, uint4* __restrict__ buf) {
+  const int nseg = a.W * a.Ep;  // segments of one part
+  const int p = a.part_lo + blockIdx.x / nseg;
+  const int sj = blockIdx.x - (p - a.part_lo) * nseg;
+  const int s = sj / a.Ep, j = sj - s * a.Ep;
+  const int e = a.me * a.El + p * a.Ep + j;
+  __shared__ int start_s;
+  if (threadIdx.x == 0) {
+    int st = 0;
+    for (int q = 0; q < s; ++q)
+      for (int jj = 0; jj < a.Ep; ++jj) st += rounded(cnt_kept(a, q, a.me * a.El + p * a.Ep + jj), cnt_cp(a, q));
+    for (int jj = 0; jj < j; ++jj) st += rounded(cnt_kept(a, s, a.me * a.El + p * a.Ep + jj), cnt_cp(a, s));
+    start_s = st;
+  }
+  __syncthreads();
+  const int cp = cnt_cp(a, s);
+  int kept = cnt_kept(a, s, e);
+  kept = kept < 0 ? 0 : (kept > cp ? cp : kept);
+  const int64_t row0 = (int64_t)start_s + kept, row1 = (int64_t)start_s + rounded(kept, cp);
+  if (row1 > a.part_rows) {
+    if (threadIdx.x == 0) flag(5);
+    return;
+  }
+  uint4* base = buf + (int64_t)p * a.part_rows * a.vec;
+  const uint4 z = make_uint4(0, 0, 0, 0);
+  for (int64_t i = row0 * a.vec + threadIdx.x; i < row1 * a.vec; i += blockDim.x) base[i] = z;
+}
+
+int check_args(const int32_t* counts, int W, int me, int E_local, int parts, int part_lo, int part_hi,
+               const uint64_t* peer, int64_t part_rows, int64_t hidden, ats_dtype dtype, XArgs* a) {
+  if (counts == nullptr || peer == nullptr) return fail(ATS_EBADARG, "moe_ep exchange: null counts or addresses");
+  if (W < 1 || W > kMaxRanks || me < 0 || me >= W || E_local < 1 || W * E_local > kMaxExperts)
+    return fail(ATS_EBADARG, "moe_ep exchange: W=%d rank=%d E_local=%d", W, me, E_local);
+  if (parts < 1 || E_local % parts != 0 || part_lo < 0 || part_hi > parts || part_lo >= part_hi)
+    return fail(ATS_EBADARG, "moe_ep exchange: parts %d [%d, %d) of %d local experts", parts, part_lo, part_hi,
+                E_local);
+  if (dtype != ATS_BF16 && dtype != ATS_F32) return fail(ATS_EBADARG, "moe_ep exchange: dtype");
+  const int64_t row_bytes = hidden * (dtype == ATS_BF16 ? 2 : 4);
+  if (hidden <= 0 || row_bytes % 16 != 0 || row_bytes / 16 > (1 << 20))
+    return fail(ATS_EUNSUPPORTED, "moe_ep exchange: rows of %lld bytes (need a multiple of 16)", (long long)row_bytes);
+  if (part_rows < 0 || part_rows * (row_bytes / 16) * parts >= ((int64_t)1 << 40))
+    return fail(ATS_EBADARG, "moe_ep exchange: part_rows %lld", (long long)part_rows);
+  a->counts = counts;
+  a->W = W;
+  a->me = me;
+  a->E = W * E_local;
+  a->El = E_local;
+  a->Ep = E_local / parts;
+  a->part_lo = part_lo;
+  a->part_hi = part_hi;
+  a->peer = peer;
+  a->part_rows = part_rows;
+  a->vec = (int)(row_bytes / 16);
+  return ATS_OK;
+}
+
+int move_grid(int64_t max_rows) {
+  const int64_t want = (max_rows + kXWarps - 1) / kXWarps;
+  const int64_t cap = (int64_t)num_sms() * 4;
+  return (int)(want < 1 ? 1 : (want < cap ? want : cap));
+}
+
+}  // namespace
+
+int ep_take_status(int* code) {
+  const int zero = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(code, g_ep_status, sizeof(int));
+  if (e == cudaSuccess && *code != 0) e = cudaMemcpyToSymbol(g_ep_status, &zero, sizeof(int));
+  if (e != cudaSuccess) return fail(ATS_ECUDA, "device_status (exchange): %s", cudaGetErrorString(e));
+  return ATS_OK;
+}
+
+}  // namespace ats
+
+using namespace ats;
+
+extern "C" {
+
+size_t ats_moe_ep_counts_ints(int E) { return E > 0 ? (size_t)(2 * E + 3) : 0; }
+
+int ats_moe_ep_push(const void* src, const int32_t* row_token, int64_t src_rows, const int32_t* counts, int W,
+                    int me, int E_local, int parts, int part_lo, int part_hi, const uint64_t* peer_bufs,
+                    int64_t part_rows, int64_t hidden, ats_dtype dtype, void* stream) {
+  XArgs a;
+  ATS_TRY(check_args(counts, W, me, E_local, parts, part_lo, part_hi, peer_bufs, part_rows, hidden, dtype, &a));
+  if (src == nullptr || src_rows < 0) return fail(ATS_EBADARG, "moe_ep_push: null source");
+  if (!aligned16(src)) return fail(ATS_EBADARG, "moe_ep_push: source not 16-byte aligned");
+  // every kept row of this rank is < W*E_local*Cp <= the rows the sender's packed layout can hold
+  ep_move_kernel<<<move_grid((int64_t)W * part_rows * parts), kXThreads, 0, (cudaStream_t)stream>>>(
+      a, static_cast<const uint4*>(src), row_token, src_rows, nullptr, 0, 1);
+  return check_launch("moe_ep_push");
+}
+
+int ats_moe_ep_pull(void* dst, int64_t dst_rows, const int32_t* counts, int W, int me, int E_local, int parts,
+                    int part_lo, int part_hi, const uint64_t* peer_bufs, int64_t part_rows, int64_t hidden,
+                    ats_dtype dtype, void* stream) {
+  XArgs a;
+  ATS_TRY(check_args(counts, W, me, E_local, parts, part_lo, part_hi, peer_bufs, part_rows, hidden, dtype, &a));
+  if (dst == nullptr || dst_rows < 0) return fail(ATS_EBADARG, "moe_ep_pull: null destination");
+  if (!aligned16(dst)) return fail(ATS_EBADARG, "moe_ep_pull: destination not 16-byte aligned");
+  ep_move_kernel<<<move_grid(dst_rows), kXThreads, 0, (cudaStream_t)stream>>>(a, nullptr, nullptr, 0,
+                                                                              static_cast<uint4*>(dst), dst_rows, 0);
+  return check_launch("moe_ep_pull");
+}
+
+int ats_moe_ep_zero_padding(void* buf, const int32_t* counts, int W, int me, int E_local, int parts, int part_lo,
+                            int part_hi, int64_t part_rows, int64_t hidden, ats_dtype dtype, void* stream) {
+  XArgs a;
+  const uint64_t dummy = 0;
+  ATS_TRY(check_args(counts, W, me, E_local, parts, part_lo, part_hi, &dummy, part_rows, hidden, dtype, &a));
+  a.peer = nullptr;
+  if (buf == nullptr || !aligned16(buf)) return fail(ATS_EBADARG, "moe_ep_zero_padding: bad buffer");
+  const int blocks = (part_hi - part_lo) * W * a.Ep;
+  ep_zero_kernel<<<blocks, kXThreads, 0, (cudaStream_t)stream>>>(a, static_cast<uint4*>(buf));
+  return check_launch("moe_ep_zero_padding");
+}
+
+}  // extern "C"

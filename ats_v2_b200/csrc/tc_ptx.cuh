@@ -47,9 +47,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking test of the phase with `parity`.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait: gives up after `budget` SM cycles or when *abort becomes
 // non-zero (another role gave up).  Returns true when the phase completed.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, long long budget) {
+  // a budget of one cycle (a test's setting) gives up unless the phase has already completed:
+  // try_wait may itself suspend the thread for longer than that
+  if (budget <= 1) return mbar_test_wait(bar, parity);
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {

@@ -301,10 +301,12 @@ class _PeerSet:
 
     NAMES = ("xr", "ys", "dyr", "dxs")
 
-    def __init__(self, rows_x: int, rows_t: int, H: int, dtype, device, group, W: int, me: int):
+    def __init__(self, rows_x: int, rows_t: int, H: int, dtype, device, group, W: int, me: int,
+                 names: tuple = NAMES, expert_side: tuple = ("xr", "dyr")):
         self.rows_x, self.rows_t, self.H, self.dtype = rows_x, rows_t, H, dtype
-        self.local = {n: torch.empty((rows_x if n in ("xr", "dyr") else rows_t, H), dtype=dtype, device=device)
-                      for n in self.NAMES}
+        self.local = {n: torch.empty((rows_x if n in expert_side else rows_t, H), dtype=dtype, device=device)
+                      for n in names}
+        self._tables: dict = {}
         hb = _lib.query("ats_ipc_handle_bytes")
         mine = {}
         for n, t in self.local.items():
@@ -335,6 +337,15 @@ class _PeerSet:
     def fits(self, rows_x: int, rows_t: int, H: int, dtype) -> bool:
         return rows_x <= self.rows_x and rows_t <= self.rows_t and H == self.H and dtype == self.dtype
 
+    def table(self, name: str) -> torch.Tensor:
+        """Every rank's buffer `name` as an address of this process, in device
+        memory (int64 [W]): what the device-driven exchange kernels index."""
+        t = self._tables.get(name)
+        if t is None:
+            t = torch.tensor([a[name] for a in self.addr], dtype=torch.int64).to(self.local[name].device)
+            self._tables[name] = t
+        return t
+
     def close(self) -> None:
         for h in self.handles:
             _ipc_close(h)
@@ -357,7 +368,8 @@ class _PeerState:
         self.flags: dict = {}
         self.host: torch.Tensor | None = None
 
-    def acquire(self, rows_x, rows_t, H, dtype, device, group, W, me) -> _PeerSet:
+    def acquire(self, rows_x, rows_t, H, dtype, device, group, W, me, names=_PeerSet.NAMES,
+                expert_side=("xr", "dyr")) -> _PeerSet:
         # every rank makes the same choice: the sizes are maxima over the ranks and
         # the ranks run the same sequence of forwards and backwards
         ps = self._free(rows_x, rows_t, H, dtype)
@@ -379,7 +391,7 @@ class _PeerState:
         if len(self.sets) >= self.MAX_SETS:
             raise RuntimeError(f"ExpertParallelMoE: {len(self.sets)} forwards are waiting for their backward; the "
                                f"peer exchange keeps one buffer set per forward")
-        ps = _PeerSet(rows_x, rows_t, H, dtype, device, group, W, me)
+        ps = _PeerSet(rows_x, rows_t, H, dtype, device, group, W, me, names, expert_side)
         ps.busy = True
         self.sets.append(ps)
         return ps
@@ -451,6 +463,14 @@ def _route(x2, gate_w, bias, E, k, C, L, lbw):
     _lib.call("ats_moe_plan_export", ws.data_ptr(), wsb, T, E, k, C, L, seg_start.data_ptr(), None,
               kept.data_ptr(), st)
     return logits, rws, w32, ws, wsb, R, gates, idx, aux, util, counts, kept, seg_start
+
+
+def _row_tokens(ws, wsb, T, E, k, C, L, R, dev):
+    """The token of every permuted row (int32 [R], -1 = padding) from the plan."""
+    rt = torch.empty(R, dtype=torch.int32, device=dev)
+    _lib.call("ats_moe_plan_export", ws.data_ptr(), wsb, T, E, k, C, L, None, rt.data_ptr(), None,
+              _lib.stream_of(rt))
+    return rt
 
 
 def _gather(x2, ws, wsb, R, E, k, C, L):
@@ -742,6 +762,136 @@ class _EPPeerFn(torch.autograd.Function):
         return (dx, dgate_w.to(gate_dtype), None, None, None, None, *grads)
 
 
+_DEVICE_SET = ("xr", "yr", "dyr", "dxr")  # every buffer of a device-exchange set is expert-side
+
+
+def _exchange_args(allv, W, me, El, parts, lo, hi, table, part_rows, H, dt):
+    return (allv.data_ptr(), W, me, El, parts, lo, hi, table.data_ptr(), part_rows, H, dt)
+
+
+class _EPDeviceFn(torch.autograd.Function):
+    """The expert-parallel layer with a device-driven exchange: no split size
+    ever reaches the host, and no gathered copy of the rows is made.
+
+      forward:  route -> all-gather the [W][2E+3] counts -> zero the padding
+                rows of this rank's expert-side buffer, push this rank's kept
+                token rows (gathered through row_token) into the expert ranks'
+                buffers -> all-reduce(flag) -> expert GEMMs into the mapped y
+                buffer -> all-reduce(flag) -> pull this rank's expert outputs
+                into the local packed layout -> combine.
+      backward: combine backward -> push the output-gradient rows ->
+                all-reduce(flag) -> expert backward into the mapped dx buffer
+                -> all-reduce(flag) -> pull the input-gradient rows -> routing
+                and router backward.
+
+    Ordering between ranks comes only from the collectives, each on the
+    current stream after the kernels it must follow; no kernel waits on
+    another rank.  A buffer set is reused only after its backward: the next
+    forward's counts all-gather completes on no rank before every rank has
+    finished the work queued before it, that backward included."""
+
+    @staticmethod
+    def forward(ctx, x2, gate_w, bias, meta, wgu_stack, wd_stack, *local_weights):
+        E, El, k, C, lbw, Fdim, W, group, parts, state, me, will_backward = meta
+        L = _lib.ATS_MOE_PACKED
+        T, H = x2.shape
+        dev = x2.device
+        dt = _lib.dtype_code(x2.dtype)
+        st = _lib.stream_of(x2)
+        Cp = slot_rows(C)
+        Ep = El // parts
+        part_rows = W * Ep * Cp
+        flag = state.flag(dev)
+        (logits, rws, w32, ws, wsb, R, gates, idx, aux, util, counts, kept,
+         seg_start) = _route(x2, gate_w, bias, E, k, C, L, lbw)
+        row_token = _row_tokens(ws, wsb, T, E, k, C, L, R, dev)
+        mine = torch.cat([kept, torch.tensor([Cp, R], dtype=torch.int32, device=dev), seg_start])
+        allv = torch.empty((W, 2 * E + 3), dtype=torch.int32, device=dev)
+        dist.all_gather_into_tensor(allv, mine, group=group)
+        ps = state.acquire(parts * part_rows, 0, H, x2.dtype, dev, group, W, me, _DEVICE_SET, _DEVICE_SET)
+        ps.owner = weakref.ref(ctx)
+        _lib.call("ats_moe_ep_zero_padding", ps.local["xr"].data_ptr(), allv.data_ptr(), W, me, El, parts, 0,
+                  parts, part_rows, H, dt, st)
+        _lib.call("ats_moe_ep_push", x2.data_ptr(), row_token.data_ptr(), T,
+                  *_exchange_args(allv, W, me, El, parts, 0, parts, ps.table("xr"), part_rows, H, dt), st)
+        dist.all_reduce(flag, group=group)
+        segb = _lib.query("ats_moe_ep_segments_bytes", W, Ep)
+        keep = []
+        for p in range(parts):
+            seg_ws = torch.empty(segb, dtype=torch.uint8, device=dev)
+            rk = allv[:, me * El + p * Ep:me * El + (p + 1) * Ep].contiguous()
+            _lib.call("ats_moe_ep_segments", rk.data_ptr(), W, Ep, C, L, seg_ws.data_ptr(), segb, st)
+            xr = ps.local["xr"][p * part_rows:(p + 1) * part_rows]
+            yr = ps.local["yr"][p * part_rows:(p + 1) * part_rows]
+            h = torch.empty((part_rows, 2 * Fdim), dtype=x2.dtype, device=dev)
+            a = torch.empty((part_rows, Fdim), dtype=x2.dtype, device=dev)
+            _lib.call("ats_moe_ep_experts_fwd", xr.data_ptr(), wgu_stack[p * Ep].data_ptr(),
+                      wd_stack[p * Ep].data_ptr(), h.data_ptr(), a.data_ptr(), yr.data_ptr(), dt, W, Ep, C, H, Fdim,
+                      seg_ws.data_ptr(), segb, st)
+            keep += [h, a, seg_ws]
+        dist.all_reduce(flag, group=group)
+        ys = torch.empty((R, H), dtype=x2.dtype, device=dev)
+        _lib.call("ats_moe_ep_pull", ys.data_ptr(), R,
+                  *_exchange_args(allv, W, me, El, parts, 0, parts, ps.table("yr"), part_rows, H, dt), st)
+        out = torch.empty((T, H), dtype=x2.dtype, device=dev)
+        _lib.call("ats_moe_combine", ys.data_ptr(), out.data_ptr(), dt, T, H, E, k, C, L, ws.data_ptr(), wsb, st)
+        ctx.save_for_backward(logits, gates, idx, ws, ys, allv, wgu_stack, wd_stack, x2, w32, rws, *keep)
+        ctx.meta = (E, El, k, C, lbw, Fdim, W, group, T, H, wsb, R, segb, gate_w.dtype, parts, part_rows, me)
+        ctx.ps, ctx.state = ps, state
+        if not will_backward:
+            state.release(ps)
+        ctx.mark_non_differentiable(util, counts, idx)
+        return out, aux, util, counts, idx
+
+    @staticmethod
+    def backward(ctx, dout, daux, _dutil, _dcounts, _didx):
+        logits, gates, idx, ws, ys, allv, wgu_stack, wd_stack, x2, w32, rws, *keep = ctx.saved_tensors
+        E, El, k, C, lbw, Fdim, W, group, T, H, wsb, R, segb, gate_dtype, parts, part_rows, me = ctx.meta
+        ps, state = ctx.ps, ctx.state
+        L = _lib.ATS_MOE_PACKED
+        Ep = El // parts
+        dev = x2.device
+        dt = _lib.dtype_code(x2.dtype)
+        st = _lib.stream_of(x2)
+        flag = state.flag(dev)
+        if dout is None:
+            dout = torch.zeros((T, H), dtype=x2.dtype, device=dev)
+        dout = dout.to(x2.dtype).contiguous()
+        dys = torch.empty((R, H), dtype=x2.dtype, device=dev)
+        dgate_row = torch.empty(R, dtype=torch.float32, device=dev)
+        _lib.call("ats_moe_combine_bwd", dout.data_ptr(), ys.data_ptr(), dys.data_ptr(), dgate_row.data_ptr(), dt,
+                  T, H, E, k, C, L, ws.data_ptr(), wsb, st)
+        _lib.call("ats_moe_ep_zero_padding", ps.local["dyr"].data_ptr(), allv.data_ptr(), W, me, El, parts, 0,
+                  parts, part_rows, H, dt, st)
+        _lib.call("ats_moe_ep_push", dys.data_ptr(), None, R,
+                  *_exchange_args(allv, W, me, El, parts, 0, parts, ps.table("dyr"), part_rows, H, dt), st)
+        dist.all_reduce(flag, group=group)
+        dwgu = torch.empty_like(wgu_stack)
+        dwd = torch.empty_like(wd_stack)
+        for p in range(parts):
+            h, a, seg_ws = keep[3 * p:3 * p + 3]
+            sl = slice(p * part_rows, (p + 1) * part_rows)
+            xr, dyr, dxr = ps.local["xr"][sl], ps.local["dyr"][sl], ps.local["dxr"][sl]
+            dh = torch.empty((part_rows, 2 * Fdim), dtype=x2.dtype, device=dev)
+            _lib.call("ats_moe_ep_experts_bwd", dyr.data_ptr(), xr.data_ptr(), h.data_ptr(), a.data_ptr(),
+                      wgu_stack[p * Ep].data_ptr(), wd_stack[p * Ep].data_ptr(), dh.data_ptr(), dxr.data_ptr(),
+                      dwgu[p * Ep].data_ptr(), dwd[p * Ep].data_ptr(), dt, W, Ep, C, H, Fdim, seg_ws.data_ptr(),
+                      segb, st)
+        # the routing gradient needs only the gate-row gradients: it is queued before the exchange's wait
+        dlogits = torch.empty((T, E), dtype=torch.float32, device=dev)
+        daux_t = daux.to(torch.float32).contiguous() if daux is not None else None
+        _lib.call("ats_moe_route_bwd", logits.data_ptr(), gates.data_ptr(), idx.data_ptr(), dgate_row.data_ptr(),
+                  _lib.ptr(daux_t), dlogits.data_ptr(), T, E, k, C, L, float(lbw), ws.data_ptr(), wsb, st)
+        dist.all_reduce(flag, group=group)
+        dxs = torch.empty((R, H), dtype=x2.dtype, device=dev)
+        _lib.call("ats_moe_ep_pull", dxs.data_ptr(), R,
+                  *_exchange_args(allv, W, me, El, parts, 0, parts, ps.table("dxr"), part_rows, H, dt), st)
+        dx, dgate_w = router_backward(dlogits, x2, w32, rws, dxs, ws, wsb, (T, E, k, C, L), True)
+        state.release(ps)
+        grads = [dwgu[e] for e in range(El)] + [dwd[e] for e in range(El)]
+        return (dx, dgate_w.to(gate_dtype), None, None, None, None, *grads)
+
+
 def balanced_placement(load: list[float], world: int) -> list[int]:
     """A permutation perm of the experts such that rank r hosts the experts
     perm[r*E_local:(r+1)*E_local] and the ranks' summed loads are close:
@@ -785,10 +935,10 @@ class ExpertParallelMoE(nn.Module):
                  group=None, exchange: str = "packed", overlap_parts: int = 1, comm_sms: int | None = None,
                  ep_size: int | None = None) -> None:
         super().__init__()
-        if exchange not in ("packed", "slots", "peer"):
-            raise ValueError(f"exchange must be 'packed', 'slots' or 'peer', got {exchange!r}")
+        if exchange not in ("packed", "slots", "peer", "device"):
+            raise ValueError(f"exchange must be 'packed', 'slots', 'peer' or 'device', got {exchange!r}")
         if comm_sms is None:
-            comm_sms = 0 if exchange == "peer" else 16
+            comm_sms = 0 if exchange in ("peer", "device") else 16
         self.exchange = exchange
         self.group = group
         if ep_size is None:  # the given group (or the default one), bound now
@@ -927,13 +1077,18 @@ class ExpertParallelMoE(nn.Module):
         bias = logit_bias.detach().float().contiguous() if logit_bias is not None else None
         head = (self.num_experts, self.num_local_experts, self.top_k, cap, self.load_balancing_weight,
                 wgu[0].shape[0] // 2, self.world, self.group)
-        if self.exchange == "peer" and self.world > 1:
+        if self.exchange == "device" and self.world > 1:
+            will_backward = torch.is_grad_enabled() and (flat.requires_grad or any(
+                p.requires_grad for p in self.parameters()))
+            meta = head + (self.overlap_parts, self._peer, self.rank, will_backward)
+            fn = _EPDeviceFn
+        elif self.exchange == "peer" and self.world > 1:
             will_backward = torch.is_grad_enabled() and (flat.requires_grad or any(
                 p.requires_grad for p in self.parameters()))
             meta = head + (self.overlap_parts, self._gemm_sms(flat.device), self._peer, self.rank, will_backward)
             fn = _EPPeerFn
         else:
-            mode = "packed" if self.exchange == "peer" else self.exchange
+            mode = "packed" if self.exchange in ("peer", "device") else self.exchange
             meta = head + (mode, self.overlap_parts, self._gemm_sms(flat.device))
             fn = _EPMoEFn
         out, aux, util, counts, _ = fn.apply(flat, self.gate.weight, bias, meta, stacked(wgu), stacked(wd), *wgu, *wd)

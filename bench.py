@@ -675,15 +675,19 @@ class MoEEPWorkload(Workload):
     metric = "moe_ep_layer_fwd_bwd_tokens_per_s"
     unit = "tokens/s"
     T, H, F, E, K, CF = 32768, 4096, 1408, 64, 2, 1.25
-    # row exchange: the kept rows copied by the copy engines into the peers' mapped buffers,
-    # in 2 expert parts so that one part's transfers overlap the other's expert GEMMs
-    EXCHANGE, PARTS, COMM_SMS = "peer", 2, 0
+    # row exchange: kernels store the kept rows into the expert ranks' mapped buffers and load the
+    # results back, with the split sizes never on the host (--ep-exchange peer: copy-engine copies
+    # planned on the host, in overlapped parts)
+    EXCHANGE, PARTS, COMM_SMS = "device", 1, 0
 
     def parts(self):
         return self.PARTS if self.world > 1 else 1
 
     def exchange_text(self):
-        if self.EXCHANGE == "peer":
+        if self.EXCHANGE == "device":
+            how = ("kernels store the kept rows into the expert ranks' IPC-mapped buffers over NVLink and load "
+                   "the results back; split sizes stay on the device")
+        elif self.EXCHANGE == "peer":
             how = "copy-engine copies of the kept rows into the peers' IPC-mapped buffers over NVLink"
         elif self.EXCHANGE == "packed":
             how = "NCCL all-to-all of the kept rows (variable splits)"
@@ -945,7 +949,14 @@ def main() -> int:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-extras", action="store_true", help="only the selected workload")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
+    ap.add_argument("--ep-exchange", default=None, choices=["device", "peer", "packed", "slots"],
+                    help="row exchange of the expert-parallel workload")
+    ap.add_argument("--ep-parts", type=int, default=None, help="expert parts of the expert-parallel exchange")
     args = ap.parse_args()
+    if args.ep_exchange:
+        MoEEPWorkload.EXCHANGE = args.ep_exchange
+    if args.ep_parts:
+        MoEEPWorkload.PARTS = args.ep_parts
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
     world, rank, local = dist_env()

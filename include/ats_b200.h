@@ -63,8 +63,10 @@ ATS_API int ats_gemm_sm_limit(void);
 
 /* Status of the bounded device waits on the current device: ATS_OK when no
  * wait of a tensor-core GEMM or an RMSNorm ring kernel has given up since the
- * last call, else ATS_ETIMEOUT with the first wait's code in *status.  Reading
- * clears it.  The outputs of a call whose wait gave up are undefined.
+ * last call, else ATS_ETIMEOUT with the first wait's code in *status; then
+ * ATS_EBADARG when a device-driven exchange kernel (ats_moe_ep_push/pull/
+ * zero_padding) skipped a row that fell outside its buffer.  Reading clears
+ * both.  The outputs of a call whose wait gave up are undefined.
  * Synchronous (copies two ints from the device): call it where the host waits
  * for the device anyway.  No reference counterpart (the reference's kernels
  * have no device-side waits). */
@@ -308,6 +310,40 @@ ATS_API int ats_moe_ep_experts_bwd(const void* dy, const void* xr, const void* h
                            void* dh, void* dxr, void* dw_gate_up, void* dw_down, ats_dtype dtype,
                            int W, int E_local, int64_t capacity, int64_t H, int64_t F,
                            const void* seg_workspace, size_t seg_workspace_bytes, void* stream);
+
+/* Device-driven row exchange of the expert-parallel layer (no reference
+ * counterpart: it replaces DeepSpeed's all-to-all dispatch and combine,
+ * ats/model/moe.py:207-214, for ranks on one node).  The split sizes never
+ * reach the host: every kernel reads the all-gathered counts
+ * [W][ats_moe_ep_counts_ints(E)] int32, each rank's row being (kept[E], Cp, R,
+ * seg_start[E+1]) from ats_moe_plan_export of its packed-layout plan.  A
+ * kept row r of rank `me` in the segment of expert e = d*E_local + p*Ep + j
+ * (Ep = E_local/parts) lives in part p of rank d's expert-side buffer at row
+ * base + r - seg_start[d*E_local + p*Ep], base = the rounded kept rows the
+ * ranks before `me` keep for those experts: the layout ats_moe_ep_segments
+ * reads.  peer_bufs [W] (device memory) holds each rank's expert-side buffer
+ * (parts x part_rows rows) as an address this process can store to or load
+ * from (CUDA IPC mappings; rank `me`'s own buffer as is).  Rows are hidden
+ * elements of dtype, a multiple of 16 bytes.  Only kept rows move; the
+ * receiver zeroes its padding rows with ats_moe_ep_zero_padding.  No kernel
+ * waits on another rank: the caller orders them with collectives (after the
+ * counts all-gather; before the expert GEMMs read, or a pull loads, the rows).
+ *   push: the kept rows of parts [part_lo, part_hi) into the peers' buffers;
+ *         source row r is src[row_token[r]] (tokens) or, with row_token NULL,
+ *         src[r] (rows in the packed layout); src has src_rows rows.
+ *   pull: the reverse, into dst [dst_rows] in the packed layout. */
+ATS_API size_t ats_moe_ep_counts_ints(int E);
+ATS_API int ats_moe_ep_push(const void* src, const int32_t* row_token, int64_t src_rows,
+                            const int32_t* counts, int W, int me, int E_local, int parts,
+                            int part_lo, int part_hi, const uint64_t* peer_bufs, int64_t part_rows,
+                            int64_t hidden, ats_dtype dtype, void* stream);
+ATS_API int ats_moe_ep_pull(void* dst, int64_t dst_rows, const int32_t* counts, int W, int me,
+                            int E_local, int parts, int part_lo, int part_hi,
+                            const uint64_t* peer_bufs, int64_t part_rows, int64_t hidden,
+                            ats_dtype dtype, void* stream);
+ATS_API int ats_moe_ep_zero_padding(void* buf, const int32_t* counts, int W, int me, int E_local,
+                                    int parts, int part_lo, int part_hi, int64_t part_rows,
+                                    int64_t hidden, ats_dtype dtype, void* stream);
 
 /* Device status of the EP expert GEMMs run with this segment workspace (as ats_moe_status). */
 ATS_API int ats_moe_ep_status(const void* seg_workspace, size_t seg_workspace_bytes, int W, int E_local,

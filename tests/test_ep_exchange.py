@@ -286,7 +286,7 @@ def test_peer_buffer_pool_reuses_free_sets_and_bounds_waiting_forwards(monkeypat
     made, closed = [], []
 
     class FakeSet:
-        def __init__(self, rows_x, rows_t, H, dtype, device, group, W, me):
+        def __init__(self, rows_x, rows_t, H, dtype, device, group, W, me, names=None, expert_side=None):
             self.rows_x, self.rows_t, self.H, self.dtype = rows_x, rows_t, H, dtype
             self.busy = False
             self.owner = None
@@ -331,7 +331,7 @@ def test_peer_buffer_sets_of_dropped_graphs_come_back_only_when_every_rank_agree
     from ats_v2_b200 import ep as epm
 
     class FakeSet:
-        def __init__(self, rows_x, rows_t, H, dtype, device, group, W, me):
+        def __init__(self, rows_x, rows_t, H, dtype, device, group, W, me, names=None, expert_side=None):
             self.rows_x, self.rows_t, self.H, self.dtype = rows_x, rows_t, H, dtype
             self.busy = False
             self.owner = None

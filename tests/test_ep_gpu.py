@@ -7,9 +7,11 @@ buffer differs).  Two ranks (runs when two GPUs are visible): every rank's outpu
 and input gradient equal the oracle run on that rank's own tokens with all
 experts' weights, and every local expert's weight gradient equals the sum
 over both ranks' tokens -- DeepSpeed's local-capacity semantics.  The
-exchange in overlapped parts (with the GEMMs held to fewer SMs), and the
-peer-memory exchange (copy-engine copies into IPC-mapped peer buffers), must
-give bit-equal results to the NCCL exchange in one piece."""
+exchange in overlapped parts (with the GEMMs held to fewer SMs), the
+peer-memory exchange (copy-engine copies into IPC-mapped peer buffers) and the
+device-driven exchange (kernels that store rows into, and load them from, the
+IPC-mapped buffers, with the split sizes never on the host) must give
+bit-equal results to the NCCL exchange in one piece."""
 
 from __future__ import annotations
 
@@ -38,7 +40,7 @@ def _init_weights(mod_gate, experts, seed):
             ex.down_proj.weight.copy_(0.02 * torch.randn(ex.down_proj.weight.shape, generator=g))
 
 
-@pytest.mark.parametrize("exchange", ["packed", "slots", "peer"])
+@pytest.mark.parametrize("exchange", ["packed", "slots", "peer", "device"])
 @pytest.mark.parametrize("T,H,F,E,k,cf", [(1024, 256, 384, 8, 2, 1.25), (700, 128, 128, 4, 2, 0.6)])
 def test_single_rank_expert_parallel_layer_equals_the_layer(T, H, F, E, k, cf, exchange):
     torch.manual_seed(0)
@@ -149,10 +151,10 @@ def _two_rank_worker(rank, world, port, errq, exchange, parts):
         out, aux = ep(x)
         torch.autograd.backward([out, aux], [gout, torch.ones_like(aux)])
         torch.cuda.synchronize()
-        if parts > 1 or exchange == "peer":
+        if parts > 1 or exchange in ("peer", "device"):
             # the overlapped and the peer-memory exchanges move the same rows to the same GEMMs:
             # bit-equal to the NCCL exchange in one piece
-            one = layer(1, "packed" if exchange == "peer" else exchange)
+            one = layer(1, "packed" if exchange in ("peer", "device") else exchange)
             x1 = x.detach().clone().requires_grad_()
             out1, aux1 = one(x1)
             torch.autograd.backward([out1, aux1], [gout, torch.ones_like(aux1)])
@@ -162,7 +164,7 @@ def _two_rank_worker(rank, world, port, errq, exchange, parts):
                 assert torch.equal(ep.experts[i].gate_up_proj.weight.grad, one.experts[i].gate_up_proj.weight.grad)
                 assert torch.equal(ep.experts[i].down_proj.weight.grad, one.experts[i].down_proj.weight.grad)
             assert torch.equal(ep.gate.weight.grad, one.gate.weight.grad)
-        if exchange == "peer":
+        if exchange in ("peer", "device"):
             # buffer sets are reused: a forward without backward, then a second step, give the same bits
             with torch.no_grad():
                 out_ng, _ = ep(x.detach())
@@ -207,7 +209,7 @@ def _two_rank_worker(rank, world, port, errq, exchange, parts):
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 @pytest.mark.parametrize("exchange,parts", [("packed", 1), ("slots", 1), ("packed", 2), ("slots", 4), ("peer", 1),
-                                            ("peer", 2)])
+                                            ("peer", 2), ("device", 1), ("device", 2)])
 def test_two_ranks_match_the_oracle_on_local_tokens(exchange, parts):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
