@@ -764,6 +764,18 @@ class _EPPeerFn(torch.autograd.Function):
 
 _DEVICE_SET = ("xr", "yr", "dyr", "dxr")  # every buffer of a device-exchange set is expert-side
 
+# When a list, the device exchange records a CUDA event on the current stream at each phase boundary
+# of its forward and backward, as (phase, event) pairs: how a benchmark splits a step between routing,
+# the exchange (waits for the slowest rank included) and the expert GEMMs.  None: nothing is recorded.
+PHASE_EVENTS: list | None = None
+
+
+def _mark(name: str) -> None:
+    if PHASE_EVENTS is not None:
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        PHASE_EVENTS.append((name, ev))
+
 
 def _exchange_args(allv, W, me, El, parts, lo, hi, table, part_rows, H, dt):
     return (allv.data_ptr(), W, me, El, parts, lo, hi, table.data_ptr(), part_rows, H, dt)
@@ -802,11 +814,13 @@ class _EPDeviceFn(torch.autograd.Function):
         Ep = El // parts
         part_rows = W * Ep * Cp
         flag = state.flag(dev)
+        _mark("start")
         (logits, rws, w32, ws, wsb, R, gates, idx, aux, util, counts, kept,
          seg_start) = _route(x2, gate_w, bias, E, k, C, L, lbw)
         row_token = _row_tokens(ws, wsb, T, E, k, C, L, R, dev)
         mine = torch.cat([kept, torch.tensor([Cp, R], dtype=torch.int32, device=dev), seg_start])
         allv = torch.empty((W, 2 * E + 3), dtype=torch.int32, device=dev)
+        _mark("route")
         dist.all_gather_into_tensor(allv, mine, group=group)
         ps = state.acquire(parts * part_rows, 0, H, x2.dtype, dev, group, W, me, _DEVICE_SET, _DEVICE_SET)
         ps.owner = weakref.ref(ctx)
@@ -815,6 +829,7 @@ class _EPDeviceFn(torch.autograd.Function):
         _lib.call("ats_moe_ep_push", x2.data_ptr(), row_token.data_ptr(), T,
                   *_exchange_args(allv, W, me, El, parts, 0, parts, ps.table("xr"), part_rows, H, dt), st)
         dist.all_reduce(flag, group=group)
+        _mark("exchange_out")
         segb = _lib.query("ats_moe_ep_segments_bytes", W, Ep)
         keep = []
         for p in range(parts):
@@ -829,12 +844,15 @@ class _EPDeviceFn(torch.autograd.Function):
                       wd_stack[p * Ep].data_ptr(), h.data_ptr(), a.data_ptr(), yr.data_ptr(), dt, W, Ep, C, H, Fdim,
                       seg_ws.data_ptr(), segb, st)
             keep += [h, a, seg_ws]
+        _mark("experts")
         dist.all_reduce(flag, group=group)
         ys = torch.empty((R, H), dtype=x2.dtype, device=dev)
         _lib.call("ats_moe_ep_pull", ys.data_ptr(), R,
                   *_exchange_args(allv, W, me, El, parts, 0, parts, ps.table("yr"), part_rows, H, dt), st)
+        _mark("exchange_back")
         out = torch.empty((T, H), dtype=x2.dtype, device=dev)
         _lib.call("ats_moe_combine", ys.data_ptr(), out.data_ptr(), dt, T, H, E, k, C, L, ws.data_ptr(), wsb, st)
+        _mark("combine")
         ctx.save_for_backward(logits, gates, idx, ws, ys, allv, wgu_stack, wd_stack, x2, w32, rws, *keep)
         ctx.meta = (E, El, k, C, lbw, Fdim, W, group, T, H, wsb, R, segb, gate_w.dtype, parts, part_rows, me)
         ctx.ps, ctx.state = ps, state
@@ -857,15 +875,18 @@ class _EPDeviceFn(torch.autograd.Function):
         if dout is None:
             dout = torch.zeros((T, H), dtype=x2.dtype, device=dev)
         dout = dout.to(x2.dtype).contiguous()
+        _mark("bwd_start")
         dys = torch.empty((R, H), dtype=x2.dtype, device=dev)
         dgate_row = torch.empty(R, dtype=torch.float32, device=dev)
         _lib.call("ats_moe_combine_bwd", dout.data_ptr(), ys.data_ptr(), dys.data_ptr(), dgate_row.data_ptr(), dt,
                   T, H, E, k, C, L, ws.data_ptr(), wsb, st)
+        _mark("combine_bwd")
         _lib.call("ats_moe_ep_zero_padding", ps.local["dyr"].data_ptr(), allv.data_ptr(), W, me, El, parts, 0,
                   parts, part_rows, H, dt, st)
         _lib.call("ats_moe_ep_push", dys.data_ptr(), None, R,
                   *_exchange_args(allv, W, me, El, parts, 0, parts, ps.table("dyr"), part_rows, H, dt), st)
         dist.all_reduce(flag, group=group)
+        _mark("exchange_out_bwd")
         dwgu = torch.empty_like(wgu_stack)
         dwd = torch.empty_like(wd_stack)
         for p in range(parts):
@@ -882,11 +903,14 @@ class _EPDeviceFn(torch.autograd.Function):
         daux_t = daux.to(torch.float32).contiguous() if daux is not None else None
         _lib.call("ats_moe_route_bwd", logits.data_ptr(), gates.data_ptr(), idx.data_ptr(), dgate_row.data_ptr(),
                   _lib.ptr(daux_t), dlogits.data_ptr(), T, E, k, C, L, float(lbw), ws.data_ptr(), wsb, st)
+        _mark("experts_bwd")
         dist.all_reduce(flag, group=group)
         dxs = torch.empty((R, H), dtype=x2.dtype, device=dev)
         _lib.call("ats_moe_ep_pull", dxs.data_ptr(), R,
                   *_exchange_args(allv, W, me, El, parts, 0, parts, ps.table("dxr"), part_rows, H, dt), st)
+        _mark("exchange_back_bwd")
         dx, dgate_w = router_backward(dlogits, x2, w32, rws, dxs, ws, wsb, (T, E, k, C, L), True)
+        _mark("router_bwd")
         state.release(ps)
         grads = [dwgu[e] for e in range(El)] + [dwd[e] for e in range(El)]
         return (dx, dgate_w.to(gate_dtype), None, None, None, None, *grads)
