@@ -100,6 +100,22 @@ def expert_fwd(xe, wgu, wd, compute: str):
     return y, g, u, s, a
 
 
+def expert_bwd(dy, xe, wgu, wd, g, u, s, a, compute: str, acc=np.float32):
+    """Backward of expert_fwd for the expert-output gradient dy (ffn.py:42-44
+    under autograd): (dxe, dwgu, dwd), each rounded to `compute`.  `acc` is the
+    accumulation type of the two weight-gradient sums over the rows (float32 as
+    torch's GEMM; float64 for a reference of a float32-accumulated kernel)."""
+    da = round_to(dy @ np.asarray(wd, np.float32), compute)
+    dwd = round_to((dy.T.astype(acc) @ np.asarray(a, acc)).astype(np.float32), compute)
+    ds = round_to(da * u, compute)
+    du = round_to(da * s, compute)
+    dg = round_to(ds * _dsilu(g), compute)
+    dh = np.concatenate([dg, du], axis=-1)
+    dxe = round_to(dh @ np.asarray(wgu, np.float32), compute)
+    dwgu = round_to((dh.T.astype(acc) @ np.asarray(xe, acc)).astype(np.float32), compute)
+    return dxe, dwgu, dwd
+
+
 def moe_forward(x, logits, wgu, wd, top_k: int, capacity_factor: float,
                 lbw: float, compute: str = "f32"):
     """Full MoE layer forward on flattened tokens x [T,H].
@@ -161,14 +177,8 @@ def moe_backward(dout, fwd: dict, x, wgu, wd, lbw: float, compute: str = "f32"):
         dw_tok = np.sum(dcontrib.astype(np.float64) * y, axis=-1).astype(np.float32)
         slot = np.argmax(idx[toks] == e, axis=-1)
         dgates[toks, slot] += dw_tok
-        da = round_to(dy @ np.asarray(wd[e], np.float32), compute)
-        dwd[e] = round_to(dy.T.astype(np.float32) @ a, compute)
-        ds = round_to(da * u, compute)
-        du = round_to(da * s, compute)
-        dg = round_to(ds * _dsilu(g), compute)
-        dh = np.concatenate([dg, du], axis=-1)
-        dx[toks] += round_to(dh @ np.asarray(wgu[e], np.float32), compute)
-        dwgu[e] = round_to(dh.T @ x32[toks], compute)
+        dxe, dwgu[e], dwd[e] = expert_bwd(dy, x32[toks], wgu[e], wd[e], g, u, s, a, compute)
+        dx[toks] += dxe
     # renormalisation backward: gates_i = p_i / S over the selected slots
     top = np.take_along_axis(probs, idx, axis=-1)
     S = np.sum(top, axis=-1, keepdims=True, dtype=np.float32)

@@ -186,8 +186,14 @@ def test_permutation_is_stable_and_capacity_bounded():
 
 
 def test_full_size_single_gpu_config_sampled_tokens():
-    """tokens 8192, hidden 2048, 8 experts top-2, ffn 5632, no drop (cf = E/k):
-    32 sampled tokens checked against the oracle's experts on their own routing."""
+    """tokens 8192, hidden 2048, 8 experts top-2, ffn 5632, no drop (cf = E/k).
+
+    Nothing is dropped, so every token's output and input gradient depend on
+    that token alone (the aux loss is left out of the backward): 32 sampled
+    tokens are checked against the oracle run on them.  The weight gradients of
+    one expert sum over all of its ~2048 rows: the oracle recomputes that
+    expert on exactly those rows, with float64 sums for the two weight
+    gradients, and both must match at the bf16 tolerance."""
     T, H, F, E, k = 8192, 2048, 5632, 8, 2
     torch.manual_seed(0)
     layer = bmoe.MoELayer(H, F, E, num_layers=2, top_k=k, capacity_factor=E / k).cuda()
@@ -198,23 +204,33 @@ def test_full_size_single_gpu_config_sampled_tokens():
             ex.down_proj.weight.normal_(0, 0.02)
     layer.moe.experts.to(torch.bfloat16)
     x = torch.randn(1, T, H, device="cuda").bfloat16().requires_grad_()
+    gout = torch.randn(1, T, H, device="cuda").bfloat16()
     out, aux = layer(x)
-    out.float().sum().add(aux).backward()
+    out.backward(gout)
     logits = layer.moe.router_logits(x.detach().view(T, H))
     gates, idx = fused_moe_routing(logits, k)
+    wg = np32(layer.moe.gate.weight)
+    wgu = np.stack([np32(ex.gate_up_proj.weight) for ex in layer.moe.experts])
+    wd = np.stack([np32(ex.down_proj.weight) for ex in layer.moe.experts])
+    xs_all, gs_all, lg_all = np32(x.view(T, H)), np32(gout.view(T, H)), np32(logits)
+    # sampled tokens: output and input gradient (router share included), no aux loss
     toks = torch.randint(0, T, (32,), generator=torch.Generator().manual_seed(3)).tolist()
-    xs = np32(x.view(T, H)[toks])
-    gts, ids = np32(gates[toks]), idx[toks].cpu().numpy()
-    ref = np.zeros((len(toks), H), np.float32)
-    for e in range(E):  # ascending expert order, as the combine accumulates
-        rows = [i for i in range(len(toks)) if e in ids[i]]
-        if not rows:
-            continue
-        ex = layer.moe.experts[e]
-        y, *_ = omoe.expert_fwd(xs[rows], np32(ex.gate_up_proj.weight), np32(ex.down_proj.weight), "bf16")
-        w = np.array([gts[i][list(ids[i]).index(e)] for i in rows], np.float32)
-        ref[rows] = round_bf16(ref[rows] + round_bf16(y * w[:, None]))
-    close(out.view(T, H)[toks], ref, "bf16")
-    assert torch.isfinite(x.grad).all()
+    fwd = omoe.moe_forward(xs_all[toks], lg_all[toks], wgu, wd, k, E / k, 0.0, "bf16")
+    assert fwd["cap"] >= len(toks)  # nothing dropped in the sample either
+    close(out.view(T, H)[toks], fwd["out"], "bf16")
+    b = omoe.moe_layer_backward_full(gs_all[toks], fwd, xs_all[toks], wg, wgu, wd, 0.0, "bf16")
+    close(x.grad.view(T, H)[toks], b["dx"], "bf16")
+    # one expert's weight gradients over all of its rows
+    e = 3
+    ids, gts = idx.cpu().numpy(), np32(gates)
+    rows = np.nonzero((ids == e).any(axis=1))[0]
+    assert rows.size > 1000
+    wgt = np.array([gts[t][list(ids[t]).index(e)] for t in rows], np.float32)
+    y, g, u, s_, a = omoe.expert_fwd(xs_all[rows], wgu[e], wd[e], "bf16")
+    dy = round_bf16(gs_all[rows] * wgt[:, None])
+    _, dwgu_e, dwd_e = omoe.expert_bwd(dy, xs_all[rows], wgu[e], wd[e], g, u, s_, a, "bf16", acc=np.float64)
+    close(layer.moe.experts[e].down_proj.weight.grad, dwd_e, "bf16")
+    close(layer.moe.experts[e].gate_up_proj.weight.grad, dwgu_e, "bf16")
     for ex in layer.moe.experts:
         assert torch.isfinite(ex.gate_up_proj.weight.grad.float()).all()
+        assert torch.isfinite(ex.down_proj.weight.grad.float()).all()
