@@ -1,9 +1,9 @@
 """Generate the golden vectors that pin the oracle to the reference.
 
-Run in a container that holds the reference source tree (default
-``/root/reference``, override with ATS_REFERENCE_DIR):
+Run it with an ats-v2 source tree, named by the first argument or by
+ATS_REFERENCE_DIR:
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py <ats-v2 checkout>
 
 It imports the reference's own modules (``ats.model.norm``, ``rope``,
 ``norm_triton``, ``rope_triton``, ``moe_triton``, ``moe``, ``ffn``,
@@ -34,13 +34,14 @@ from pathlib import Path
 import numpy as np
 import torch
 
-REF = os.environ.get("ATS_REFERENCE_DIR", "/root/reference")
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("ATS_REFERENCE_DIR", "")
 OUT = Path(__file__).resolve().parent
 
 
 def _import_reference():
-    if not Path(REF, "ats", "model").is_dir():
-        raise SystemExit(f"reference tree not found at {REF}")
+    if not REF or not Path(REF, "ats", "model").is_dir():
+        raise SystemExit("name an ats-v2 source tree: make_golden.py <checkout> (or set ATS_REFERENCE_DIR); "
+                         f"got {REF!r}")
     sys.path.insert(0, REF)
     import ats.model.mla_triton as mla_triton
     import ats.model.moe as moe
