@@ -229,8 +229,13 @@ def test_full_size_single_gpu_config_sampled_tokens():
     y, g, u, s_, a = omoe.expert_fwd(xs_all[rows], wgu[e], wd[e], "bf16")
     dy = round_bf16(gs_all[rows] * wgt[:, None])
     _, dwgu_e, dwd_e = omoe.expert_bwd(dy, xs_all[rows], wgu[e], wd[e], g, u, s_, a, "bf16", acc=np.float64)
-    close(layer.moe.experts[e].down_proj.weight.grad, dwd_e, "bf16")
-    close(layer.moe.experts[e].gate_up_proj.weight.grad, dwgu_e, "bf16")
+    # each summand (dy*a, dh*x) is a product of bf16 values that the two sides may round a half ulp apart (the
+    # kernel's SwiGLU derivative uses the SFU exponential): over ~2048 rows those differences add up to a
+    # fixed fraction of the gradient's typical size, whatever the element's own size -- hence the bf16
+    # tolerance applied to the tensor's scale (2e-2 of its rms) beside the 2e-2 relative bound
+    for got, ref in ((layer.moe.experts[e].down_proj.weight.grad, dwd_e),
+                     (layer.moe.experts[e].gate_up_proj.weight.grad, dwgu_e)):
+        close(got, ref, "bf16", atol=2e-2 * float(np.sqrt(np.mean(np.square(ref, dtype=np.float64)))))
     for ex in layer.moe.experts:
         assert torch.isfinite(ex.gate_up_proj.weight.grad.float()).all()
         assert torch.isfinite(ex.down_proj.weight.grad.float()).all()
