@@ -103,9 +103,12 @@ SIGNATURES: dict[str, tuple] = {
     "ats_moe_ep_status": (c_int, [c_void_p, c_size_t, c_int, c_int, POINTER(c_int)]),
     "ats_moe_ep_counts_ints": (c_size_t, [c_int]),
     "ats_moe_ep_push": (c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int,
-                                c_void_p, c_int64, c_int64, c_int, c_void_p]),
+                                c_void_p, c_int64, c_int64, c_int, c_int, c_void_p]),
     "ats_moe_ep_pull": (c_int, [c_void_p, c_int64, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p,
-                                c_int64, c_int64, c_int, c_void_p]),
+                                c_int64, c_int64, c_int, c_int, c_void_p]),
+    "ats_moe_ep_experts_bwd_staged": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                              c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int64, c_int64,
+                                              c_int64, c_void_p, c_size_t, c_int, c_void_p]),
     "ats_moe_ep_zero_padding": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int64,
                                         c_int64, c_int, c_void_p]),
     "ats_swiglu_supported": (c_int, [c_int, c_int64, c_int64, c_int64]),

@@ -227,9 +227,11 @@ int check_args(const int32_t* counts, int W, int me, int E_local, int parts, int
   return ATS_OK;
 }
 
-int move_grid(int64_t max_rows) {
+// CTAs of a move kernel: enough warps for the rows, at most 4 per SM, or 4 per SM of the `sms` SMs a caller
+// leaves to the exchange beside a GEMM held to the others (ats_set_gemm_sm_limit).
+int move_grid(int64_t max_rows, int sms) {
   const int64_t want = (max_rows + kXWarps - 1) / kXWarps;
-  const int64_t cap = (int64_t)num_sms() * 4;
+  const int64_t cap = (int64_t)(sms > 0 && sms < num_sms() ? sms : num_sms()) * 4;
   return (int)(want < 1 ? 1 : (want < cap ? want : cap));
 }
 
@@ -253,25 +255,25 @@ size_t ats_moe_ep_counts_ints(int E) { return E > 0 ? (size_t)(2 * E + 3) : 0; }
 
 int ats_moe_ep_push(const void* src, const int32_t* row_token, int64_t src_rows, const int32_t* counts, int W,
                     int me, int E_local, int parts, int part_lo, int part_hi, const uint64_t* peer_bufs,
-                    int64_t part_rows, int64_t hidden, ats_dtype dtype, void* stream) {
+                    int64_t part_rows, int64_t hidden, ats_dtype dtype, int sms, void* stream) {
   XArgs a;
   ATS_TRY(check_args(counts, W, me, E_local, parts, part_lo, part_hi, peer_bufs, part_rows, hidden, dtype, &a));
   if (src == nullptr || src_rows < 0) return fail(ATS_EBADARG, "moe_ep_push: null source");
   if (!aligned16(src)) return fail(ATS_EBADARG, "moe_ep_push: source not 16-byte aligned");
   // every kept row of this rank is < W*E_local*Cp <= the rows the sender's packed layout can hold
-  ep_move_kernel<<<move_grid((int64_t)W * part_rows * parts), kXThreads, 0, (cudaStream_t)stream>>>(
+  ep_move_kernel<<<move_grid((int64_t)W * part_rows * parts, sms), kXThreads, 0, (cudaStream_t)stream>>>(
       a, static_cast<const uint4*>(src), row_token, src_rows, nullptr, 0, 1);
   return check_launch("moe_ep_push");
 }
 
 int ats_moe_ep_pull(void* dst, int64_t dst_rows, const int32_t* counts, int W, int me, int E_local, int parts,
                     int part_lo, int part_hi, const uint64_t* peer_bufs, int64_t part_rows, int64_t hidden,
-                    ats_dtype dtype, void* stream) {
+                    ats_dtype dtype, int sms, void* stream) {
   XArgs a;
   ATS_TRY(check_args(counts, W, me, E_local, parts, part_lo, part_hi, peer_bufs, part_rows, hidden, dtype, &a));
   if (dst == nullptr || dst_rows < 0) return fail(ATS_EBADARG, "moe_ep_pull: null destination");
   if (!aligned16(dst)) return fail(ATS_EBADARG, "moe_ep_pull: destination not 16-byte aligned");
-  ep_move_kernel<<<move_grid(dst_rows), kXThreads, 0, (cudaStream_t)stream>>>(a, nullptr, nullptr, 0,
+  ep_move_kernel<<<move_grid(dst_rows, sms), kXThreads, 0, (cudaStream_t)stream>>>(a, nullptr, nullptr, 0,
                                                                               static_cast<uint4*>(dst), dst_rows, 0);
   return check_launch("moe_ep_pull");
 }

@@ -154,20 +154,23 @@ int simt_experts_fwd(const void* xp, const void* wgu, const void* wd, void* h, v
 template <typename T>
 int simt_experts_bwd(const void* dy, const void* xp, const void* h, const void* a, const void* wgu, const void* wd,
                      void* dh, void* dxp, void* dwgu, void* dwd, int64_t H, int64_t F, const SegTable& sg,
-                     cudaStream_t st) {
+                     cudaStream_t st, int stages) {
   T* dhp = static_cast<T*>(dh);
-  // da = dy Wd_e into the du half of dh : B(k=h,n=f) = Wd_e[h*F+f]
-  ATS_TRY(simt_gemm<T>(Opnd{dy, H, 1, 0}, Opnd{wd, F, 1, H * F}, dhp + F, 2 * F, 0, 0, (int)F, (int)H, false, sg,
-                       st));
-  const dim3 eg((unsigned)(num_sms() * 2), (unsigned)sg.nseg);
-  swiglu_bwd_kernel<T><<<eg, 256, 0, st>>>(static_cast<const T*>(h), dhp, F, sg);
-  ATS_TRY(check_launch("moe_swiglu_bwd"));
+  if (stages & kBwdData) {
+    // da = dy Wd_e into the du half of dh : B(k=h,n=f) = Wd_e[h*F+f]
+    ATS_TRY(simt_gemm<T>(Opnd{dy, H, 1, 0}, Opnd{wd, F, 1, H * F}, dhp + F, 2 * F, 0, 0, (int)F, (int)H, false, sg,
+                         st));
+    const dim3 eg((unsigned)(num_sms() * 2), (unsigned)sg.nseg);
+    swiglu_bwd_kernel<T><<<eg, 256, 0, st>>>(static_cast<const T*>(h), dhp, F, sg);
+    ATS_TRY(check_launch("moe_swiglu_bwd"));
+    // dxp = dh Wgu_e : B(k=j,n=h) = Wgu_e[j*H+h]
+    ATS_TRY(simt_gemm<T>(Opnd{dh, 2 * F, 1, 0}, Opnd{wgu, H, 1, 2 * F * H}, static_cast<T*>(dxp), H, 0, 0, (int)H,
+                         (int)(2 * F), false, sg, st));
+  }
+  if (!(stages & kBwdWeights)) return ATS_OK;
   // dWd_e[h,f] = sum over the expert's rows r of dy[r,h] a[r,f]
   ATS_TRY(simt_gemm<T>(Opnd{dy, 1, H, 0}, Opnd{a, F, 1, 0}, static_cast<T*>(dwd), F, H * F, (int)H, (int)F, 0, true,
                        sg, st));
-  // dxp = dh Wgu_e : B(k=j,n=h) = Wgu_e[j*H+h]
-  ATS_TRY(simt_gemm<T>(Opnd{dh, 2 * F, 1, 0}, Opnd{wgu, H, 1, 2 * F * H}, static_cast<T*>(dxp), H, 0, 0, (int)H,
-                       (int)(2 * F), false, sg, st));
   // dWgu_e[j,h] = sum over the expert's rows r of dh[r,j] xp[r,h]
   return simt_gemm<T>(Opnd{dh, 1, 2 * F, 0}, Opnd{xp, H, 1, 0}, static_cast<T*>(dwgu), H, 2 * F * H, (int)(2 * F),
                       (int)H, 0, true, sg, st);
@@ -185,13 +188,13 @@ int experts_fwd(const void* xp, const void* wgu, const void* wd, void* h, void* 
 
 int experts_bwd(const void* dy, const void* xp, const void* h, const void* a, const void* wgu, const void* wd,
                 void* dh, void* dxp, void* dwgu, void* dwd, ats_dtype dtype, int E, int64_t H, int64_t F,
-                const SegTable& sg, cudaStream_t st) {
+                const SegTable& sg, cudaStream_t st, int stages = kBwdAll) {
   if (dtype == ATS_BF16) {
-    const int r = tc_experts_bwd(dy, xp, h, a, wgu, wd, dh, dxp, dwgu, dwd, E, H, F, sg, st);
+    const int r = tc_experts_bwd(dy, xp, h, a, wgu, wd, dh, dxp, dwgu, dwd, E, H, F, sg, st, 0, stages);
     if (r != ATS_EUNSUPPORTED) return r;
-    return simt_experts_bwd<bf16>(dy, xp, h, a, wgu, wd, dh, dxp, dwgu, dwd, H, F, sg, st);
+    return simt_experts_bwd<bf16>(dy, xp, h, a, wgu, wd, dh, dxp, dwgu, dwd, H, F, sg, st, stages);
   }
-  return simt_experts_bwd<float>(dy, xp, h, a, wgu, wd, dh, dxp, dwgu, dwd, H, F, sg, st);
+  return simt_experts_bwd<float>(dy, xp, h, a, wgu, wd, dh, dxp, dwgu, dwd, H, F, sg, st, stages);
 }
 
 // ---------------------------------------------------------- EP segment table
@@ -478,6 +481,23 @@ int ats_moe_ep_experts_fwd(const void* xr, const void* w_gate_up, const void* w_
   ATS_TRY(check_experts(w_gate_up, w_down, H, F, dtype));
   if (xr == nullptr || h == nullptr || a == nullptr || y == nullptr) return fail(ATS_EBADARG, "moe_ep_experts_fwd: null");
   return experts_fwd(xr, w_gate_up, w_down, h, a, y, dtype, E_local, H, F, sg, (cudaStream_t)stream);
+}
+
+int ats_moe_ep_experts_bwd_staged(const void* dy, const void* xr, const void* h, const void* a,
+                                  const void* w_gate_up, const void* w_down, void* dh, void* dxr, void* dw_gate_up,
+                                  void* dw_down, ats_dtype dtype, int W, int E_local, int64_t capacity, int64_t H,
+                                  int64_t F, const void* seg_workspace, size_t seg_workspace_bytes, int stages,
+                                  void* stream) {
+  SegTable sg;
+  ATS_TRY(ep_table(seg_workspace, seg_workspace_bytes, W, E_local, capacity, &sg));
+  ATS_TRY(check_experts(w_gate_up, w_down, H, F, dtype));
+  if (stages < 1 || stages > kBwdAll) return fail(ATS_EBADARG, "moe_ep_experts_bwd_staged: stages %d", stages);
+  if (dy == nullptr || xr == nullptr || h == nullptr || a == nullptr || dh == nullptr ||
+      ((stages & kBwdData) && dxr == nullptr) ||
+      ((stages & kBwdWeights) && (dw_gate_up == nullptr || dw_down == nullptr)))
+    return fail(ATS_EBADARG, "moe_ep_experts_bwd_staged: null");
+  return experts_bwd(dy, xr, h, a, w_gate_up, w_down, dh, dxr, dw_gate_up, dw_down, dtype, E_local, H, F, sg,
+                     (cudaStream_t)stream, stages);
 }
 
 int ats_moe_ep_experts_bwd(const void* dy, const void* xr, const void* h, const void* a, const void* w_gate_up,

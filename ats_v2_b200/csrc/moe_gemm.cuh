@@ -60,9 +60,13 @@ int tc_gemm_nt_bwd(const void* dc, const void* a, const void* b, void* da, void*
                    const SegTable& sg, cudaStream_t st, int64_t io_rows);
 int tc_experts_fwd(const void* xp, const void* wgu, const void* wd, void* h, void* a, void* y, int E, int64_t H,
                    int64_t F, const SegTable& sg, cudaStream_t st, int64_t io_rows = 0);
+// Stages of the expert backward: the data gradient (dh through the SwiGLU backward, then dxp) and the
+// weight gradients (dWd, dWgu, which need dh).  A caller may run them as two calls, data first, to send dxp
+// on while the weight gradients compute.
+constexpr int kBwdData = 1, kBwdWeights = 2, kBwdAll = 3;
 int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a, const void* wgu, const void* wd,
                    void* dh, void* dxp, void* dwgu, void* dwd, int E, int64_t H, int64_t F, const SegTable& sg,
-                   cudaStream_t st, int64_t io_rows = 0);
+                   cudaStream_t st, int64_t io_rows = 0, int stages = kBwdAll);
 
 // Router GEMMs on the tensor cores (bf16 tokens, float32 router weight as three bf16 parts).
 // The expert count is padded to kRouterEp (one 64-wide tile holds every expert).

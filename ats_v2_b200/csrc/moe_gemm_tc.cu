@@ -730,7 +730,7 @@ int tc_experts_fwd(const void* xp, const void* wgu, const void* wd, void* h, voi
 
 int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a, const void* wgu, const void* wd,
                    void* dh, void* dxp, void* dwgu, void* dwd, int E, int64_t H, int64_t F, const SegTable& sg,
-                   cudaStream_t st, int64_t io_rows) {
+                   cudaStream_t st, int64_t io_rows, int stages) {
   if (!tc_shape_supported(H, F)) return ATS_EUNSUPPORTED;
   const int64_t R = sg.max_rows;
   const int64_t IO = io_rows > 0 ? io_rows : R;  // rows of dy, xp and dxp
@@ -739,7 +739,7 @@ int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a,
   p.seg = sg;
   p.F = (int)F;
   // da = dy Wd_e (B N-major: Wd_e[h][f]) with the SwiGLU backward epilogue -> dh
-  {
+  if (stages & kBwdData) {
     const int bn = pick_bn(F);
     ATS_TRY(make_map(&ma, dy, H, IO, H * 2, 128));
     ATS_TRY(make_map(&mb, wd, F, (uint64_t)E * H, F * 2, 64));
@@ -756,7 +756,7 @@ int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a,
       ATS_TRY((launch_tc<128, false, true, EPI_SWIGLU_BWD, false>(ma, mb, p, (R / BM) * (F / 128), st, &mdh)));
   }
   // dxp = dh Wgu_e (B N-major: Wgu_e[j][h])
-  {
+  if (stages & kBwdData) {
     const int bn = pick_bn(H);
     ATS_TRY(make_map(&ma, dh, 2 * F, R, 2 * F * 2, 128));
     ATS_TRY(make_map(&mb, wgu, H, (uint64_t)E * 2 * F, H * 2, 64));
@@ -772,6 +772,7 @@ int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a,
     else
       ATS_TRY((launch_tc<128, false, true, EPI_STORE, false>(ma, mb, p, (R / BM) * (H / 128), st, &mo)));
   }
+  if (!(stages & kBwdWeights)) return ATS_OK;
   // dWd_e[h][f] = sum over the expert's rows r of dy[r][h] a[r][f]   (A M-major, B N-major)
   {
     const int bn = pick_bn(F);

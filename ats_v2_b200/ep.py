@@ -777,8 +777,8 @@ def _mark(name: str) -> None:
         PHASE_EVENTS.append((name, ev))
 
 
-def _exchange_args(allv, W, me, El, parts, lo, hi, table, part_rows, H, dt):
-    return (allv.data_ptr(), W, me, El, parts, lo, hi, table.data_ptr(), part_rows, H, dt)
+def _exchange_args(allv, W, me, El, parts, lo, hi, table, part_rows, H, dt, sms=0):
+    return (allv.data_ptr(), W, me, El, parts, lo, hi, table.data_ptr(), part_rows, H, dt, sms)
 
 
 class _EPDeviceFn(torch.autograd.Function):
@@ -792,9 +792,13 @@ class _EPDeviceFn(torch.autograd.Function):
                 buffer -> all-reduce(flag) -> pull this rank's expert outputs
                 into the local packed layout -> combine.
       backward: combine backward -> push the output-gradient rows ->
-                all-reduce(flag) -> expert backward into the mapped dx buffer
-                -> all-reduce(flag) -> pull the input-gradient rows -> routing
-                and router backward.
+                all-reduce(flag) -> expert data gradient into the mapped dx
+                buffer -> all-reduce(flag) -> pull the input-gradient rows ->
+                routing and router backward.  The expert weight gradients
+                come after the data gradient; with ``comm_sms`` > 0 they run
+                on the other SMs while the all-reduce and the pull run on a
+                side stream with those SMs, so the return transfer hides
+                behind them.
 
     Ordering between ranks comes only from the collectives, each on the
     current stream after the kernels it must follow; no kernel waits on
@@ -804,7 +808,7 @@ class _EPDeviceFn(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, x2, gate_w, bias, meta, wgu_stack, wd_stack, *local_weights):
-        E, El, k, C, lbw, Fdim, W, group, parts, state, me, will_backward = meta
+        E, El, k, C, lbw, Fdim, W, group, parts, comm_sms, state, me, will_backward = meta
         L = _lib.ATS_MOE_PACKED
         T, H = x2.shape
         dev = x2.device
@@ -854,7 +858,8 @@ class _EPDeviceFn(torch.autograd.Function):
         _lib.call("ats_moe_combine", ys.data_ptr(), out.data_ptr(), dt, T, H, E, k, C, L, ws.data_ptr(), wsb, st)
         _mark("combine")
         ctx.save_for_backward(logits, gates, idx, ws, ys, allv, wgu_stack, wd_stack, x2, w32, rws, *keep)
-        ctx.meta = (E, El, k, C, lbw, Fdim, W, group, T, H, wsb, R, segb, gate_w.dtype, parts, part_rows, me)
+        ctx.meta = (E, El, k, C, lbw, Fdim, W, group, T, H, wsb, R, segb, gate_w.dtype, parts, part_rows, me,
+                    comm_sms)
         ctx.ps, ctx.state = ps, state
         if not will_backward:
             state.release(ps)
@@ -864,7 +869,7 @@ class _EPDeviceFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dout, daux, _dutil, _dcounts, _didx):
         logits, gates, idx, ws, ys, allv, wgu_stack, wd_stack, x2, w32, rws, *keep = ctx.saved_tensors
-        E, El, k, C, lbw, Fdim, W, group, T, H, wsb, R, segb, gate_dtype, parts, part_rows, me = ctx.meta
+        E, El, k, C, lbw, Fdim, W, group, T, H, wsb, R, segb, gate_dtype, parts, part_rows, me, comm_sms = ctx.meta
         ps, state = ctx.ps, ctx.state
         L = _lib.ATS_MOE_PACKED
         Ep = El // parts
@@ -889,26 +894,59 @@ class _EPDeviceFn(torch.autograd.Function):
         _mark("exchange_out_bwd")
         dwgu = torch.empty_like(wgu_stack)
         dwd = torch.empty_like(wd_stack)
-        for p in range(parts):
-            h, a, seg_ws = keep[3 * p:3 * p + 3]
-            sl = slice(p * part_rows, (p + 1) * part_rows)
-            xr, dyr, dxr = ps.local["xr"][sl], ps.local["dyr"][sl], ps.local["dxr"][sl]
-            dh = torch.empty((part_rows, 2 * Fdim), dtype=x2.dtype, device=dev)
-            _lib.call("ats_moe_ep_experts_bwd", dyr.data_ptr(), xr.data_ptr(), h.data_ptr(), a.data_ptr(),
-                      wgu_stack[p * Ep].data_ptr(), wd_stack[p * Ep].data_ptr(), dh.data_ptr(), dxr.data_ptr(),
-                      dwgu[p * Ep].data_ptr(), dwd[p * Ep].data_ptr(), dt, W, Ep, C, H, Fdim, seg_ws.data_ptr(),
-                      segb, st)
-        # the routing gradient needs only the gate-row gradients: it is queued before the exchange's wait
+        dhs = []
+
+        def expert_bwd(stages):
+            for p in range(parts):
+                h, a, seg_ws = keep[3 * p:3 * p + 3]
+                sl = slice(p * part_rows, (p + 1) * part_rows)
+                xr, dyr, dxr = ps.local["xr"][sl], ps.local["dyr"][sl], ps.local["dxr"][sl]
+                if stages & 1:
+                    dhs.append(torch.empty((part_rows, 2 * Fdim), dtype=x2.dtype, device=dev))
+                _lib.call("ats_moe_ep_experts_bwd_staged", dyr.data_ptr(), xr.data_ptr(), h.data_ptr(),
+                          a.data_ptr(), wgu_stack[p * Ep].data_ptr(), wd_stack[p * Ep].data_ptr(), dhs[p].data_ptr(),
+                          dxr.data_ptr(), dwgu[p * Ep].data_ptr(), dwd[p * Ep].data_ptr(), dt, W, Ep, C, H, Fdim,
+                          seg_ws.data_ptr(), segb, stages, st)
+
         dlogits = torch.empty((T, E), dtype=torch.float32, device=dev)
         daux_t = daux.to(torch.float32).contiguous() if daux is not None else None
-        _lib.call("ats_moe_route_bwd", logits.data_ptr(), gates.data_ptr(), idx.data_ptr(), dgate_row.data_ptr(),
-                  _lib.ptr(daux_t), dlogits.data_ptr(), T, E, k, C, L, float(lbw), ws.data_ptr(), wsb, st)
-        _mark("experts_bwd")
-        dist.all_reduce(flag, group=group)
+
+        def route_bwd():  # the routing gradient needs only the gate-row gradients
+            _lib.call("ats_moe_route_bwd", logits.data_ptr(), gates.data_ptr(), idx.data_ptr(),
+                      dgate_row.data_ptr(), _lib.ptr(daux_t), dlogits.data_ptr(), T, E, k, C, L, float(lbw),
+                      ws.data_ptr(), wsb, st)
+
         dxs = torch.empty((R, H), dtype=x2.dtype, device=dev)
-        _lib.call("ats_moe_ep_pull", dxs.data_ptr(), R,
-                  *_exchange_args(allv, W, me, El, parts, 0, parts, ps.table("dxr"), part_rows, H, dt), st)
-        _mark("exchange_back_bwd")
+        if comm_sms > 0:
+            # data gradient, then the return transfer on a side stream with comm_sms SMs while the weight
+            # gradients run on the others
+            expert_bwd(1)
+            _mark("experts_bwd_data")
+            cur = torch.cuda.current_stream(dev)
+            side = state.copy_streams(dev, W)[0]
+            side.wait_stream(cur)
+            with torch.cuda.stream(side):
+                dist.all_reduce(flag, group=group)
+                _lib.call("ats_moe_ep_pull", dxs.data_ptr(), R,
+                          *_exchange_args(allv, W, me, El, parts, 0, parts, ps.table("dxr"), part_rows, H, dt,
+                                          comm_sms), side.cuda_stream)
+            for t in (dxs, allv, flag):
+                t.record_stream(side)
+            sms = torch.cuda.get_device_properties(dev).multi_processor_count
+            with _lib.gemm_sm_limit(max(1, sms - comm_sms)):
+                expert_bwd(2)
+            route_bwd()
+            _mark("experts_bwd_weights")
+            cur.wait_stream(side)
+            _mark("exchange_back_bwd")
+        else:
+            expert_bwd(3)
+            route_bwd()
+            _mark("experts_bwd")
+            dist.all_reduce(flag, group=group)
+            _lib.call("ats_moe_ep_pull", dxs.data_ptr(), R,
+                      *_exchange_args(allv, W, me, El, parts, 0, parts, ps.table("dxr"), part_rows, H, dt), st)
+            _mark("exchange_back_bwd")
         dx, dgate_w = router_backward(dlogits, x2, w32, rws, dxs, ws, wsb, (T, E, k, C, L), True)
         _mark("router_bwd")
         state.release(ps)
@@ -1104,7 +1142,7 @@ class ExpertParallelMoE(nn.Module):
         if self.exchange == "device" and self.world > 1:
             will_backward = torch.is_grad_enabled() and (flat.requires_grad or any(
                 p.requires_grad for p in self.parameters()))
-            meta = head + (self.overlap_parts, self._peer, self.rank, will_backward)
+            meta = head + (self.overlap_parts, self.comm_sms, self._peer, self.rank, will_backward)
             fn = _EPDeviceFn
         elif self.exchange == "peer" and self.world > 1:
             will_backward = torch.is_grad_enabled() and (flat.requires_grad or any(

@@ -1175,11 +1175,15 @@ def main() -> int:
     ap.add_argument("--ep-exchange", default=None, choices=["device", "peer", "packed", "slots"],
                     help="row exchange of the expert-parallel workload")
     ap.add_argument("--ep-parts", type=int, default=None, help="expert parts of the expert-parallel exchange")
+    ap.add_argument("--ep-comm-sms", type=int, default=None,
+                    help="SMs the expert-parallel exchange keeps while it overlaps the expert GEMMs")
     args = ap.parse_args()
     if args.ep_exchange:
         MoEEPWorkload.EXCHANGE = args.ep_exchange
     if args.ep_parts:
         MoEEPWorkload.PARTS = args.ep_parts
+    if args.ep_comm_sms is not None:
+        MoEEPWorkload.COMM_SMS = args.ep_comm_sms
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
     world, rank, local = dist_env()
@@ -1215,6 +1219,8 @@ def main() -> int:
             "gpu_launches": res["gpu_launches"]}
     if "cpu_baseline" in res:
         line["cpu_baseline"] = res["cpu_baseline"]
+    if "phases_ms" in res:
+        line["phases_ms"] = {k: _r(v, 3) for k, v in res["phases_ms"].items()}
     if not args.no_extras:
         extras = {}
         for name, cls in WORKLOADS.items():

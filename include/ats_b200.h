@@ -336,14 +336,26 @@ ATS_API size_t ats_moe_ep_counts_ints(int E);
 ATS_API int ats_moe_ep_push(const void* src, const int32_t* row_token, int64_t src_rows,
                             const int32_t* counts, int W, int me, int E_local, int parts,
                             int part_lo, int part_hi, const uint64_t* peer_bufs, int64_t part_rows,
-                            int64_t hidden, ats_dtype dtype, void* stream);
+                            int64_t hidden, ats_dtype dtype, int sms, void* stream);
 ATS_API int ats_moe_ep_pull(void* dst, int64_t dst_rows, const int32_t* counts, int W, int me,
                             int E_local, int parts, int part_lo, int part_hi,
                             const uint64_t* peer_bufs, int64_t part_rows, int64_t hidden,
-                            ats_dtype dtype, void* stream);
+                            ats_dtype dtype, int sms, void* stream);
+/* `sms` > 0 sizes a push or pull for that many SMs (it runs beside a GEMM held to the others with
+ * ats_set_gemm_sm_limit); 0 sizes it for the whole GPU. */
 ATS_API int ats_moe_ep_zero_padding(void* buf, const int32_t* counts, int W, int me, int E_local,
                                     int parts, int part_lo, int part_hi, int64_t part_rows,
                                     int64_t hidden, ats_dtype dtype, void* stream);
+
+/* ats_moe_ep_experts_bwd in stages: bit 1 the data gradient (dh through the SwiGLU backward, then dxr),
+ * bit 2 the weight gradients (dw_gate_up, dw_down; they read dh).  Run data first, then weights, to send
+ * dxr on while the weight gradients compute; 3 is ats_moe_ep_experts_bwd. */
+ATS_API int ats_moe_ep_experts_bwd_staged(const void* dy, const void* xr, const void* h, const void* a,
+                                          const void* w_gate_up, const void* w_down, void* dh, void* dxr,
+                                          void* dw_gate_up, void* dw_down, ats_dtype dtype, int W,
+                                          int E_local, int64_t capacity, int64_t hidden, int64_t F,
+                                          const void* seg_workspace, size_t seg_workspace_bytes,
+                                          int stages, void* stream);
 
 /* Device status of the EP expert GEMMs run with this segment workspace (as ats_moe_status). */
 ATS_API int ats_moe_ep_status(const void* seg_workspace, size_t seg_workspace_bytes, int W, int E_local,

@@ -77,10 +77,10 @@ def test_push_pull_and_padding_match_the_copy_plan(W, El, parts, C, H, tokens):
         if tokens:
             _lib.call("ats_moe_ep_push", toks[s].data_ptr(), row_tok[s].data_ptr(), toks[s].shape[0],
                       counts.data_ptr(), W, s, El, parts, 0, parts, table.data_ptr(), part_rows, H, _lib.ATS_BF16,
-                      st)
+                      0, st)
         else:
             _lib.call("ats_moe_ep_push", srcs[s].data_ptr(), None, srcs[s].shape[0], counts.data_ptr(), W, s, El,
-                      parts, 0, parts, table.data_ptr(), part_rows, H, _lib.ATS_BF16, st)
+                      parts, 0, parts, table.data_ptr(), part_rows, H, _lib.ATS_BF16, 0, st)
     torch.cuda.synchronize()
     code = ctypes.c_int(0)
     assert _lib.query("ats_device_status", ctypes.byref(code)) == 0 and code.value == 0
@@ -107,7 +107,7 @@ def test_push_pull_and_padding_match_the_copy_plan(W, El, parts, C, H, tokens):
         R = int(allv[s, E + 1])
         out = torch.zeros(R, H, device=dev).bfloat16()
         _lib.call("ats_moe_ep_pull", out.data_ptr(), R, counts.data_ptr(), W, s, El, parts, 0, parts,
-                  table.data_ptr(), part_rows, H, _lib.ATS_BF16, st)
+                  table.data_ptr(), part_rows, H, _lib.ATS_BF16, 16 if s % 2 else 0, st)
         torch.cuda.synchronize()
         seg = allv[s, E + 2:]
         for e in range(E):
@@ -129,7 +129,7 @@ def test_unequal_capacities_are_refused_on_the_device():
     table = torch.tensor([b.data_ptr() for b in bufs], dtype=torch.int64, device=dev)
     src = torch.randn(int(allv[0, E + 1]), H, device=dev).bfloat16()
     _lib.call("ats_moe_ep_push", src.data_ptr(), None, src.shape[0], counts.data_ptr(), W, 0, El, 1, 0, 1,
-              table.data_ptr(), part_rows, H, _lib.ATS_BF16, torch.cuda.current_stream().cuda_stream)
+              table.data_ptr(), part_rows, H, _lib.ATS_BF16, 0, torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
     assert all(torch.count_nonzero(b) == 0 for b in bufs)  # nothing moved
     code = ctypes.c_int(0)
