@@ -65,6 +65,11 @@ SIGNATURES: dict[str, tuple] = {
                                          c_int64, c_float, c_void_p]),
     "ats_rmsnorm_residual_bwd": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p,
                                          c_void_p, c_void_p, c_size_t, c_int64, c_int64, c_float, c_void_p]),
+    "ats_add_rmsnorm_fwd": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int64, c_int64,
+                                    c_float, c_void_p]),
+    "ats_add_rmsnorm_bwd_workspace_bytes": (c_size_t, [c_int64, c_int64]),
+    "ats_add_rmsnorm_bwd": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p,
+                                    c_void_p, c_size_t, c_int64, c_int64, c_float, c_void_p]),
     "ats_rope_apply": (c_int, [c_void_p, c_void_p, c_int64, POINTER(c_int64), POINTER(c_int64),
                                c_void_p, c_void_p, c_int64, POINTER(c_int64), POINTER(c_int64),
                                c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int, c_int, c_void_p]),

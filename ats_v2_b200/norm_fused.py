@@ -99,3 +99,70 @@ def fused_rmsnorm_residual(x: torch.Tensor, residual: torch.Tensor, weight: torc
     if _lib.on_cpu("fused_rmsnorm_residual", x, residual, weight):
         return _pytorch_rmsnorm_residual(x, residual, weight, eps)
     return _cuda_rmsnorm_residual(x, residual, weight, eps)
+
+
+class _AddRMSNormFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, residual, weight, eps):
+        H = x.shape[-1]
+        a = x.reshape(-1, H).contiguous()
+        b = residual.reshape(-1, H).contiguous()
+        w = weight.contiguous()
+        s = torch.empty_like(a)
+        y = torch.empty_like(a)
+        _lib.call("ats_add_rmsnorm_fwd", a.data_ptr(), b.data_ptr(), _lib.dtype_code(a.dtype), w.data_ptr(),
+                  _lib.dtype_code(w.dtype), s.data_ptr(), y.data_ptr(), a.shape[0], H, float(eps),
+                  _lib.stream_of(a))
+        ctx.save_for_backward(s, w)
+        ctx.eps = eps
+        ctx.shape = x.shape
+        return y.view(x.shape), s.view(x.shape)
+
+    @staticmethod
+    def backward(ctx, dy, ds_in):
+        s, w = ctx.saved_tensors
+        rows, H = s.shape
+        dy2 = (dy if dy is not None else torch.zeros_like(s)).reshape(rows, H).to(s.dtype).contiguous()
+        di = ds_in.reshape(rows, H).to(s.dtype).contiguous() if ds_in is not None else None
+        ds = torch.empty_like(s)
+        dw = torch.empty(H, dtype=w.dtype, device=w.device)
+        wsb = _lib.query("ats_add_rmsnorm_bwd_workspace_bytes", rows, H)
+        ws = torch.empty(wsb, dtype=torch.uint8, device=s.device)
+        _lib.call("ats_add_rmsnorm_bwd", dy2.data_ptr(), s.data_ptr(), _lib.ptr(di), _lib.dtype_code(s.dtype),
+                  w.data_ptr(), _lib.dtype_code(w.dtype), ds.data_ptr(), dw.data_ptr(), ws.data_ptr(), wsb, rows, H,
+                  float(ctx.eps), _lib.stream_of(s))
+        ds = ds.view(ctx.shape)
+        return ds, ds, dw, None
+
+
+def add_rmsnorm_supported(x: torch.Tensor, weight: torch.Tensor) -> bool:
+    """Whether the fused kernel covers this shape (16-byte rows of at most 512 chunks)."""
+    H = x.shape[-1]
+    n = 16 // x.element_size()
+    return x.dtype in (torch.float32, torch.bfloat16) and weight.dtype in (torch.float32, torch.bfloat16) \
+        and H % n == 0 and H // n <= 512
+
+
+def fused_add_rmsnorm(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor,
+                      eps: float = 1e-6) -> tuple[torch.Tensor, torch.Tensor]:
+    """``s = residual + x; (rms_norm(s) * weight, s)`` -- the post-attention residual add
+    and RMSNorm of TransformerBlock.forward (ats/model/transformer.py:208-212), whose
+    ``s`` is the block's next residual.  CUDA tensors: one kernel each way (the
+    backward adds the gradient that reaches ``s`` from the next residual add, as
+    autograd would).  CPU tensors: the reference's two torch operations."""
+    if x.shape != residual.shape:
+        raise ValueError(f"fused_add_rmsnorm: x shape {tuple(x.shape)} must match residual shape "
+                         f"{tuple(residual.shape)}.")
+    if weight.shape != (x.shape[-1],):
+        raise ValueError(f"fused_add_rmsnorm: weight shape {tuple(weight.shape)} must be ({x.shape[-1]},).")
+    if _lib.on_cpu("fused_add_rmsnorm", x, residual, weight):
+        s = residual + x
+        return torch.nn.functional.rms_norm(s, (s.shape[-1],), weight, eps), s
+    if residual.dtype != x.dtype:
+        raise TypeError(f"fused_add_rmsnorm: residual dtype {residual.dtype} must equal x dtype {x.dtype}")
+    if not add_rmsnorm_supported(x, weight):
+        from ats_v2_b200.norm import rms_norm
+
+        s = residual + x
+        return rms_norm(s, weight, eps), s
+    return _AddRMSNormFn.apply(x, residual, weight, eps)

@@ -150,6 +150,30 @@ ATS_API int ats_rmsnorm_residual_bwd(const void* dout, const void* x, ats_dtype 
                              void* workspace, size_t workspace_bytes,
                              int64_t rows, int64_t hidden, float eps, void* stream);
 
+/* Residual add fused with the RMSNorm after it, the post-attention step of
+ * TransformerBlock.forward (ats/model/transformer.py:208-212: x = residual +
+ * attn_out; residual = x; h = post_attention_norm(x)).  sum = round(a + b),
+ * the block's next residual, and y = round((sum * rstd(sum)) * w), as
+ * ats_rmsnorm_fwd computes it, in one pass over the rows.  a, b, sum, y:
+ * rows x hidden contiguous, dtype; w: [hidden] in w_dtype.  Rows of at most
+ * 512 16-byte chunks (hidden <= 4096 bf16 or 2048 float32); other shapes return
+ * ATS_EUNSUPPORTED. */
+ATS_API int ats_add_rmsnorm_fwd(const void* a, const void* b, ats_dtype dtype, const void* w,
+                                ats_dtype w_dtype, void* sum, void* y, int64_t rows, int64_t hidden,
+                                float eps, void* stream);
+
+/* Backward: dsum = round(round(dnorm) + dsum_in), the gradient of both a and
+ * b, where dnorm is the RMSNorm backward of dy and dsum_in (may be NULL: zero)
+ * the gradient that reaches sum from its other use (the next residual add) --
+ * the order in which autograd sums them; dw (w_dtype) as ats_rmsnorm_bwd, from
+ * per-block partial rows in ats_add_rmsnorm_bwd_workspace_bytes() of workspace
+ * summed in a fixed order. */
+ATS_API size_t ats_add_rmsnorm_bwd_workspace_bytes(int64_t rows, int64_t hidden);
+ATS_API int ats_add_rmsnorm_bwd(const void* dy, const void* sum, const void* dsum_in, ats_dtype dtype,
+                                const void* w, ats_dtype w_dtype, void* dsum, void* dw, void* workspace,
+                                size_t workspace_bytes, int64_t rows, int64_t hidden, float eps,
+                                void* stream);
+
 /* ------------------------------------------------------------------- RoPE
  * Rotate-half RoPE on q [B,Hq,S,D] and k [B,Hk,S,D] in one launch:
  *   out = round(round(x*cos) + round(rotate_half(x)*sin)),

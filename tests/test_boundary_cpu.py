@@ -133,3 +133,14 @@ def test_ep_size_in_a_process_group_shards_the_experts():
     q = ctx.SimpleQueue()
     mp.start_processes(_ep_worker, args=(2, _free_port(), q), nprocs=2, join=True, start_method="spawn")
     assert q.empty()
+
+
+def test_fused_add_rmsnorm_cpu_is_the_block_step():
+    from ats_v2_b200.norm_fused import fused_add_rmsnorm
+
+    x, r, w = torch.randn(3, 5, 16), torch.randn(3, 5, 16), 1 + 0.1 * torch.randn(16)
+    h, s = fused_add_rmsnorm(x, r, w, 1e-6)
+    assert torch.equal(s, r + x)
+    assert torch.equal(h, torch.nn.functional.rms_norm(r + x, (16,), w, 1e-6))
+    with pytest.raises(ValueError):
+        fused_add_rmsnorm(x, r[:, :4], w)
