@@ -45,6 +45,8 @@ SIGNATURES: dict[str, tuple] = {
                              c_void_p]),
     "ats_gemm_bwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int64, c_int64, c_int64,
                              c_void_p, c_size_t, c_void_p]),
+    "ats_gemm_rope_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int64, c_int64, c_int64, c_void_p,
+                                  c_void_p, c_int64, c_void_p, c_size_t, c_void_p]),
     "ats_ipc_handle_bytes": (c_size_t, []),
     "ats_ipc_export": (c_int, [c_void_p, c_void_p, POINTER(ctypes.c_uint64), POINTER(ctypes.c_uint64)]),
     "ats_ipc_open": (c_int, [c_void_p, POINTER(c_void_p)]),

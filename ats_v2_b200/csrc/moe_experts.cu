@@ -423,6 +423,26 @@ int ats_gemm_bwd(const void* dc, const void* a, const void* b, void* da, void* d
   return tc_gemm_nt_bwd(dc, a, b, da, db, N, K, sg, st, M);
 }
 
+int ats_gemm_rope_fwd(const void* x, const void* w, void* out, int64_t ld_out, ats_dtype dtype, int64_t M, int64_t N,
+                      int64_t K, const void* cos, const void* sin, int64_t seq_len, void* workspace,
+                      size_t workspace_bytes, void* stream) {
+  if (!ats_gemm_supported(dtype, M, N, K))
+    return fail(ATS_EUNSUPPORTED, "gemm_rope_fwd: needs bf16, M >= 128 and N, K multiples of 128 (M=%lld N=%lld "
+                "K=%lld)", (long long)M, (long long)N, (long long)K);
+  if (x == nullptr || w == nullptr || out == nullptr || cos == nullptr || sin == nullptr)
+    return fail(ATS_EBADARG, "gemm_rope_fwd: null");
+  if (seq_len < 1 || M % seq_len != 0 || ld_out < N || (ld_out * 2) % 16 != 0 || !aligned16(out) || !aligned16(cos) ||
+      !aligned16(sin))
+    return fail(ATS_EBADARG, "gemm_rope_fwd: seq_len %lld must divide M=%lld; output stride %lld >= N=%lld, "
+                "16-byte aligned rows and tables", (long long)seq_len, (long long)M, (long long)ld_out, (long long)N);
+  SegTable sg;
+  ATS_TRY(dense_table(workspace, workspace_bytes, M, &sg));
+  cudaStream_t st = (cudaStream_t)stream;
+  dense_table_kernel<<<1, 1, 0, st>>>(static_cast<int*>(workspace), (int)dense_rows(M));
+  ATS_TRY(check_launch("gemm_table"));
+  return tc_gemm_rope_fwd(x, w, out, ld_out, N, K, cos, sin, seq_len, sg, st, M);
+}
+
 int ats_swiglu_status(const void* workspace, size_t workspace_bytes, int* status) {
   if (workspace == nullptr || workspace_bytes < kDenseWsBytes || status == nullptr)
     return fail(ATS_EBADARG, "swiglu_status: bad arguments");

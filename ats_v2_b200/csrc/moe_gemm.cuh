@@ -26,21 +26,48 @@ __device__ __forceinline__ void swiglu_grad(float g, float u, float da, float& d
   dg = round_to<T>((ds * sig) * (1.0f + g * (1.0f - sig)));
 }
 
-// Epilogue forms of the two functions above for bf16 results: the
-// exponential and reciprocal use the SFU (__expf, __frcp_rn); their float32
-// error (a few ulp) is far below half a bf16 ulp, so the rounded results
-// match the accurate forms except at rare exact ties.
-__device__ __forceinline__ float silu_mul_fast_bf16(float g, float u) {
-  const float s = round_to<bf16>(g * __frcp_rn(1.0f + __expf(-g)));
-  return round_to<bf16>(s * u);
+// Packed forms for the tensor-core epilogues, on pairs of columns.  A product of two bf16 values is exact
+// in float32, so mul.rn.bf16x2 rounds the same product the float32 path rounds, once.  The sigmoid's
+// reciprocal is rcp.approx (relative error below 2^-22, far under half a bf16 ulp): the rounded results
+// equal those of a correctly rounded reciprocal except at rare exact ties.
+__device__ __forceinline__ uint32_t bf2_mul(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t bf2_add(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t bf2_pack(float lo, float hi) {  // round both to bf16, lo in the low half
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+__device__ __forceinline__ float bf2_lo(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float bf2_hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
+__device__ __forceinline__ float rcp_approx(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ float sigmoid_fast(float g) { return rcp_approx(1.0f + __expf(-g)); }
+
+// SwiGLU forward on a column pair: g2, u2 hold bf16 gate and up values; returns a = round(round(g*sig(g)) * u).
+__device__ __forceinline__ uint32_t silu_mul_bf2(uint32_t g2, uint32_t u2) {
+  const float gl = bf2_lo(g2), gh = bf2_hi(g2);
+  return bf2_mul(bf2_pack(gl * sigmoid_fast(gl), gh * sigmoid_fast(gh)), u2);
 }
 
-__device__ __forceinline__ void swiglu_grad_fast_bf16(float g, float u, float da, float& dg, float& du) {
-  const float sig = __frcp_rn(1.0f + __expf(-g));
-  const float s = round_to<bf16>(g * sig);
-  du = round_to<bf16>(da * s);
-  const float ds = round_to<bf16>(da * u);
-  dg = round_to<bf16>((ds * sig) * (1.0f + g * (1.0f - sig)));
+// SwiGLU backward on a column pair (the formulas of swiglu_grad): g2, u2 the bf16 pre-activations, da2 the
+// bf16 gradient of a; dg2, du2 the bf16 gradients of the gate and up columns.
+__device__ __forceinline__ void swiglu_grad_bf2(uint32_t g2, uint32_t u2, uint32_t da2, uint32_t& dg2,
+                                                uint32_t& du2) {
+  const float gl = bf2_lo(g2), gh = bf2_hi(g2);
+  const float sl = sigmoid_fast(gl), sh = sigmoid_fast(gh);
+  du2 = bf2_mul(da2, bf2_pack(gl * sl, gh * sh));
+  const uint32_t ds2 = bf2_mul(da2, u2);
+  dg2 = bf2_pack((bf2_lo(ds2) * sl) * fmaf(gl, 1.0f - sl, 1.0f), (bf2_hi(ds2) * sh) * fmaf(gh, 1.0f - sh, 1.0f));
 }
 
 // Shapes the tcgen05 tiling covers: hidden and ffn multiples of 128.
@@ -58,6 +85,10 @@ int tc_gemm_nt_fwd(const void* a, const void* b, void* c, int64_t N, int64_t K, 
                    int64_t io_rows);
 int tc_gemm_nt_bwd(const void* dc, const void* a, const void* b, void* da, void* db, int64_t N, int64_t K,
                    const SegTable& sg, cudaStream_t st, int64_t io_rows);
+// C = A B^T with the rotary embedding of each 128-column head applied in the epilogue; C's row stride is ldc.
+// cos/sin: [seq, 128] bf16; row r of C is position r % seq.
+int tc_gemm_rope_fwd(const void* a, const void* b, void* c, int64_t ldc, int64_t N, int64_t K, const void* cos,
+                     const void* sin, int64_t seq, const SegTable& sg, cudaStream_t st, int64_t io_rows);
 int tc_experts_fwd(const void* xp, const void* wgu, const void* wd, void* h, void* a, void* y, int E, int64_t H,
                    int64_t F, const SegTable& sg, cudaStream_t st, int64_t io_rows = 0);
 // Stages of the expert backward: the data gradient (dh through the SwiGLU backward, then dxp) and the

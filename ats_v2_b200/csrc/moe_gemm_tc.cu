@@ -54,7 +54,7 @@ constexpr int kStageBox = 32 * 32 * 2;           // staging box: 32 rows x 32 bf
 constexpr int kBoxesPerWarp = 2;
 constexpr int kBandM = 16;  // M tiles per band of the tile order
 
-enum Epi { EPI_STORE = 0, EPI_SWIGLU_FWD = 1, EPI_SWIGLU_BWD = 2, EPI_F32 = 3, EPI_SCATTER = 4 };
+enum Epi { EPI_STORE = 0, EPI_SWIGLU_FWD = 1, EPI_SWIGLU_BWD = 2, EPI_F32 = 3, EPI_SCATTER = 4, EPI_ROPE = 5 };
 constexpr int kMaxParts = 6;
 
 // Where B (the stacked expert weights in M-grouped GEMMs) is read.
@@ -85,6 +85,9 @@ struct GemmArgs {
   const bf16* dxp;       // EPI_SCATTER: permuted-row gradients summed into each token (may be null)
   const int* tok_row;    // EPI_SCATTER: [T*topk] permuted row of (token, slot), -1 = dropped
   int topk;
+  const bf16* rope_cos;  // EPI_ROPE: [rope_seq, 128] cos and sin tables; row r of the output is position
+  const bf16* rope_sin;  //   r % rope_seq (rows are [batch, seq] flattened)
+  int rope_seq;
 };
 
 // tile -> (group, weight index, m tile, n tile, k blocks).  Groups are the
@@ -149,7 +152,8 @@ __device__ __forceinline__ void decode_tile(const GemmArgs& p, TileCursor& cur, 
 
 // Shared memory of the epilogue's staging boxes: the bf16-output epilogues write through them.
 __host__ __device__ constexpr int staging_bytes(int epi) {
-  return (epi == EPI_STORE || epi == EPI_SWIGLU_FWD || epi == EPI_SWIGLU_BWD || epi == EPI_SCATTER)
+  return (epi == EPI_STORE || epi == EPI_SWIGLU_FWD || epi == EPI_SWIGLU_BWD || epi == EPI_SCATTER ||
+          epi == EPI_ROPE)
              ? kEpiWarps * kBoxesPerWarp * kStageBox
              : 0;
 }
@@ -446,17 +450,14 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
         const int x0 = ti.nt * BN + c0;
 #pragma unroll 1
         for (int c = 0; c < BN / 2; c += 32) {
-          float dv[32], gv[32], uv[32];
+          float dv[32];
           tc::tmem_ld32(t_row + c, dv);
+          // column pairs: word i of a chunk holds columns 2i (low half) and 2i+1
+          uint32_t g2[16], u2[16];
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            const bf16* ge = reinterpret_cast<const bf16*>(&gq[q]);
-            const bf16* ue = reinterpret_cast<const bf16*>(&uq[q]);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              gv[q * 8 + e] = __bfloat162float(ge[e]);
-              uv[q * 8 + e] = __bfloat162float(ue[e]);
-            }
+            g2[4 * q] = gq[q].x, g2[4 * q + 1] = gq[q].y, g2[4 * q + 2] = gq[q].z, g2[4 * q + 3] = gq[q].w;
+            u2[4 * q] = uq[q].x, u2[4 * q + 1] = uq[q].y, u2[4 * q + 2] = uq[q].z, u2[4 * q + 3] = uq[q].w;
           }
           if (c + 32 < BN / 2) {  // prefetch the next chunk while this one computes
 #pragma unroll
@@ -465,18 +466,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
               uq[q] = reinterpret_cast<const uint4*>(hu + c + 32)[q];
             }
           }
+          uint32_t pkg[16], pku[16];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float dg, du;
-            swiglu_grad_fast_bf16(gv[j], uv[j], round_to<bf16>(dv[j]), dg, du);
-            gv[j] = dg;
-            uv[j] = du;
-          }
-          uint32_t pk[16];
-          pack32(gv, pk);
-          bw.put(pk, &tmO, x0 + c, row_base, lane);        // dg into dh[:, :F]
-          pack32(uv, pk);
-          bw.put(pk, &tmO, p.F + x0 + c, row_base, lane);  // du into dh[:, F:]
+          for (int i = 0; i < 16; ++i)
+            swiglu_grad_bf2(g2[i], u2[i], bf2_pack(dv[2 * i], dv[2 * i + 1]), pkg[i], pku[i]);
+          bw.put(pkg, &tmO, x0 + c, row_base, lane);        // dg into dh[:, :F]
+          bw.put(pku, &tmO, p.F + x0 + c, row_base, lane);  // du into dh[:, F:]
         }
       } else {
         if (!tc::mbar_wait(&tfull_bar[acc], acc_phase, &abort_flag, budget)) {
@@ -491,22 +486,19 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
           const int row_base = p.seg.row0[ti.g] + ti.mt * BM + quad * 32;
 #pragma unroll 1
           for (int c = 0; c < BN / 4; c += 32) {
-            float gv[32], uv[32], av[32];
+            float gv[32], uv[32];
             tc::tmem_ld32(t_row + c0 + c, gv);
             tc::tmem_ld32(t_row + BN / 2 + c0 + c, uv);
+            uint32_t pg[16], pu[16], pa[16];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              gv[j] = round_to<bf16>(gv[j]);
-              uv[j] = round_to<bf16>(uv[j]);
-              av[j] = silu_mul_fast_bf16(gv[j], uv[j]);
+            for (int i = 0; i < 16; ++i) {  // h rounded to bf16 once; a from those rounded values
+              pg[i] = bf2_pack(gv[2 * i], gv[2 * i + 1]);
+              pu[i] = bf2_pack(uv[2 * i], uv[2 * i + 1]);
+              pa[i] = silu_mul_bf2(pg[i], pu[i]);
             }
-            uint32_t pk[16];
-            pack32(gv, pk);
-            bw.put(pk, &tmO, n0 + c, row_base, lane);        // gate half of h
-            pack32(uv, pk);
-            bw.put(pk, &tmO, p.F + n0 + c, row_base, lane);  // up half of h
-            pack32(av, pk);
-            bw.put(pk, &tmO2, n0 + c, row_base, lane);       // a
+            bw.put(pg, &tmO, n0 + c, row_base, lane);        // gate half of h
+            bw.put(pu, &tmO, p.F + n0 + c, row_base, lane);  // up half of h
+            bw.put(pa, &tmO2, n0 + c, row_base, lane);       // a
           }
         } else if constexpr (EPI == EPI_F32) {
           // float32 tile, rows below m_valid and columns below n_valid, plus a per-column bias
@@ -589,6 +581,40 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
             pack32(v, pk);
             bw.put(pk, &tmO, (int)(col_base + c), row_base, lane);
           }
+        } else if constexpr (EPI == EPI_ROPE) {
+          // one head of 128 dims per tile (BN = 128).  The warp of column half `chalf` takes the column
+          // pairs (d, d + 64), d in [32*chalf, 32*chalf + 32), which rotate-half mixes:
+          //   out[d]      = q[d]*cos[d]           - q[d+64]*sin[d]
+          //   out[d + 64] = q[d+64]*cos[d+64]     + q[d]*sin[d+64]
+          // q is the GEMM result rounded to bf16; each product and the sum round to bf16, as the bf16
+          // torch operations of apply_rotary_pos_emb round them (ats/model/rope.py:83-86)
+          const int d0 = chalf * 32;
+          const int64_t tok = (int64_t)p.seg.row0[ti.g] + ti.mt * BM + row_in_tile;
+          const int64_t pos = tok < p.m_valid ? tok % p.rope_seq : 0;  // rows past the end are clipped
+          float q1[32], q2[32];
+          tc::tmem_ld32(t_row + d0, q1);
+          tc::tmem_ld32(t_row + 64 + d0, q2);
+          const uint4* cs1 = reinterpret_cast<const uint4*>(p.rope_cos + pos * 128 + d0);
+          const uint4* cs2 = reinterpret_cast<const uint4*>(p.rope_cos + pos * 128 + 64 + d0);
+          const uint4* sn1 = reinterpret_cast<const uint4*>(p.rope_sin + pos * 128 + d0);
+          const uint4* sn2 = reinterpret_cast<const uint4*>(p.rope_sin + pos * 128 + 64 + d0);
+          uint32_t o1[16], o2[16];
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            const uint4 c1 = cs1[q4], c2 = cs2[q4], s1 = sn1[q4], s2 = sn2[q4];
+            const uint32_t cw1[4] = {c1.x, c1.y, c1.z, c1.w}, cw2[4] = {c2.x, c2.y, c2.z, c2.w};
+            const uint32_t sw1[4] = {s1.x, s1.y, s1.z, s1.w}, sw2[4] = {s2.x, s2.y, s2.z, s2.w};
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const int i = 4 * q4 + kk;
+              const uint32_t a = bf2_pack(q1[2 * i], q1[2 * i + 1]), b = bf2_pack(q2[2 * i], q2[2 * i + 1]);
+              o1[i] = bf2_add(bf2_mul(a, cw1[kk]), bf2_mul(b ^ 0x80008000u, sw1[kk]));  // rotate_half: -q[d+64]
+              o2[i] = bf2_add(bf2_mul(b, cw2[kk]), bf2_mul(a, sw2[kk]));
+            }
+          }
+          const int row_base = p.seg.row0[ti.g] + ti.mt * BM + quad * 32;
+          bw.put(o1, &tmO, ti.nt * 128 + d0, row_base, lane);
+          bw.put(o2, &tmO, ti.nt * 128 + 64 + d0, row_base, lane);
         } else {
           // plain bf16 store: each 32 x 32 chunk (this warp's 32 rows) goes through shared memory in
           // the 64-byte swizzled layout and out with one TMA store, so global writes are whole lines
@@ -812,6 +838,30 @@ int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a,
 }
 
 
+
+// C[M,N] = A[M,K] B[N,K]^T with the rotary embedding applied to each 128-column head of C in the epilogue
+// (the q/k projection of attention followed by apply_rotary_pos_emb).  C has row stride ldc elements.
+int tc_gemm_rope_fwd(const void* a, const void* b, void* c, int64_t ldc, int64_t N, int64_t K, const void* cos,
+                     const void* sin, int64_t seq, const SegTable& sg, cudaStream_t st, int64_t io_rows) {
+  if (!tc_shape_supported(N, K)) return ATS_EUNSUPPORTED;
+  const int64_t R = sg.max_rows;
+  CUtensorMap ma, mb, mo;
+  GemmArgs p{};
+  p.seg = sg;
+  ATS_TRY(make_map(&ma, a, K, io_rows, K * 2, 128));
+  ATS_TRY(make_map(&mb, b, K, N, K * 2, 128));
+  p.N = (int)N;
+  p.K = (int)K;
+  p.b = OpSpec{(int)N, 0};
+  p.out = static_cast<bf16*>(c);
+  p.ldo = ldc;
+  p.m_valid = (int)io_rows;
+  p.rope_cos = static_cast<const bf16*>(cos);
+  p.rope_sin = static_cast<const bf16*>(sin);
+  p.rope_seq = (int)seq;
+  ATS_TRY(make_out_map(&mo, c, N, io_rows, ldc * 2));
+  return launch_tc<128, false, false, EPI_ROPE, false>(ma, mb, p, (R / BM) * (N / 128), st, &mo);
+}
 
 // Plain GEMM on the same kernel, one segment over the rows (the dense table):
 // C[M,N] = A[M,K] B[N,K]^T.  A and C have io_rows rows (reads past them are zero,

@@ -830,13 +830,21 @@ class _EPDeviceFn(torch.autograd.Function):
         ps.owner = weakref.ref(ctx)
         _lib.call("ats_moe_ep_zero_padding", ps.local["xr"].data_ptr(), allv.data_ptr(), W, me, El, parts, 0,
                   parts, part_rows, H, dt, st)
-        _lib.call("ats_moe_ep_push", x2.data_ptr(), row_token.data_ptr(), T,
-                  *_exchange_args(allv, W, me, El, parts, 0, parts, ps.table("xr"), part_rows, H, dt), st)
-        dist.all_reduce(flag, group=group)
-        _mark("exchange_out")
         segb = _lib.query("ats_moe_ep_segments_bytes", W, Ep)
         keep = []
-        for p in range(parts):
+        ys = torch.empty((R, H), dtype=x2.dtype, device=dev)
+
+        def push(lo, hi, sms, stream):
+            _lib.call("ats_moe_ep_push", x2.data_ptr(), row_token.data_ptr(), T,
+                      *_exchange_args(allv, W, me, El, parts, lo, hi, ps.table("xr"), part_rows, H, dt, sms),
+                      stream.cuda_stream)
+
+        def pull(lo, hi, sms, stream):
+            _lib.call("ats_moe_ep_pull", ys.data_ptr(), R,
+                      *_exchange_args(allv, W, me, El, parts, lo, hi, ps.table("yr"), part_rows, H, dt, sms),
+                      stream.cuda_stream)
+
+        def experts(p):
             seg_ws = torch.empty(segb, dtype=torch.uint8, device=dev)
             rk = allv[:, me * El + p * Ep:me * El + (p + 1) * Ep].contiguous()
             _lib.call("ats_moe_ep_segments", rk.data_ptr(), W, Ep, C, L, seg_ws.data_ptr(), segb, st)
@@ -847,13 +855,47 @@ class _EPDeviceFn(torch.autograd.Function):
             _lib.call("ats_moe_ep_experts_fwd", xr.data_ptr(), wgu_stack[p * Ep].data_ptr(),
                       wd_stack[p * Ep].data_ptr(), h.data_ptr(), a.data_ptr(), yr.data_ptr(), dt, W, Ep, C, H, Fdim,
                       seg_ws.data_ptr(), segb, st)
-            keep += [h, a, seg_ws]
-        _mark("experts")
-        dist.all_reduce(flag, group=group)
-        ys = torch.empty((R, H), dtype=x2.dtype, device=dev)
-        _lib.call("ats_moe_ep_pull", ys.data_ptr(), R,
-                  *_exchange_args(allv, W, me, El, parts, 0, parts, ps.table("yr"), part_rows, H, dt), st)
-        _mark("exchange_back")
+            keep.extend([h, a, seg_ws])
+
+        cur = torch.cuda.current_stream(dev)
+        if parts > 1 and comm_sms > 0:
+            # part p+1's rows go out, and part p-1's results come back, on side streams with comm_sms SMs
+            # while part p's GEMMs run on the others; each transfer is ordered by its own all-reduce
+            out_s, back_s = state.copy_streams(dev, max(W, 2))[:2]
+            push(0, 1, 0, cur)
+            dist.all_reduce(flag, group=group)
+            _mark("exchange_out")
+            out_s.wait_stream(cur)
+            for t in (x2, row_token, allv, ys, flag):
+                t.record_stream(out_s)
+                t.record_stream(back_s)
+            sms = max(1, torch.cuda.get_device_properties(dev).multi_processor_count - comm_sms)
+            for p in range(parts):
+                if p + 1 < parts:
+                    with torch.cuda.stream(out_s):
+                        push(p + 1, p + 2, comm_sms, out_s)
+                        dist.all_reduce(flag, group=group)
+                with _lib.gemm_sm_limit(sms):
+                    experts(p)
+                back_s.wait_stream(cur)
+                with torch.cuda.stream(back_s):
+                    dist.all_reduce(flag, group=group)
+                    pull(p, p + 1, comm_sms, back_s)
+                if p + 1 < parts:
+                    cur.wait_stream(out_s)
+            _mark("experts")
+            cur.wait_stream(back_s)
+            _mark("exchange_back")
+        else:
+            push(0, parts, 0, cur)
+            dist.all_reduce(flag, group=group)
+            _mark("exchange_out")
+            for p in range(parts):
+                experts(p)
+            _mark("experts")
+            dist.all_reduce(flag, group=group)
+            pull(0, parts, 0, cur)
+            _mark("exchange_back")
         out = torch.empty((T, H), dtype=x2.dtype, device=dev)
         _lib.call("ats_moe_combine", ys.data_ptr(), out.data_ptr(), dt, T, H, E, k, C, L, ws.data_ptr(), wsb, st)
         _mark("combine")

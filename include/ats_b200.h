@@ -401,6 +401,19 @@ ATS_API int ats_gemm_fwd(const void* a, const void* b, void* c, ats_dtype dtype,
 ATS_API int ats_gemm_bwd(const void* dc, const void* a, const void* b, void* da, void* db, ats_dtype dtype, int64_t M,
                          int64_t N, int64_t K, void* workspace, size_t workspace_bytes, void* stream);
 
+/* The q/k projection of attention with the rotary embedding in the GEMM's epilogue (row f2 of the hot
+ * path: ats/model/attention.py:179-199, q = q_proj(x) viewed [B,S,heads,128], then
+ * apply_rotary_pos_emb of ats/model/rope.py:71-87).  out[M,N] (row stride ld_out elements) =
+ * rope(x[M,K] . w[N,K]^T), each 128-column head rotated: out[d] = q[d]*cos[d] - q[d+64]*sin[d],
+ * out[d+64] = q[d+64]*cos[d+64] + q[d]*sin[d+64], with q the product rounded to bf16 and each product
+ * and the sum rounded to bf16 as the reference's bf16 ops round them.  Rows are [batch, seq_len]
+ * flattened: row r takes position r % seq_len of cos/sin ([seq_len, 128] bf16, the RotaryEmbedding
+ * cache).  bf16 only; M >= 128, N and K multiples of 128.  Workspace as ats_gemm_fwd.  The backward
+ * is the RoPE adjoint (ats_rope_apply with backward = 1) followed by ats_gemm_bwd. */
+ATS_API int ats_gemm_rope_fwd(const void* x, const void* w, void* out, int64_t ld_out, ats_dtype dtype,
+                              int64_t M, int64_t N, int64_t K, const void* cos, const void* sin,
+                              int64_t seq_len, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Peer-memory row exchange.  Instead of NCCL all-to-alls, a rank can copy
  * its rows straight into the receive buffers of the experts' ranks with the
  * copy engines (no SMs taken, so the copies run beside the expert GEMMs).

@@ -144,3 +144,16 @@ def test_fused_add_rmsnorm_cpu_is_the_block_step():
     assert torch.equal(h, torch.nn.functional.rms_norm(r + x, (16,), w, 1e-6))
     with pytest.raises(ValueError):
         fused_add_rmsnorm(x, r[:, :4], w)
+
+
+def test_fused_qk_proj_rope_cpu_is_the_reference_attention_step():
+    from ats_v2_b200.rope_fused import fused_qk_proj_rope
+
+    x = torch.randn(2, 8, 32)
+    wq, wk = torch.randn(2 * 16, 32), torch.randn(16, 32)
+    cos, sin = RotaryEmbedding(16, 8)(8, torch.device("cpu"), torch.float32)
+    q, k = fused_qk_proj_rope(x, wq, wk, cos, sin)
+    rq = (x @ wq.t()).view(2, 8, 2, 16).transpose(1, 2)
+    rk = (x @ wk.t()).view(2, 8, 1, 16).transpose(1, 2)
+    eq, ek = apply_rotary_pos_emb(rq, rk, cos, sin)
+    assert torch.equal(q, eq) and torch.equal(k, ek)
