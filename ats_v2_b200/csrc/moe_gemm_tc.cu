@@ -96,9 +96,11 @@ struct TileInfo {
   int g, e, mt, nt, kb;
 };
 
+// N tiles of a group.  N need not be a multiple of BN for the plain store: the last tile's columns past N read
+// zero-filled B tiles and are not stored.
 template <int BN, bool KGROUP, int EPI>
 __device__ __forceinline__ int n_tiles(const GemmArgs& p) {
-  return EPI == EPI_SWIGLU_FWD ? p.F / (BN / 2) : p.N / BN;
+  return EPI == EPI_SWIGLU_FWD ? p.F / (BN / 2) : (p.N + BN - 1) / BN;
 }
 
 template <bool KGROUP>
@@ -624,6 +626,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
           const int row_base = (KGROUP ? ti.e * p.M : p.seg.row0[ti.g]) + ti.mt * BM + quad * 32;
 #pragma unroll 1
           for (int c = 0; c < BN / 2; c += 32) {
+            if (ti.nt * BN + c0 + c >= p.N) break;  // a chunk past N (the last tile of an N not a multiple of BN)
             float v[32];
             if (!zero) {
               tc::tmem_ld32(t_row + c0 + c, v);
@@ -799,9 +802,11 @@ int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a,
       ATS_TRY((launch_tc<128, false, true, EPI_STORE, false>(ma, mb, p, (R / BM) * (H / 128), st, &mo)));
   }
   if (!(stages & kBwdWeights)) return ATS_OK;
-  // dWd_e[h][f] = sum over the expert's rows r of dy[r][h] a[r][f]   (A M-major, B N-major)
+  // dWd_e[h][f] = sum over the expert's rows r of dy[r][h] a[r][f]   (A M-major, B N-major).  256-wide tiles
+  // even when F is an odd multiple of 128: the last tile's upper half reads zeros and stores nothing, and the
+  // wider tiles read each row's operands half as often (these GEMMs have a short K: an expert's rows)
   {
-    const int bn = pick_bn(F);
+    const int bn = 256;
     ATS_TRY(make_map(&ma, dy, H, IO, H * 2, 64));
     ATS_TRY(make_map(&mb, a, F, R, F * 2, 64));
     p.M = (int)H;
@@ -813,11 +818,8 @@ int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a,
     p.out_group = H * F;
     CUtensorMap mo;
     ATS_TRY(make_out_map(&mo, dwd, F, (uint64_t)sg.E * H, F * 2));
-    const int64_t tiles = (int64_t)sg.E * (H / BM) * (F / bn);
-    if (bn == 256)
-      ATS_TRY((launch_tc<256, true, true, EPI_STORE, true>(ma, mb, p, tiles, st, &mo)));
-    else
-      ATS_TRY((launch_tc<128, true, true, EPI_STORE, true>(ma, mb, p, tiles, st, &mo)));
+    const int64_t tiles = (int64_t)sg.E * (H / BM) * ((F + bn - 1) / bn);
+    ATS_TRY((launch_tc<256, true, true, EPI_STORE, true>(ma, mb, p, tiles, st, &mo)));
   }
   // dWgu_e[j][h] = sum over the expert's rows r of dh[r][j] xp[r][h]
   {
