@@ -20,7 +20,7 @@ from __future__ import annotations
 import torch
 
 from ats_v2_b200 import _lib
-from ats_v2_b200.rope import _prepare, _RopeFn, rotate_half
+from ats_v2_b200.rope import _launch, _prepare, _RopeFn, rotate_half
 
 HAS_TRITON = _lib.LIB_PATH.exists()  # the reference's flag name: fused GPU kernel available
 
