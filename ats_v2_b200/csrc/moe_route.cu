@@ -163,95 +163,91 @@ __device__ __forceinline__ int warp_incl_scan(int v, int lane) {
   return v;
 }
 
-// One block of 1024 threads.  Phase 1: warp w scans the per-block counts of
-// experts w, w+32, ...: lane l owns a contiguous run of route blocks, so the
-// exclusive block prefix of every (block, expert) is the warp prefix of the
-// lane sums plus the running sum inside the run.  Probability sums go the
-// same fixed way (run sums, then lane order), so the plan is deterministic.
-// Phase 2: block scan of the padded segment sizes in expert order.
-__global__ void __launch_bounds__(1024) plan_kernel(MoePlan plan, float lbw, float* __restrict__ aux_loss,
-                                                    float* __restrict__ util, int* __restrict__ counts_out) {
-  __shared__ int padded[kMaxExperts];
-  __shared__ float prod[kMaxExperts];
-  __shared__ int wsum[32];
-  __shared__ float wprod[32], wfrac[32];
-  const int E = plan.E, nb = plan.nb;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const float Tf = (float)plan.T;
-  const int per = (nb + 31) / 32;
-  const int b0 = lane * per, b1 = min(nb, b0 + per);
-  for (int e = warp; e < E; e += 32) {
-    int c = 0;
-    float ps = 0.f;
-    for (int b = b0; b < b1; ++b) {
-      c += plan.cnt_partial[(size_t)b * E + e];
-      ps += plan.prob_partial[(size_t)b * E + e];
-    }
-    const int incl = warp_incl_scan(c, lane);
-    int run = incl - c;  // exclusive prefix of this lane's run
-    for (int b = b0; b < b1; ++b) {
-      plan.blk_prefix[(size_t)b * E + e] = run;
-      run += plan.cnt_partial[(size_t)b * E + e];
-    }
-    // probability total in lane order (fixed)
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ps += __shfl_down_sync(0xffffffffu, ps, o);
-    const int total = __shfl_sync(0xffffffffu, incl, 31);
-    if (lane == 0) {
-      const int kept = (int64_t)total < plan.C ? total : (int)plan.C;
-      const int kept_pad = (kept + kSegAlign - 1) / kSegAlign * kSegAlign;
-      plan.counts[e] = total;
-      plan.kept[e] = kept;
-      plan.seg_rows[e] = kept_pad;
-      plan.seg_expert[e] = e;
-      padded[e] = plan.layout == ATS_MOE_SLOTS ? (int)slot_rows(plan.C) : kept_pad;
-      const float fr = plan.T > 0 ? (float)total / Tf : 0.f;
-      const float pm = plan.T > 0 ? ps / Tf : 0.f;
-      plan.frac[e] = fr;
-      plan.prob_mean[e] = pm;
-      prod[e] = pm * fr;
-      if (counts_out) counts_out[e] = total;
-    }
-  }
-  __syncthreads();
-  // block scan of padded[0..E) in expert order; sums of prod and frac in the same fixed tree
-  const int e = threadIdx.x;
-  const int v = e < E ? padded[e] : 0;
-  const float pv = e < E ? prod[e] : 0.f, fv = e < E ? plan.frac[e] : 0.f;
+// Block-wide exclusive scan of one int per thread (thread order), with the block total, and a float sum over
+// the block in a fixed tree (warp shuffles, then the warps in order); blockDim.x a multiple of 32, at most 1024.
+__device__ __forceinline__ void block_scan_sum(int v, float f, int& excl, int& total, float& fsum) {
+  __shared__ int ws[32];
+  __shared__ float wf[32];
+  __shared__ int wtotal;
+  __shared__ float wfsum;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const int incl = warp_incl_scan(v, lane);
-  float pr = pv, fr = fv;
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    pr += __shfl_down_sync(0xffffffffu, pr, o);
-    fr += __shfl_down_sync(0xffffffffu, fr, o);
-  }
-  if (lane == 31) wsum[warp] = incl;
-  if (lane == 0) {
-    wprod[warp] = pr;
-    wfrac[warp] = fr;
-  }
+  for (int o = 16; o > 0; o >>= 1) f += __shfl_down_sync(0xffffffffu, f, o);
+  if (lane == 31) ws[warp] = incl;
+  if (lane == 0) wf[warp] = f;
   __syncthreads();
   if (warp == 0) {
-    const int ws = wsum[lane];
-    const int wi = warp_incl_scan(ws, lane);
-    wsum[lane] = wi - ws;  // exclusive prefix of the warps
-    float a = wprod[lane], f = wfrac[lane];
+    const int w = lane < nw ? ws[lane] : 0;
+    const int wi = warp_incl_scan(w, lane);
+    float a = lane < nw ? wf[lane] : 0.f;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      a += __shfl_down_sync(0xffffffffu, a, o);
-      f += __shfl_down_sync(0xffffffffu, f, o);
-    }
-    if (lane == 0) {
-      plan.dev_err[0] = 0;
-      if (aux_loss) aux_loss[0] = (float)E * a * lbw;
-      wfrac[0] = f;  // the frac total
-    }
+    for (int o = 16; o > 0; o >>= 1) a += __shfl_down_sync(0xffffffffu, a, o);
+    ws[lane] = wi - w;  // exclusive prefix of the warps
+    if (lane == 0) wfsum = a;
+    if (lane == 31) wtotal = wi;
   }
   __syncthreads();
-  if (e < E) plan.seg_start[e] = wsum[warp] + incl - v;
-  if (e == E - 1) plan.seg_start[E] = wsum[warp] + incl;
-  const float fs = fmaxf(wfrac[0], 1e-8f);
-  if (util && e < E) util[e] = plan.frac[e] / fs;
+  excl = ws[warp] + incl - v;
+  total = wtotal;
+  fsum = wfsum;
+  __syncthreads();  // the shared words are reused by the next call
+}
+
+// Phase 1 of the plan, one block per expert: thread i owns a contiguous run of route blocks; the exclusive
+// prefix of every (route block, expert) is the block scan of the run sums plus the running sum inside the
+// run.  The probability sum goes the same fixed way (run sums, then the block tree): the plan is
+// deterministic.
+__global__ void __launch_bounds__(1024) plan_expert_kernel(MoePlan plan, int* __restrict__ counts_out) {
+  const int e = blockIdx.x, E = plan.E, nb = plan.nb;
+  const int per = (nb + (int)blockDim.x - 1) / (int)blockDim.x;
+  const int b0 = (int)threadIdx.x * per, b1 = min(nb, b0 + per);
+  int c = 0;
+  float ps = 0.f;
+  for (int b = b0; b < b1; ++b) {
+    c += plan.cnt_partial[(size_t)b * E + e];
+    ps += plan.prob_partial[(size_t)b * E + e];
+  }
+  int run, total;
+  float psum;
+  block_scan_sum(c, ps, run, total, psum);
+  for (int b = b0; b < b1; ++b) {
+    plan.blk_prefix[(size_t)b * E + e] = run;
+    run += plan.cnt_partial[(size_t)b * E + e];
+  }
+  if (threadIdx.x == 0) {
+    const int kept = (int64_t)total < plan.C ? total : (int)plan.C;
+    plan.counts[e] = total;
+    plan.kept[e] = kept;
+    plan.seg_rows[e] = (kept + kSegAlign - 1) / kSegAlign * kSegAlign;
+    plan.seg_expert[e] = e;
+    const float Tf = (float)plan.T;
+    plan.frac[e] = plan.T > 0 ? (float)total / Tf : 0.f;
+    plan.prob_mean[e] = plan.T > 0 ? psum / Tf : 0.f;
+    if (counts_out) counts_out[e] = total;
+  }
+}
+
+// Phase 2, one block of 1024 threads: block scan of the padded segment sizes in expert order (the segment
+// starts), the aux loss E * lbw * sum(prob_mean * frac) and the utilization frac / sum(frac), the sums in one
+// fixed tree.
+__global__ void __launch_bounds__(1024) plan_finish_kernel(MoePlan plan, float lbw, float* __restrict__ aux_loss,
+                                                           float* __restrict__ util) {
+  const int E = plan.E, e = threadIdx.x;
+  const int pad = e < E ? (plan.layout == ATS_MOE_SLOTS ? (int)slot_rows(plan.C) : plan.seg_rows[e]) : 0;
+  const float fr = e < E ? plan.frac[e] : 0.f;
+  int excl, total, unused_excl, unused_total;
+  float prod_sum, frac_sum;
+  block_scan_sum(pad, e < E ? plan.prob_mean[e] * fr : 0.f, excl, total, prod_sum);
+  block_scan_sum(0, fr, unused_excl, unused_total, frac_sum);
+  if (e < E) plan.seg_start[e] = excl;
+  if (e == 0) {
+    plan.seg_start[E] = total;
+    plan.dev_err[0] = 0;
+    if (aux_loss) aux_loss[0] = (float)E * prod_sum * lbw;
+  }
+  const float fs = fmaxf(frac_sum, 1e-8f);
+  if (util && e < E) util[e] = fr / fs;
 }
 
 __global__ void __launch_bounds__(kRouteTokensPerBlock) permute_kernel(const int64_t* __restrict__ idx,
@@ -588,8 +584,10 @@ int ats_moe_route_plan(const float* logits, int64_t T, int E, int k, int64_t cap
     if (cudaMemsetAsync(plan.row_token, 0xff, (size_t)plan.max_rows * 4, st) != cudaSuccess)
       return fail(ATS_ECUDA, "moe_route_plan: memset failed");
   }
-  plan_kernel<<<1, 1024, 0, st>>>(plan, lbw, aux_loss, utilization, counts);
-  ATS_TRY(check_launch("moe_plan"));
+  plan_expert_kernel<<<E, 1024, 0, st>>>(plan, counts);
+  ATS_TRY(check_launch("moe_plan_experts"));
+  plan_finish_kernel<<<1, 1024, 0, st>>>(plan, lbw, aux_loss, utilization);
+  ATS_TRY(check_launch("moe_plan_finish"));
   if (T > 0) {
     permute_kernel<<<plan.nb, kRouteTokensPerBlock, (size_t)kRouteTokensPerBlock * k * 4, st>>>(idx, gates, plan);
     ATS_TRY(check_launch("moe_permute"));

@@ -1032,7 +1032,10 @@ class ExpertParallelMoE(nn.Module):
     row transfers overlap the expert GEMMs of the others (P must divide the
     local expert count; 1 exchanges everything at once); meanwhile the GEMMs
     leave ``comm_sms`` SMs to the collectives (default: 16 for the NCCL
-    exchanges, whose transfers run on SMs, none for "peer")."""
+    exchanges, whose transfers run on SMs, none for "peer").  "device" moves
+    the rows with kernels of its own; with ``comm_sms`` > 0 (default 16) its
+    backward loads the returning input gradients on that many SMs while the
+    weight-gradient GEMMs run on the rest."""
 
     def __init__(self, hidden_size: int, intermediate_size: int, num_experts: int, num_layers: int,
                  top_k: int = 2, capacity_factor: float = 1.25, load_balancing_weight: float = 0.01,
@@ -1042,7 +1045,7 @@ class ExpertParallelMoE(nn.Module):
         if exchange not in ("packed", "slots", "peer", "device"):
             raise ValueError(f"exchange must be 'packed', 'slots', 'peer' or 'device', got {exchange!r}")
         if comm_sms is None:
-            comm_sms = 0 if exchange in ("peer", "device") else 16
+            comm_sms = 0 if exchange == "peer" else 16
         self.exchange = exchange
         self.group = group
         if ep_size is None:  # the given group (or the default one), bound now

@@ -477,7 +477,7 @@ class MoELayer(nn.Module):
             self.moe = ExpertParallelMoE(hidden_size, intermediate_size, num_experts, num_layers, top_k=top_k,
                                          capacity_factor=capacity_factor,
                                          load_balancing_weight=load_balancing_weight, ep_size=ep_size,
-                                         exchange="peer")
+                                         exchange="device")
         else:
             self.moe = _CudaMoE(hidden_size, intermediate_size, num_experts, top_k, capacity_factor,
                                 load_balancing_weight, num_layers=num_layers, quantization=quantization)

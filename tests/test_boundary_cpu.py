@@ -116,7 +116,7 @@ def _ep_worker(rank, world, port, q):
         layer = MoELayer(16, 32, 8, num_layers=2, ep_size=world)
         from ats_v2_b200.ep import ExpertParallelMoE
 
-        assert isinstance(layer.moe, ExpertParallelMoE)
+        assert isinstance(layer.moe, ExpertParallelMoE) and layer.moe.exchange == "device"
         assert len(layer.moe.experts) == 8 // world and layer.moe.gate.weight.shape == (8, 16)
         layer.moe._bind()
         assert layer.moe.rank == rank and layer.moe.world == world
