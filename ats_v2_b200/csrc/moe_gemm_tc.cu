@@ -475,6 +475,98 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
           bw.put(pkg, &tmO, x0 + c, row_base, lane);        // dg into dh[:, :F]
           bw.put(pku, &tmO, p.F + x0 + c, row_base, lane);  // du into dh[:, F:]
         }
+      } else if constexpr (EPI == EPI_SCATTER) {
+        // token gradient: the router's share (this tile, cast to bf16) plus the token's kept
+        // permuted-row gradients summed in ascending row (= expert) order, as two bf16 gradients add.
+        // The row gradients do not depend on the accumulator: the first kPre kept rows' first chunk
+        // loads before the accumulator wait, and each next chunk while the current one is summed.
+        constexpr int kPre = 2;
+        const int c0 = chalf * (BN / 2);
+        const int64_t tok = (int64_t)p.seg.row0[ti.g] + ti.mt * BM + row_in_tile;
+        const bool ok = tok < p.m_valid;
+        int rows[kMaxTopK];
+        int n = 0;
+        if (ok && p.dxp != nullptr) {
+          for (int s2 = 0; s2 < p.topk; ++s2) {
+            const int r = p.tok_row[tok * p.topk + s2];
+            if (r < 0) continue;
+            int q = n++;
+            while (q > 0 && rows[q - 1] > r) {
+              rows[q] = rows[q - 1];
+              --q;
+            }
+            rows[q] = r;
+          }
+        }
+        const int npre = n < kPre ? n : kPre;
+        const int64_t col_base = (int64_t)ti.nt * BN + c0;
+        const int row_base = p.seg.row0[ti.g] + ti.mt * BM + quad * 32;  // rows at or past T are clipped
+        const bf16* prow[kPre];
+#pragma unroll
+        for (int r = 0; r < kPre; ++r) prow[r] = p.dxp + (int64_t)(r < npre ? rows[r] : 0) * p.ldo + col_base;
+        uint4 pre[kPre][4];
+#pragma unroll
+        for (int r = 0; r < kPre; ++r)
+          if (r < npre) {
+            const uint4* src = reinterpret_cast<const uint4*>(prow[r]);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) pre[r][q] = src[q];
+          }
+        if (!tc::mbar_wait(&tfull_bar[acc], acc_phase, &abort_flag, budget)) {
+          fail_abort(p.seg.err, &abort_flag, 4);
+          break;
+        }
+        tc::tc_fence_after();
+        const uint32_t t_row = tmem_base + (uint32_t)(acc * BN) + ((uint32_t)(quad * 32) << 16);
+#pragma unroll 1
+        for (int c = 0; c < BN / 2; c += 32) {
+          float v[32];
+          tc::tmem_ld32(t_row + c0 + c, v);
+          uint4 cur[kPre][4];
+#pragma unroll
+          for (int r = 0; r < kPre; ++r)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) cur[r][q] = pre[r][q];
+          if (c + 32 < BN / 2) {
+#pragma unroll
+            for (int r = 0; r < kPre; ++r)
+              if (r < npre) {
+                const uint4* src = reinterpret_cast<const uint4*>(prow[r] + c + 32);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) pre[r][q] = src[q];
+              }
+          }
+          if (ok) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = round_to<bf16>(v[j]);
+            if (n > 0) {
+              float m[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) m[j] = 0.f;
+#pragma unroll
+              for (int r = 0; r < kPre; ++r)
+                if (r < npre) {
+#pragma unroll
+                  for (int q = 0; q < 4; ++q) {
+                    const bf16* e = reinterpret_cast<const bf16*>(&cur[r][q]);
+#pragma unroll
+                    for (int i2 = 0; i2 < 8; ++i2) m[q * 8 + i2] += __bfloat162float(e[i2]);
+                  }
+                }
+              for (int i2 = kPre; i2 < n; ++i2) {  // more than kPre kept experts: loaded in place
+                float u[32];
+                load32(p.dxp + (int64_t)rows[i2] * p.ldo + col_base + c, u);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) m[j] += u[j];
+              }
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(round_to<bf16>(m[j]), v[j]);
+            }
+          }
+          uint32_t pk[16];
+          pack32(v, pk);
+          bw.put(pk, &tmO, (int)(col_base + c), row_base, lane);
+        }
       } else {
         if (!tc::mbar_wait(&tfull_bar[acc], acc_phase, &abort_flag, budget)) {
           fail_abort(p.seg.err, &abort_flag, 4);
@@ -536,52 +628,6 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
                   if (col0 + j < p.n_valid) outp[col0 + j] = v[j];
               }
             }
-          }
-        } else if constexpr (EPI == EPI_SCATTER) {
-          // token gradient: the router's share (this tile, cast to bf16) plus the token's kept
-          // permuted-row gradients summed in ascending row (= expert) order, as two bf16 gradients add
-          const int c0 = chalf * (BN / 2);
-          const int64_t tok = (int64_t)p.seg.row0[ti.g] + ti.mt * BM + row_in_tile;
-          const bool ok = tok < p.m_valid;
-          int rows[kMaxTopK];
-          int n = 0;
-          if (ok && p.dxp != nullptr) {
-            for (int s2 = 0; s2 < p.topk; ++s2) {
-              const int r = p.tok_row[tok * p.topk + s2];
-              if (r < 0) continue;
-              int q = n++;
-              while (q > 0 && rows[q - 1] > r) {
-                rows[q] = rows[q - 1];
-                --q;
-              }
-              rows[q] = r;
-            }
-          }
-          const int64_t col_base = (int64_t)ti.nt * BN + c0;
-          const int row_base = p.seg.row0[ti.g] + ti.mt * BM + quad * 32;  // rows at or past T are clipped
-#pragma unroll 1
-          for (int c = 0; c < BN / 2; c += 32) {
-            float v[32];
-            tc::tmem_ld32(t_row + c0 + c, v);
-            if (ok) {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] = round_to<bf16>(v[j]);
-              if (n > 0) {
-                float m[32], u[32];
-#pragma unroll
-                for (int j = 0; j < 32; ++j) m[j] = 0.f;
-                for (int i2 = 0; i2 < n; ++i2) {
-                  load32(p.dxp + (int64_t)rows[i2] * p.ldo + col_base + c, u);
-#pragma unroll
-                  for (int j = 0; j < 32; ++j) m[j] += u[j];
-                }
-#pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(round_to<bf16>(m[j]), v[j]);
-              }
-            }
-            uint32_t pk[16];
-            pack32(v, pk);
-            bw.put(pk, &tmO, (int)(col_base + c), row_base, lane);
           }
         } else if constexpr (EPI == EPI_ROPE) {
           // one head of 128 dims per tile (BN = 128).  The warp of column half `chalf` takes the column
