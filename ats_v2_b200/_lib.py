@@ -53,6 +53,8 @@ SIGNATURES: dict[str, tuple] = {
     "ats_ipc_close": (c_int, [c_void_p]),
     "ats_peer_copies": (c_int, [c_int, POINTER(c_void_p), POINTER(c_void_p), POINTER(ctypes.c_uint64), c_void_p]),
     "ats_gemm_sm_limit": (c_int, []),
+    "ats_set_gemm_pairs": (c_int, [c_int]),
+    "ats_gemm_pairs": (c_int, []),
     "ats_device_status": (c_int, [POINTER(c_int)]),
     "ats_set_wait_budget": (c_int, [c_int64]),
     "ats_rmsnorm_fwd": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_int, c_void_p, c_int64, c_void_p,
@@ -212,6 +214,19 @@ def gemm_sm_limit(sms: int):
         yield
     finally:
         call("ats_set_gemm_sm_limit", prev)
+
+
+@contextlib.contextmanager
+def gemm_pairs(enabled: bool):
+    """Run the tensor-core expert, dense-FFN and MLA GEMMs inside the block on
+    CTA pairs (256-row tiles) or on single CTAs (128-row tiles, the default).
+    The setting is process-wide; both give identical results."""
+    prev = query("ats_gemm_pairs")
+    call("ats_set_gemm_pairs", 1 if enabled else 0)
+    try:
+        yield
+    finally:
+        call("ats_set_gemm_pairs", prev)
 
 
 def dtype_code(t: torch.dtype) -> int:

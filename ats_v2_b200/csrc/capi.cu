@@ -43,6 +43,13 @@ int gemm_ctas() {
   return (g_gemm_sm_limit > 0 && g_gemm_sm_limit < n) ? g_gemm_sm_limit : n;
 }
 
+// Whether the expert, dense and MLA GEMMs run 256-row tiles on CTA pairs (cta_group::2) or 128-row tiles on
+// single CTAs (the default: as fast on long-K GEMMs, faster on the short expert segments of an
+// expert-parallel step).  Process-wide; each GEMM entry point reads it once.
+static std::atomic<int> g_gemm_pairs{0};
+
+bool gemm_pairs() { return g_gemm_pairs.load(std::memory_order_relaxed) != 0; }
+
 }  // namespace ats
 
 extern "C" {
@@ -71,6 +78,13 @@ int ats_set_gemm_sm_limit(int sms) {
 }
 
 int ats_gemm_sm_limit(void) { return ats::g_gemm_sm_limit; }
+
+int ats_set_gemm_pairs(int enable) {
+  ats::g_gemm_pairs.store(enable != 0 ? 1 : 0, std::memory_order_relaxed);
+  return ATS_OK;
+}
+
+int ats_gemm_pairs(void) { return ats::g_gemm_pairs.load(std::memory_order_relaxed); }
 
 int ats_set_wait_budget(int64_t cycles) {
   ATS_TRY(ats::gemm_set_wait_budget((long long)cycles));

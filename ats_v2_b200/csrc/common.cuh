@@ -54,6 +54,7 @@ int ring_take_status(int* code);
 // device since the last call (0: none), which this call clears.
 int ep_take_status(int* code);
 int gemm_ctas();  // CTAs of a persistent GEMM: num_sms() or this thread's lower limit
+bool gemm_pairs();  // expert / dense / MLA GEMMs on CTA pairs (ats_set_gemm_pairs)
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 

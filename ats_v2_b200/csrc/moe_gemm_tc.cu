@@ -53,6 +53,7 @@ __device__ int g_gemm_status;
 constexpr int kStageBox = 32 * 32 * 2;           // staging box: 32 rows x 32 bf16 columns, 64-byte swizzle
 constexpr int kBoxesPerWarp = 2;
 constexpr int kBandM = 16;  // M tiles per band of the tile order
+constexpr int kMaxDevices = 64;
 
 enum Epi { EPI_STORE = 0, EPI_SWIGLU_FWD = 1, EPI_SWIGLU_BWD = 2, EPI_F32 = 3, EPI_SCATTER = 4, EPI_ROPE = 5 };
 constexpr int kMaxParts = 6;
@@ -108,10 +109,11 @@ __device__ __forceinline__ int n_groups(const GemmArgs& p) {
   return KGROUP ? p.seg.E : p.seg.nseg;
 }
 
-// Tiles of group g: its M tiles times the N tiles.
-template <int BN, bool KGROUP, int EPI>
+// Tiles of group g: its M tiles (TM rows: 128, or 256 for a CTA pair, whose last tile may have only its first
+// 128-row half inside the group) times the N tiles.
+template <int BN, bool KGROUP, int EPI, int TM>
 __device__ __forceinline__ int group_tiles(const GemmArgs& p, int g) {
-  return (KGROUP ? p.M / BM : p.seg.rows[g] / BM) * n_tiles<BN, KGROUP, EPI>(p);
+  return ((KGROUP ? p.M : p.seg.rows[g]) + TM - 1) / TM * n_tiles<BN, KGROUP, EPI>(p);
 }
 
 // Walks the groups in order: a role visits its tiles t = blockIdx.x + i*gridDim.x in increasing order,
@@ -120,14 +122,14 @@ struct TileCursor {
   int g = 0, first = 0;
 };
 
-template <int BN, bool KGROUP, int EPI, int SPLIT>
+template <int BN, bool KGROUP, int EPI, int SPLIT, int TM>
 __device__ __forceinline__ void decode_tile(const GemmArgs& p, TileCursor& cur, int t, TileInfo& ti) {
   const int NT = n_tiles<BN, KGROUP, EPI>(p);
-  int n = group_tiles<BN, KGROUP, EPI>(p, cur.g);
+  int n = group_tiles<BN, KGROUP, EPI, TM>(p, cur.g);
   while (t >= cur.first + n) {  // t < total, so a later group holds it
     cur.first += n;
     ++cur.g;
-    n = group_tiles<BN, KGROUP, EPI>(p, cur.g);
+    n = group_tiles<BN, KGROUP, EPI, TM>(p, cur.g);
   }
   const int g = cur.g;
   const int q = t - cur.first;
@@ -150,6 +152,16 @@ __device__ __forceinline__ void decode_tile(const GemmArgs& p, TileCursor& cur, 
     ti.e = p.seg.expert[g];
     ti.kb = (p.K / BK) * SPLIT;
   }
+}
+
+// Ring of a launch: one A tile (128 x 64) and BPARTS B tiles per stage; a CTA of a pair holds half of the
+// B rows.  Single CTAs keep STAGES stages; pairs fill the same bytes with more (smaller) stages.
+constexpr int kRingBytes = STAGES * (BM * BK * 2 + 256 * BK * 2);
+__host__ __device__ constexpr int stage_bytes(int bn, int bparts, bool pair) {
+  return BM * BK * 2 + bparts * (pair ? bn / 2 : bn) * BK * 2;
+}
+__host__ __device__ constexpr int ring_stages(int bn, int bparts, bool pair) {
+  return pair ? kRingBytes / stage_bytes(bn, bparts, pair) : STAGES;
 }
 
 // Shared memory of the epilogue's staging boxes: the bf16-output epilogues write through them.
@@ -220,56 +232,99 @@ __device__ __forceinline__ void load32(const bf16* src, float (&v)[32]) {
   }
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI, bool KGROUP, int SPLIT, int BPARTS>
+// PAIR: a cluster of two CTAs on two SMs computes each 256 x BN tile with cta_group::2 MMAs.  CTA r of the
+// pair loads rows [128 r, 128 r + 128) of the tile's A and rows [r BN/2, (r + 1) BN/2) of its B (the D
+// columns; for the SwiGLU forward the gate rows in CTA 0 and the up rows in CTA 1), each into its own
+// ring, so a CTA reads half the B bytes of a single-CTA 128 x BN tile for the same MMA work and the ring
+// holds more stages.  Both CTAs' loads of a stage complete on CTA 0's full barrier, which CTA 0's producer
+// arms for both halves; CTA 0's MMA thread waits on it alone.  CTA 0's MMA commits free the stage and hand
+// over the accumulator on both CTAs' barriers; both CTAs' epilogues (each its 128 rows, all BN columns, in
+// its own TMEM) release the accumulator on CTA 0's barrier.  A tile whose second half lies past the group
+// is computed whole, its second half not stored.  At the end the CTAs meet at a cluster barrier; CTA 0
+// then settles the stages that only one producer reached (a role gave up) and waits until every load of
+// both CTAs has landed; a second cluster barrier keeps CTA 1 alive until then.
+template <int BN, bool A_MN, bool B_MN, int EPI, bool KGROUP, int SPLIT, int BPARTS, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                                                               const __grid_constant__ CUtensorMap tmB,
                                                               const __grid_constant__ CUtensorMap tmO,
                                                               const __grid_constant__ CUtensorMap tmO2,
                                                               GemmArgs p) {
+  constexpr int B_ROWS = PAIR ? BN / 2 : BN;  // rows of a B tile (columns of D) held by this CTA
   constexpr uint32_t A_BYTES = BM * BK * 2;
-  constexpr uint32_t B_BYTES = BN * BK * 2;
+  constexpr uint32_t B_BYTES = B_ROWS * BK * 2;
   constexpr uint32_t STAGE_BYTES = A_BYTES + BPARTS * B_BYTES;  // one A tile, BPARTS B tiles
+  static_assert(STAGE_BYTES == (uint32_t)stage_bytes(BN, BPARTS, PAIR), "stage layout");
+  constexpr int NST = ring_stages(BN, BPARTS, PAIR);
+  constexpr int TM = PAIR ? 2 * BM : BM;  // rows of an output tile
   static_assert(SPLIT == 1 || BPARTS == 1, "operand parts along K or in the stage, not both");
-  constexpr uint32_t IDESC = tc::idesc_bf16(BM, BN, A_MN, B_MN);
+  static_assert(!PAIR || (SPLIT == 1 && BPARTS == 1 && (BN == 128 || BN == 256) &&
+                          (EPI == EPI_STORE || EPI == EPI_SWIGLU_FWD || EPI == EPI_SWIGLU_BWD)),
+                "CTA pairs run the plain, SwiGLU-forward and SwiGLU-backward expert GEMMs");
+  constexpr uint32_t IDESC = tc::idesc_bf16(TM, BN, A_MN, B_MN);
   extern __shared__ uint8_t smem_raw[];
   // dynamic shared memory: the 1024-byte aligned ring (the 128-byte swizzle atom spans 1024 bytes),
   // the epilogue's store staging (EPI_STORE: one 2 KB 32 x 32 bf16 box per epilogue warp), then the
   // per-group tile prefix
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* staging = ring + STAGES * STAGE_BYTES;
-  __shared__ __align__(8) uint64_t full_bar[STAGES], empty_bar[STAGES], tfull_bar[2], tempty_bar[2], done_bar;
+  uint8_t* staging = ring + NST * STAGE_BYTES;
+  __shared__ __align__(8) uint64_t full_bar[NST], empty_bar[NST], tfull_bar[2], tempty_bar[2], done_bar;
   __shared__ uint32_t tmem_base_s;
+  __shared__ int peer_issued_s;  // PAIR, CTA 0: stages CTA 1's producer loaded
   __shared__ int total_s;
   __shared__ volatile int abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long budget = g_gemm_wait_budget;
+  const uint32_t cta = PAIR ? tc::cluster_ctarank() : 0u;  // this CTA's half of a pair tile
+  const int t_first = PAIR ? (int)tc::cluster_id_x() : (int)blockIdx.x;
+  const int t_step = PAIR ? (int)tc::ncluster_x() : (int)gridDim.x;
+  // a role that gives up stops the other roles of this CTA and, in a pair, of the other CTA
+  auto give_up = [&](int code) {
+    fail_abort(p.seg.err, &abort_flag, code);
+    if constexpr (PAIR) tc::st_cluster_u32(tc::cluster_addr(tc::smem_u32((const void*)&abort_flag), cta ^ 1u), 1u);
+  };
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < NST; ++s) {
       tc::mbar_init(&full_bar[s], 1);
       tc::mbar_init(&empty_bar[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       tc::mbar_init(&tfull_bar[a], 1);
-      tc::mbar_init(&tempty_bar[a], kEpiWarps);
+      tc::mbar_init(&tempty_bar[a], PAIR ? 2 * kEpiWarps : kEpiWarps);
     }
     tc::mbar_init(&done_bar, 1);
     tc::fence_barrier_init();
     tc::fence_proxy_async_smem();
     abort_flag = 0;
     int total = 0;
-    for (int g = 0; g < n_groups<KGROUP>(p); ++g) total += group_tiles<BN, KGROUP, EPI>(p, g);
+    for (int g = 0; g < n_groups<KGROUP>(p); ++g) total += group_tiles<BN, KGROUP, EPI, TM>(p, g);
     total_s = total;
   }
   if (warp == 1) {
-    tc::tmem_alloc(&tmem_base_s, 2 * BN);
-    tc::tmem_relinquish();
+    if constexpr (PAIR) {
+      tc::tmem_alloc_pair(&tmem_base_s, 2 * BN);
+      tc::tmem_relinquish_pair();
+    } else {
+      tc::tmem_alloc(&tmem_base_s, 2 * BN);
+      tc::tmem_relinquish();
+    }
   }
   tc::tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) tc::cluster_sync();  // both CTAs' barriers exist before either signals the other's
   tc::tc_fence_after();
   const uint32_t tmem_base = tmem_base_s;
   const int total = total_s;
+  // every load issued lands before the CTA may exit: wait for the last phase of each stage used by the
+  // first `issued` stage loads (phases of a stage complete in order)
+  auto drain_loads = [&](int issued) {
+    for (int s = 0; s < NST && s < issued; ++s) {
+      const int klast = s + (issued - 1 - s) / NST * NST;
+      if (!tc::mbar_wait(&full_bar[s], (uint32_t)((klast / NST) & 1), nullptr, kWaitBudget))
+        fail_drain(p.seg.err, 11);
+    }
+  };
+  int issued_k = 0;  // producer: stage loads issued
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -278,14 +333,19 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
       tc::prefetch_tensormap(&tmB);
       int stage = 0;
       uint32_t phase = 0;
-      int last_parity[STAGES];
-#pragma unroll
-      for (int s = 0; s < STAGES; ++s) last_parity[s] = -1;
+      // a pair's loads count on CTA 0's full barriers
+      const uint32_t full0 = PAIR ? tc::cluster_addr(tc::smem_u32(&full_bar[0]), 0u) : 0u;
+      auto load = [&](void* dst, const CUtensorMap* map, int x, int y) {
+        if constexpr (PAIR)
+          tc::tma_load_2d_pair(dst, map, x, y, full0 + (uint32_t)stage * 8u);
+        else
+          tc::tma_load_2d(dst, map, x, y, &full_bar[stage]);
+      };
       TileCursor cur;
-      for (int t = blockIdx.x; t < total && !abort_flag; t += gridDim.x) {
+      for (int t = t_first; t < total && !abort_flag; t += t_step) {
         TileInfo ti;
-        decode_tile<BN, KGROUP, EPI, SPLIT>(p, cur, t, ti);
-        const int m0 = ti.mt * BM;
+        decode_tile<BN, KGROUP, EPI, SPLIT, TM>(p, cur, t, ti);
+        const int m0 = ti.mt * TM + (int)cta * BM;
         const int n0 = EPI == EPI_SWIGLU_FWD ? ti.nt * (BN / 2) : ti.nt * BN;
         // K blocks: M-grouped = kb of the fixed K; K-grouped = the expert's segments' rows, in order.
         // The segment's first row and k-block count live in registers; the table is read only
@@ -314,66 +374,82 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
             }
           }
           if (!tc::mbar_wait(&empty_bar[stage], phase ^ 1u, &abort_flag, budget)) {
-            fail_abort(p.seg.err, &abort_flag, 1);
+            give_up(1);
             break;
           }
           uint8_t* sa = ring + stage * STAGE_BYTES;
           uint8_t* sb = sa + A_BYTES;
-          tc::mbar_arrive_expect_tx(&full_bar[stage], STAGE_BYTES);
+          if (cta == 0) tc::mbar_arrive_expect_tx(&full_bar[stage], PAIR ? 2 * STAGE_BYTES : STAGE_BYTES);
           if (!A_MN) {  // M-grouped A: rows of the tile's segment, K contiguous
-            tc::tma_load_2d(sa, &tmA, a_ko + kq * BK, seg_r0 + m0, &full_bar[stage]);
+            load(sa, &tmA, a_ko + kq * BK, seg_r0 + m0);
           } else {      // K-grouped A: M contiguous, K = rows of the current segment
             const int krow = seg_r0 + lkb * BK + a_ko;
-            tc::tma_load_2d(sa, &tmA, m0, krow, &full_bar[stage]);
-            tc::tma_load_2d(sa + 8192, &tmA, m0 + 64, krow, &full_bar[stage]);
+            load(sa, &tmA, m0, krow);
+            load(sa + 8192, &tmA, m0 + 64, krow);
           }
           if (!B_MN) {  // stacked weights, K contiguous
+            if constexpr (PAIR) {  // this CTA's B_ROWS rows: the gate or up half (SwiGLU), or the cta-th half
+              const int brow = b_row0 + n0 + (p.b.sub_offset ? (cta ? p.b.sub_offset : 0) : (int)cta * B_ROWS);
+              load(sb, &tmB, kq * BK, brow);
+            } else {
 #pragma unroll
-            for (int j = 0; j < BPARTS; ++j) {
-              const int brow = b_row0 + n0 + b_no + (BPARTS > 1 ? p.b_noff[j] : 0);
-              tc::tma_load_2d(sb + j * B_BYTES, &tmB, b_ko + kq * BK, brow, &full_bar[stage]);
-              if (BPARTS == 1 && p.b.sub_offset)
-                tc::tma_load_2d(sb + (BN / 2) * 128, &tmB, b_ko + kq * BK, brow + p.b.sub_offset, &full_bar[stage]);
+              for (int j = 0; j < BPARTS; ++j) {
+                const int brow = b_row0 + n0 + b_no + (BPARTS > 1 ? p.b_noff[j] : 0);
+                tc::tma_load_2d(sb + j * B_BYTES, &tmB, b_ko + kq * BK, brow, &full_bar[stage]);
+                if (BPARTS == 1 && p.b.sub_offset)
+                  tc::tma_load_2d(sb + (BN / 2) * 128, &tmB, b_ko + kq * BK, brow + p.b.sub_offset,
+                                  &full_bar[stage]);
+              }
             }
           } else {
             const int krow = (KGROUP ? seg_r0 + lkb * BK : b_row0 + kq * BK) + b_ko;
+            const int ncol = n0 + (int)cta * B_ROWS + b_no;
 #pragma unroll
             for (int j = 0; j < BPARTS; ++j)
 #pragma unroll
-              for (int b = 0; b < BN / 64; ++b)
-                tc::tma_load_2d(sb + j * B_BYTES + b * 8192, &tmB, n0 + b_no + (BPARTS > 1 ? p.b_noff[j] : 0) + b * 64,
-                                krow, &full_bar[stage]);
+              for (int b = 0; b < B_ROWS / 64; ++b)
+                load(sb + j * B_BYTES + b * 8192, &tmB, ncol + (BPARTS > 1 ? p.b_noff[j] : 0) + b * 64, krow);
           }
           if (part == SPLIT - 1) ++lkb;
-          last_parity[stage] = (int)phase;
-          if (++stage == STAGES) {
+          ++issued_k;
+          if (++stage == NST) {
             stage = 0;
             phase ^= 1u;
           }
         }
       }
-      // drain: every issued load lands before the CTA may exit
-      for (int s = 0; s < STAGES; ++s)
-        if (last_parity[s] >= 0 && !tc::mbar_wait(&full_bar[s], (uint32_t)last_parity[s], nullptr, kWaitBudget))
-          fail_drain(p.seg.err, 11);
+      if constexpr (PAIR) {  // CTA 0 drains both CTAs' loads after the first cluster barrier
+        if (cta != 0) tc::st_cluster_u32(tc::cluster_addr(tc::smem_u32(&peer_issued_s), 0u), (uint32_t)issued_k);
+      } else {
+        drain_loads(issued_k);
+      }
     }
   } else if (warp == 1) {
-    // ---------------------------------------------------------------- MMA
-    if (lane == 0) {
+    if ((!PAIR || cta == 0) && lane == 0) {
+      // ---------------------------------------------------------------- MMA
       int stage = 0;
       uint32_t phase = 0;
       int i = 0;
       bool issued = false;
       const uint32_t a_lbo = A_MN ? 8192u : 16u, b_lbo = B_MN ? 8192u : 16u;
       const uint32_t a_step = A_MN ? 2048u : 32u, b_step = B_MN ? 2048u : 32u;
+      // a pair's commits arrive on the barrier of each CTA (this CTA's address, then the other's)
+      auto commit = [&](uint64_t* bar) {
+        if constexpr (PAIR) {
+          tc::mma_commit_pair(tc::cluster_addr(tc::smem_u32(bar), 0u));
+          tc::mma_commit_pair(tc::cluster_addr(tc::smem_u32(bar), 1u));
+        } else {
+          tc::mma_commit(bar);
+        }
+      };
       TileCursor cur;
-      for (int t = blockIdx.x; t < total && !abort_flag; t += gridDim.x, ++i) {
+      for (int t = t_first; t < total && !abort_flag; t += t_step, ++i) {
         TileInfo ti;
-        decode_tile<BN, KGROUP, EPI, SPLIT>(p, cur, t, ti);
+        decode_tile<BN, KGROUP, EPI, SPLIT, TM>(p, cur, t, ti);
         const int acc = i & 1;
         const uint32_t acc_phase = (uint32_t)(i >> 1) & 1u;
         if (!tc::mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, &abort_flag, budget)) {
-          fail_abort(p.seg.err, &abort_flag, 2);
+          give_up(2);
           break;
         }
         tc::tc_fence_after();
@@ -381,7 +457,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
         bool ok = true;
         for (int kb = 0; kb < ti.kb; ++kb) {
           if (!tc::mbar_wait(&full_bar[stage], phase, &abort_flag, budget)) {
-            fail_abort(p.seg.err, &abort_flag, 3);
+            give_up(3);
             ok = false;
             break;
           }
@@ -394,25 +470,33 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
 #pragma unroll
             for (int j = 0; j < BPARTS; ++j) {  // the B parts of the stage share the A tile
               const uint64_t bd = tc::smem_desc(sb + j * B_BYTES + k * b_step, b_lbo, 1024u, tc::kLayoutSW128);
-              tc::mma_bf16(d_tmem, ad, bd, IDESC, (kb > 0 || k > 0 || j > 0) ? 1u : 0u);
+              if constexpr (PAIR)
+                tc::mma_bf16_pair(d_tmem, ad, bd, IDESC, (kb > 0 || k > 0 || j > 0) ? 1u : 0u);
+              else
+                tc::mma_bf16(d_tmem, ad, bd, IDESC, (kb > 0 || k > 0 || j > 0) ? 1u : 0u);
             }
           }
-          tc::mma_commit(&empty_bar[stage]);
+          commit(&empty_bar[stage]);
           issued = true;
-          if (++stage == STAGES) {
+          if (++stage == NST) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        if (ti.kb > 0)
-          tc::mma_commit(&tfull_bar[acc]);
-        else
+        if (ti.kb > 0) {
+          commit(&tfull_bar[acc]);
+        } else {  // no K blocks (an expert without rows): the epilogue writes zeros
           tc::mbar_arrive(&tfull_bar[acc]);
+          if constexpr (PAIR) tc::mbar_arrive_cluster(tc::cluster_addr(tc::smem_u32(&tfull_bar[acc]), 1u));
+        }
       }
       // drain: all issued MMAs complete before TMEM may be freed
       if (issued) {
-        tc::mma_commit(&done_bar);
+        if constexpr (PAIR)
+          tc::mma_commit_pair(tc::cluster_addr(tc::smem_u32(&done_bar), 0u));
+        else
+          tc::mma_commit(&done_bar);
         if (!tc::mbar_wait(&done_bar, 0u, nullptr, kWaitBudget)) fail_drain(p.seg.err, 12);
       }
     }
@@ -424,34 +508,40 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
     BoxWriter bw{staging + (warp - 2) * kBoxesPerWarp * kStageBox, 0};
     int i = 0;
     TileCursor cur;
-    for (int t = blockIdx.x; t < total && !abort_flag; t += gridDim.x, ++i) {
+    for (int t = t_first; t < total && !abort_flag; t += t_step, ++i) {
       TileInfo ti;
-      decode_tile<BN, KGROUP, EPI, SPLIT>(p, cur, t, ti);
+      decode_tile<BN, KGROUP, EPI, SPLIT, TM>(p, cur, t, ti);
       const int acc = i & 1;
       const uint32_t acc_phase = (uint32_t)(i >> 1) & 1u;
+      // first row of this CTA's 128 rows in the group; a pair tile's second half may lie past the group's
+      // rows (it is computed with whatever the loads brought and not stored)
+      const int mrow = ti.mt * TM + (int)cta * BM;
+      const bool half_ok = !PAIR || mrow < (KGROUP ? p.M : p.seg.rows[ti.g]);
       if constexpr (EPI == EPI_SWIGLU_BWD) {
         // the pre-activations do not depend on the accumulator: start loading them now
-        const int64_t row = (int64_t)p.seg.row0[ti.g] + ti.mt * BM + row_in_tile;
+        const int64_t row = (int64_t)p.seg.row0[ti.g] + mrow + row_in_tile;
         const int64_t F2 = 2 * (int64_t)p.F;
         const int c0 = chalf * (BN / 2);
         const bf16* hg = p.h + row * F2 + ti.nt * BN + c0;
         const bf16* hu = hg + p.F;
         uint4 gq[4], uq[4];
+        if (half_ok) {
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          gq[q] = reinterpret_cast<const uint4*>(hg)[q];
-          uq[q] = reinterpret_cast<const uint4*>(hu)[q];
+          for (int q = 0; q < 4; ++q) {
+            gq[q] = reinterpret_cast<const uint4*>(hg)[q];
+            uq[q] = reinterpret_cast<const uint4*>(hu)[q];
+          }
         }
         if (!tc::mbar_wait(&tfull_bar[acc], acc_phase, &abort_flag, budget)) {
-          fail_abort(p.seg.err, &abort_flag, 4);
+          give_up(4);
           break;
         }
         tc::tc_fence_after();
         const uint32_t t_row = tmem_base + (uint32_t)(acc * BN + c0) + ((uint32_t)(quad * 32) << 16);
-        const int row_base = p.seg.row0[ti.g] + ti.mt * BM + quad * 32;
+        const int row_base = p.seg.row0[ti.g] + mrow + quad * 32;
         const int x0 = ti.nt * BN + c0;
 #pragma unroll 1
-        for (int c = 0; c < BN / 2; c += 32) {
+        for (int c = 0; c < (half_ok ? BN / 2 : 0); c += 32) {
           float dv[32];
           tc::tmem_ld32(t_row + c, dv);
           // column pairs: word i of a chunk holds columns 2i (low half) and 2i+1
@@ -482,7 +572,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
         // loads before the accumulator wait, and each next chunk while the current one is summed.
         constexpr int kPre = 2;
         const int c0 = chalf * (BN / 2);
-        const int64_t tok = (int64_t)p.seg.row0[ti.g] + ti.mt * BM + row_in_tile;
+        const int64_t tok = (int64_t)p.seg.row0[ti.g] + mrow + row_in_tile;
         const bool ok = tok < p.m_valid;
         int rows[kMaxTopK];
         int n = 0;
@@ -500,7 +590,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
         }
         const int npre = n < kPre ? n : kPre;
         const int64_t col_base = (int64_t)ti.nt * BN + c0;
-        const int row_base = p.seg.row0[ti.g] + ti.mt * BM + quad * 32;  // rows at or past T are clipped
+        const int row_base = p.seg.row0[ti.g] + mrow + quad * 32;  // rows at or past T are clipped
         const bf16* prow[kPre];
 #pragma unroll
         for (int r = 0; r < kPre; ++r) prow[r] = p.dxp + (int64_t)(r < npre ? rows[r] : 0) * p.ldo + col_base;
@@ -513,7 +603,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
             for (int q = 0; q < 4; ++q) pre[r][q] = src[q];
           }
         if (!tc::mbar_wait(&tfull_bar[acc], acc_phase, &abort_flag, budget)) {
-          fail_abort(p.seg.err, &abort_flag, 4);
+          give_up(4);
           break;
         }
         tc::tc_fence_after();
@@ -569,15 +659,17 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
         }
       } else {
         if (!tc::mbar_wait(&tfull_bar[acc], acc_phase, &abort_flag, budget)) {
-          fail_abort(p.seg.err, &abort_flag, 4);
+          give_up(4);
           break;
         }
         tc::tc_fence_after();
         const uint32_t t_row = tmem_base + (uint32_t)(acc * BN) + ((uint32_t)(quad * 32) << 16);
-        if constexpr (EPI == EPI_SWIGLU_FWD) {
+        if (!half_ok) {
+          // the half of a pair tile past the group: nothing to store
+        } else if constexpr (EPI == EPI_SWIGLU_FWD) {
           const int c0 = chalf * (BN / 4);
           const int n0 = ti.nt * (BN / 2) + c0;
-          const int row_base = p.seg.row0[ti.g] + ti.mt * BM + quad * 32;
+          const int row_base = p.seg.row0[ti.g] + mrow + quad * 32;
 #pragma unroll 1
           for (int c = 0; c < BN / 4; c += 32) {
             float gv[32], uv[32];
@@ -598,8 +690,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
           // float32 tile, rows below m_valid and columns below n_valid, plus a per-column bias
           const bool zero = ti.kb == 0;
           const int c0 = chalf * (BN / 2);
-          const int64_t row = KGROUP ? (int64_t)ti.mt * BM + row_in_tile
-                                     : (int64_t)p.seg.row0[ti.g] + ti.mt * BM + row_in_tile;
+          const int64_t row = KGROUP ? (int64_t)mrow + row_in_tile
+                                     : (int64_t)p.seg.row0[ti.g] + mrow + row_in_tile;
           float* outp = p.out_f32 + (KGROUP ? (int64_t)ti.e * p.out_group : 0) + row * p.ldo;
           const bool vec4 = (p.ldo & 3) == 0;
 #pragma unroll 1
@@ -637,7 +729,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
           // q is the GEMM result rounded to bf16; each product and the sum round to bf16, as the bf16
           // torch operations of apply_rotary_pos_emb round them (ats/model/rope.py:83-86)
           const int d0 = chalf * 32;
-          const int64_t tok = (int64_t)p.seg.row0[ti.g] + ti.mt * BM + row_in_tile;
+          const int64_t tok = (int64_t)p.seg.row0[ti.g] + mrow + row_in_tile;
           const int64_t pos = tok < p.m_valid ? tok % p.rope_seq : 0;  // rows past the end are clipped
           float q1[32], q2[32];
           tc::tmem_ld32(t_row + d0, q1);
@@ -660,7 +752,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
               o2[i] = bf2_add(bf2_mul(b, cw2[kk]), bf2_mul(a, sw2[kk]));
             }
           }
-          const int row_base = p.seg.row0[ti.g] + ti.mt * BM + quad * 32;
+          const int row_base = p.seg.row0[ti.g] + mrow + quad * 32;
           bw.put(o1, &tmO, ti.nt * 128 + d0, row_base, lane);
           bw.put(o2, &tmO, ti.nt * 128 + 64 + d0, row_base, lane);
         } else {
@@ -669,7 +761,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
           const bool zero = ti.kb == 0;
           const int c0 = chalf * (BN / 2);
           // first of this warp's rows in the output map: [E][M] stacked weight rows, or the permuted rows
-          const int row_base = (KGROUP ? ti.e * p.M : p.seg.row0[ti.g]) + ti.mt * BM + quad * 32;
+          const int row_base = (KGROUP ? ti.e * p.M : p.seg.row0[ti.g]) + mrow + quad * 32;
 #pragma unroll 1
           for (int c = 0; c < BN / 2; c += 32) {
             if (ti.nt * BN + c0 + c >= p.N) break;  // a chunk past N (the last tile of an N not a multiple of BN)
@@ -688,15 +780,47 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
       }
       tc::tc_fence_before();
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&tempty_bar[acc]);
+      if (lane == 0) {  // the accumulator is free again (a pair's MMA thread counts both CTAs' warps)
+        if (PAIR && cta != 0)
+          tc::mbar_arrive_cluster(tc::cluster_addr(tc::smem_u32(&tempty_bar[acc]), 0u));
+        else
+          tc::mbar_arrive(&tempty_bar[acc]);
+      }
     }
     if (staging_bytes(EPI) > 0 && lane == 0) tc::bulk_wait<0>();  // every TMA store done before the CTA exits
   }
   tc::tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) {
+    // CTA 0's MMAs read CTA 1's ring and write its TMEM, and CTA 1's loads and epilogue signal CTA 0's
+    // barriers: after the first barrier CTA 0 knows how many stages each producer loaded.  Where only one
+    // of them loaded a stage (the other gave up), CTA 0 settles that stage's transaction count -- the
+    // missing half counted as done, or the half on its way expected -- and then waits for every phase, so
+    // no load of either CTA is in flight when the second barrier lets them free TMEM and exit.
+    tc::cluster_sync();
+    if (cta == 0 && warp == 0 && lane == 0) {
+      const int kl = issued_k, kp = peer_issued_s;
+      const int lo = kl < kp ? kl : kp, hi = kl < kp ? kp : kl;
+      if (hi - lo > NST) {  // cannot happen: a stage is reloaded only after both halves of its last load
+        fail_drain(p.seg.err, 13);
+      } else {
+        for (int k = lo; k < hi; ++k) {
+          if (k < kl)
+            tc::mbar_complete_tx(&full_bar[k % NST], STAGE_BYTES);  // CTA 1's half never came
+          else
+            tc::mbar_arrive_expect_tx(&full_bar[k % NST], STAGE_BYTES);  // only CTA 1's half is coming
+        }
+        drain_loads(hi);
+      }
+    }
+    tc::cluster_sync();
+  }
   if (warp == 1) {
     tc::tc_fence_after();
-    tc::tmem_dealloc(tmem_base, 2 * BN);
+    if constexpr (PAIR)
+      tc::tmem_dealloc_pair(tmem_base, 2 * BN);
+    else
+      tc::tmem_dealloc(tmem_base, 2 * BN);
   }
 }
 
@@ -747,21 +871,67 @@ int make_out_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t oute
   return encode_map(m, base, inner, outer, row_bytes, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI, bool KGROUP, int SPLIT = 1, int BPARTS = 1>
+template <int BN, bool A_MN, bool B_MN, int EPI, bool KGROUP, int SPLIT = 1, int BPARTS = 1, bool PAIR = false>
 int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& p, int64_t max_tiles,
               cudaStream_t st, const CUtensorMap* to = nullptr, const CUtensorMap* to2 = nullptr) {
-  auto kfn = tc_gemm_kernel<BN, A_MN, B_MN, EPI, KGROUP, SPLIT, BPARTS>;
+  auto kfn = tc_gemm_kernel<BN, A_MN, B_MN, EPI, KGROUP, SPLIT, BPARTS, PAIR>;
   if (staging_bytes(EPI) > 0 && to == nullptr) return fail(ATS_EBADARG, "moe_gemm: bf16 epilogue needs an output map");
   if (EPI == EPI_SWIGLU_FWD && to2 == nullptr) return fail(ATS_EBADARG, "moe_gemm: SwiGLU epilogue needs the a map");
-  const int smem = 1024 + STAGES * (BM * BK * 2 + BPARTS * BN * BK * 2) + staging_bytes(EPI);
+  const int smem = 1024 + ring_stages(BN, BPARTS, PAIR) * stage_bytes(BN, BPARTS, PAIR) + staging_bytes(EPI);
   cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return fail(ATS_ECUDA, "moe_gemm: smem attribute: %s", cudaGetErrorString(e));
-  int grid = gemm_ctas();
-  if (max_tiles < grid) grid = (int)(max_tiles > 0 ? max_tiles : 1);
-  kfn<<<grid, kThreads, smem, st>>>(ta, tb, to != nullptr ? *to : ta, to2 != nullptr ? *to2 : ta, p);
+  const CUtensorMap& mo = to != nullptr ? *to : ta;
+  const CUtensorMap& mo2 = to2 != nullptr ? *to2 : ta;
+  if constexpr (!PAIR) {
+    int grid = gemm_ctas();
+    if (max_tiles < grid) grid = (int)(max_tiles > 0 ? max_tiles : 1);
+    kfn<<<grid, kThreads, smem, st>>>(ta, tb, mo, mo2, p);
+  } else {
+    // clusters of two CTAs: as many pairs as fit at once on the SMs this GEMM may use
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int pairs = gemm_ctas() / 2;
+    static thread_local int fit[kMaxDevices] = {};  // co-resident pairs of this kernel, per device
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+      return fail(ATS_ECUDA, "moe_gemm: no current device");
+    if (fit[dev] == 0) {
+      cfg.gridDim = dim3(2 * (unsigned)(pairs > 0 ? pairs : 1), 1, 1);
+      int n = 0;
+      e = cudaOccupancyMaxActiveClusters(&n, kfn, &cfg);
+      if (e != cudaSuccess || n < 1) return fail(ATS_ECUDA, "moe_gemm: no CTA pair fits (%s)", cudaGetErrorString(e));
+      fit[dev] = n;
+    }
+    if (pairs > fit[dev]) pairs = fit[dev];
+    if (max_tiles < pairs) pairs = (int)(max_tiles > 0 ? max_tiles : 1);
+    if (pairs < 1) pairs = 1;
+    cfg.gridDim = dim3(2 * (unsigned)pairs, 1, 1);
+    e = cudaLaunchKernelEx(&cfg, kfn, ta, tb, mo, mo2, p);
+    if (e != cudaSuccess) return fail(ATS_ECUDA, "moe_gemm: pair launch: %s", cudaGetErrorString(e));
+  }
   return check_launch("moe_tc_gemm");
 }
 
+// The expert GEMMs (one B part, no K parts) on CTA pairs or on single CTAs.  `pair` is read once per entry
+// point (gemm_pairs()), so its tensor maps and its launches agree.  A K-major B operand's tensor map has
+// boxes of b_box_rows(bn, pair) rows.
+template <int BN, bool A_MN, bool B_MN, int EPI, bool KGROUP>
+int launch_gemm(bool pair, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& p, int64_t max_tiles,
+                cudaStream_t st, const CUtensorMap* to, const CUtensorMap* to2 = nullptr) {
+  if (pair) return launch_tc<BN, A_MN, B_MN, EPI, KGROUP, 1, 1, true>(ta, tb, p, max_tiles, st, to, to2);
+  return launch_tc<BN, A_MN, B_MN, EPI, KGROUP, 1, 1, false>(ta, tb, p, max_tiles, st, to, to2);
+}
+
+uint32_t b_box_rows(int bn, bool pair) { return pair ? (uint32_t)bn / 2 : (uint32_t)bn; }
 
 int pick_bn(int64_t n) { return n % 256 == 0 ? 256 : 128; }
 
@@ -772,6 +942,7 @@ int tc_experts_fwd(const void* xp, const void* wgu, const void* wd, void* h, voi
   if (!tc_shape_supported(H, F)) return ATS_EUNSUPPORTED;
   const int64_t R = sg.max_rows;
   const int64_t IO = io_rows > 0 ? io_rows : R;  // rows of xp and y (reads past them are zero, stores clipped)
+  const bool pair = gemm_pairs();
   CUtensorMap ma, mb;
   GemmArgs p{};
   p.seg = sg;
@@ -787,11 +958,12 @@ int tc_experts_fwd(const void* xp, const void* wgu, const void* wd, void* h, voi
   CUtensorMap mh, mact;
   ATS_TRY(make_out_map(&mh, h, 2 * F, R, 2 * F * 2));
   ATS_TRY(make_out_map(&mact, a, F, R, F * 2));
-  ATS_TRY((launch_tc<256, false, false, EPI_SWIGLU_FWD, false>(ma, mb, p, (R / BM) * (F / 128), st, &mh, &mact)));
+  ATS_TRY((launch_gemm<256, false, false, EPI_SWIGLU_FWD, false>(pair, ma, mb, p, (R / BM) * (F / 128), st, &mh,
+                                                                  &mact)));
   // y = a Wd_e^T
   const int bn = pick_bn(H);
   ATS_TRY(make_map(&ma, a, F, R, F * 2, 128));
-  ATS_TRY(make_map(&mb, wd, F, (uint64_t)E * H, F * 2, bn));
+  ATS_TRY(make_map(&mb, wd, F, (uint64_t)E * H, F * 2, b_box_rows(bn, pair)));
   p.N = (int)H;
   p.K = (int)F;
   p.b = OpSpec{(int)H, 0};
@@ -799,8 +971,8 @@ int tc_experts_fwd(const void* xp, const void* wgu, const void* wd, void* h, voi
   p.ldo = H;
   CUtensorMap mo;
   ATS_TRY(make_out_map(&mo, y, H, IO, H * 2));
-  if (bn == 256) return launch_tc<256, false, false, EPI_STORE, false>(ma, mb, p, (R / BM) * (H / 256), st, &mo);
-  return launch_tc<128, false, false, EPI_STORE, false>(ma, mb, p, (R / BM) * (H / 128), st, &mo);
+  if (bn == 256) return launch_gemm<256, false, false, EPI_STORE, false>(pair, ma, mb, p, (R / BM) * (H / 256), st, &mo);
+  return launch_gemm<128, false, false, EPI_STORE, false>(pair, ma, mb, p, (R / BM) * (H / 128), st, &mo);
 }
 
 int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a, const void* wgu, const void* wd,
@@ -809,6 +981,7 @@ int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a,
   if (!tc_shape_supported(H, F)) return ATS_EUNSUPPORTED;
   const int64_t R = sg.max_rows;
   const int64_t IO = io_rows > 0 ? io_rows : R;  // rows of dy, xp and dxp
+  const bool pair = gemm_pairs();
   CUtensorMap ma, mb;
   GemmArgs p{};
   p.seg = sg;
@@ -826,9 +999,9 @@ int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a,
     CUtensorMap mdh;
     ATS_TRY(make_out_map(&mdh, dh, 2 * F, R, 2 * F * 2));
     if (bn == 256)
-      ATS_TRY((launch_tc<256, false, true, EPI_SWIGLU_BWD, false>(ma, mb, p, (R / BM) * (F / 256), st, &mdh)));
+      ATS_TRY((launch_gemm<256, false, true, EPI_SWIGLU_BWD, false>(pair, ma, mb, p, (R / BM) * (F / 256), st, &mdh)));
     else
-      ATS_TRY((launch_tc<128, false, true, EPI_SWIGLU_BWD, false>(ma, mb, p, (R / BM) * (F / 128), st, &mdh)));
+      ATS_TRY((launch_gemm<128, false, true, EPI_SWIGLU_BWD, false>(pair, ma, mb, p, (R / BM) * (F / 128), st, &mdh)));
   }
   // dxp = dh Wgu_e (B N-major: Wgu_e[j][h])
   if (stages & kBwdData) {
@@ -843,9 +1016,9 @@ int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a,
     CUtensorMap mo;
     ATS_TRY(make_out_map(&mo, dxp, H, IO, H * 2));
     if (bn == 256)
-      ATS_TRY((launch_tc<256, false, true, EPI_STORE, false>(ma, mb, p, (R / BM) * (H / 256), st, &mo)));
+      ATS_TRY((launch_gemm<256, false, true, EPI_STORE, false>(pair, ma, mb, p, (R / BM) * (H / 256), st, &mo)));
     else
-      ATS_TRY((launch_tc<128, false, true, EPI_STORE, false>(ma, mb, p, (R / BM) * (H / 128), st, &mo)));
+      ATS_TRY((launch_gemm<128, false, true, EPI_STORE, false>(pair, ma, mb, p, (R / BM) * (H / 128), st, &mo)));
   }
   if (!(stages & kBwdWeights)) return ATS_OK;
   // dWd_e[h][f] = sum over the expert's rows r of dy[r][h] a[r][f]   (A M-major, B N-major).  256-wide tiles
@@ -865,7 +1038,7 @@ int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a,
     CUtensorMap mo;
     ATS_TRY(make_out_map(&mo, dwd, F, (uint64_t)sg.E * H, F * 2));
     const int64_t tiles = (int64_t)sg.E * (H / BM) * ((F + bn - 1) / bn);
-    ATS_TRY((launch_tc<256, true, true, EPI_STORE, true>(ma, mb, p, tiles, st, &mo)));
+    ATS_TRY((launch_gemm<256, true, true, EPI_STORE, true>(pair, ma, mb, p, tiles, st, &mo)));
   }
   // dWgu_e[j][h] = sum over the expert's rows r of dh[r][j] xp[r][h]
   {
@@ -880,8 +1053,8 @@ int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a,
     CUtensorMap mo;
     ATS_TRY(make_out_map(&mo, dwgu, H, (uint64_t)sg.E * 2 * F, H * 2));
     const int64_t tiles = (int64_t)sg.E * (2 * F / BM) * (H / bn);
-    if (bn == 256) return launch_tc<256, true, true, EPI_STORE, true>(ma, mb, p, tiles, st, &mo);
-    return launch_tc<128, true, true, EPI_STORE, true>(ma, mb, p, tiles, st, &mo);
+    if (bn == 256) return launch_gemm<256, true, true, EPI_STORE, true>(pair, ma, mb, p, tiles, st, &mo);
+    return launch_gemm<128, true, true, EPI_STORE, true>(pair, ma, mb, p, tiles, st, &mo);
   }
 }
 
@@ -919,19 +1092,20 @@ int tc_gemm_nt_fwd(const void* a, const void* b, void* c, int64_t N, int64_t K, 
   if (!tc_shape_supported(N, K)) return ATS_EUNSUPPORTED;
   const int64_t R = sg.max_rows;
   const int bn = pick_bn(N);
+  const bool pair = gemm_pairs();
   CUtensorMap ma, mb, mo;
   GemmArgs p{};
   p.seg = sg;
   ATS_TRY(make_map(&ma, a, K, io_rows, K * 2, 128));
-  ATS_TRY(make_map(&mb, b, K, N, K * 2, bn));
+  ATS_TRY(make_map(&mb, b, K, N, K * 2, b_box_rows(bn, pair)));
   p.N = (int)N;
   p.K = (int)K;
   p.b = OpSpec{(int)N, 0};
   p.out = static_cast<bf16*>(c);
   p.ldo = N;
   ATS_TRY(make_out_map(&mo, c, N, io_rows, N * 2));
-  if (bn == 256) return launch_tc<256, false, false, EPI_STORE, false>(ma, mb, p, (R / BM) * (N / 256), st, &mo);
-  return launch_tc<128, false, false, EPI_STORE, false>(ma, mb, p, (R / BM) * (N / 128), st, &mo);
+  if (bn == 256) return launch_gemm<256, false, false, EPI_STORE, false>(pair, ma, mb, p, (R / BM) * (N / 256), st, &mo);
+  return launch_gemm<128, false, false, EPI_STORE, false>(pair, ma, mb, p, (R / BM) * (N / 128), st, &mo);
 }
 
 // Its gradients: dA[M,K] = dC[M,N] B[N,K] (B N-major), dB[N,K] = dC^T A summed over the
@@ -940,6 +1114,7 @@ int tc_gemm_nt_bwd(const void* dc, const void* a, const void* b, void* da, void*
                    const SegTable& sg, cudaStream_t st, int64_t io_rows) {
   if (!tc_shape_supported(N, K)) return ATS_EUNSUPPORTED;
   const int64_t R = sg.max_rows;
+  const bool pair = gemm_pairs();
   if (da != nullptr) {
     const int bn = pick_bn(K);
     CUtensorMap ma, mb, mo;
@@ -954,9 +1129,9 @@ int tc_gemm_nt_bwd(const void* dc, const void* a, const void* b, void* da, void*
     p.ldo = K;
     ATS_TRY(make_out_map(&mo, da, K, io_rows, K * 2));
     if (bn == 256)
-      ATS_TRY((launch_tc<256, false, true, EPI_STORE, false>(ma, mb, p, (R / BM) * (K / 256), st, &mo)));
+      ATS_TRY((launch_gemm<256, false, true, EPI_STORE, false>(pair, ma, mb, p, (R / BM) * (K / 256), st, &mo)));
     else
-      ATS_TRY((launch_tc<128, false, true, EPI_STORE, false>(ma, mb, p, (R / BM) * (K / 128), st, &mo)));
+      ATS_TRY((launch_gemm<128, false, true, EPI_STORE, false>(pair, ma, mb, p, (R / BM) * (K / 128), st, &mo)));
   }
   if (db != nullptr) {
     const int bn = pick_bn(K);
@@ -974,8 +1149,8 @@ int tc_gemm_nt_bwd(const void* dc, const void* a, const void* b, void* da, void*
     p.out_group = N * K;
     ATS_TRY(make_out_map(&mo, db, K, N, K * 2));
     const int64_t tiles = (N / BM) * (K / bn);
-    if (bn == 256) return launch_tc<256, true, true, EPI_STORE, true>(ma, mb, p, tiles, st, &mo);
-    return launch_tc<128, true, true, EPI_STORE, true>(ma, mb, p, tiles, st, &mo);
+    if (bn == 256) return launch_gemm<256, true, true, EPI_STORE, true>(pair, ma, mb, p, tiles, st, &mo);
+    return launch_gemm<128, true, true, EPI_STORE, true>(pair, ma, mb, p, tiles, st, &mo);
   }
   return ATS_OK;
 }

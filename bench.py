@@ -1184,6 +1184,8 @@ def main() -> int:
     ap.add_argument("--ep-parts", type=int, default=None, help="expert parts of the expert-parallel exchange")
     ap.add_argument("--ep-comm-sms", type=int, default=None,
                     help="SMs the expert-parallel exchange keeps while it overlaps the expert GEMMs")
+    ap.add_argument("--gemm-pairs", type=int, default=0, choices=[0, 1],
+                    help="1: tensor-core GEMMs on CTA pairs (256-row tiles); 0: single CTAs (128-row tiles)")
     args = ap.parse_args()
     if args.ep_exchange:
         MoEEPWorkload.EXCHANGE = args.ep_exchange
@@ -1213,6 +1215,7 @@ def main() -> int:
         dist = tdist
     from ats_v2_b200 import _lib
     lib = _lib.load()
+    _lib.call("ats_set_gemm_pairs", args.gemm_pairs)
     gpu_index = int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local]) \
         if os.environ.get("CUDA_VISIBLE_DEVICES") else local
     main_wl = WORKLOADS[args.workload](torch, rank, world, peaks, pk)

@@ -61,6 +61,14 @@ ATS_API uint64_t ats_kernel_launches(void);
 ATS_API int ats_set_gemm_sm_limit(int sms);
 ATS_API int ats_gemm_sm_limit(void);
 
+/* Tile shape of the tensor-core expert, dense-FFN and MLA GEMMs, process-wide:
+ * nonzero runs 256-row tiles on pairs of CTAs on two SMs (tcgen05 cta_group::2,
+ * each SM loading half of the B tile), zero (the default) runs 128-row tiles on
+ * single CTAs.  Both give identical results; a GEMM call reads the setting
+ * once.  ats_gemm_pairs returns it.  No reference counterpart. */
+ATS_API int ats_set_gemm_pairs(int enable);
+ATS_API int ats_gemm_pairs(void);
+
 /* Status of the bounded device waits on the current device: ATS_OK when no
  * wait of a tensor-core GEMM or an RMSNorm ring kernel has given up since the
  * last call, else ATS_ETIMEOUT with the first wait's code in *status; then
