@@ -341,6 +341,15 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
         else
           tc::tma_load_2d(dst, map, x, y, &full_bar[stage]);
       };
+      // MN-major operands: one load of `blocks` 64-column blocks of 64 K rows (a 3-D map: 64 columns, the K
+      // rows, the column blocks), each block 8 KB in shared memory -- the layout of that many 2-D 64 x 64
+      // boxes in one TMA instruction instead of one per block
+      auto load_mn = [&](void* dst, const CUtensorMap* map, int col, int krow) {
+        if constexpr (PAIR)
+          tc::tma_load_3d_pair(dst, map, 0, krow, col >> 6, full0 + (uint32_t)stage * 8u);
+        else
+          tc::tma_load_3d(dst, map, 0, krow, col >> 6, &full_bar[stage]);
+      };
       TileCursor cur;
       for (int t = t_first; t < total && !abort_flag; t += t_step) {
         TileInfo ti;
@@ -383,9 +392,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
           if (!A_MN) {  // M-grouped A: rows of the tile's segment, K contiguous
             load(sa, &tmA, a_ko + kq * BK, seg_r0 + m0);
           } else {      // K-grouped A: M contiguous, K = rows of the current segment
-            const int krow = seg_r0 + lkb * BK + a_ko;
-            load(sa, &tmA, m0, krow);
-            load(sa + 8192, &tmA, m0 + 64, krow);
+            load_mn(sa, &tmA, m0, seg_r0 + lkb * BK + a_ko);
           }
           if (!B_MN) {  // stacked weights, K contiguous
             if constexpr (PAIR) {  // this CTA's B_ROWS rows: the gate or up half (SwiGLU), or the cta-th half
@@ -405,10 +412,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
             const int krow = (KGROUP ? seg_r0 + lkb * BK : b_row0 + kq * BK) + b_ko;
             const int ncol = n0 + (int)cta * B_ROWS + b_no;
 #pragma unroll
-            for (int j = 0; j < BPARTS; ++j)
-#pragma unroll
-              for (int b = 0; b < B_ROWS / 64; ++b)
-                load(sb + j * B_BYTES + b * 8192, &tmB, ncol + (BPARTS > 1 ? p.b_noff[j] : 0) + b * 64, krow);
+            for (int j = 0; j < BPARTS; ++j) load_mn(sb + j * B_BYTES, &tmB, ncol + (BPARTS > 1 ? p.b_noff[j] : 0), krow);
           }
           if (part == SPLIT - 1) ++lkb;
           ++issued_k;
@@ -860,6 +864,31 @@ int encode_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer,
   return ATS_OK;
 }
 
+// MN-major operand map: the 2-D tensor [outer rows][inner] (inner a multiple of 64) seen in three dimensions
+// {64 columns, the rows, inner / 64 column blocks} with strides {row_bytes, 128 B}, 128-byte swizzle, box
+// {64, 64, blocks}: one load brings `blocks` consecutive 64 x 64 blocks, block-major in shared memory.  Blocks
+// and rows past the tensor read as zeros.
+int make_map_mn(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                uint32_t blocks) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc;
+  ATS_TRY(encode_fn(&enc));
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (row_bytes & 15) || inner % 64 != 0 || inner == 0 || outer == 0)
+    return fail(ATS_EBADARG, "moe_gemm: operand not TMA-compatible (base %p, row %llu B, %llu x %llu)", base,
+                (unsigned long long)row_bytes, (unsigned long long)inner, (unsigned long long)outer);
+  cuuint64_t dims[3] = {64, outer, inner / 64};
+  cuuint64_t strides[2] = {row_bytes, 128};
+  cuuint32_t box[3] = {64, 64, blocks};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(ATS_ECUDA, "moe_gemm: cuTensorMapEncodeTiled (3-D) failed (%d)", (int)r);
+  return ATS_OK;
+}
+
+// 64-column blocks of an MN-major B tile held by one CTA.
+uint32_t b_blocks(int bn, bool pair) { return (pair ? (uint32_t)bn / 2 : (uint32_t)bn) / 64u; }
+
 // Operand map: 128-byte swizzle, box {64, box_outer}.
 int make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
              uint32_t box_outer) {
@@ -990,7 +1019,7 @@ int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a,
   if (stages & kBwdData) {
     const int bn = pick_bn(F);
     ATS_TRY(make_map(&ma, dy, H, IO, H * 2, 128));
-    ATS_TRY(make_map(&mb, wd, F, (uint64_t)E * H, F * 2, 64));
+    ATS_TRY(make_map_mn(&mb, wd, F, (uint64_t)E * H, F * 2, b_blocks(bn, pair)));
     p.N = (int)F;
     p.K = (int)H;
     p.b = OpSpec{(int)H, 0};
@@ -1007,7 +1036,7 @@ int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a,
   if (stages & kBwdData) {
     const int bn = pick_bn(H);
     ATS_TRY(make_map(&ma, dh, 2 * F, R, 2 * F * 2, 128));
-    ATS_TRY(make_map(&mb, wgu, H, (uint64_t)E * 2 * F, H * 2, 64));
+    ATS_TRY(make_map_mn(&mb, wgu, H, (uint64_t)E * 2 * F, H * 2, b_blocks(bn, pair)));
     p.N = (int)H;
     p.K = (int)(2 * F);
     p.b = OpSpec{(int)(2 * F), 0};
@@ -1026,8 +1055,8 @@ int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a,
   // wider tiles read each row's operands half as often (these GEMMs have a short K: an expert's rows)
   {
     const int bn = 256;
-    ATS_TRY(make_map(&ma, dy, H, IO, H * 2, 64));
-    ATS_TRY(make_map(&mb, a, F, R, F * 2, 64));
+    ATS_TRY(make_map_mn(&ma, dy, H, IO, H * 2, 2));
+    ATS_TRY(make_map_mn(&mb, a, F, R, F * 2, b_blocks(bn, pair)));
     p.M = (int)H;
     p.N = (int)F;
     p.K = 0;
@@ -1043,8 +1072,8 @@ int tc_experts_bwd(const void* dy, const void* xp, const void* h, const void* a,
   // dWgu_e[j][h] = sum over the expert's rows r of dh[r][j] xp[r][h]
   {
     const int bn = pick_bn(H);
-    ATS_TRY(make_map(&ma, dh, 2 * F, R, 2 * F * 2, 64));
-    ATS_TRY(make_map(&mb, xp, H, IO, H * 2, 64));
+    ATS_TRY(make_map_mn(&ma, dh, 2 * F, R, 2 * F * 2, 2));
+    ATS_TRY(make_map_mn(&mb, xp, H, IO, H * 2, b_blocks(bn, pair)));
     p.M = (int)(2 * F);
     p.N = (int)H;
     p.out = static_cast<bf16*>(dwgu);
@@ -1121,7 +1150,7 @@ int tc_gemm_nt_bwd(const void* dc, const void* a, const void* b, void* da, void*
     GemmArgs p{};
     p.seg = sg;
     ATS_TRY(make_map(&ma, dc, N, io_rows, N * 2, 128));
-    ATS_TRY(make_map(&mb, b, K, N, K * 2, 64));
+    ATS_TRY(make_map_mn(&mb, b, K, N, K * 2, b_blocks(bn, pair)));
     p.N = (int)K;
     p.K = (int)N;
     p.b = OpSpec{(int)N, 0};
@@ -1138,8 +1167,8 @@ int tc_gemm_nt_bwd(const void* dc, const void* a, const void* b, void* da, void*
     CUtensorMap ma, mb, mo;
     GemmArgs p{};
     p.seg = sg;
-    ATS_TRY(make_map(&ma, dc, N, io_rows, N * 2, 64));
-    ATS_TRY(make_map(&mb, a, K, io_rows, K * 2, 64));
+    ATS_TRY(make_map_mn(&ma, dc, N, io_rows, N * 2, 2));
+    ATS_TRY(make_map_mn(&mb, a, K, io_rows, K * 2, b_blocks(bn, pair)));
     p.M = (int)N;
     p.N = (int)K;
     p.K = 0;
@@ -1203,11 +1232,11 @@ int tc_router_dx(const void* dlparts, const void* wparts, const void* dxp, const
   p.tok_row = tok_row;
   p.topk = k;
   ATS_TRY(make_map(&ma, dlparts, (uint64_t)3 * Ep, T, (uint64_t)3 * Ep * 2, 128));
-  ATS_TRY(make_map(&mb, wparts, H, (uint64_t)3 * Ep, H * 2, 64));
+  if (Ep != kRouterEp) return fail(ATS_EUNSUPPORTED, "moe_router: padded expert count %d", Ep);
+  ATS_TRY(make_map_mn(&mb, wparts, H, (uint64_t)3 * Ep, H * 2, b_blocks(pick_bn(H), false)));
   CUtensorMap mo;
   ATS_TRY(make_out_map(&mo, dx, H, T, H * 2));
   const int64_t mt = (T + BM - 1) / BM;
-  if (Ep != kRouterEp) return fail(ATS_EUNSUPPORTED, "moe_router: padded expert count %d", Ep);
   if (pick_bn(H) == 256)
     return launch_tc<256, false, true, EPI_SCATTER, false, 6>(ma, mb, p, mt * (H / 256), st, &mo);
   return launch_tc<128, false, true, EPI_SCATTER, false, 6>(ma, mb, p, mt * (H / 128), st, &mo);
@@ -1229,8 +1258,8 @@ int tc_router_dw(const void* x, const void* dlparts, float* partial, int64_t T, 
   p.out_group = H * Ep;
   p.m_valid = (int)H;
   p.n_valid = Ep;
-  ATS_TRY(make_map(&ma, x, H, T, H * 2, 64));
-  ATS_TRY(make_map(&mb, dlparts, (uint64_t)3 * Ep, T, (uint64_t)3 * Ep * 2, 64));
+  ATS_TRY(make_map_mn(&ma, x, H, T, H * 2, 2));
+  ATS_TRY(make_map_mn(&mb, dlparts, (uint64_t)3 * Ep, T, (uint64_t)3 * Ep * 2, 1));
   return launch_tc<kRouterEp, true, true, EPI_F32, true, 1, 3>(ma, mb, p, (int64_t)chunks.E * (H / BM), st);
 }
 
