@@ -29,6 +29,7 @@ ATS_BF16 = 1
 
 ATS_MOE_PACKED = 0
 ATS_MOE_SLOTS = 1
+ATS_ROUTER_BWD_DW, ATS_ROUTER_BWD_DX, ATS_ROUTER_BWD_ALL = 1, 2, 3  # stages of ats_moe_router_bwd_staged
 
 _I64x3 = c_int64 * 3
 
@@ -135,6 +136,9 @@ SIGNATURES: dict[str, tuple] = {
     "ats_moe_router_bwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_int, c_int64,
                                    c_int, c_void_p, c_void_p, c_int64, c_int64, c_int, c_void_p, c_size_t,
                                    c_void_p]),
+    "ats_moe_router_bwd_staged": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_int,
+                                          c_int64, c_int, c_void_p, c_void_p, c_int64, c_int64, c_int, c_void_p,
+                                          c_size_t, c_int, c_void_p]),
     "ats_moe_router_status": (c_int, [c_void_p, c_size_t, c_int64, c_int64, c_int, POINTER(c_int)]),
 }
 

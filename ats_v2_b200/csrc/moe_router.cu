@@ -232,28 +232,44 @@ int ats_moe_router_fwd(const void* x, const float* w, const float* bias, float* 
 int ats_moe_router_bwd(const float* dlogits, const void* x, const float* w, const void* dxp, const void* moe_workspace,
                        size_t moe_workspace_bytes, int k, int64_t capacity, int layout, void* dx, float* dw,
                        int64_t T, int64_t H, int E, void* workspace, size_t workspace_bytes, void* stream) {
+  return ats_moe_router_bwd_staged(dlogits, x, w, dxp, moe_workspace, moe_workspace_bytes, k, capacity, layout, dx,
+                                   dw, T, H, E, workspace, workspace_bytes, ATS_ROUTER_BWD_ALL, stream);
+}
+
+int ats_moe_router_bwd_staged(const float* dlogits, const void* x, const float* w, const void* dxp,
+                              const void* moe_workspace, size_t moe_workspace_bytes, int k, int64_t capacity,
+                              int layout, void* dx, float* dw, int64_t T, int64_t H, int E, void* workspace,
+                              size_t workspace_bytes, int stages, void* stream) {
+  if (stages < 1 || stages > ATS_ROUTER_BWD_ALL) return fail(ATS_EBADARG, "moe_router_bwd: stages %d", stages);
   if (!router_supported(ATS_BF16, T, H, E))
     return fail(ATS_EUNSUPPORTED, "moe_router_bwd: unsupported shape (T=%lld hidden=%lld E=%d)", (long long)T,
                 (long long)H, E);
-  if (dlogits == nullptr || x == nullptr || w == nullptr || dx == nullptr || dw == nullptr)
-    return fail(ATS_EBADARG, "moe_router_bwd: null pointer");
-  const int* tok_row = nullptr;
-  if (dxp != nullptr) {
-    MoePlan plan;
-    ATS_TRY(moe_plan_from_ws(moe_workspace, moe_workspace_bytes, T, E, k, capacity, layout, &plan));
-    tok_row = plan.tok_row;
-  }
   RouterWs q;
   ATS_TRY(router_ws(workspace, workspace_bytes, T, H, E, &q));
   cudaStream_t st = (cudaStream_t)stream;
-  ATS_TRY(prepare(q, w, T, H, E, st));
-  split_dl_kernel<<<grid_for(T * q.Ep), 256, 0, st>>>(dlogits, T, E, q.Ep, q.dlparts);
-  ATS_TRY(check_launch("moe_router_split_dl"));
-  ATS_TRY(tc_router_dx(q.dlparts, q.wparts, dxp, tok_row, k, dx, T, H, q.Ep, one_table(q, T), st));
-  ATS_TRY(tc_router_dw(x, q.dlparts, q.partial, T, H, q.Ep, chunk_table(q, T), st));
-  router_dw_reduce_kernel<<<dim3((unsigned)((H + 31) / 32), (unsigned)(q.Ep / 32)), dim3(32, 8), 0, st>>>(
-      q.partial, q.KS, H, E, q.Ep, dw);
-  return check_launch("moe_router_dw_reduce");
+  if (stages & ATS_ROUTER_BWD_DW) {
+    // the split weight and gradient parts stay in the workspace for the token-gradient stage
+    if (dlogits == nullptr || x == nullptr || w == nullptr || dw == nullptr)
+      return fail(ATS_EBADARG, "moe_router_bwd: null pointer");
+    ATS_TRY(prepare(q, w, T, H, E, st));
+    split_dl_kernel<<<grid_for(T * q.Ep), 256, 0, st>>>(dlogits, T, E, q.Ep, q.dlparts);
+    ATS_TRY(check_launch("moe_router_split_dl"));
+    ATS_TRY(tc_router_dw(x, q.dlparts, q.partial, T, H, q.Ep, chunk_table(q, T), st));
+    router_dw_reduce_kernel<<<dim3((unsigned)((H + 31) / 32), (unsigned)(q.Ep / 32)), dim3(32, 8), 0, st>>>(
+        q.partial, q.KS, H, E, q.Ep, dw);
+    ATS_TRY(check_launch("moe_router_dw_reduce"));
+  }
+  if (stages & ATS_ROUTER_BWD_DX) {
+    if (dx == nullptr) return fail(ATS_EBADARG, "moe_router_bwd: null token gradient");
+    const int* tok_row = nullptr;
+    if (dxp != nullptr) {
+      MoePlan plan;
+      ATS_TRY(moe_plan_from_ws(moe_workspace, moe_workspace_bytes, T, E, k, capacity, layout, &plan));
+      tok_row = plan.tok_row;
+    }
+    ATS_TRY(tc_router_dx(q.dlparts, q.wparts, dxp, tok_row, k, dx, T, H, q.Ep, one_table(q, T), st));
+  }
+  return ATS_OK;
 }
 
 int ats_moe_router_status(const void* workspace, size_t workspace_bytes, int64_t T, int64_t H, int E, int* status) {

@@ -57,7 +57,7 @@ from torch import nn
 from ats_v2_b200 import _lib
 from ats_v2_b200.ffn import SwiGLU
 from ats_v2_b200.moe import (LazyUtilization, capacity_for, init_residual_projection, router_backward,
-                             router_forward, stacked)
+                             router_forward, router_weight_grad, stacked)
 
 SLOTS = _lib.ATS_MOE_SLOTS
 
@@ -762,6 +762,10 @@ class _EPPeerFn(torch.autograd.Function):
         return (dx, dgate_w.to(gate_dtype), None, None, None, None, *grads)
 
 
+# The device exchange's backward runs the router weight gradient beside the output-gradient push (needs
+# comm_sms > 0 and the tensor-core router).
+_ROUTER_BESIDE_PUSH = True
+
 _DEVICE_SET = ("xr", "yr", "dyr", "dxr")  # every buffer of a device-exchange set is expert-side
 
 # When a list, the device exchange records a CUDA event on the current stream at each phase boundary
@@ -826,6 +830,7 @@ class _EPDeviceFn(torch.autograd.Function):
         allv = torch.empty((W, 2 * E + 3), dtype=torch.int32, device=dev)
         _mark("route")
         dist.all_gather_into_tensor(allv, mine, group=group)
+        _mark("exchange_counts")
         ps = state.acquire(parts * part_rows, 0, H, x2.dtype, dev, group, W, me, _DEVICE_SET, _DEVICE_SET)
         ps.owner = weakref.ref(ctx)
         _lib.call("ats_moe_ep_zero_padding", ps.local["xr"].data_ptr(), allv.data_ptr(), W, me, El, parts, 0,
@@ -888,12 +893,14 @@ class _EPDeviceFn(torch.autograd.Function):
             _mark("exchange_back")
         else:
             push(0, parts, 0, cur)
+            _mark("exchange_push")
             dist.all_reduce(flag, group=group)
             _mark("exchange_out")
             for p in range(parts):
                 experts(p)
             _mark("experts")
             dist.all_reduce(flag, group=group)
+            _mark("exchange_back_flag")
             pull(0, parts, 0, cur)
             _mark("exchange_back")
         out = torch.empty((T, H), dtype=x2.dtype, device=dev)
@@ -927,12 +934,44 @@ class _EPDeviceFn(torch.autograd.Function):
         dgate_row = torch.empty(R, dtype=torch.float32, device=dev)
         _lib.call("ats_moe_combine_bwd", dout.data_ptr(), ys.data_ptr(), dys.data_ptr(), dgate_row.data_ptr(), dt,
                   T, H, E, k, C, L, ws.data_ptr(), wsb, st)
-        _mark("combine_bwd")
-        _lib.call("ats_moe_ep_zero_padding", ps.local["dyr"].data_ptr(), allv.data_ptr(), W, me, El, parts, 0,
-                  parts, part_rows, H, dt, st)
-        _lib.call("ats_moe_ep_push", dys.data_ptr(), None, R,
-                  *_exchange_args(allv, W, me, El, parts, 0, parts, ps.table("dyr"), part_rows, H, dt), st)
-        dist.all_reduce(flag, group=group)
+        dlogits = torch.empty((T, E), dtype=torch.float32, device=dev)
+        daux_t = daux.to(torch.float32).contiguous() if daux is not None else None
+
+        def route_bwd():  # the routing gradient needs only the gate-row gradients
+            _lib.call("ats_moe_route_bwd", logits.data_ptr(), gates.data_ptr(), idx.data_ptr(),
+                      dgate_row.data_ptr(), _lib.ptr(daux_t), dlogits.data_ptr(), T, E, k, C, L, float(lbw),
+                      ws.data_ptr(), wsb, st)
+
+        cur = torch.cuda.current_stream(dev)
+        nsm = torch.cuda.get_device_properties(dev).multi_processor_count
+        dgate_w = None
+        early_router = comm_sms > 0 and rws is not None and _ROUTER_BESIDE_PUSH
+        if early_router:
+            # the output-gradient rows go out on a side stream with comm_sms SMs while the router's weight
+            # gradient, which needs only the routing gradient, runs on the other SMs
+            route_bwd()
+            _mark("combine_bwd")
+            side = state.copy_streams(dev, W)[0]
+            side.wait_stream(cur)
+            with torch.cuda.stream(side):
+                _lib.call("ats_moe_ep_zero_padding", ps.local["dyr"].data_ptr(), allv.data_ptr(), W, me, El, parts,
+                          0, parts, part_rows, H, dt, side.cuda_stream)
+                _lib.call("ats_moe_ep_push", dys.data_ptr(), None, R,
+                          *_exchange_args(allv, W, me, El, parts, 0, parts, ps.table("dyr"), part_rows, H, dt,
+                                          comm_sms), side.cuda_stream)
+                dist.all_reduce(flag, group=group)
+            for t in (dys, allv, flag):
+                t.record_stream(side)
+            with _lib.gemm_sm_limit(max(1, nsm - comm_sms)):
+                dgate_w = router_weight_grad(dlogits, x2, w32, rws)
+            cur.wait_stream(side)
+        else:
+            _mark("combine_bwd")
+            _lib.call("ats_moe_ep_zero_padding", ps.local["dyr"].data_ptr(), allv.data_ptr(), W, me, El, parts, 0,
+                      parts, part_rows, H, dt, st)
+            _lib.call("ats_moe_ep_push", dys.data_ptr(), None, R,
+                      *_exchange_args(allv, W, me, El, parts, 0, parts, ps.table("dyr"), part_rows, H, dt), st)
+            dist.all_reduce(flag, group=group)
         _mark("exchange_out_bwd")
         dwgu = torch.empty_like(wgu_stack)
         dwd = torch.empty_like(wd_stack)
@@ -950,21 +989,12 @@ class _EPDeviceFn(torch.autograd.Function):
                           dxr.data_ptr(), dwgu[p * Ep].data_ptr(), dwd[p * Ep].data_ptr(), dt, W, Ep, C, H, Fdim,
                           seg_ws.data_ptr(), segb, stages, st)
 
-        dlogits = torch.empty((T, E), dtype=torch.float32, device=dev)
-        daux_t = daux.to(torch.float32).contiguous() if daux is not None else None
-
-        def route_bwd():  # the routing gradient needs only the gate-row gradients
-            _lib.call("ats_moe_route_bwd", logits.data_ptr(), gates.data_ptr(), idx.data_ptr(),
-                      dgate_row.data_ptr(), _lib.ptr(daux_t), dlogits.data_ptr(), T, E, k, C, L, float(lbw),
-                      ws.data_ptr(), wsb, st)
-
         dxs = torch.empty((R, H), dtype=x2.dtype, device=dev)
         if comm_sms > 0:
             # data gradient, then the return transfer on a side stream with comm_sms SMs while the weight
             # gradients run on the others
             expert_bwd(1)
             _mark("experts_bwd_data")
-            cur = torch.cuda.current_stream(dev)
             side = state.copy_streams(dev, W)[0]
             side.wait_stream(cur)
             with torch.cuda.stream(side):
@@ -974,10 +1004,10 @@ class _EPDeviceFn(torch.autograd.Function):
                                           comm_sms), side.cuda_stream)
             for t in (dxs, allv, flag):
                 t.record_stream(side)
-            sms = torch.cuda.get_device_properties(dev).multi_processor_count
-            with _lib.gemm_sm_limit(max(1, sms - comm_sms)):
+            with _lib.gemm_sm_limit(max(1, nsm - comm_sms)):
                 expert_bwd(2)
-            route_bwd()
+            if not early_router:
+                route_bwd()
             _mark("experts_bwd_weights")
             cur.wait_stream(side)
             _mark("exchange_back_bwd")
@@ -989,7 +1019,7 @@ class _EPDeviceFn(torch.autograd.Function):
             _lib.call("ats_moe_ep_pull", dxs.data_ptr(), R,
                       *_exchange_args(allv, W, me, El, parts, 0, parts, ps.table("dxr"), part_rows, H, dt), st)
             _mark("exchange_back_bwd")
-        dx, dgate_w = router_backward(dlogits, x2, w32, rws, dxs, ws, wsb, (T, E, k, C, L), True)
+        dx, dgate_w = router_backward(dlogits, x2, w32, rws, dxs, ws, wsb, (T, E, k, C, L), True, dw=dgate_w)
         _mark("router_bwd")
         state.release(ps)
         grads = [dwgu[e] for e in range(El)] + [dwd[e] for e in range(El)]

@@ -236,20 +236,38 @@ class _MoEFn(torch.autograd.Function):
         return (dx, None, dgate_w.to(gate_dtype), None, None, None, None, *grads)
 
 
-def router_backward(dlogits, x2, w32, rws, dxp, ws, ws_bytes, plan, has_router):
+def router_weight_grad(dlogits, x2, w32, rws):
+    """First stage of the tensor-core router backward: the router weight gradient
+    (float32 [E, H]); the split gradient parts stay in ``rws`` for
+    ``router_backward(..., dw=...)``.  It needs no expert result, so an
+    expert-parallel backward runs it while rows are in flight."""
+    T, H = x2.shape
+    E = dlogits.shape[1]
+    dw = torch.empty((E, H), dtype=torch.float32, device=x2.device)
+    _lib.call("ats_moe_router_bwd_staged", dlogits.data_ptr(), x2.data_ptr(), w32.data_ptr(), None, None, 0, 1, 1,
+              _lib.ATS_MOE_PACKED, None, dw.data_ptr(), T, H, E, rws.data_ptr(), rws.numel(), _lib.ATS_ROUTER_BWD_DW,
+              _lib.stream_of(x2))
+    return dw
+
+
+def router_backward(dlogits, x2, w32, rws, dxp, ws, ws_bytes, plan, has_router, dw=None):
     """(dx, dgate_w): the token gradient (the permuted-row gradients summed per
     token, plus the router's share when the router ran inside) and the router
-    weight gradient (float32, None without a router)."""
+    weight gradient (float32, None without a router).  ``dw`` from
+    ``router_weight_grad`` (same ``rws``) skips that stage here."""
     T, E, k, C, L = plan
     H = x2.shape[1]
     st = _lib.stream_of(x2)
     dt = _lib.dtype_code(x2.dtype)
     dx = torch.empty((T, H), dtype=x2.dtype, device=x2.device)
     if has_router and rws is not None:
-        dw = torch.empty((E, H), dtype=torch.float32, device=x2.device)
-        _lib.call("ats_moe_router_bwd", dlogits.data_ptr(), x2.data_ptr(), w32.data_ptr(), dxp.data_ptr(),
+        stages = _lib.ATS_ROUTER_BWD_DX
+        if dw is None:
+            dw = torch.empty((E, H), dtype=torch.float32, device=x2.device)
+            stages = _lib.ATS_ROUTER_BWD_ALL
+        _lib.call("ats_moe_router_bwd_staged", dlogits.data_ptr(), x2.data_ptr(), w32.data_ptr(), dxp.data_ptr(),
                   ws.data_ptr(), ws_bytes, k, C, L, dx.data_ptr(), dw.data_ptr(), T, H, E, rws.data_ptr(),
-                  rws.numel(), st)
+                  rws.numel(), stages, st)
         return dx, dw
     _lib.call("ats_moe_scatter_grad", dxp.data_ptr(), dx.data_ptr(), dt, T, H, E, k, C, L, ws.data_ptr(), ws_bytes,
               st)

@@ -490,6 +490,21 @@ ATS_API int ats_moe_router_bwd(const float* dlogits, const void* x, const float*
                        int layout, void* dx, float* dw, int64_t T, int64_t hidden, int E,
                        void* workspace, size_t workspace_bytes, void* stream);
 
+/* ats_moe_router_bwd in stages, on the same workspace: ATS_ROUTER_BWD_DW splits
+ * w and dlogits into their bf16 parts (kept in the workspace) and computes dw;
+ * ATS_ROUTER_BWD_DX then computes dx from those parts (x, w and dlogits may be
+ * NULL in that call).  The weight gradient needs no expert result, so an
+ * expert-parallel backward runs it while the output-gradient rows are in
+ * flight.  ATS_ROUTER_BWD_ALL (both) is ats_moe_router_bwd.  No reference
+ * counterpart (the reference's router is one nn.Linear). */
+#define ATS_ROUTER_BWD_DW 1
+#define ATS_ROUTER_BWD_DX 2
+#define ATS_ROUTER_BWD_ALL 3
+ATS_API int ats_moe_router_bwd_staged(const float* dlogits, const void* x, const float* w, const void* dxp,
+                       const void* moe_workspace, size_t moe_workspace_bytes, int k, int64_t capacity,
+                       int layout, void* dx, float* dw, int64_t T, int64_t hidden, int E,
+                       void* workspace, size_t workspace_bytes, int stages, void* stream);
+
 /* Device status of the router GEMMs run with this workspace (as ats_moe_status). */
 ATS_API int ats_moe_router_status(const void* workspace, size_t workspace_bytes, int64_t T, int64_t hidden,
                           int E, int* status);
