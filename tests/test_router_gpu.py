@@ -109,6 +109,31 @@ def test_router_backward_token_and_weight_gradients(T, H, E, k, cf):
     assert s.value == 0
 
 
+def test_staged_router_backward_equals_the_one_call():
+    """ats_moe_router_bwd_staged: the weight-gradient stage, then (on the same
+    workspace) the token-gradient stage, give exactly the one-call results --
+    the form the expert-parallel backward uses to overlap the first stage with
+    the output-gradient exchange."""
+    T, H, E, k, cf = 2048, 1024, 64, 2, 1.25
+    x, w, _ = _inputs(T, H, E, 77)
+    logits, rws, w32 = router_forward(x, w, None)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    dl = torch.randn(T, E, device="cuda", generator=g) * 1e-2
+    ws, wsb, C, R = _plan(x, logits, k, cf)
+    dxp = torch.randn(R, H, device="cuda", generator=g).bfloat16()
+    st = _lib.stream_of(x)
+    out = []
+    for stages in ((_lib.ATS_ROUTER_BWD_ALL,), (_lib.ATS_ROUTER_BWD_DW, _lib.ATS_ROUTER_BWD_DX)):
+        dx = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+        dw = torch.empty(E, H, device="cuda")
+        for sg in stages:
+            _lib.call("ats_moe_router_bwd_staged", dl.data_ptr(), x.data_ptr(), w32.data_ptr(), dxp.data_ptr(),
+                      ws.data_ptr(), wsb, k, C, _lib.ATS_MOE_PACKED, dx.data_ptr(), dw.data_ptr(), T, H, E,
+                      rws.data_ptr(), rws.numel(), sg, st)
+        out.append((dx, dw))
+    assert torch.equal(out[0][0], out[1][0]) and torch.equal(out[0][1], out[1][1])
+
+
 def test_router_without_expert_rows_gives_the_router_share_only():
     T, H, E = 512, 256, 16
     x, w, _ = _inputs(T, H, E, 11)
