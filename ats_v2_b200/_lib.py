@@ -119,6 +119,9 @@ SIGNATURES: dict[str, tuple] = {
     "ats_moe_ep_experts_bwd_staged": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                               c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int64, c_int64,
                                               c_int64, c_void_p, c_size_t, c_int, c_void_p]),
+    "ats_moe_ep_combine": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int, c_int64, c_void_p, c_size_t,
+                                   c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int64, c_int64, c_int,
+                                   c_void_p]),
     "ats_moe_ep_zero_padding": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int64,
                                         c_int64, c_int, c_void_p]),
     "ats_swiglu_supported": (c_int, [c_int, c_int64, c_int64, c_int64]),

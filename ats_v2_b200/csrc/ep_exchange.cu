@@ -169,6 +169,65 @@ __global__ void __launch_bounds__(kXThreads) ep_move_kernel(XArgs a, const uint4
   __threadfence_system();
 }
 
+// The pull fused with the combine: token t's output is the sum, in ascending row (= expert) order, of its
+// kept rows' expert outputs times their gates, loaded straight from the expert ranks' buffers; every product
+// and partial sum is rounded as ats_moe_combine rounds them, so the result is the pull followed by the
+// combine, bit for bit.  Each kept row is also stored into the local packed layout `ys`, which the backward's
+// combine reads.  A warp per token; the rows of a token are at most kMaxTopK.
+template <typename T>
+__global__ void __launch_bounds__(kXThreads) ep_combine_kernel(XArgs a, MoePlan plan, T* __restrict__ ys,
+                                                               int64_t ys_rows, T* __restrict__ out) {
+  __shared__ XShared sh;
+  load_shared(a, sh);
+  if (!sh.ok) return;
+  constexpr int N = Chunk<T>::N;
+  const int parts = a.El / a.Ep;
+  const int lane = threadIdx.x & 31;
+  const int64_t H = (int64_t)a.vec * N;
+  for (int64_t t = (int64_t)blockIdx.x * kXWarps + (threadIdx.x >> 5); t < plan.T;
+       t += (int64_t)gridDim.x * kXWarps) {
+    int rows[kMaxTopK];
+    const int n = token_rows(plan, t, rows);
+    const uint4* src[kMaxTopK];
+    float g[kMaxTopK];
+    bool ok = true;
+    for (int i = 0; i < n; ++i) {
+      const int r = rows[i];
+      const int e = seg_of(sh, a.E, r);
+      const int d = e / a.El, p = (e - d * a.El) / a.Ep;
+      const int64_t prow = (int64_t)sh.base[d * parts + p] + (r - sh.seg[d * a.El + p * a.Ep]);
+      if (r - sh.seg[e] >= sh.kept[e] || prow < 0 || prow >= a.part_rows || r >= ys_rows) {
+        ok = false;
+        break;
+      }
+      src[i] = reinterpret_cast<const uint4*>(a.peer[d]) + ((int64_t)p * a.part_rows + prow) * a.vec;
+      g[i] = plan.row_gate[r];
+    }
+    if (!ok) {  // a row outside its buffer: the token is left alone
+      if (lane == 0) flag(6);
+      continue;
+    }
+    for (int c = lane; c < a.vec; c += 32) {
+      uint4 w[2];  // the first two rows' chunks load together
+#pragma unroll
+      for (int i = 0; i < 2; ++i)
+        if (i < n) w[i] = src[i][c];
+      float acc[N];
+#pragma unroll
+      for (int q = 0; q < N; ++q) acc[q] = 0.f;
+      for (int i = 0; i < n; ++i) {
+        const uint4 raw = i < 2 ? w[i] : src[i][c];
+        reinterpret_cast<uint4*>(ys + (int64_t)rows[i] * H)[c] = raw;
+        const T* v = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+        for (int q = 0; q < N; ++q)
+          acc[q] = round_to<T>(__fadd_rn(acc[q], round_to<T>(__fmul_rn(Cvt<T>::to_f(v[q]), g[i]))));
+      }
+      store_chunk<T>(out + t * H + (int64_t)c * N, acc);
+    }
+  }
+}
+
 // The receiving rank zeroes the padding rows of parts [part_lo, part_hi) of
 // its expert-side buffer: one block per (part, source, local expert) segment.
 __global__ void __launch_bounds__(kXThreads) ep_zero_kernel(XArgs a, uint4* __restrict__ buf) {
@@ -276,6 +335,29 @@ int ats_moe_ep_pull(void* dst, int64_t dst_rows, const int32_t* counts, int W, i
   ep_move_kernel<<<move_grid(dst_rows, sms), kXThreads, 0, (cudaStream_t)stream>>>(a, nullptr, nullptr, 0,
                                                                               static_cast<uint4*>(dst), dst_rows, 0);
   return check_launch("moe_ep_pull");
+}
+
+int ats_moe_ep_combine(void* ys, int64_t ys_rows, void* out, int64_t T, int k, int64_t capacity,
+                       const void* moe_workspace, size_t moe_workspace_bytes, const int32_t* counts, int W, int me,
+                       int E_local, int parts, const uint64_t* peer_bufs, int64_t part_rows, int64_t hidden,
+                       ats_dtype dtype, void* stream) {
+  XArgs a;
+  ATS_TRY(check_args(counts, W, me, E_local, parts, 0, parts, peer_bufs, part_rows, hidden, dtype, &a));
+  MoePlan plan;
+  ATS_TRY(moe_plan_from_ws(moe_workspace, moe_workspace_bytes, T, W * E_local, k, capacity, ATS_MOE_PACKED, &plan));
+  if (T == 0) return ATS_OK;
+  if (ys == nullptr || out == nullptr || ys_rows < 0 || !aligned16(ys) || !aligned16(out))
+    return fail(ATS_EBADARG, "moe_ep_combine: bad output buffers");
+  const int64_t want = (T + kXWarps - 1) / kXWarps, cap = (int64_t)num_sms() * 8;
+  const unsigned grid = (unsigned)(want < cap ? want : cap);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (dtype == ATS_BF16)
+    ep_combine_kernel<bf16><<<grid, kXThreads, 0, st>>>(a, plan, static_cast<bf16*>(ys), ys_rows,
+                                                        static_cast<bf16*>(out));
+  else
+    ep_combine_kernel<float><<<grid, kXThreads, 0, st>>>(a, plan, static_cast<float*>(ys), ys_rows,
+                                                         static_cast<float*>(out));
+  return check_launch("moe_ep_combine");
 }
 
 int ats_moe_ep_zero_padding(void* buf, const int32_t* counts, int W, int me, int E_local, int parts, int part_lo,

@@ -155,13 +155,14 @@ __device__ __forceinline__ void decode_tile(const GemmArgs& p, TileCursor& cur, 
 }
 
 // Ring of a launch: one A tile (128 x 64) and BPARTS B tiles per stage; a CTA of a pair holds half of the
-// B rows.  Single CTAs keep STAGES stages; pairs fill the same bytes with more (smaller) stages.
+// B rows.  Every launch fills the same 192 KB with as many stages as fit (4 for 128 x 256 tiles, 6 for
+// 128 x 128 tiles or pair halves): the GEMMs wait on load latency, and more bytes in flight hide more of it.
 constexpr int kRingBytes = STAGES * (BM * BK * 2 + 256 * BK * 2);
 __host__ __device__ constexpr int stage_bytes(int bn, int bparts, bool pair) {
   return BM * BK * 2 + bparts * (pair ? bn / 2 : bn) * BK * 2;
 }
 __host__ __device__ constexpr int ring_stages(int bn, int bparts, bool pair) {
-  return pair ? kRingBytes / stage_bytes(bn, bparts, pair) : STAGES;
+  return kRingBytes / stage_bytes(bn, bparts, pair);
 }
 
 // Shared memory of the epilogue's staging boxes: the bf16-output epilogues write through them.
@@ -398,21 +399,17 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
             if constexpr (PAIR) {  // this CTA's B_ROWS rows: the gate or up half (SwiGLU), or the cta-th half
               const int brow = b_row0 + n0 + (p.b.sub_offset ? (cta ? p.b.sub_offset : 0) : (int)cta * B_ROWS);
               load(sb, &tmB, kq * BK, brow);
+            } else if constexpr (BPARTS > 1) {  // the parts are consecutive rows: one box holds them all
+              load(sb, &tmB, b_ko + kq * BK, b_row0 + n0 + b_no);
             } else {
-#pragma unroll
-              for (int j = 0; j < BPARTS; ++j) {
-                const int brow = b_row0 + n0 + b_no + (BPARTS > 1 ? p.b_noff[j] : 0);
-                tc::tma_load_2d(sb + j * B_BYTES, &tmB, b_ko + kq * BK, brow, &full_bar[stage]);
-                if (BPARTS == 1 && p.b.sub_offset)
-                  tc::tma_load_2d(sb + (BN / 2) * 128, &tmB, b_ko + kq * BK, brow + p.b.sub_offset,
-                                  &full_bar[stage]);
-              }
+              const int brow = b_row0 + n0 + b_no;
+              load(sb, &tmB, b_ko + kq * BK, brow);
+              if (p.b.sub_offset) load(sb + (BN / 2) * 128, &tmB, b_ko + kq * BK, brow + p.b.sub_offset);
             }
           } else {
             const int krow = (KGROUP ? seg_r0 + lkb * BK : b_row0 + kq * BK) + b_ko;
             const int ncol = n0 + (int)cta * B_ROWS + b_no;
-#pragma unroll
-            for (int j = 0; j < BPARTS; ++j) load_mn(sb + j * B_BYTES, &tmB, ncol + (BPARTS > 1 ? p.b_noff[j] : 0), krow);
+            load_mn(sb, &tmB, ncol, krow);  // B_ROWS / 64 blocks per part, the parts consecutive: one load
           }
           if (part == SPLIT - 1) ++lkb;
           ++issued_k;
@@ -1201,14 +1198,14 @@ int tc_router_logits(const void* x, const void* wparts, const float* bias, float
   p.N = Ep;
   p.K = (int)H;
   p.b = OpSpec{0, 0};
-  set_parts(p.b_noff, {0, Ep, 2 * Ep});  // the three weight parts, one stage each k block
+  set_parts(p.b_noff, {0, Ep, 2 * Ep});  // the three weight parts, consecutive rows: one box per k block
   p.out_f32 = logits;
   p.ldo = E;
   p.bias = bias;
   p.m_valid = (int)T;
   p.n_valid = E;
   ATS_TRY(make_map(&ma, x, H, T, H * 2, 128));
-  ATS_TRY(make_map(&mb, wparts, H, (uint64_t)3 * Ep, H * 2, Ep));
+  ATS_TRY(make_map(&mb, wparts, H, (uint64_t)3 * Ep, H * 2, 3 * Ep));
   return launch_tc<kRouterEp, false, false, EPI_F32, false, 1, 3>(ma, mb, p, (T + BM - 1) / BM, st);
 }
 
@@ -1252,14 +1249,14 @@ int tc_router_dw(const void* x, const void* dlparts, float* partial, int64_t T, 
   p.N = Ep;
   p.K = 0;
   p.b = OpSpec{0, 0};
-  set_parts(p.b_noff, {0, Ep, 2 * Ep});  // the three gradient parts, one stage each k block
+  set_parts(p.b_noff, {0, Ep, 2 * Ep});  // the three gradient parts, consecutive columns: one load per k block
   p.out_f32 = partial;
   p.ldo = Ep;
   p.out_group = H * Ep;
   p.m_valid = (int)H;
   p.n_valid = Ep;
   ATS_TRY(make_map_mn(&ma, x, H, T, H * 2, 2));
-  ATS_TRY(make_map_mn(&mb, dlparts, (uint64_t)3 * Ep, T, (uint64_t)3 * Ep * 2, 1));
+  ATS_TRY(make_map_mn(&mb, dlparts, (uint64_t)3 * Ep, T, (uint64_t)3 * Ep * 2, 3));
   return launch_tc<kRouterEp, true, true, EPI_F32, true, 1, 3>(ma, mb, p, (int64_t)chunks.E * (H / BM), st);
 }
 

@@ -57,6 +57,22 @@ struct MoePlan {
 
 __host__ __device__ inline int64_t slot_rows(int64_t C) { return (C + kSegAlign - 1) / kSegAlign * kSegAlign; }
 
+// The kept permuted rows of token t, ascending (= ascending expert): the order the combine sums them in.
+__device__ __forceinline__ int token_rows(const MoePlan& plan, int64_t t, int (&rows)[kMaxTopK]) {
+  int n = 0;
+  for (int s = 0; s < plan.k; ++s) {
+    const int r = plan.tok_row[t * plan.k + s];
+    if (r < 0) continue;
+    int p = n++;
+    while (p > 0 && rows[p - 1] > r) {
+      rows[p] = rows[p - 1];
+      --p;
+    }
+    rows[p] = r;
+  }
+  return n;
+}
+
 inline int64_t moe_cap_rows(int64_t T, int E, int k, int64_t C, int layout) {
   if (layout == ATS_MOE_SLOTS) return (int64_t)E * slot_rows(C);
   const int64_t per = C < T ? C : T;

@@ -277,20 +277,6 @@ __global__ void __launch_bounds__(kRouteTokensPerBlock) permute_kernel(const int
 
 // Kept rows of a token in ascending expert order.  Segments are laid out in
 // expert order, so ascending row index is ascending expert index.
-__device__ __forceinline__ int token_rows(const MoePlan& plan, int64_t t, int (&rows)[kMaxTopK]) {
-  int n = 0;
-  for (int s = 0; s < plan.k; ++s) {
-    const int r = plan.tok_row[t * plan.k + s];
-    if (r < 0) continue;
-    int p = n++;
-    while (p > 0 && rows[p - 1] > r) {
-      rows[p] = rows[p - 1];
-      --p;
-    }
-    rows[p] = r;
-  }
-  return n;
-}
 
 // Rows the grouped GEMMs read: every row of the packed layout; in the slot
 // layout only the first align128(kept) rows of each expert's slot (the rest

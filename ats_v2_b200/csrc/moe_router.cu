@@ -33,12 +33,25 @@ struct RouterWs {
 
 int router_ep(int) { return kRouterEp; }
 
-int router_chunks(int64_t T, int64_t H) {
+// Token chunks of the router weight gradient: the chunk count whose tiles (H/128 per chunk) fill `ctas` CTAs
+// in the fewest, least ragged waves -- cost = waves x (K blocks of a chunk + 4, the fixed cost of a tile in K
+// blocks); ties go to fewer chunks (fewer partial sums).  At 32768 tokens, hidden 4096 and 148 SMs: 9 chunks
+// (288 tiles, 2 waves of 57 K blocks) where one chunk per 32 SMs gave 5 (160 tiles: 12 SMs ran a second
+// 103-block tile while the others idled).
+int router_chunks(int64_t T, int64_t H, int ctas) {
   const int64_t tiles = H / 128;
-  int64_t ks = (num_sms() + tiles - 1) / tiles;
-  const int64_t maxk = (T + 63) / 64;
-  if (ks > maxk) ks = maxk;
-  return (int)(ks < 1 ? 1 : ks > kMaxChunks ? kMaxChunks : ks);
+  const int64_t kb = (T + 63) / 64;
+  const int64_t maxk = kb < kMaxChunks ? kb : kMaxChunks;
+  int64_t best = 1, best_cost = -1;
+  for (int64_t ks = 1; ks <= maxk; ++ks) {
+    const int64_t waves = (ks * tiles + ctas - 1) / ctas;
+    const int64_t cost = waves * ((kb + ks - 1) / ks + 4);
+    if (best_cost < 0 || cost < best_cost) {
+      best = ks;
+      best_cost = cost;
+    }
+  }
+  return (int)best;
 }
 
 bool router_supported(ats_dtype dt, int64_t T, int64_t H, int E) {
@@ -49,7 +62,9 @@ bool router_supported(ats_dtype dt, int64_t T, int64_t H, int E) {
 size_t router_carve(void* ws, int64_t T, int64_t H, int E, RouterWs* o) {
   RouterWs q;
   q.Ep = router_ep(E);
-  q.KS = router_chunks(T, H);
+  // the device's SM count, not a caller's SM limit: the chunks fix the summation order of the weight gradient,
+  // which must not depend on what runs beside it
+  q.KS = router_chunks(T, H, num_sms());
   const int64_t tk = (T + 63) / 64 * 64;
   q.chunk = ((tk + q.KS - 1) / q.KS + 63) / 64 * 64;
   size_t off = 0;

@@ -765,6 +765,9 @@ class _EPPeerFn(torch.autograd.Function):
 # The device exchange's backward runs the router weight gradient beside the output-gradient push (needs
 # comm_sms > 0 and the tensor-core router).
 _ROUTER_BESIDE_PUSH = True
+# The device exchange's forward combines straight from the expert ranks' buffers (ats_moe_ep_combine)
+# instead of pulling the rows, then combining them.
+_FUSED_COMBINE = True
 
 _DEVICE_SET = ("xr", "yr", "dyr", "dxr")  # every buffer of a device-exchange set is expert-side
 
@@ -901,11 +904,23 @@ class _EPDeviceFn(torch.autograd.Function):
             _mark("experts")
             dist.all_reduce(flag, group=group)
             _mark("exchange_back_flag")
+        out = torch.empty((T, H), dtype=x2.dtype, device=dev)
+        if parts > 1 and comm_sms > 0:  # the parts' results were pulled on the side stream
+            _lib.call("ats_moe_combine", ys.data_ptr(), out.data_ptr(), dt, T, H, E, k, C, L, ws.data_ptr(), wsb,
+                      st)
+            _mark("combine")
+        elif _FUSED_COMBINE:
+            # the combine reads the expert outputs straight from the expert ranks' buffers (and keeps the
+            # packed copy the backward needs): the pull and the combine in one pass
+            _lib.call("ats_moe_ep_combine", ys.data_ptr(), R, out.data_ptr(), T, k, C, ws.data_ptr(), wsb,
+                      allv.data_ptr(), W, me, El, parts, ps.table("yr").data_ptr(), part_rows, H, dt, st)
+            _mark("exchange_back_combine")
+        else:
             pull(0, parts, 0, cur)
             _mark("exchange_back")
-        out = torch.empty((T, H), dtype=x2.dtype, device=dev)
-        _lib.call("ats_moe_combine", ys.data_ptr(), out.data_ptr(), dt, T, H, E, k, C, L, ws.data_ptr(), wsb, st)
-        _mark("combine")
+            _lib.call("ats_moe_combine", ys.data_ptr(), out.data_ptr(), dt, T, H, E, k, C, L, ws.data_ptr(), wsb,
+                      st)
+            _mark("combine")
         ctx.save_for_backward(logits, gates, idx, ws, ys, allv, wgu_stack, wd_stack, x2, w32, rws, *keep)
         ctx.meta = (E, El, k, C, lbw, Fdim, W, group, T, H, wsb, R, segb, gate_w.dtype, parts, part_rows, me,
                     comm_sms)

@@ -375,6 +375,20 @@ ATS_API int ats_moe_ep_pull(void* dst, int64_t dst_rows, const int32_t* counts, 
                             ats_dtype dtype, int sms, void* stream);
 /* `sms` > 0 sizes a push or pull for that many SMs (it runs beside a GEMM held to the others with
  * ats_set_gemm_sm_limit); 0 sizes it for the whole GPU. */
+/* The pull fused with the combine (ats_moe_ep_pull of every part, then
+ * ats_moe_combine, bit for bit, in one pass): out[T,hidden] = for each token
+ * the gate-weighted sum, ascending expert, of its kept rows' expert outputs,
+ * read straight from the expert ranks' buffers (peer_bufs: their mapped
+ * addresses, as for ats_moe_ep_pull); each kept row is also stored into the
+ * local packed layout ys[ys_rows, hidden] for the backward's
+ * ats_moe_combine_bwd.  moe_workspace holds this rank's routing plan (T, k,
+ * capacity, W*E_local experts, ATS_MOE_PACKED).  Ordered after the expert
+ * GEMMs by the caller's collective, like a pull.  Replaces the reference's
+ * index_add_ unpermute (ats/model/moe.py:119-122) across ranks. */
+ATS_API int ats_moe_ep_combine(void* ys, int64_t ys_rows, void* out, int64_t T, int k, int64_t capacity,
+                               const void* moe_workspace, size_t moe_workspace_bytes, const int32_t* counts,
+                               int W, int me, int E_local, int parts, const uint64_t* peer_bufs, int64_t part_rows,
+                               int64_t hidden, ats_dtype dtype, void* stream);
 ATS_API int ats_moe_ep_zero_padding(void* buf, const int32_t* counts, int W, int me, int E_local,
                                     int parts, int part_lo, int part_hi, int64_t part_rows,
                                     int64_t hidden, ats_dtype dtype, void* stream);

@@ -135,3 +135,53 @@ def test_unequal_capacities_are_refused_on_the_device():
     code = ctypes.c_int(0)
     assert _lib.query("ats_device_status", ctypes.byref(code)) == _lib.ATS_EBADARG and code.value == 1
     assert _lib.query("ats_device_status", ctypes.byref(code)) == 0
+
+
+@pytest.mark.parametrize("W,El,parts,T,H,k,cf", [(2, 4, 1, 700, 256, 2, 1.25), (4, 2, 2, 500, 128, 2, 1.0),
+                                                 (3, 2, 1, 300, 512, 3, 2.0)])
+def test_fused_combine_equals_pull_then_combine(W, El, parts, T, H, k, cf):
+    """``ats_moe_ep_combine`` (the combine reading the expert outputs straight from
+    the expert ranks' buffers) against ``ats_moe_ep_pull`` followed by
+    ``ats_moe_combine``: the same output bit for bit, and the same packed copy of
+    every kept row.  W ranks emulated by W routing plans and W expert-side
+    buffers of random expert outputs on one GPU."""
+    from ats_v2_b200.ep import _route, _row_tokens
+    from ats_v2_b200.moe import capacity_for
+
+    E = W * El
+    Ep = El // parts
+    L = _lib.ATS_MOE_PACKED
+    C = capacity_for(T, k, E, cf)
+    Cp = (C + 127) // 128 * 128
+    part_rows = W * Ep * Cp
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(W * 10 + El)
+    st = torch.cuda.current_stream().cuda_stream
+    ranks = []
+    for s in range(W):
+        x = torch.randn(T, H, device=dev, generator=g).bfloat16()
+        gate_w = 0.05 * torch.randn(E, H, device=dev, generator=g)
+        (_, _, _, ws, wsb, R, _, _, _, _, _, kept, seg_start) = _route(x, gate_w, None, E, k, C, L, 0.01)
+        mine = torch.cat([kept, torch.tensor([Cp, R], dtype=torch.int32, device=dev), seg_start])
+        ranks.append((ws, wsb, R, mine, _row_tokens(ws, wsb, T, E, k, C, L, R, dev)))
+    allv = torch.stack([r[3] for r in ranks]).contiguous()
+    yr = [torch.randn(parts * part_rows, H, device=dev, generator=g).bfloat16() for _ in range(W)]
+    table = torch.tensor([b.data_ptr() for b in yr], dtype=torch.int64, device=dev)
+    for me, (ws, wsb, R, _, row_token) in enumerate(ranks):
+        ys1 = torch.zeros(R, H, device=dev).bfloat16()
+        _lib.call("ats_moe_ep_pull", ys1.data_ptr(), R, allv.data_ptr(), W, me, El, parts, 0, parts,
+                  table.data_ptr(), part_rows, H, _lib.ATS_BF16, 0, st)
+        out1 = torch.empty(T, H, device=dev).bfloat16()
+        _lib.call("ats_moe_combine", ys1.data_ptr(), out1.data_ptr(), _lib.ATS_BF16, T, H, E, k, C, L,
+                  ws.data_ptr(), wsb, st)
+        ys2 = torch.zeros(R, H, device=dev).bfloat16()
+        out2 = torch.empty(T, H, device=dev).bfloat16()
+        _lib.call("ats_moe_ep_combine", ys2.data_ptr(), R, out2.data_ptr(), T, k, C, ws.data_ptr(), wsb,
+                  allv.data_ptr(), W, me, El, parts, table.data_ptr(), part_rows, H, _lib.ATS_BF16, st)
+        torch.cuda.synchronize()
+        assert torch.equal(out1, out2), f"rank {me}: fused combine differs"
+        kept_rows = row_token >= 0
+        assert int(kept_rows.sum()) > 0
+        assert torch.equal(ys1[kept_rows], ys2[kept_rows]), f"rank {me}: packed copy differs"
+    code = ctypes.c_int(0)
+    assert _lib.query("ats_device_status", ctypes.byref(code)) == _lib.ATS_OK and code.value == 0
