@@ -207,23 +207,31 @@ __global__ void __launch_bounds__(kXThreads) ep_combine_kernel(XArgs a, MoePlan 
       if (lane == 0) flag(6);
       continue;
     }
-    for (int c = lane; c < a.vec; c += 32) {
-      uint4 w[2];  // the first two rows' chunks load together
+    // kUnroll chunks of the first two rows in flight per lane (remote loads are latency-bound), then the sums
+    for (int c0 = lane; c0 < a.vec; c0 += 32 * kUnroll) {
+      uint4 w[2][kUnroll];
 #pragma unroll
       for (int i = 0; i < 2; ++i)
-        if (i < n) w[i] = src[i][c];
-      float acc[N];
 #pragma unroll
-      for (int q = 0; q < N; ++q) acc[q] = 0.f;
-      for (int i = 0; i < n; ++i) {
-        const uint4 raw = i < 2 ? w[i] : src[i][c];
-        reinterpret_cast<uint4*>(ys + (int64_t)rows[i] * H)[c] = raw;
-        const T* v = reinterpret_cast<const T*>(&raw);
+        for (int u = 0; u < kUnroll; ++u)
+          if (i < n && c0 + 32 * u < a.vec) w[i][u] = src[i][c0 + 32 * u];
 #pragma unroll
-        for (int q = 0; q < N; ++q)
-          acc[q] = round_to<T>(__fadd_rn(acc[q], round_to<T>(__fmul_rn(Cvt<T>::to_f(v[q]), g[i]))));
+      for (int u = 0; u < kUnroll; ++u) {
+        const int c = c0 + 32 * u;
+        if (c >= a.vec) break;
+        float acc[N];
+#pragma unroll
+        for (int q = 0; q < N; ++q) acc[q] = 0.f;
+        for (int i = 0; i < n; ++i) {
+          const uint4 raw = i == 0 ? w[0][u] : (i == 1 ? w[1][u] : src[i][c]);
+          reinterpret_cast<uint4*>(ys + (int64_t)rows[i] * H)[c] = raw;
+          const T* v = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+          for (int q = 0; q < N; ++q)
+            acc[q] = round_to<T>(__fadd_rn(acc[q], round_to<T>(__fmul_rn(Cvt<T>::to_f(v[q]), g[i]))));
+        }
+        store_chunk<T>(out + t * H + (int64_t)c * N, acc);
       }
-      store_chunk<T>(out + t * H + (int64_t)c * N, acc);
     }
   }
 }
