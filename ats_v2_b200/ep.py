@@ -767,7 +767,7 @@ class _EPPeerFn(torch.autograd.Function):
 _ROUTER_BESIDE_PUSH = True
 # The device exchange's forward combines straight from the expert ranks' buffers (ats_moe_ep_combine)
 # instead of pulling the rows, then combining them.
-_FUSED_COMBINE = False
+_FUSED_COMBINE = True
 
 _DEVICE_SET = ("xr", "yr", "dyr", "dxr")  # every buffer of a device-exchange set is expert-side
 
