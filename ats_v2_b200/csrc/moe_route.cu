@@ -321,18 +321,40 @@ __global__ void __launch_bounds__(256) combine_kernel(const T* __restrict__ y, T
   float g[kMaxTopK];
   for (int i = 0; i < n; ++i) g[i] = plan.row_gate[rows[i]];
   if (vec) {
-    constexpr int N = Chunk<T>::N;
-    for (int64_t c = lane; c < H / N; c += 32) {
-      float acc[N];
+    // four chunks of the first two rows in flight per lane (the loads are latency-bound), then the sums in the
+    // same order as one chunk at a time
+    constexpr int N = Chunk<T>::N, U = 4;
+    const int64_t nc = H / N;
+    for (int64_t c0 = lane; c0 < nc; c0 += 32 * U) {
+      uint4 w[2][U];
 #pragma unroll
-      for (int e = 0; e < N; ++e) acc[e] = 0.f;
-      for (int i = 0; i < n; ++i) {
-        float v[N];
-        load_chunk<T>(y + (int64_t)rows[i] * H + c * N, v);
+      for (int i = 0; i < 2; ++i)
 #pragma unroll
-        for (int e = 0; e < N; ++e) acc[e] = round_to<T>(__fadd_rn(acc[e], round_to<T>(__fmul_rn(v[e], g[i]))));
+        for (int u = 0; u < U; ++u)
+          if (i < n && c0 + 32 * u < nc)
+            w[i][u] = *reinterpret_cast<const uint4*>(y + (int64_t)rows[i] * H + (c0 + 32 * u) * N);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int64_t c = c0 + 32 * u;
+        if (c >= nc) break;
+        float acc[N];
+#pragma unroll
+        for (int e = 0; e < N; ++e) acc[e] = 0.f;
+        for (int i = 0; i < n; ++i) {
+          uint4 raw;
+          if (i == 0)
+            raw = w[0][u];
+          else if (i == 1)
+            raw = w[1][u];
+          else
+            raw = *reinterpret_cast<const uint4*>(y + (int64_t)rows[i] * H + c * N);
+          const T* v = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+          for (int e = 0; e < N; ++e)
+            acc[e] = round_to<T>(__fadd_rn(acc[e], round_to<T>(__fmul_rn(Cvt<T>::to_f(v[e]), g[i]))));
+        }
+        store_chunk<T>(out + t * H + c * N, acc);
       }
-      store_chunk<T>(out + t * H + c * N, acc);
     }
   } else {
     for (int64_t h = lane; h < H; h += 32) {
