@@ -107,6 +107,9 @@ SIGNATURES: dict[str, tuple] = {
     "ats_moe_ep_segments": (c_int, [c_void_p, c_int, c_int, c_int64, c_int, c_void_p, c_size_t, c_void_p]),
     "ats_moe_ep_experts_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
                                        c_int, c_int64, c_int64, c_int64, c_void_p, c_size_t, c_void_p]),
+    "ats_moe_ep_experts_fwd_sources": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
+                                               c_int, c_int, c_int64, c_int64, c_int64, c_void_p, c_size_t, c_int,
+                                               c_int, c_void_p]),
     "ats_moe_ep_experts_bwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                        c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int64, c_int64,
                                        c_int64, c_void_p, c_size_t, c_void_p]),
@@ -114,6 +117,8 @@ SIGNATURES: dict[str, tuple] = {
     "ats_moe_ep_counts_ints": (c_size_t, [c_int]),
     "ats_moe_ep_push": (c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int,
                                 c_void_p, c_int64, c_int64, c_int, c_int, c_void_p]),
+    "ats_moe_ep_push_split": (c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_int, c_int, c_int, c_int, c_int,
+                                      c_int, c_void_p, c_int64, c_int64, c_int, c_int, c_int, c_void_p]),
     "ats_moe_ep_pull": (c_int, [c_void_p, c_int64, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p,
                                 c_int64, c_int64, c_int, c_int, c_void_p]),
     "ats_moe_ep_experts_bwd_staged": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

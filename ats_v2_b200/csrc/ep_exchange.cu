@@ -53,6 +53,7 @@ struct XArgs {
   const uint64_t* peer;  // [W] part-0 addresses of each rank's expert-side buffer
   int64_t part_rows;     // rows of one part of an expert-side buffer
   int vec;               // 16-byte chunks per row
+  int dest_self;         // push: -1 every row; 1 only the rows whose expert rank is this rank; 0 only the others
 };
 
 __device__ __forceinline__ int cnt_kept(const XArgs& a, int s, int e) { return a.counts[s * (2 * a.E + 3) + e]; }
@@ -144,6 +145,7 @@ __global__ void __launch_bounds__(kXThreads) ep_move_kernel(XArgs a, const uint4
     if (r - sh.seg[e] >= sh.kept[e]) continue;  // padding row: the receiver zeroes its own
     const int d = e / a.El, p = (e - d * a.El) / a.Ep;
     if (p < a.part_lo || p >= a.part_hi) continue;
+    if (a.dest_self >= 0 && (d == a.me) != (a.dest_self == 1)) continue;
     const int64_t prow = (int64_t)sh.base[d * parts + p] + (r - sh.seg[d * a.El + p * a.Ep]);
     if (prow < 0 || prow >= a.part_rows) {
       if (lane == 0) flag(2);
@@ -291,6 +293,7 @@ int check_args(const int32_t* counts, int W, int me, int E_local, int parts, int
   a->peer = peer;
   a->part_rows = part_rows;
   a->vec = (int)(row_bytes / 16);
+  a->dest_self = -1;
   return ATS_OK;
 }
 
@@ -331,6 +334,19 @@ int ats_moe_ep_push(const void* src, const int32_t* row_token, int64_t src_rows,
   ep_move_kernel<<<move_grid((int64_t)W * part_rows * parts, sms), kXThreads, 0, (cudaStream_t)stream>>>(
       a, static_cast<const uint4*>(src), row_token, src_rows, nullptr, 0, 1);
   return check_launch("moe_ep_push");
+}
+
+int ats_moe_ep_push_split(const void* src, const int32_t* row_token, int64_t src_rows, const int32_t* counts, int W,
+                          int me, int E_local, int parts, int part_lo, int part_hi, const uint64_t* peer_bufs,
+                          int64_t part_rows, int64_t hidden, ats_dtype dtype, int to_self, int sms, void* stream) {
+  XArgs a;
+  ATS_TRY(check_args(counts, W, me, E_local, parts, part_lo, part_hi, peer_bufs, part_rows, hidden, dtype, &a));
+  if (src == nullptr || src_rows < 0) return fail(ATS_EBADARG, "moe_ep_push_split: null source");
+  if (!aligned16(src)) return fail(ATS_EBADARG, "moe_ep_push_split: source not 16-byte aligned");
+  a.dest_self = to_self ? 1 : 0;
+  ep_move_kernel<<<move_grid((int64_t)W * part_rows * parts, sms), kXThreads, 0, (cudaStream_t)stream>>>(
+      a, static_cast<const uint4*>(src), row_token, src_rows, nullptr, 0, 1);
+  return check_launch("moe_ep_push_split");
 }
 
 int ats_moe_ep_pull(void* dst, int64_t dst_rows, const int32_t* counts, int W, int me, int E_local, int parts,

@@ -493,6 +493,26 @@ int ats_moe_ep_segments(const int32_t* recv_kept, int W, int E_local, int64_t ca
   return check_launch("moe_ep_segments");
 }
 
+int ats_moe_ep_experts_fwd_sources(const void* xr, const void* w_gate_up, const void* w_down, void* h, void* a,
+                                   void* y, ats_dtype dtype, int W, int E_local, int64_t capacity, int64_t H,
+                                   int64_t F, const void* seg_workspace, size_t seg_workspace_bytes, int src_lo,
+                                   int src_hi, void* stream) {
+  SegTable sg;
+  ATS_TRY(ep_table(seg_workspace, seg_workspace_bytes, W, E_local, capacity, &sg));
+  ATS_TRY(check_experts(w_gate_up, w_down, H, F, dtype));
+  if (xr == nullptr || h == nullptr || a == nullptr || y == nullptr)
+    return fail(ATS_EBADARG, "moe_ep_experts_fwd_sources: null");
+  if (src_lo < 0 || src_hi > W || src_lo > src_hi)
+    return fail(ATS_EBADARG, "moe_ep_experts_fwd_sources: sources [%d, %d) of %d", src_lo, src_hi, W);
+  if (src_lo == src_hi) return ATS_OK;
+  // segments are source-major (segment = source * E_local + expert): the sources' segments are one range
+  sg.row0 += src_lo * E_local;
+  sg.rows += src_lo * E_local;
+  sg.expert += src_lo * E_local;
+  sg.nseg = (src_hi - src_lo) * E_local;
+  return experts_fwd(xr, w_gate_up, w_down, h, a, y, dtype, E_local, H, F, sg, (cudaStream_t)stream);
+}
+
 int ats_moe_ep_experts_fwd(const void* xr, const void* w_gate_up, const void* w_down, void* h, void* a, void* y,
                            ats_dtype dtype, int W, int E_local, int64_t capacity, int64_t H, int64_t F,
                            const void* seg_workspace, size_t seg_workspace_bytes, void* stream) {

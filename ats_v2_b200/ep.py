@@ -768,6 +768,9 @@ _ROUTER_BESIDE_PUSH = True
 # The device exchange's forward combines straight from the expert ranks' buffers (ats_moe_ep_combine)
 # instead of pulling the rows, then combining them.
 _FUSED_COMBINE = True
+# The device exchange's forward computes a rank's own rows beside the transfer of the others' (one part,
+# comm_sms > 0).  Off: measured slower (the GEMMs beside the transfer run 1.8x longer than alone).
+_OWN_ROWS_FIRST = False
 
 _DEVICE_SET = ("xr", "yr", "dyr", "dxr")  # every buffer of a device-exchange set is expert-side
 
@@ -852,7 +855,7 @@ class _EPDeviceFn(torch.autograd.Function):
                       *_exchange_args(allv, W, me, El, parts, lo, hi, ps.table("yr"), part_rows, H, dt, sms),
                       stream.cuda_stream)
 
-        def experts(p):
+        def experts_prep(p):
             seg_ws = torch.empty(segb, dtype=torch.uint8, device=dev)
             rk = allv[:, me * El + p * Ep:me * El + (p + 1) * Ep].contiguous()
             _lib.call("ats_moe_ep_segments", rk.data_ptr(), W, Ep, C, L, seg_ws.data_ptr(), segb, st)
@@ -860,10 +863,20 @@ class _EPDeviceFn(torch.autograd.Function):
             yr = ps.local["yr"][p * part_rows:(p + 1) * part_rows]
             h = torch.empty((part_rows, 2 * Fdim), dtype=x2.dtype, device=dev)
             a = torch.empty((part_rows, Fdim), dtype=x2.dtype, device=dev)
-            _lib.call("ats_moe_ep_experts_fwd", xr.data_ptr(), wgu_stack[p * Ep].data_ptr(),
-                      wd_stack[p * Ep].data_ptr(), h.data_ptr(), a.data_ptr(), yr.data_ptr(), dt, W, Ep, C, H, Fdim,
-                      seg_ws.data_ptr(), segb, st)
             keep.extend([h, a, seg_ws])
+            return p, xr, yr, h, a, seg_ws
+
+        def experts_run(bufs, sources=None):  # sources: a range of source ranks, or all
+            p, xr, yr, h, a, seg_ws = bufs
+            args = (xr.data_ptr(), wgu_stack[p * Ep].data_ptr(), wd_stack[p * Ep].data_ptr(), h.data_ptr(),
+                    a.data_ptr(), yr.data_ptr(), dt, W, Ep, C, H, Fdim, seg_ws.data_ptr(), segb)
+            if sources is None:
+                _lib.call("ats_moe_ep_experts_fwd", *args, st)
+            elif sources[0] < sources[1]:
+                _lib.call("ats_moe_ep_experts_fwd_sources", *args, sources[0], sources[1], st)
+
+        def experts(p):
+            experts_run(experts_prep(p))
 
         cur = torch.cuda.current_stream(dev)
         if parts > 1 and comm_sms > 0:
@@ -894,6 +907,35 @@ class _EPDeviceFn(torch.autograd.Function):
             _mark("experts")
             cur.wait_stream(back_s)
             _mark("exchange_back")
+        elif parts == 1 and comm_sms > 0 and _OWN_ROWS_FIRST:
+            # this rank's rows for its own experts need no transfer: they are stored locally, and their expert
+            # GEMMs run on the other SMs while the rows for the other ranks go out (and theirs come in) on a side
+            # stream with comm_sms SMs; the other sources' rows follow once the all-reduce says they landed
+            def push_split(to_self, sms, stream):
+                _lib.call("ats_moe_ep_push_split", x2.data_ptr(), row_token.data_ptr(), T,
+                          *_exchange_args(allv, W, me, El, 1, 0, 1, ps.table("xr"), part_rows, H, dt)[:-1],
+                          1 if to_self else 0, sms, stream.cuda_stream)
+
+            bufs = experts_prep(0)
+            push_split(True, 0, cur)
+            side = state.copy_streams(dev, max(W, 2))[0]
+            side.wait_stream(cur)
+            with torch.cuda.stream(side):
+                push_split(False, comm_sms, side)
+                dist.all_reduce(flag, group=group)
+            for t in (x2, row_token, allv, flag):
+                t.record_stream(side)
+            nsm = torch.cuda.get_device_properties(dev).multi_processor_count
+            with _lib.gemm_sm_limit(max(1, nsm - comm_sms)):
+                experts_run(bufs, (me, me + 1))
+            _mark("experts_own")
+            cur.wait_stream(side)
+            _mark("exchange_out")
+            experts_run(bufs, (0, me))
+            experts_run(bufs, (me + 1, W))
+            _mark("experts")
+            dist.all_reduce(flag, group=group)
+            _mark("exchange_back_flag")
         else:
             push(0, parts, 0, cur)
             _mark("exchange_push")

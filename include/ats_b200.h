@@ -337,6 +337,14 @@ ATS_API int ats_moe_ep_experts_fwd(const void* xr, const void* w_gate_up, const 
                            void* h, void* a, void* y, ats_dtype dtype, int W, int E_local,
                            int64_t capacity, int64_t H, int64_t F,
                            const void* seg_workspace, size_t seg_workspace_bytes, void* stream);
+/* ats_moe_ep_experts_fwd on the segments of source ranks [src_lo, src_hi) only
+ * (segments are source-major, so they are one range): the rows a rank keeps
+ * for its own experts can run while the other ranks' rows are in flight.  The
+ * same h, a and y rows as the full call. */
+ATS_API int ats_moe_ep_experts_fwd_sources(const void* xr, const void* w_gate_up, const void* w_down,
+                           void* h, void* a, void* y, ats_dtype dtype, int W, int E_local,
+                           int64_t capacity, int64_t H, int64_t F, const void* seg_workspace,
+                           size_t seg_workspace_bytes, int src_lo, int src_hi, void* stream);
 ATS_API int ats_moe_ep_experts_bwd(const void* dy, const void* xr, const void* h, const void* a,
                            const void* w_gate_up, const void* w_down,
                            void* dh, void* dxr, void* dw_gate_up, void* dw_down, ats_dtype dtype,
@@ -369,6 +377,12 @@ ATS_API int ats_moe_ep_push(const void* src, const int32_t* row_token, int64_t s
                             const int32_t* counts, int W, int me, int E_local, int parts,
                             int part_lo, int part_hi, const uint64_t* peer_bufs, int64_t part_rows,
                             int64_t hidden, ats_dtype dtype, int sms, void* stream);
+/* ats_moe_ep_push of only the rows whose expert rank is this rank (to_self
+ * nonzero: local stores into its own buffer) or only the others' (zero). */
+ATS_API int ats_moe_ep_push_split(const void* src, const int32_t* row_token, int64_t src_rows,
+                            const int32_t* counts, int W, int me, int E_local, int parts,
+                            int part_lo, int part_hi, const uint64_t* peer_bufs, int64_t part_rows,
+                            int64_t hidden, ats_dtype dtype, int to_self, int sms, void* stream);
 ATS_API int ats_moe_ep_pull(void* dst, int64_t dst_rows, const int32_t* counts, int W, int me,
                             int E_local, int parts, int part_lo, int part_hi,
                             const uint64_t* peer_bufs, int64_t part_rows, int64_t hidden,

@@ -1,5 +1,6 @@
-"""The device-driven row exchange kernels (``ats_moe_ep_push``, ``_pull``,
-``_zero_padding``) on one GPU, with W ranks emulated by W buffers.
+"""The device-driven row exchange kernels (``ats_moe_ep_push``, ``_push_split``,
+``_pull``, ``_zero_padding``, ``_combine``) on one GPU, with W ranks emulated by
+W buffers.
 
 Each emulated rank holds kept rows in the packed layout (segment sizes its
 kept counts rounded up to 128) and an expert-side buffer.  Every rank pushes
@@ -75,12 +76,15 @@ def test_push_pull_and_padding_match_the_copy_plan(W, El, parts, C, H, tokens):
                   part_rows, H, _lib.ATS_BF16, st)
     for s in range(W):
         if tokens:
-            _lib.call("ats_moe_ep_push", toks[s].data_ptr(), row_tok[s].data_ptr(), toks[s].shape[0],
-                      counts.data_ptr(), W, s, El, parts, 0, parts, table.data_ptr(), part_rows, H, _lib.ATS_BF16,
-                      0, st)
+            src_args = (toks[s].data_ptr(), row_tok[s].data_ptr(), toks[s].shape[0])
         else:
-            _lib.call("ats_moe_ep_push", srcs[s].data_ptr(), None, srcs[s].shape[0], counts.data_ptr(), W, s, El,
-                      parts, 0, parts, table.data_ptr(), part_rows, H, _lib.ATS_BF16, 0, st)
+            src_args = (srcs[s].data_ptr(), None, srcs[s].shape[0])
+        xargs = (counts.data_ptr(), W, s, El, parts, 0, parts, table.data_ptr(), part_rows, H, _lib.ATS_BF16)
+        if s % 2:  # the rows for the rank itself, then the others' (ats_moe_ep_push_split): one push together
+            for to_self in (1, 0):
+                _lib.call("ats_moe_ep_push_split", *src_args, *xargs, to_self, 0, st)
+        else:
+            _lib.call("ats_moe_ep_push", *src_args, *xargs, 0, st)
     torch.cuda.synchronize()
     code = ctypes.c_int(0)
     assert _lib.query("ats_device_status", ctypes.byref(code)) == 0 and code.value == 0
