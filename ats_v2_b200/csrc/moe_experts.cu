@@ -204,6 +204,7 @@ struct EpSegs {
   int* expert;
   int* eseg;
   int* err;
+  int* kept;
 };
 
 size_t ep_carve(void* ws, int W, int El, EpSegs* o) {
@@ -221,6 +222,7 @@ size_t ep_carve(void* ws, int W, int El, EpSegs* o) {
   q.expert = (int*)take(n * 4);
   q.eseg = (int*)take(n * 4);
   q.err = (int*)take(4);
+  q.kept = (int*)take(n * 4);
   if (o) *o = q;
   return off;
 }
@@ -248,6 +250,7 @@ int ep_table(const void* ws, size_t bytes, int W, int El, int64_t C, SegTable* s
   sg->max_rows = (int64_t)W * El * slot_rows(C);
   sg->max_seg_rows = slot_rows(C);
   sg->err = q.err;
+  sg->kept = q.kept;
   return ATS_OK;
 }
 
@@ -259,9 +262,9 @@ __global__ void ep_segments_kernel(const int* __restrict__ recv_kept, int W, int
   __shared__ int wsum[32];
   const int n = W * El;  // <= kMaxExperts = blockDim.x
   const int s = threadIdx.x, lane = s & 31, warp = s >> 5;
-  int rows = 0;
+  int rows = 0, kept = 0;
   if (s < n) {
-    int kept = recv_kept[s];
+    kept = recv_kept[s];
     kept = kept < 0 ? 0 : (kept > Cp ? Cp : kept);
     rows = (kept + kSegAlign - 1) / kSegAlign * kSegAlign;
   }
@@ -291,6 +294,7 @@ __global__ void ep_segments_kernel(const int* __restrict__ recv_kept, int W, int
     q.rows[s] = rows;
     q.expert[s] = el;
     q.eseg[el * W + src] = s;
+    q.kept[s] = kept;
   }
   if (s == 0) q.err[0] = 0;
 }

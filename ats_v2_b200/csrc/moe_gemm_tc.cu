@@ -116,6 +116,15 @@ __device__ __forceinline__ int group_tiles(const GemmArgs& p, int g) {
   return ((KGROUP ? p.M : p.seg.rows[g]) + TM - 1) / TM * n_tiles<BN, KGROUP, EPI>(p);
 }
 
+// Rows a K-grouped GEMM reduces over in segment s: its kept rows rounded up to one K block (the rest of the
+// segment is zero padding), or all its rows when the table has no kept counts.
+__device__ __forceinline__ int seg_krows(const SegTable& sg, int s) {
+  const int r = sg.rows[s];
+  if (sg.kept == nullptr) return r;
+  const int k = (sg.kept[s] + BK - 1) / BK * BK;
+  return k < 0 ? 0 : (k < r ? k : r);
+}
+
 // Walks the groups in order: a role visits its tiles t = blockIdx.x + i*gridDim.x in increasing order,
 // so a cursor (group, first tile of the group) that only moves forward decodes every tile.
 struct TileCursor {
@@ -146,7 +155,7 @@ __device__ __forceinline__ void decode_tile(const GemmArgs& p, TileCursor& cur, 
   if (KGROUP) {
     ti.e = g;
     int kb = 0;
-    for (int u = 0; u < p.seg.spe; ++u) kb += p.seg.rows[p.seg.eseg[g * p.seg.spe + u]] / BK;
+    for (int u = 0; u < p.seg.spe; ++u) kb += seg_krows(p.seg, p.seg.eseg[g * p.seg.spe + u]) / BK;
     ti.kb = kb * SPLIT;
   } else {
     ti.e = p.seg.expert[g];
@@ -364,7 +373,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
         int seg_kb = 0, seg_r0 = KGROUP ? 0 : p.seg.row0[ti.g];
         if (KGROUP) {
           const int s0 = p.seg.eseg[ti.g * p.seg.spe];
-          seg_kb = p.seg.rows[s0] / BK;
+          seg_kb = seg_krows(p.seg, s0) / BK;
           seg_r0 = p.seg.row0[s0];
         }
         const int b_row0 = ti.e * p.b.group_rows;
@@ -379,7 +388,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
               ++u;
               lkb = 0;
               const int sn = p.seg.eseg[ti.g * p.seg.spe + u];
-              seg_kb = p.seg.rows[sn] / BK;
+              seg_kb = seg_krows(p.seg, sn) / BK;
               seg_r0 = p.seg.row0[sn];
             }
           }

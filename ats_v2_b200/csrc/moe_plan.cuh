@@ -30,6 +30,9 @@ struct SegTable {
   int64_t max_rows;      // rows of the permuted buffers
   int64_t max_seg_rows;  // upper bound of rows[s]
   int* err;              // device status word
+  const int* kept = nullptr;  // [nseg] kept (non-padding) rows of the segment, or null: every row.  The
+                              // K-grouped GEMMs reduce over them rounded up to 64 (one K block), not over
+                              // the zero padding to 128
 };
 
 struct MoePlan {
@@ -146,6 +149,7 @@ inline SegTable plan_segments(const MoePlan& p) {
   const int64_t per = p.C < p.T ? p.C : p.T;
   s.max_seg_rows = (int64_t)align_up((size_t)(per > 0 ? per : 1), kSegAlign);
   s.err = p.dev_err;
+  s.kept = p.kept;
   return s;
 }
 
