@@ -163,23 +163,24 @@ __device__ __forceinline__ void decode_tile(const GemmArgs& p, TileCursor& cur, 
   }
 }
 
-// Ring of a launch: one A tile (128 x 64) and BPARTS B tiles per stage; a CTA of a pair holds half of the
-// B rows.  Every launch fills the same 192 KB with as many stages as fit (4 for 128 x 256 tiles, 6 for
-// 128 x 128 tiles or pair halves): the GEMMs wait on load latency, and more bytes in flight hide more of it.
-constexpr int kRingBytes = STAGES * (BM * BK * 2 + 256 * BK * 2);
-__host__ __device__ constexpr int stage_bytes(int bn, int bparts, bool pair) {
-  return BM * BK * 2 + bparts * (pair ? bn / 2 : bn) * BK * 2;
-}
-__host__ __device__ constexpr int ring_stages(int bn, int bparts, bool pair) {
-  return kRingBytes / stage_bytes(bn, bparts, pair);
-}
-
 // Shared memory of the epilogue's staging boxes: the bf16-output epilogues write through them.
 __host__ __device__ constexpr int staging_bytes(int epi) {
   return (epi == EPI_STORE || epi == EPI_SWIGLU_FWD || epi == EPI_SWIGLU_BWD || epi == EPI_SCATTER ||
           epi == EPI_ROPE)
              ? kEpiWarps * kBoxesPerWarp * kStageBox
              : 0;
+}
+
+// Ring of a launch: one A tile (128 x 64) and BPARTS B tiles per stage; a CTA of a pair holds half of the
+// B rows.  Every launch fills the same 224 KB, less its epilogue's staging boxes, with as many stages as
+// fit (4 for 128 x 256 tiles, 6 for 128 x 128 tiles or pair halves, 5 for the float32 router tiles, which
+// stage nothing): the GEMMs wait on load latency, and more bytes in flight hide more of it.
+constexpr int kRingBytes = STAGES * (BM * BK * 2 + 256 * BK * 2);
+__host__ __device__ constexpr int stage_bytes(int bn, int bparts, bool pair) {
+  return BM * BK * 2 + bparts * (pair ? bn / 2 : bn) * BK * 2;
+}
+__host__ __device__ constexpr int ring_stages(int bn, int bparts, bool pair, int epi) {
+  return (kRingBytes + kEpiWarps * kBoxesPerWarp * kStageBox - staging_bytes(epi)) / stage_bytes(bn, bparts, pair);
 }
 
 // One epilogue warp's bf16 output path: a 32 x 32 chunk (row = lane, 32 packed bf16 pairs per lane
@@ -264,7 +265,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const __grid_const
   constexpr uint32_t B_BYTES = B_ROWS * BK * 2;
   constexpr uint32_t STAGE_BYTES = A_BYTES + BPARTS * B_BYTES;  // one A tile, BPARTS B tiles
   static_assert(STAGE_BYTES == (uint32_t)stage_bytes(BN, BPARTS, PAIR), "stage layout");
-  constexpr int NST = ring_stages(BN, BPARTS, PAIR);
+  constexpr int NST = ring_stages(BN, BPARTS, PAIR, EPI);
   constexpr int TM = PAIR ? 2 * BM : BM;  // rows of an output tile
   static_assert(SPLIT == 1 || BPARTS == 1, "operand parts along K or in the stage, not both");
   static_assert(!PAIR || (SPLIT == 1 && BPARTS == 1 && (BN == 128 || BN == 256) &&
@@ -912,7 +913,7 @@ int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& p, i
   auto kfn = tc_gemm_kernel<BN, A_MN, B_MN, EPI, KGROUP, SPLIT, BPARTS, PAIR>;
   if (staging_bytes(EPI) > 0 && to == nullptr) return fail(ATS_EBADARG, "moe_gemm: bf16 epilogue needs an output map");
   if (EPI == EPI_SWIGLU_FWD && to2 == nullptr) return fail(ATS_EBADARG, "moe_gemm: SwiGLU epilogue needs the a map");
-  const int smem = 1024 + ring_stages(BN, BPARTS, PAIR) * stage_bytes(BN, BPARTS, PAIR) + staging_bytes(EPI);
+  const int smem = 1024 + ring_stages(BN, BPARTS, PAIR, EPI) * stage_bytes(BN, BPARTS, PAIR) + staging_bytes(EPI);
   cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return fail(ATS_ECUDA, "moe_gemm: smem attribute: %s", cudaGetErrorString(e));
   const CUtensorMap& mo = to != nullptr ? *to : ta;
